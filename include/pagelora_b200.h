@@ -1,0 +1,311 @@
+/*
+ * pagelora_b200.h -- C ABI of the B200 (sm_100a) PageLoRA decode hot path.
+ *
+ * Every entry point takes raw device pointers, sizes, strides (in elements)
+ * and a CUDA stream (`void *stream` is a cudaStream_t; NULL = legacy default
+ * stream).  Nothing here allocates device memory, synchronises the stream or
+ * throws: every function returns a pl_status and kernels that detect bad
+ * input at run time (a page id outside the pool, a malformed span) write a
+ * pl_status code into the caller-owned device word `status_dev` (an int32
+ * the caller zeroes once and reads whenever it wants to check).  All
+ * launches are capturable in a CUDA graph.
+ *
+ * Tensor dtypes: bf16 activations / weights / KV, fp32 partial states,
+ * int32 page-table metadata, matching the reference's defaults.
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths relative to the PageLoRA project root).
+ */
+#ifndef PAGELORA_B200_H_
+#define PAGELORA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PL_ABI_VERSION 1
+
+typedef enum pl_status {
+  PL_OK = 0,
+  PL_ERR_INVALID_ARGUMENT = 1,   /* null pointer, negative size, bad stride        */
+  PL_ERR_UNSUPPORTED = 2,        /* head_dim / page_size / group / K not compiled   */
+  PL_ERR_PAGE_OUT_OF_RANGE = 3,  /* device: a page id >= num_pages (access skipped)  */
+  PL_ERR_WORKSPACE_TOO_SMALL = 4,
+  PL_ERR_SPAN_START = 5,         /* "page spans must start at page offset 0"        */
+  PL_ERR_SPAN_LENGTH = 6,        /* "page span length is out of range"              */
+  PL_ERR_SPAN_NOT_FULL = 7,      /* "non-last page spans must be full pages"        */
+  PL_ERR_CUDA = 8,               /* a CUDA runtime call failed (see pl_last_cuda_error) */
+  PL_ERR_TIMEOUT = 9,            /* device: a bounded wait ran out (kernel returned) */
+  PL_ERR_NO_DEVICE = 10
+} pl_status;
+
+/* ---------------------------------------------------------------- library */
+
+/* ABI version (PL_ABI_VERSION) of the loaded library. */
+int32_t pl_abi_version(void);
+
+/* Human-readable name of a status code. */
+const char *pl_status_string(int32_t status);
+
+/* cudaGetErrorString of the last CUDA failure seen by this library on the
+ * calling thread ("" if none). */
+const char *pl_last_cuda_error(void);
+
+/* Number of SMs of the current device (cached per device), or -1. */
+int32_t pl_device_sm_count(void);
+
+/* ------------------------------------------------------------ page tables */
+
+/*
+ * Build CSR page tables from per-row KV block spans, on the device.
+ * Replaces model/kvcache/flashinfer_page_table.py:137-181
+ * (build_flashinfer_page_table / build_flashinfer_batch_page_table) and
+ * the buffer updates at :40-59 and :89-121, including the coalescing of
+ * adjacent slices of one page (:184-197) and the validation (:200-221).
+ *
+ * Input (device, int32): spans of row r are span_* [row_indptr[r],
+ * row_indptr[r+1]).  Output (device, int32): out_indptr[num_rows+1],
+ * out_indices[<= num_spans], out_last_page_len[num_rows].
+ * On a malformed span nothing is written; *status_dev receives
+ * PL_ERR_SPAN_START / _LENGTH / _NOT_FULL of the first failing coalesced
+ * span in row order and *err_row_dev (nullable) its row.
+ * Single launch; num_rows <= 4096, num_spans < 2^31.
+ */
+int32_t pl_page_table_build(const int32_t *span_block_id,
+                            const int32_t *span_start,
+                            const int32_t *span_length,
+                            const int32_t *row_indptr,
+                            int32_t num_rows, int32_t page_size,
+                            int32_t *out_indptr, int32_t *out_indices,
+                            int32_t *out_last_page_len,
+                            int32_t *status_dev, int32_t *err_row_dev,
+                            void *stream);
+
+/*
+ * Advance a device-resident page table by one decode token per row without
+ * any host work (graph-replayable).  Row r keeps its pages in
+ * row_pages[r*row_capacity + 0 .. row_num_pages[r]); the row grows by one
+ * slot and, when it is empty or its last page is full, the page
+ * new_page_ids[r] is appended first.  Writes the append slot of the new
+ * token (slot_page_id[r], slot_offset[r]) and, when positions_out is not
+ * NULL, its position (tokens in the row - 1), updates row_num_pages and
+ * last_page_len in place, and rebuilds the contiguous CSR page table
+ * (out_indptr[num_rows+1], out_indices) that pl_paged_decode reads.
+ * No reference counterpart as a kernel: it replaces the per-token host
+ * rebuild of model/flashinfer/generation.py:188-247 (_plan_decode*) and
+ * paged_kvcache_manager.py:195-213 (reserve_chunk) for one-token chunks.
+ * Single launch; num_rows <= 4096.
+ */
+int32_t pl_page_table_advance(int32_t *row_num_pages, int32_t *last_page_len,
+                              int32_t *row_pages, const int32_t *new_page_ids,
+                              int32_t num_rows, int32_t row_capacity,
+                              int32_t page_size, int32_t *out_indptr,
+                              int32_t *out_indices, int32_t *slot_page_id,
+                              int32_t *slot_offset, int32_t *positions_out,
+                              int32_t *status_dev, void *stream);
+
+/* ------------------------------------------------------- decode attention */
+
+typedef struct pl_decode_plan_t {
+  int32_t num_splits;        /* KV splits per (row, kv head); 1 = no merge      */
+  int32_t ctas;              /* grid size = batch * num_kv_heads * num_splits   */
+  int64_t workspace_bytes;   /* bytes of workspace pl_paged_decode needs         */
+} pl_decode_plan_t;
+
+/*
+ * Host planning of one decode step (no device access, no sync).
+ * Replaces model/flashinfer/attention_backend.py:63-118 (plan_decode) and
+ * the FlashInfer plan() it calls (:229-285): picks the split-KV factor so
+ * that batch*num_kv_heads*num_splits fills the device.  total_pages is an
+ * upper bound of the pages of all rows (e.g. indices.numel()).
+ */
+int32_t pl_decode_plan(int32_t batch, int32_t num_qo_heads,
+                       int32_t num_kv_heads, int32_t head_dim,
+                       int32_t page_size, int64_t total_pages,
+                       int32_t max_splits, pl_decode_plan_t *plan_out);
+
+/*
+ * Paged GQA decode attention, one query token per row.
+ * Replaces attention_backend.py:120-131 (run_decode) and FlashInfer's
+ * BatchDecodeWithPagedKVCacheWrapper.run it wraps.
+ *
+ *   q        bf16 [batch, num_qo_heads, head_dim], strides (q_stride_b, q_stride_h)
+ *   kv_cache bf16 NHD pool of ONE layer [num_pages, 2, page_size, num_kv_heads, head_dim]
+ *            (K at [:,0], V at [:,1]), contiguous (paged_kv_store.py:559-570)
+ *   indptr/indices/last_page_len int32 CSR page table (device)
+ *   out      bf16 [batch, num_qo_heads, head_dim] (strides as q's, o_stride_*)
+ *   out_lse  fp32 [batch, num_qo_heads] natural-log LSE, nullable
+ *   sm_scale softmax scale applied to q.k (the reference's
+ *            (q / 16) * (16 / sqrt(D)) == q / sqrt(D))
+ *   num_splits from pl_decode_plan; with num_splits > 1 the partial states
+ *            go to `workspace` and the last CTA of each (row, kv head) merges
+ *            them (no second launch).  The first 4*batch*num_kv_heads bytes of
+ *            the workspace are arrival counters that must be zero before the
+ *            first call; every call leaves them zero again.
+ * Supported: head_dim 64 or 128, page_size 16 or 32, group (qo/kv) <= 16.
+ * A row with no pages yields O = 0 and LSE = -inf.
+ */
+int32_t pl_paged_decode(const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                        const void *kv_cache, int64_t num_pages,
+                        const int32_t *indptr, const int32_t *indices,
+                        const int32_t *last_page_len,
+                        int32_t batch, int32_t num_qo_heads,
+                        int32_t num_kv_heads, int32_t head_dim,
+                        int32_t page_size, float sm_scale,
+                        int32_t num_splits,
+                        void *out, int64_t o_stride_b, int64_t o_stride_h,
+                        float *out_lse,
+                        void *workspace, int64_t workspace_bytes,
+                        int32_t *status_dev, void *stream);
+
+/*
+ * Merge S partial attention states per (row, head) by log-sum-exp.
+ * No reference counterpart in the project (FlashInfer merges internally);
+ * it is the merge step of split-KV decode and of the cross-GPU split-KV
+ * path (partials gathered over NCCL).
+ *   v_partial   fp32 [num_rows, num_states, head_dim] (row = (batch, head))
+ *   lse_partial fp32 [num_rows, num_states] natural log; -inf = empty state
+ *   out         bf16 [num_rows, head_dim] (row stride out_stride), out_lse nullable
+ */
+int32_t pl_merge_states(const float *v_partial, const float *lse_partial,
+                        int32_t num_rows, int32_t num_states,
+                        int32_t head_dim, void *out, int64_t out_stride,
+                        float *out_lse, void *stream);
+
+/* --------------------------------------------------------------- LoRA path */
+
+/*
+ * Segment-grouped LoRA shrink: down[t, :] = x[t, :] . A[adapter(seg(t))]^T
+ * Replaces the x.A^T half of multilora/linear.py:226-227 and
+ * model/flashinfer/packed_ops.py:324 (F.linear(hidden, packed.a)).
+ *   x      bf16 [num_tokens, in_features] (row stride x_stride)
+ *   a      bf16 [num_adapters, rank, in_features] (stacked, contiguous)
+ *   seg_indptr int32 [num_segments+1] token ranges, seg_adapter int32
+ *          [num_segments] adapter index (-1 = no LoRA: writes zeros)
+ *   down   fp32 [num_tokens, rank] (row stride down_stride)
+ */
+int32_t pl_lora_shrink_seg(const void *x, int64_t x_stride,
+                           const void *a, int32_t num_adapters,
+                           int32_t rank, int32_t in_features,
+                           const int32_t *seg_indptr,
+                           const int32_t *seg_adapter, int32_t num_segments,
+                           int32_t num_tokens,
+                           float *down, int64_t down_stride, void *stream);
+
+/* Epilogue/prologue selectors of pl_linear_lora_expand_fused. */
+#define PL_PROLOGUE_NONE 0     /* x used as given                                    */
+#define PL_PROLOGUE_RMSNORM 1  /* x <- bf16(x * rsqrt(mean(x^2)+eps) * norm_w)       */
+#define PL_PROLOGUE_SILU_MUL 2 /* x[t] <- bf16(silu(x[t,:K]) * x[t,K:2K]) (gate_up)  */
+#define PL_FLAG_WEIGHTS_STATIC 1
+
+/*
+ * Base projection with the LoRA expand and residual fused into its epilogue:
+ *   base   = x . W^T (+ bias)                              (W bf16 [n_out, K])
+ *   delta  = bf16( B_s[adapter(t)][o, :] . bf16(down[t, roff(o) : roff(o)+rank]) )
+ *   y      = bf16( bf16(base) + delta )                     (lora_b != NULL)
+ *   y      = bf16( residual + bf16(y) )                     (residual != NULL)
+ * roff(o) = rank * (slice of o), slices are [0, slice_end[0]), [slice_end[0],
+ * slice_end[1]), ... (up to 4, e.g. q/k/v) -- the packed block-diagonal B of
+ * packed_ops.py:328-384 without its zero blocks.  B_s holds B * scale
+ * (bf16, [num_adapters, n_out, rank]); adapter(t) = tok_adapter[t] (device,
+ * -1 = none) or 0 when tok_adapter is NULL.
+ * Optionally extra "shrink rows": rows n_out .. n_out+n_shrink of the
+ * weight stream are taken from shrink_a (bf16 [n_shrink, K]) and their
+ * fp32 results x . shrink_a^T are written to shrink_out[t, :] (row stride
+ * shrink_stride) -- the LoRA shrink of the NEXT stage fused into this pass.
+ * Replaces packed_ops.py:105-165 (project_qkv_packed), :251-265
+ * (project_linear), :314-325 (_packed_lora_delta) and
+ * multilora/linear.py:200-231 (LoRALinear.forward) for num_tokens <= 8.
+ * The input prologue (PL_PROLOGUE_*) folds the preceding RMSNorm
+ * (model/flashinfer/norm.py:15-24) or SiLU-and-mul (packed_ops.py:230-239).
+ * Requires K % 16 == 0; x rows are read with stride x_stride.
+ * slice_end is a HOST array (num_slices-1 row bounds, read during the call).
+ * flags: PL_FLAG_WEIGHTS_STATIC lets the kernel stream w / shrink_a before
+ * the preceding kernel on the stream has finished (programmatic dependent
+ * launch); pass it only when no upstream kernel writes those weights.
+ */
+int32_t pl_linear_lora_expand_fused(
+    const void *x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
+    int32_t prologue, const void *norm_w, float norm_eps,
+    const void *w, int32_t n_out, const void *bias,
+    const float *lora_down, int64_t down_stride, const void *lora_b,
+    int32_t lora_rank, const int32_t *slice_end, int32_t num_slices,
+    const int32_t *tok_adapter,
+    const void *residual, int64_t res_stride,
+    void *y, int64_t y_stride,
+    const void *shrink_a, int32_t n_shrink, float *shrink_out,
+    int64_t shrink_stride, int32_t flags,
+    int32_t *status_dev, void *stream);
+
+/*
+ * Merged ("effective") weight builder: w_out = w_in + sign * scale * (B @ A)
+ * with the reference's rounding points (bf16 tensors):
+ *   mode 0: bf16(w + bf16(bf16(B@A) * scale))  -- linear.py:143-146,166-172
+ *                                                 and effective_weights.py:70-72
+ *   mode 1: bf16(w + scale * bf16(B@A))        -- effective_weights.py:111-113
+ *   sign -1 is unmerge (linear.py:157-159).  w_out may alias w_in.
+ *   w bf16 [n_out, k_in]; a bf16 [rank, k_in]; b bf16 [n_out, rank].
+ */
+int32_t pl_lora_merge_weight(const void *w_in, void *w_out, const void *a,
+                             const void *b, int32_t n_out, int32_t k_in,
+                             int32_t rank, float scale, int32_t sign,
+                             int32_t mode, void *stream);
+
+/* ------------------------------------------------- decode-step glue kernels */
+
+/*
+ * Scatter one token per row into the paged KV pool (NHD layout).
+ * Replaces model/flashinfer/layer_runner.py:399-412 (_append_decode_kv_static)
+ * and paged_kv_append.py:45-118 for single-token rows.
+ *   k, v bf16 [num_tokens, num_kv_heads, head_dim] (row strides k_stride/v_stride)
+ *   page_id/page_offset int32 [num_tokens]
+ */
+int32_t pl_kv_append(const void *k, int64_t k_stride, const void *v,
+                     int64_t v_stride, void *kv_cache, int64_t num_pages,
+                     const int32_t *page_id, const int32_t *page_offset,
+                     int32_t num_tokens, int32_t num_kv_heads,
+                     int32_t head_dim, int32_t page_size,
+                     int32_t *status_dev, void *stream);
+
+/*
+ * Post-projection step of one decode token: optional packed-LoRA expand
+ * (when lora_down != NULL, same rounding as pl_linear_lora_expand_fused),
+ * optional per-head RMSNorm of q and k (Qwen3 q_norm / k_norm with the HF
+ * module's rounding), RoPE (non-interleaved, theta, positions) on q and k,
+ * then K/V appended to the paged pool and q written for attention.
+ * Replaces model/flashinfer/projection.py:34-190 (head norms +
+ * apply_rope_pos_ids) and layer_runner.py:310-329 (static append).
+ *   qkv bf16 [num_tokens, (Hq+2*Hkv)*D] row stride qkv_stride
+ *   lora_b bf16 [num_adapters, (Hq+2*Hkv)*D, rank] (scale folded), slices q/k/v
+ *   positions int32 [num_tokens]; q_out bf16 [num_tokens, Hq, D]
+ */
+int32_t pl_qkv_rope_append(const void *qkv, int64_t qkv_stride,
+                           const float *lora_down, int64_t down_stride,
+                           const void *lora_b, int32_t lora_rank,
+                           const int32_t *tok_adapter,
+                           const void *q_norm_w, const void *k_norm_w,
+                           float norm_eps, const int32_t *positions,
+                           float rope_theta, void *q_out, void *kv_cache,
+                           int64_t num_pages, const int32_t *page_id,
+                           const int32_t *page_offset, int32_t num_tokens,
+                           int32_t num_qo_heads, int32_t num_kv_heads,
+                           int32_t head_dim, int32_t page_size,
+                           int32_t *status_dev, void *stream);
+
+/* out[t, :] = table[token_ids[t], :] (bf16 rows of width dim). */
+int32_t pl_embed(const int64_t *token_ids, const void *table, int64_t vocab,
+                 int32_t dim, int32_t num_tokens, void *out,
+                 int32_t *status_dev, void *stream);
+
+/* First-index argmax over bf16 rows: out_ids[t] = argmax(logits[t, :vocab]).
+ * Replaces model/flashinfer/sampling.py:8-15 (greedy_argmax_token). */
+int32_t pl_argmax(const void *logits, int64_t stride, int32_t vocab,
+                  int32_t num_tokens, int64_t *out_ids, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PAGELORA_B200_H_ */

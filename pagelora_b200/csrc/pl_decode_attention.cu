@@ -1,0 +1,595 @@
+// Paged-KV GQA decode attention for sm_100a, plus the split-KV LSE merge.
+//
+// One CTA per (row, kv head, kv split).  All `group` query heads that share
+// the kv head sit in one CTA, so each KV page is read from HBM exactly once.
+// Warp 0 is the producer: one lane walks the page table and issues TMA tile
+// loads (one 64-dim x page_size box per half head, 128B-swizzled) into a
+// ring of shared-memory stages, each guarded by a full/empty mbarrier pair.
+// Warps 1..4 are consumers: each takes whole pages round-robin and runs
+// Q.K^T and P.V on the tensor cores (mma.sync m16n8k16, fp32 accumulate;
+// query heads are the M rows, only `group` of 16 used) with an online
+// softmax in the log2 domain.  The four per-warp states are merged through
+// shared memory; with several splits the partial states go to the
+// workspace and the last CTA of each (row, kv head) to arrive merges them,
+// so split-KV needs no second launch.
+//
+// Semantics follow model/flashinfer/attention_backend.py:97,120-131:
+// O = softmax((q/16) . K^T * 16/sqrt(D)) . V = softmax(q.K^T * sm_scale) . V
+// over the pages indices[indptr[b] .. indptr[b+1]) of the NHD pool
+// [P, 2, page_size, Hkv, D]; the last page holds last_page_len[b] tokens.
+#include <mutex>
+
+#include "pl_common.cuh"
+
+namespace pl {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeThreads = 32 * (1 + kConsumerWarps);
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct DecodeArgs {
+  const bf16* q;
+  int64_t q_stride_b, q_stride_h;
+  const int32_t* indptr;
+  const int32_t* indices;
+  const int32_t* last_page_len;
+  int64_t num_pages;
+  int32_t num_qo_heads, num_kv_heads, group;
+  float scale_log2;  // sm_scale * log2(e)
+  int32_t num_splits;
+  bf16* out;
+  int64_t o_stride_b, o_stride_h;
+  float* out_lse;       // natural log, nullable
+  int32_t* counters;    // [batch * Hkv], zero between calls
+  float* partial_o;     // [batch, Hq, splits, D]
+  float* partial_lse;   // [batch, Hq, splits] (log2 domain)
+  int32_t* status;
+};
+
+template <int D, int PS>
+struct DecodeCfg {
+  static constexpr int kHalves = D / 64;              // 64-dim (128 B) boxes per tile
+  static constexpr int kHalfBytes = PS * 128;         // one box: PS rows x 128 B
+  static constexpr int kTileBytes = kHalves * kHalfBytes;  // K (or V) of one page/head
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kStages = (65536 / kStageBytes) < 4 ? 4 : ((65536 / kStageBytes) > 8 ? 8 : 65536 / kStageBytes);
+  static constexpr int kQRowBytes = D * 2 + 16;       // padded rows: conflict-free ldmatrix
+  static constexpr int kNT = PS / 8;                  // score n-tiles per page
+  static constexpr int kDT = D / 8;                   // output n-tiles
+  // shared-memory carve-up (offsets from a 1024-aligned base)
+  static constexpr int kStageOff = 0;
+  static constexpr int kQOff = kStages * kStageBytes;
+  static constexpr int kMLOff = kQOff + 16 * kQRowBytes;                 // [warps][16] m, l
+  static constexpr int kBarOff = kMLOff + 2 * kConsumerWarps * 16 * 4;   // full[], empty[]
+  static constexpr int kNtokOff = kBarOff + 2 * kStages * 8;
+  static constexpr int kFlagOff = kNtokOff + kStages * 4;
+  static constexpr int kSmemBytes = kFlagOff + 16 + 1024;  // + alignment slack
+  static_assert(kConsumerWarps * 16 * D * 4 <= kStages * kStageBytes, "merge scratch must fit the stage ring");
+};
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128B-swizzled box.
+__device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+template <int D, int PS>
+__global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                                       const DecodeArgs args) {
+  using C = DecodeCfg<D, PS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* empty_bar = full_bar + C::kStages;
+  int32_t* stage_ntok = reinterpret_cast<int32_t*>(smem + C::kNtokOff);
+  volatile int32_t* flags = reinterpret_cast<volatile int32_t*>(smem + C::kFlagOff);  // [0]=abort [1]=is_last
+  float* ml = reinterpret_cast<float*>(smem + C::kMLOff);                            // m[w][16], l[w][16]
+
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int group = args.group;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x == 32) prefetch_tensormap(&kv_map);
+  __syncthreads();
+
+  pdl_launch_dependents();
+  pdl_wait();  // q, the page table and the freshly appended KV come from upstream kernels
+
+  const int32_t row_begin = args.indptr[b];
+  const int32_t n_pages = args.indptr[b + 1] - row_begin;
+  const int32_t pps = (n_pages + args.num_splits - 1) / args.num_splits;
+  const int32_t p0 = min(split * pps, n_pages);
+  const int32_t p1 = min(p0 + pps, n_pages);
+  const int32_t n = p1 - p0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n > 0) {
+      int32_t last_len = args.last_page_len[b];
+      last_len = last_len < 0 ? 0 : (last_len > PS ? PS : last_len);
+      int issued = 0;
+      for (int i = 0; i < n; ++i) {
+        const int s = i % C::kStages;
+        if (i >= C::kStages) {
+          if (!mbar_wait(&empty_bar[s], ((i / C::kStages) - 1) & 1)) {
+            set_status(args.status, PL_ERR_TIMEOUT);
+            flags[0] = 1;
+            break;
+          }
+        }
+        if (flags[0]) break;
+        const int32_t page_idx = p0 + i;
+        const int32_t pid = args.indices[row_begin + page_idx];
+        const int32_t ntok = (page_idx == n_pages - 1) ? last_len : PS;
+        if (pid < 0 || static_cast<int64_t>(pid) >= args.num_pages || ntok == 0) {
+          if (ntok != 0) set_status(args.status, PL_ERR_PAGE_OUT_OF_RANGE);
+          stage_ntok[s] = 0;
+          mbar_arrive(&full_bar[s]);  // nothing to load: consumers skip the page
+          ++issued;
+          continue;
+        }
+        stage_ntok[s] = ntok;
+        mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
+        uint8_t* kdst = smem + C::kStageOff + s * C::kStageBytes;
+        uint8_t* vdst = kdst + C::kTileBytes;
+#pragma unroll
+        for (int hh = 0; hh < C::kHalves; ++hh) {
+          tma_load_4d(kdst + hh * C::kHalfBytes, &kv_map, hh * 64, kvh, 0, 2 * pid + 0, &full_bar[s]);
+          tma_load_4d(vdst + hh * C::kHalfBytes, &kv_map, hh * 64, kvh, 0, 2 * pid + 1, &full_bar[s]);
+        }
+        ++issued;
+      }
+      if (flags[0]) {
+        // Abort: wait (bounded) for the loads still in flight before the CTA exits.
+        for (int i = issued - C::kStages < 0 ? 0 : issued - C::kStages; i < issued; ++i)
+          (void)mbar_wait(&full_bar[i % C::kStages], (i / C::kStages) & 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int cw = warp - 1;        // consumer warp 0..3
+    const int ctid = threadIdx.x - 32;
+    const int g = lane >> 2;        // fragment row (query head within group)
+    const int t = lane & 3;
+
+    // Stage q rows (zero-padded to 16) into shared memory.
+    uint8_t* qs = smem + C::kQOff;
+    {
+      constexpr int kChunksPerRow = D / 8;
+      for (int idx = ctid; idx < 16 * kChunksPerRow; idx += 32 * kConsumerWarps) {
+        const int r = idx / kChunksPerRow, c = idx % kChunksPerRow;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < group) {
+          const bf16* src = args.q + b * args.q_stride_b + (int64_t)(kvh * group + r) * args.q_stride_h + c * 8;
+          v = *reinterpret_cast<const uint4*>(src);
+        }
+        *reinterpret_cast<uint4*>(qs + r * C::kQRowBytes + c * 16) = v;
+      }
+    }
+    named_barrier(1, 32 * kConsumerWarps);
+
+    uint32_t qa[D / 16][4];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int r = (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int col = kk * 16 + 8 * (lane >> 4);
+      ldsm_x4(smem_u32(qs + r * C::kQRowBytes + col * 2), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+    }
+
+    float o[C::kDT][4];
+#pragma unroll
+    for (int j = 0; j < C::kDT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    const float sl2 = args.scale_log2;
+
+    for (int i = cw; i < n; i += kConsumerWarps) {
+      const int s = i % C::kStages;
+      if (!mbar_wait(&full_bar[s], (i / C::kStages) & 1)) {
+        set_status(args.status, PL_ERR_TIMEOUT);
+        flags[0] = 1;
+        break;
+      }
+      if (flags[0]) break;
+      const int ntok = stage_ntok[s];
+      if (ntok > 0) {
+        const uint8_t* kbase = smem + C::kStageOff + s * C::kStageBytes;
+        const uint8_t* vbase = kbase + C::kTileBytes;
+        // ---- S = Q . K^T  (16 x PS)
+        float sc[C::kNT][4];
+#pragma unroll
+        for (int j = 0; j < C::kNT; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+          for (int jp = 0; jp < C::kNT / 2; ++jp) {
+            const int m = lane >> 3;
+            const int tok = jp * 16 + (m >> 1) * 8 + (lane & 7);
+            const int gc = 2 * kk + (m & 1);
+            const uint32_t addr = smem_u32(kbase + (gc >> 3) * C::kHalfBytes + swz128(tok, gc & 7));
+            uint32_t kb[4];
+            ldsm_x4(addr, kb[0], kb[1], kb[2], kb[3]);
+            mma_bf16_16816(sc[2 * jp + 0], qa[kk], &kb[0]);
+            mma_bf16_16816(sc[2 * jp + 1], qa[kk], &kb[2]);
+          }
+        }
+        // ---- online softmax (rows g and g+8), log2 domain
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < C::kNT; ++j) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int tok = 8 * j + 2 * t + c;
+            const bool valid = tok < ntok;
+            sc[j][c] = valid ? sc[j][c] * sl2 : -INFINITY;
+            sc[j][2 + c] = valid ? sc[j][2 + c] * sl2 : -INFINITY;
+            mx0 = fmaxf(mx0, sc[j][c]);
+            mx1 = fmaxf(mx1, sc[j][2 + c]);
+          }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float a0 = exp2f(m0 - mn0), a1 = exp2f(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < C::kNT; ++j) {
+          sc[j][0] = exp2f(sc[j][0] - mn0);
+          sc[j][1] = exp2f(sc[j][1] - mn0);
+          sc[j][2] = exp2f(sc[j][2] - mn1);
+          sc[j][3] = exp2f(sc[j][3] - mn1);
+          ps0 += sc[j][0] + sc[j][1];
+          ps1 += sc[j][2] + sc[j][3];
+        }
+        l0 = l0 * a0 + ps0;
+        l1 = l1 * a1 + ps1;
+#pragma unroll
+        for (int j = 0; j < C::kDT; ++j) {
+          o[j][0] *= a0;
+          o[j][1] *= a0;
+          o[j][2] *= a1;
+          o[j][3] *= a1;
+        }
+        // ---- O += P . V
+#pragma unroll
+        for (int kt = 0; kt < PS / 16; ++kt) {
+          uint32_t pa[4];
+          pa[0] = pack_bf16x2(sc[2 * kt][0], sc[2 * kt][1]);
+          pa[1] = pack_bf16x2(sc[2 * kt][2], sc[2 * kt][3]);
+          pa[2] = pack_bf16x2(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
+          pa[3] = pack_bf16x2(sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
+#pragma unroll
+          for (int dc = 0; dc < C::kDT; dc += 2) {
+            const int m = lane >> 3;
+            const int tok = kt * 16 + (m & 1) * 8 + (lane & 7);
+            const int gc = dc + (m >> 1);
+            const uint32_t addr = smem_u32(vbase + (gc >> 3) * C::kHalfBytes + swz128(tok, gc & 7));
+            uint32_t vb[4];
+            ldsm_x4_trans(addr, vb[0], vb[1], vb[2], vb[3]);
+            mma_bf16_16816(o[dc], pa, &vb[0]);
+            mma_bf16_16816(o[dc + 1], pa, &vb[2]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+    }
+
+    // ---- merge the consumer warps' states (scratch aliases the drained stage ring)
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    named_barrier(1, 32 * kConsumerWarps);  // every warp is done reading its stages
+    float* scratch = reinterpret_cast<float*>(smem + C::kStageOff);  // [warp][16][D]
+    float* mw = ml;                                                   // [warp][16]
+    float* lw = ml + kConsumerWarps * 16;
+    {
+      float* ow = scratch + cw * 16 * D;
+#pragma unroll
+      for (int j = 0; j < C::kDT; ++j) {
+        const int d = 8 * j + 2 * t;
+        ow[g * D + d] = o[j][0];
+        ow[g * D + d + 1] = o[j][1];
+        ow[(g + 8) * D + d] = o[j][2];
+        ow[(g + 8) * D + d + 1] = o[j][3];
+      }
+      if (t == 0) {
+        mw[cw * 16 + g] = m0;
+        mw[cw * 16 + g + 8] = m1;
+        lw[cw * 16 + g] = l0;
+        lw[cw * 16 + g + 8] = l1;
+      }
+    }
+    named_barrier(1, 32 * kConsumerWarps);
+
+    const int hq0 = kvh * group;
+    const bool single = args.num_splits == 1;
+    for (int idx = ctid; idx < group * D; idx += 32 * kConsumerWarps) {
+      const int r = idx / D, d = idx % D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mw[w * 16 + r]);
+      float L = 0.f, acc = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float wt = exp2f(mw[w * 16 + r] - M);
+          L += wt * lw[w * 16 + r];
+          acc += wt * scratch[(w * 16 + r) * D + d];
+        }
+      }
+      const float val = (L > 0.f) ? acc / L : 0.f;
+      const float lse2 = (L > 0.f) ? M + log2f(L) : -INFINITY;
+      if (single) {
+        args.out[b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d] = f2bf(val);
+        if (args.out_lse != nullptr && d == 0) args.out_lse[(int64_t)b * args.num_qo_heads + hq0 + r] = lse2 * kLn2;
+      } else {
+        const int64_t rowid = (int64_t)b * args.num_qo_heads + hq0 + r;
+        args.partial_o[(rowid * args.num_splits + split) * D + d] = val;
+        if (d == 0) args.partial_lse[rowid * args.num_splits + split] = lse2;
+      }
+    }
+    if (!single) {
+      __threadfence();
+      named_barrier(1, 32 * kConsumerWarps);
+      if (ctid == 0) {
+        const int32_t ticket = atomicAdd(&args.counters[b * args.num_kv_heads + kvh], 1);
+        flags[1] = (ticket == args.num_splits - 1) ? 1 : 0;
+      }
+      named_barrier(1, 32 * kConsumerWarps);
+      if (flags[1]) {
+        __threadfence();
+        const int S = args.num_splits;
+        for (int idx = ctid; idx < group * D; idx += 32 * kConsumerWarps) {
+          const int r = idx / D, d = idx % D;
+          const int64_t rowid = (int64_t)b * args.num_qo_heads + hq0 + r;
+          const float* lse = args.partial_lse + rowid * S;
+          float M = -INFINITY;
+          for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(lse + s));
+          float L = 0.f, acc = 0.f;
+          if (M != -INFINITY) {
+            for (int s = 0; s < S; ++s) {
+              const float wt = exp2f(__ldcg(lse + s) - M);
+              L += wt;
+              acc += wt * __ldcg(args.partial_o + (rowid * S + s) * D + d);
+            }
+          }
+          const float val = (L > 0.f) ? acc / L : 0.f;
+          args.out[b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d] = f2bf(val);
+          if (args.out_lse != nullptr && d == 0)
+            args.out_lse[rowid] = (L > 0.f) ? (M + log2f(L)) * kLn2 : -INFINITY;
+        }
+        if (ctid == 0) args.counters[b * args.num_kv_heads + kvh] = 0;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- LSE merge
+__global__ void merge_states_kernel(const float* __restrict__ v, const float* __restrict__ lse, int num_rows,
+                                    int num_states, int head_dim, bf16* __restrict__ out, int64_t out_stride,
+                                    float* __restrict__ out_lse) {
+  pdl_wait();
+  const int row = blockIdx.x;
+  if (row >= num_rows) return;
+  const float* l = lse + (int64_t)row * num_states;
+  float M = -INFINITY;
+  for (int s = 0; s < num_states; ++s) M = fmaxf(M, l[s]);
+  float L = 0.f;
+  if (M != -INFINITY)
+    for (int s = 0; s < num_states; ++s) L += expf(l[s] - M);
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float acc = 0.f;
+    if (M != -INFINITY)
+      for (int s = 0; s < num_states; ++s) acc += expf(l[s] - M) * v[((int64_t)row * num_states + s) * head_dim + d];
+    out[(int64_t)row * out_stride + d] = f2bf(L > 0.f ? acc / L : 0.f);
+  }
+  if (out_lse != nullptr && threadIdx.x == 0) out_lse[row] = L > 0.f ? M + logf(L) : -INFINITY;
+}
+
+}  // namespace pl
+
+// =================================================================== host
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  int64_t pages;
+  int32_t hkv, d, ps, dev;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && pages == o.pages && hkv == o.hkv && d == o.d && ps == o.ps && dev == o.dev;
+  }
+};
+
+constexpr int kMapCache = 128;
+struct MapCache {
+  std::mutex mu;
+  MapKey key[kMapCache];
+  CUtensorMap map[kMapCache];
+  int used = 0, next = 0;
+};
+MapCache g_maps;
+
+// Tensor map over one layer's pool viewed as [2*P][PS][Hkv][D] (innermost last):
+// dims (inner->outer) {D, Hkv, PS, 2P}, box {64, 1, PS, 1}, 128B swizzle.
+int32_t kv_tensor_map(const void* cache, int64_t pages, int hkv, int d, int ps, CUtensorMap* out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  MapKey k{cache, pages, hkv, d, ps, dev};
+  std::lock_guard<std::mutex> lock(g_maps.mu);
+  for (int i = 0; i < g_maps.used; ++i)
+    if (g_maps.key[i] == k) {
+      *out = g_maps.map[i];
+      return PL_OK;
+    }
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return PL_ERR_CUDA;
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)hkv, (cuuint64_t)ps, (cuuint64_t)(2 * pages)};
+  cuuint64_t strides[3] = {(cuuint64_t)d * 2, (cuuint64_t)hkv * d * 2, (cuuint64_t)ps * hkv * d * 2};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)ps, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMap m;
+  CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(cache), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return PL_ERR_INVALID_ARGUMENT;
+  int slot;
+  if (g_maps.used < kMapCache) {
+    slot = g_maps.used++;
+  } else {
+    slot = g_maps.next;
+    g_maps.next = (g_maps.next + 1) % kMapCache;
+  }
+  g_maps.key[slot] = k;
+  g_maps.map[slot] = m;
+  *out = m;
+  return PL_OK;
+}
+
+int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
+
+int64_t decode_workspace_bytes(int batch, int hq, int hkv, int d, int splits) {
+  if (splits <= 1) return align256((int64_t)batch * hkv * 4);
+  return align256((int64_t)batch * hkv * 4) + align256((int64_t)batch * hq * splits * d * 4) +
+         align256((int64_t)batch * hq * splits * 4);
+}
+
+template <int D, int PS>
+int32_t launch_decode(const CUtensorMap& map, const pl::DecodeArgs& a, int batch, int hkv, int splits, void* stream) {
+  using C = pl::DecodeCfg<D, PS>;
+  auto kern = pl::paged_decode_kernel<D, PS>;
+  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+  if (st != PL_OK) return st;
+  return pl_host::launch_pdl(kern, dim3(splits, hkv, batch), dim3(pl::kDecodeThreads), C::kSmemBytes, stream, map, a);
+}
+
+}  // namespace
+
+extern "C" int32_t pl_decode_plan(int32_t batch, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+                                  int32_t page_size, int64_t total_pages, int32_t max_splits,
+                                  pl_decode_plan_t* plan_out) {
+  if (plan_out == nullptr || batch < 0 || num_kv_heads <= 0 || num_qo_heads % num_kv_heads != 0 || head_dim <= 0 ||
+      page_size <= 0 || total_pages < 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  int sms = pl_host::sm_count();
+  if (sms <= 0) sms = 148;
+  const int64_t base = (int64_t)batch * num_kv_heads;
+  int splits = 1;
+  if (base > 0) {
+    const int64_t target = 2LL * sms;  // two resident CTAs per SM
+    const int64_t avg_pages = (total_pages + batch - 1) / (batch > 0 ? batch : 1);
+    int64_t by_fill = (target + base - 1) / base;
+    int64_t by_len = avg_pages / 2;  // at least ~2 pages of work per split
+    int64_t s = by_fill < by_len ? by_fill : by_len;
+    if (max_splits > 0 && s > max_splits) s = max_splits;
+    splits = s < 1 ? 1 : static_cast<int>(s);
+  }
+  plan_out->num_splits = splits;
+  plan_out->ctas = static_cast<int32_t>(base * splits);
+  plan_out->workspace_bytes = decode_workspace_bytes(batch, num_qo_heads, num_kv_heads, head_dim, splits);
+  return PL_OK;
+}
+
+extern "C" int32_t pl_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* kv_cache,
+                                   int64_t num_pages, const int32_t* indptr, const int32_t* indices,
+                                   const int32_t* last_page_len, int32_t batch, int32_t num_qo_heads,
+                                   int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float sm_scale,
+                                   int32_t num_splits, void* out, int64_t o_stride_b, int64_t o_stride_h,
+                                   float* out_lse, void* workspace, int64_t workspace_bytes, int32_t* status_dev,
+                                   void* stream) {
+  if (batch == 0) return PL_OK;
+  if (q == nullptr || kv_cache == nullptr || indptr == nullptr || indices == nullptr || last_page_len == nullptr ||
+      out == nullptr || batch < 0 || num_pages <= 0 || num_kv_heads <= 0 || num_qo_heads % num_kv_heads != 0 ||
+      num_splits < 1)
+    return PL_ERR_INVALID_ARGUMENT;
+  const int group = num_qo_heads / num_kv_heads;
+  if (group > 16 || (head_dim != 64 && head_dim != 128) || (page_size != 16 && page_size != 32))
+    return PL_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(kv_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(q) & 15) != 0 ||
+      (q_stride_b % 8) != 0 || (q_stride_h % 8) != 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  const int64_t need = decode_workspace_bytes(batch, num_qo_heads, num_kv_heads, head_dim, num_splits);
+  if (num_splits > 1 && (workspace == nullptr || workspace_bytes < need)) return PL_ERR_WORKSPACE_TOO_SMALL;
+
+  CUtensorMap map;
+  int32_t st = kv_tensor_map(kv_cache, num_pages, num_kv_heads, head_dim, page_size, &map);
+  if (st != PL_OK) return st;
+
+  pl::DecodeArgs a;
+  a.q = static_cast<const pl::bf16*>(q);
+  a.q_stride_b = q_stride_b;
+  a.q_stride_h = q_stride_h;
+  a.indptr = indptr;
+  a.indices = indices;
+  a.last_page_len = last_page_len;
+  a.num_pages = num_pages;
+  a.num_qo_heads = num_qo_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.scale_log2 = sm_scale * pl::kLog2e;
+  a.num_splits = num_splits;
+  a.out = static_cast<pl::bf16*>(out);
+  a.o_stride_b = o_stride_b;
+  a.o_stride_h = o_stride_h;
+  a.out_lse = out_lse;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  a.counters = reinterpret_cast<int32_t*>(ws);
+  a.partial_o = nullptr;
+  a.partial_lse = nullptr;
+  if (num_splits > 1) {
+    const int64_t c_bytes = align256((int64_t)batch * num_kv_heads * 4);
+    const int64_t o_bytes = align256((int64_t)batch * num_qo_heads * num_splits * head_dim * 4);
+    a.partial_o = reinterpret_cast<float*>(ws + c_bytes);
+    a.partial_lse = reinterpret_cast<float*>(ws + c_bytes + o_bytes);
+  }
+  a.status = status_dev;
+
+  if (head_dim == 128 && page_size == 16) return launch_decode<128, 16>(map, a, batch, num_kv_heads, num_splits, stream);
+  if (head_dim == 128 && page_size == 32) return launch_decode<128, 32>(map, a, batch, num_kv_heads, num_splits, stream);
+  if (head_dim == 64 && page_size == 16) return launch_decode<64, 16>(map, a, batch, num_kv_heads, num_splits, stream);
+  return launch_decode<64, 32>(map, a, batch, num_kv_heads, num_splits, stream);
+}
+
+extern "C" int32_t pl_merge_states(const float* v_partial, const float* lse_partial, int32_t num_rows,
+                                   int32_t num_states, int32_t head_dim, void* out, int64_t out_stride,
+                                   float* out_lse, void* stream) {
+  if (num_rows == 0) return PL_OK;
+  if (v_partial == nullptr || lse_partial == nullptr || out == nullptr || num_rows < 0 || num_states < 1 ||
+      head_dim <= 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  return pl_host::launch_pdl(pl::merge_states_kernel, dim3(num_rows), dim3(128), 0, stream, v_partial, lse_partial,
+                             (int)num_rows, (int)num_states, (int)head_dim, static_cast<pl::bf16*>(out), out_stride,
+                             out_lse);
+}

@@ -1,0 +1,574 @@
+// Page-table construction and the small per-token kernels of one decode
+// step: q/k head RMSNorm + RoPE + paged KV append, the plain KV append,
+// embedding gather and first-index argmax.
+#include "pl_common.cuh"
+
+namespace pl {
+
+constexpr int kPtThreads = 1024;
+constexpr int kPtMaxRows = 4096;
+
+// Warp-uniform scan state of one row of spans.
+struct RowScan {
+  bool have_prev;
+  int32_t prev_blk, prev_end;
+  bool open;
+  int32_t open_start;
+  long long open_sum;
+  int32_t n_groups;
+};
+
+// Pass 1 of the page-table build for one row (one warp): coalesce adjacent
+// slices of one page (flashinfer_page_table.py:184-197), validate every
+// coalesced span in order (:210-220) and count them.  Returns the status
+// kind of the first failing coalesced span (0 if none) and the last length.
+__device__ int32_t pt_scan_row(const int32_t* blk, const int32_t* st, const int32_t* ln, int32_t s0, int32_t s1,
+                               int32_t PS, int32_t* n_groups_out, int32_t* last_len_out) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  RowScan rs = {false, 0, 0, false, 0, 0, 0};
+  int32_t err = 0;
+  for (int32_t c = s0; c < s1; c += 32) {
+    const int32_t i = c + lane;
+    const bool in = i < s1;
+    const int32_t b = in ? blk[i] : 0;
+    const int32_t s = in ? st[i] : 0;
+    const int32_t l = in ? ln[i] : 0;
+    const bool ne = in && l > 0;  // empty slices are skipped by the coalescer
+    const uint32_t M = __ballot_sync(0xffffffffu, ne);
+    const uint32_t below = M & lt;
+    const int jp = below ? 31 - __clz(below) : lane;
+    const int32_t pb_l = __shfl_sync(0xffffffffu, b, jp);
+    const int32_t pe_l = __shfl_sync(0xffffffffu, s + l, jp);
+    const bool hp = below ? true : rs.have_prev;
+    const int32_t pb = below ? pb_l : rs.prev_blk;
+    const int32_t pe = below ? pe_l : rs.prev_end;
+    const bool cont = ne && hp && b == pb && s == pe;
+    const bool head = ne && !cont;
+    const uint32_t H = __ballot_sync(0xffffffffu, head);
+    long long P = ne ? (long long)l : 0ll;
+    const long long val = P;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, P, o);
+      if (lane >= o) P += y;
+    }
+    const long long Pex = P - val;
+    const uint32_t hbelow = H & lt;
+    const int hl = hbelow ? 31 - __clz(hbelow) : lane;
+    const int32_t hp_start = __shfl_sync(0xffffffffu, s, hl);
+    const long long hp_pex = __shfl_sync(0xffffffffu, Pex, hl);
+    int32_t kind = 0;
+    if (head) {
+      bool closes = false;
+      int32_t cstart = 0;
+      long long clen = 0;
+      if (hbelow) {
+        closes = true;
+        cstart = hp_start;
+        clen = Pex - hp_pex;
+      } else if (rs.open) {
+        closes = true;
+        cstart = rs.open_start;
+        clen = rs.open_sum + Pex;
+      }
+      if (closes) {  // a head follows, so the closed span is not the row's last
+        if (cstart != 0)
+          kind = PL_ERR_SPAN_START;
+        else if (clen <= 0 || clen > PS)
+          kind = PL_ERR_SPAN_LENGTH;
+        else if (clen != PS)
+          kind = PL_ERR_SPAN_NOT_FULL;
+      }
+    }
+    const uint32_t E = __ballot_sync(0xffffffffu, kind != 0);
+    if (E) {
+      err = __shfl_sync(0xffffffffu, kind, __ffs(E) - 1);
+      break;
+    }
+    const long long Ptot = __shfl_sync(0xffffffffu, P, 31);
+    if (H) {
+      const int hh = 31 - __clz(H);
+      rs.open = true;
+      rs.open_start = __shfl_sync(0xffffffffu, s, hh);
+      rs.open_sum = Ptot - __shfl_sync(0xffffffffu, Pex, hh);
+    } else if (rs.open) {
+      rs.open_sum += Ptot;
+    }
+    rs.n_groups += __popc(H);
+    if (M) {
+      const int ln_ = 31 - __clz(M);
+      rs.have_prev = true;
+      rs.prev_blk = __shfl_sync(0xffffffffu, b, ln_);
+      rs.prev_end = __shfl_sync(0xffffffffu, s + l, ln_);
+    }
+  }
+  if (err == 0 && rs.open) {  // the row's last coalesced span may be partial
+    if (rs.open_start != 0)
+      err = PL_ERR_SPAN_START;
+    else if (rs.open_sum <= 0 || rs.open_sum > PS)
+      err = PL_ERR_SPAN_LENGTH;
+  }
+  *n_groups_out = rs.n_groups;
+  *last_len_out = rs.open ? (int32_t)rs.open_sum : 0;
+  return err;
+}
+
+// Pass 2: write the page id of every coalesced span of one row.
+__device__ void pt_write_row(const int32_t* blk, const int32_t* st, const int32_t* ln, int32_t s0, int32_t s1,
+                             int32_t* out) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  bool have_prev = false;
+  int32_t prev_blk = 0, prev_end = 0, n_groups = 0;
+  for (int32_t c = s0; c < s1; c += 32) {
+    const int32_t i = c + lane;
+    const bool in = i < s1;
+    const int32_t b = in ? blk[i] : 0;
+    const int32_t s = in ? st[i] : 0;
+    const int32_t l = in ? ln[i] : 0;
+    const bool ne = in && l > 0;
+    const uint32_t M = __ballot_sync(0xffffffffu, ne);
+    const uint32_t below = M & lt;
+    const int jp = below ? 31 - __clz(below) : lane;
+    const int32_t pb_l = __shfl_sync(0xffffffffu, b, jp);
+    const int32_t pe_l = __shfl_sync(0xffffffffu, s + l, jp);
+    const bool hp = below ? true : have_prev;
+    const int32_t pb = below ? pb_l : prev_blk;
+    const int32_t pe = below ? pe_l : prev_end;
+    const bool head = ne && !(hp && b == pb && s == pe);
+    const uint32_t H = __ballot_sync(0xffffffffu, head);
+    if (head) out[n_groups + __popc(H & lt)] = b;
+    n_groups += __popc(H);
+    if (M) {
+      const int ln_ = 31 - __clz(M);
+      have_prev = true;
+      prev_blk = __shfl_sync(0xffffffffu, b, ln_);
+      prev_end = __shfl_sync(0xffffffffu, s + l, ln_);
+    }
+  }
+}
+
+// Block-wide exclusive scan of vals[0..n) (n <= kPtMaxRows) in place; returns the total.
+__device__ int32_t block_exclusive_scan(int32_t* vals, int n, int32_t* tmp32) {
+  constexpr int kPer = kPtMaxRows / kPtThreads;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int32_t loc[kPer];
+  int32_t sum = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int r = tid * kPer + i;
+    loc[i] = r < n ? vals[r] : 0;
+    sum += loc[i];
+  }
+  int32_t inc = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) tmp32[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t w = lane < (kPtThreads / 32) ? tmp32[lane] : 0;
+    int32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    tmp32[lane] = wi - w;  // exclusive warp offsets
+    if (lane == 31) tmp32[32] = wi;
+  }
+  __syncthreads();
+  int32_t run = tmp32[warp] + inc - sum;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int r = tid * kPer + i;
+    if (r < n) vals[r] = run;
+    run += loc[i];
+  }
+  const int32_t total = tmp32[32];
+  __syncthreads();
+  return total;
+}
+
+__global__ void __launch_bounds__(kPtThreads) page_table_build_kernel(
+    const int32_t* __restrict__ blk, const int32_t* __restrict__ st, const int32_t* __restrict__ ln,
+    const int32_t* __restrict__ row_indptr, int num_rows, int PS, int32_t* __restrict__ out_indptr,
+    int32_t* __restrict__ out_indices, int32_t* __restrict__ out_last, int32_t* status, int32_t* err_row) {
+  extern __shared__ int32_t pt_sm[];
+  int32_t* counts = pt_sm;
+  int32_t* lastl = pt_sm + num_rows;
+  int32_t* errk = pt_sm + 2 * num_rows;
+  __shared__ int32_t tmp32[33];
+  __shared__ int32_t first_bad;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kPtThreads / 32;
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x == 0) first_bad = num_rows;
+  for (int r = warp; r < num_rows; r += kWarps) {
+    int32_t ng = 0, ll = 0;
+    const int32_t e = pt_scan_row(blk, st, ln, row_indptr[r], row_indptr[r + 1], PS, &ng, &ll);
+    if (lane == 0) {
+      counts[r] = ng;
+      lastl[r] = ll;
+      errk[r] = e;
+    }
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < num_rows; r += kPtThreads)
+    if (errk[r] != 0) atomicMin(&first_bad, r);
+  __syncthreads();
+  if (first_bad < num_rows) {
+    if (threadIdx.x == 0) {
+      if (status != nullptr) atomicCAS(status, 0, errk[first_bad]);
+      if (err_row != nullptr) *err_row = first_bad;
+    }
+    return;
+  }
+  const int32_t total = block_exclusive_scan(counts, num_rows, tmp32);
+  for (int r = threadIdx.x; r < num_rows; r += kPtThreads) {
+    out_indptr[r] = counts[r];
+    out_last[r] = lastl[r];
+  }
+  if (threadIdx.x == 0) out_indptr[num_rows] = total;
+  for (int r = warp; r < num_rows; r += kWarps)
+    pt_write_row(blk, st, ln, row_indptr[r], row_indptr[r + 1], out_indices + counts[r]);
+}
+
+// One decode token per row: extend the row by one slot (appending
+// new_page_ids[r] when its last page is full or the row is empty), record
+// the append slot, then rebuild the CSR page table from the per-row pages.
+__global__ void __launch_bounds__(kPtThreads) page_table_advance_kernel(
+    int32_t* __restrict__ row_num_pages, int32_t* __restrict__ last_page_len, int32_t* __restrict__ row_pages,
+    const int32_t* __restrict__ new_page_ids, int num_rows, int cap, int PS, int32_t* __restrict__ out_indptr,
+    int32_t* __restrict__ out_indices, int32_t* __restrict__ slot_page, int32_t* __restrict__ slot_off,
+    int32_t* __restrict__ positions, int32_t* status) {
+  extern __shared__ int32_t pt_sm[];
+  int32_t* counts = pt_sm;
+  __shared__ int32_t tmp32[33];
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int r = threadIdx.x; r < num_rows; r += kPtThreads) {
+    int32_t n = row_num_pages[r];
+    int32_t last = last_page_len[r];
+    if (n == 0 || last >= PS) {
+      if (n >= cap) {
+        set_status(status, PL_ERR_INVALID_ARGUMENT);
+        counts[r] = n;
+        slot_page[r] = -1;
+        slot_off[r] = 0;
+        continue;
+      }
+      row_pages[(int64_t)r * cap + n] = new_page_ids[r];
+      ++n;
+      last = 1;
+    } else {
+      ++last;
+    }
+    row_num_pages[r] = n;
+    last_page_len[r] = last;
+    slot_page[r] = row_pages[(int64_t)r * cap + n - 1];
+    slot_off[r] = last - 1;
+    if (positions != nullptr) positions[r] = (n - 1) * PS + last - 1;
+    counts[r] = n;
+  }
+  __syncthreads();
+  const int32_t total = block_exclusive_scan(counts, num_rows, tmp32);
+  for (int r = threadIdx.x; r < num_rows; r += kPtThreads) out_indptr[r] = counts[r];
+  if (threadIdx.x == 0) out_indptr[num_rows] = total;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < num_rows; r += kPtThreads / 32) {
+    const int32_t off = counts[r];
+    const int32_t n = (r + 1 < num_rows ? counts[r + 1] : total) - off;
+    for (int i = lane; i < n; i += 32) out_indices[off + i] = row_pages[(int64_t)r * cap + i];
+  }
+}
+
+// ---------------------------------------------------------------- KV append
+__global__ void kv_append_kernel(const bf16* __restrict__ k, int64_t k_stride, const bf16* __restrict__ v,
+                                 int64_t v_stride, bf16* __restrict__ cache, int64_t num_pages,
+                                 const int32_t* __restrict__ page_id, const int32_t* __restrict__ page_off, int T,
+                                 int Hkv, int D, int PS, int32_t* status) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int per_tok = Hkv * D / 8;
+  const int64_t total = (int64_t)T * per_tok;
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < total; c += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(c / per_tok);
+    const int rem = (int)(c % per_tok);
+    const int32_t pid = page_id[t], off = page_off[t];
+    if (pid < 0 || pid >= num_pages || off < 0 || off >= PS) {
+      set_status(status, PL_ERR_PAGE_OUT_OF_RANGE);
+      continue;
+    }
+    const int64_t kbase = (((int64_t)pid * 2 + 0) * PS + off) * Hkv * D;
+    const int64_t vbase = (((int64_t)pid * 2 + 1) * PS + off) * Hkv * D;
+    const int e = rem * 8;  // element within [Hkv*D]
+    *reinterpret_cast<uint4*>(cache + kbase + e) = *reinterpret_cast<const uint4*>(k + t * k_stride + e);
+    *reinterpret_cast<uint4*>(cache + vbase + e) = *reinterpret_cast<const uint4*>(v + t * v_stride + e);
+  }
+}
+
+// ------------------------------------------- q/k norm + RoPE + KV append
+// One warp per (token, head) over the packed [q | k | v] projection row.
+template <int D>
+__global__ void __launch_bounds__(128) qkv_rope_append_kernel(
+    const bf16* __restrict__ qkv, int64_t qkv_stride, const float* __restrict__ down, int64_t down_stride,
+    const bf16* __restrict__ lora_b, int rank, const int32_t* __restrict__ tok_adapter,
+    const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w, float eps,
+    const int32_t* __restrict__ positions, float rope_theta, bf16* __restrict__ q_out, bf16* __restrict__ cache,
+    int64_t num_pages, const int32_t* __restrict__ page_id, const int32_t* __restrict__ page_off, int T, int Hq,
+    int Hkv, int PS, int32_t* status) {
+  constexpr int E = D / 32;  // elements per lane; lanes 0..15 hold [0, D/2), 16..31 hold [D/2, D)
+  pdl_launch_dependents();
+  pdl_wait();
+  const int heads = Hq + 2 * Hkv;
+  const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (gw >= T * heads) return;
+  const int lane = threadIdx.x & 31;
+  const int t = gw / heads, hh = gw % heads;
+  const int kind = hh < Hq ? 0 : (hh < Hq + Hkv ? 1 : 2);  // q, k, v
+  const int col = hh * D;                                     // packed column of this head
+  const int d0 = lane * E;
+  float v[E];
+  {
+    const bf16* src = qkv + (int64_t)t * qkv_stride + col + d0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = bf2f(src[e]);
+  }
+  if (down != nullptr && lora_b != nullptr) {
+    const int ad = tok_adapter != nullptr ? tok_adapter[t] : 0;
+    if (ad >= 0) {
+      const int n_out = heads * D;
+      const float* drow = down + (int64_t)t * down_stride + kind * rank;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const bf16* brow = lora_b + ((int64_t)ad * n_out + col + d0 + e) * rank;
+        float d = 0.f;
+        for (int j = 0; j < rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
+        v[e] = bfr(v[e] + bfr(d));
+      }
+    }
+  }
+  if (kind < 2) {
+    const bf16* nw = kind == 0 ? q_norm_w : k_norm_w;
+    if (nw != nullptr) {  // HF RMSNorm module: fp32 normalise, round, scale, round
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss += v[e] * v[e];
+      ss = warp_sum(ss);
+      const float r = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = bfr(bf2f(nw[d0 + e]) * bfr(v[e] * r));
+    }
+    const float pos = (float)positions[t];
+    float out[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+      const int i = (d0 + e) % (D / 2);
+      const float inv_freq = 1.0f / powf(rope_theta, (float)(2 * i) / (float)D);
+      float sn, cs;
+      sincosf(pos * inv_freq, &sn, &cs);
+      out[e] = lane < 16 ? v[e] * cs - partner * sn : v[e] * cs + partner * sn;
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = out[e];
+  }
+  if (kind == 0) {
+    bf16* dst = q_out + ((int64_t)t * Hq + hh) * D + d0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) dst[e] = f2bf(v[e]);
+  } else {
+    const int32_t pid = page_id[t], off = page_off[t];
+    if (pid < 0 || pid >= num_pages || off < 0 || off >= PS) {
+      if (lane == 0) set_status(status, PL_ERR_PAGE_OUT_OF_RANGE);
+      return;
+    }
+    const int h = kind == 1 ? hh - Hq : hh - Hq - Hkv;
+    bf16* dst = cache + ((((int64_t)pid * 2 + (kind - 1)) * PS + off) * Hkv + h) * D + d0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) dst[e] = f2bf(v[e]);
+  }
+}
+
+// ----------------------------------------------------------------- embed
+__global__ void embed_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ table, int64_t vocab, int dim,
+                             bf16* __restrict__ out, int32_t* status) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int64_t id = ids[t];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) set_status(status, PL_ERR_INVALID_ARGUMENT);
+    return;
+  }
+  for (int c = threadIdx.x; c < dim / 8; c += blockDim.x)
+    reinterpret_cast<uint4*>(out + (int64_t)t * dim)[c] = reinterpret_cast<const uint4*>(table + id * dim)[c];
+}
+
+// ---------------------------------------------------------------- argmax
+__global__ void __launch_bounds__(1024) argmax_kernel(const bf16* __restrict__ logits, int64_t stride, int vocab,
+                                                      int64_t* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const bf16* row = logits + (int64_t)t * stride;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = bf2f(row[i]);
+    if (v > best || (v == best && i < bi) || (v != v && best == best)) {
+      best = v;
+      bi = i;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi) || (ov != ov && best == best) || (ov != ov && best != best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
+    bi = lane < (int)(blockDim.x / 32) ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi) || (ov != ov && best == best) ||
+          (ov != ov && best != best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) out[t] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+}  // namespace pl
+
+// =================================================================== host
+extern "C" int32_t pl_page_table_build(const int32_t* span_block_id, const int32_t* span_start,
+                                       const int32_t* span_length, const int32_t* row_indptr, int32_t num_rows,
+                                       int32_t page_size, int32_t* out_indptr, int32_t* out_indices,
+                                       int32_t* out_last_page_len, int32_t* status_dev, int32_t* err_row_dev,
+                                       void* stream) {
+  if (num_rows < 0 || page_size <= 0 || row_indptr == nullptr || out_indptr == nullptr || status_dev == nullptr)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (num_rows > pl::kPtMaxRows) return PL_ERR_UNSUPPORTED;
+  if (num_rows > 0 && (span_block_id == nullptr || span_start == nullptr || span_length == nullptr ||
+                       out_indices == nullptr || out_last_page_len == nullptr))
+    return PL_ERR_INVALID_ARGUMENT;
+  const int smem = 3 * (num_rows > 0 ? num_rows : 1) * 4;
+  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::page_table_build_kernel), smem);
+  if (st != PL_OK) return st;
+  return pl_host::launch_pdl(pl::page_table_build_kernel, dim3(1), dim3(pl::kPtThreads), smem, stream,
+                             span_block_id, span_start, span_length, row_indptr, (int)num_rows, (int)page_size,
+                             out_indptr, out_indices, out_last_page_len, status_dev, err_row_dev);
+}
+
+extern "C" int32_t pl_page_table_advance(int32_t* row_num_pages, int32_t* last_page_len, int32_t* row_pages,
+                                         const int32_t* new_page_ids, int32_t num_rows, int32_t row_capacity,
+                                         int32_t page_size, int32_t* out_indptr, int32_t* out_indices,
+                                         int32_t* slot_page_id, int32_t* slot_offset, int32_t* positions_out,
+                                         int32_t* status_dev, void* stream) {
+  if (num_rows == 0) return PL_OK;
+  if (row_num_pages == nullptr || last_page_len == nullptr || row_pages == nullptr || new_page_ids == nullptr ||
+      out_indptr == nullptr || out_indices == nullptr || slot_page_id == nullptr || slot_offset == nullptr ||
+      num_rows < 0 || row_capacity <= 0 || page_size <= 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (num_rows > pl::kPtMaxRows) return PL_ERR_UNSUPPORTED;
+  return pl_host::launch_pdl(pl::page_table_advance_kernel, dim3(1), dim3(pl::kPtThreads), (size_t)num_rows * 4,
+                             stream, row_num_pages, last_page_len, row_pages, new_page_ids, (int)num_rows,
+                             (int)row_capacity, (int)page_size, out_indptr, out_indices, slot_page_id, slot_offset,
+                             positions_out, status_dev);
+}
+
+extern "C" int32_t pl_kv_append(const void* k, int64_t k_stride, const void* v, int64_t v_stride, void* kv_cache,
+                                int64_t num_pages, const int32_t* page_id, const int32_t* page_offset,
+                                int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                int32_t* status_dev, void* stream) {
+  if (num_tokens == 0) return PL_OK;
+  if (k == nullptr || v == nullptr || kv_cache == nullptr || page_id == nullptr || page_offset == nullptr ||
+      num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || page_size <= 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  if ((num_kv_heads * head_dim) % 8 || (k_stride % 8) || (v_stride % 8) || (reinterpret_cast<uintptr_t>(k) & 15) ||
+      (reinterpret_cast<uintptr_t>(v) & 15) || (reinterpret_cast<uintptr_t>(kv_cache) & 15))
+    return PL_ERR_UNSUPPORTED;
+  const int64_t chunks = (int64_t)num_tokens * num_kv_heads * head_dim / 8;
+  const int blocks = (int)((chunks + 255) / 256 < 4096 ? (chunks + 255) / 256 : 4096);
+  return pl_host::launch_pdl(pl::kv_append_kernel, dim3(blocks), dim3(256), 0, stream,
+                             static_cast<const pl::bf16*>(k), k_stride, static_cast<const pl::bf16*>(v), v_stride,
+                             static_cast<pl::bf16*>(kv_cache), num_pages, page_id, page_offset, (int)num_tokens,
+                             (int)num_kv_heads, (int)head_dim, (int)page_size, status_dev);
+}
+
+extern "C" int32_t pl_qkv_rope_append(const void* qkv, int64_t qkv_stride, const float* lora_down,
+                                      int64_t down_stride, const void* lora_b, int32_t lora_rank,
+                                      const int32_t* tok_adapter, const void* q_norm_w, const void* k_norm_w,
+                                      float norm_eps, const int32_t* positions, float rope_theta, void* q_out,
+                                      void* kv_cache, int64_t num_pages, const int32_t* page_id,
+                                      const int32_t* page_offset, int32_t num_tokens, int32_t num_qo_heads,
+                                      int32_t num_kv_heads, int32_t head_dim, int32_t page_size, int32_t* status_dev,
+                                      void* stream) {
+  if (num_tokens == 0) return PL_OK;
+  if (qkv == nullptr || positions == nullptr || q_out == nullptr || kv_cache == nullptr || page_id == nullptr ||
+      page_offset == nullptr || num_tokens < 0 || num_qo_heads <= 0 || num_kv_heads <= 0 || page_size <= 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (lora_down != nullptr && lora_b != nullptr && lora_rank <= 0) return PL_ERR_INVALID_ARGUMENT;
+  const int warps = num_tokens * (num_qo_heads + 2 * num_kv_heads);
+  const int blocks = (warps + 3) / 4;
+  if (head_dim == 128)
+    return pl_host::launch_pdl(pl::qkv_rope_append_kernel<128>, dim3(blocks), dim3(128), 0, stream,
+                               static_cast<const pl::bf16*>(qkv), qkv_stride, lora_down, down_stride,
+                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, tok_adapter,
+                               static_cast<const pl::bf16*>(q_norm_w), static_cast<const pl::bf16*>(k_norm_w),
+                               norm_eps, positions, rope_theta, static_cast<pl::bf16*>(q_out),
+                               static_cast<pl::bf16*>(kv_cache), num_pages, page_id, page_offset, (int)num_tokens,
+                               (int)num_qo_heads, (int)num_kv_heads, (int)page_size, status_dev);
+  if (head_dim == 64)
+    return pl_host::launch_pdl(pl::qkv_rope_append_kernel<64>, dim3(blocks), dim3(128), 0, stream,
+                               static_cast<const pl::bf16*>(qkv), qkv_stride, lora_down, down_stride,
+                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, tok_adapter,
+                               static_cast<const pl::bf16*>(q_norm_w), static_cast<const pl::bf16*>(k_norm_w),
+                               norm_eps, positions, rope_theta, static_cast<pl::bf16*>(q_out),
+                               static_cast<pl::bf16*>(kv_cache), num_pages, page_id, page_offset, (int)num_tokens,
+                               (int)num_qo_heads, (int)num_kv_heads, (int)page_size, status_dev);
+  return PL_ERR_UNSUPPORTED;
+}
+
+extern "C" int32_t pl_embed(const int64_t* token_ids, const void* table, int64_t vocab, int32_t dim,
+                            int32_t num_tokens, void* out, int32_t* status_dev, void* stream) {
+  if (num_tokens == 0) return PL_OK;
+  if (token_ids == nullptr || table == nullptr || out == nullptr || num_tokens < 0 || dim <= 0 || vocab <= 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (dim % 8 || (reinterpret_cast<uintptr_t>(table) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return PL_ERR_UNSUPPORTED;
+  return pl_host::launch_pdl(pl::embed_kernel, dim3(num_tokens), dim3(256), 0, stream, token_ids,
+                             static_cast<const pl::bf16*>(table), vocab, (int)dim, static_cast<pl::bf16*>(out),
+                             status_dev);
+}
+
+extern "C" int32_t pl_argmax(const void* logits, int64_t stride, int32_t vocab, int32_t num_tokens,
+                             int64_t* out_ids, void* stream) {
+  if (num_tokens == 0) return PL_OK;
+  if (logits == nullptr || out_ids == nullptr || num_tokens < 0 || vocab <= 0) return PL_ERR_INVALID_ARGUMENT;
+  return pl_host::launch_pdl(pl::argmax_kernel, dim3(num_tokens), dim3(1024), 0, stream,
+                             static_cast<const pl::bf16*>(logits), stride, (int)vocab, out_ids);
+}

@@ -1,0 +1,518 @@
+// LoRA linear path for decode (num_tokens <= 8) on sm_100a.
+//
+// pl_linear_lora_expand_fused streams the weight matrix exactly once: the
+// CTA-persistent grid (one CTA per SM) gives each CTA a contiguous range of
+// output rows; a producer warp streams 16-row x 512-column tiles of those
+// rows into a 5-deep shared-memory ring with 1-D TMA bulk copies (one row
+// segment per lane, L2 evict-first), and four consumer warps multiply them
+// against the (RMS-normalised / SiLU-gated) activations with mma.sync
+// m16n8k16 (weight rows = M, tokens = N, fp32 accumulate).  The epilogue
+// adds bias, the LoRA expand (B . down, scale folded into B) and the
+// residual with the same bf16 rounding points as the reference's torch ops.
+// Rows past n_out come from a second matrix (the LoRA A of the packed
+// q/k/v shrink), so the shrink rides along the base projection for free.
+//
+// pl_lora_shrink_seg and pl_lora_merge_weight are small bandwidth kernels.
+#include "pl_common.cuh"
+
+namespace pl {
+
+constexpr int kGemvConsumers = 4;
+constexpr int kGemvThreads = 32 * (1 + kGemvConsumers);
+constexpr int kKC = 512;                      // columns per tile
+constexpr int kTileRows = 16;                 // rows per tile (mma M)
+constexpr int kRowBytes = kKC * 2 + 16;       // padded smem row: conflict-free ldmatrix
+constexpr int kGemvStageBytes = kTileRows * kRowBytes;
+constexpr int kGemvStages = 5;
+constexpr int kMaxTok = 8;                    // mma N
+
+struct GemvArgs {
+  const bf16* x;
+  int64_t x_stride;
+  int32_t T, K;
+  int32_t prologue;
+  const bf16* norm_w;
+  float eps;
+  const bf16* w;
+  int32_t n_out;
+  const bf16* bias;
+  const float* lora_down;
+  int64_t down_stride;
+  const bf16* lora_b;
+  int32_t rank;
+  int32_t slice_end[4];
+  int32_t num_slices;
+  const int32_t* tok_adapter;
+  const bf16* residual;
+  int64_t res_stride;
+  bf16* y;
+  int64_t y_stride;
+  const bf16* shrink_a;
+  int32_t n_shrink;
+  float* shrink_out;
+  int64_t shrink_stride;
+  int32_t early_weights;  // weights are not produced upstream: stream them before the dependency resolves
+  int32_t* status;
+};
+
+struct GemvSmem {
+  // offsets from a 128-aligned base
+  int x_off, zero_off, red_off, bar_off, misc_off, total;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem_layout(int T, int K) {
+  GemvSmem L;
+  int off = kGemvStages * kGemvStageBytes;
+  L.x_off = off;
+  off += T * (K * 2 + 16);
+  off = (off + 15) & ~15;
+  L.zero_off = off;
+  off += 16;
+  L.red_off = off;
+  off += 2 * kGemvConsumers * kTileRows * kMaxTok * 4;
+  L.bar_off = off;
+  off += 2 * kGemvStages * 8;
+  L.misc_off = off;
+  off += 64;
+  L.total = off + 128;
+  return L;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+__global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const GemvArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const GemvSmem L = gemv_smem_layout(a.T, a.K);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* empty_bar = full_bar + kGemvStages;
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + L.misc_off);
+  float* red = reinterpret_cast<float*>(smem + L.red_off);  // [2][warps][16][8]
+  uint8_t* xs = smem + L.x_off;
+  const int XROW = a.K * 2 + 16;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int K = a.K;
+  const int64_t rows_total = (int64_t)a.n_out + a.n_shrink;
+  const int64_t r0 = rows_total * blockIdx.x / gridDim.x;
+  const int64_t r1 = rows_total * (blockIdx.x + 1) / gridDim.x;
+  const int n_tiles = (int)((r1 - r0 + kTileRows - 1) / kTileRows);
+  const int n_kc = (K + kKC - 1) / kKC;
+  const int n_units = n_tiles * n_kc;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemvStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kGemvConsumers);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(smem + L.zero_off)[threadIdx.x] = 0u;
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // --------------------------------------------------------- producer warp
+    if (!a.early_weights) pdl_wait();
+    const uint64_t pol = l2_evict_first_policy();
+    int issued = 0;
+    for (int u = 0; u < n_units; ++u) {
+      const int s = u % kGemvStages;
+      if (u >= kGemvStages) {
+        if (!mbar_wait(&empty_bar[s], ((u / kGemvStages) - 1) & 1)) {
+          if (lane == 0) {
+            set_status(a.status, PL_ERR_TIMEOUT);
+            *abort_flag = 1;
+          }
+        }
+      }
+      __syncwarp();
+      if (*abort_flag) break;
+      const int tile = u / n_kc, kc = u % n_kc;
+      const int64_t row0 = r0 + (int64_t)tile * kTileRows;
+      const int rows = (int)((r1 - row0) < kTileRows ? (r1 - row0) : kTileRows);
+      const int k0 = kc * kKC;
+      const int kw = min(kKC, K - k0);
+      if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(rows * kw * 2));
+      __syncwarp();
+      if (lane < rows) {
+        const int64_t row = row0 + lane;
+        const bf16* src = row < a.n_out ? a.w + row * K : a.shrink_a + (row - a.n_out) * K;
+        bulk_g2s(smem + s * kGemvStageBytes + lane * kRowBytes, src + k0, (uint32_t)(kw * 2), &full_bar[s], pol);
+      }
+      ++issued;
+    }
+    if (lane == 0 && *abort_flag) {
+      for (int u = issued - kGemvStages < 0 ? 0 : issued - kGemvStages; u < issued; ++u)
+        (void)mbar_wait(&full_bar[u % kGemvStages], (u / kGemvStages) & 1);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int ctid = threadIdx.x - 32;
+  constexpr int NC = 32 * kGemvConsumers;
+  pdl_wait();
+
+  // Prologue: activations -> bf16 rows in shared memory.
+  for (int t = 0; t < a.T; ++t) {
+    const bf16* xr = a.x + (int64_t)t * a.x_stride;
+    uint8_t* dst = xs + t * XROW;
+    if (a.prologue == PL_PROLOGUE_RMSNORM) {
+      float ss = 0.f;
+      for (int k = ctid * 8; k < K; k += NC * 8) {
+        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f = unpack_bf16x2(u[i]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      }
+      ss = warp_sum(ss);
+      float* part = red;  // reuse the reduction scratch
+      if (lane == 0) part[cw] = ss;
+      named_barrier(1, NC);
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGemvConsumers; ++w) tot += part[w];
+      const float rstd = rsqrtf(tot / (float)K + a.eps);
+      named_barrier(1, NC);
+      for (int k = ctid * 8; k < K; k += NC * 8) {
+        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+        uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + k);
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+        const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+        uint4 o;
+        uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f = unpack_bf16x2(u[i]);
+          float2 g = unpack_bf16x2(uw[i]);
+          uo[i] = pack_bf16x2(f.x * rstd * g.x, f.y * rstd * g.y);
+        }
+        *reinterpret_cast<uint4*>(dst + k * 2) = o;
+      }
+    } else if (a.prologue == PL_PROLOGUE_SILU_MUL) {
+      for (int k = ctid * 8; k < K; k += NC * 8) {
+        uint4 gv = *reinterpret_cast<const uint4*>(xr + k);
+        uint4 uv = *reinterpret_cast<const uint4*>(xr + K + k);
+        const uint32_t* ug = reinterpret_cast<const uint32_t*>(&gv);
+        const uint32_t* uu = reinterpret_cast<const uint32_t*>(&uv);
+        uint4 o;
+        uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 g = unpack_bf16x2(ug[i]);
+          float2 up = unpack_bf16x2(uu[i]);
+          uo[i] = pack_bf16x2(silu_mul(g.x, up.x), silu_mul(g.y, up.y));
+        }
+        *reinterpret_cast<uint4*>(dst + k * 2) = o;
+      }
+    } else {
+      for (int k = ctid * 8; k < K; k += NC * 8)
+        *reinterpret_cast<uint4*>(dst + k * 2) = *reinterpret_cast<const uint4*>(xr + k);
+    }
+  }
+  named_barrier(1, NC);
+
+  const int g = lane >> 2, tq = lane & 3;
+  const uint32_t zero_addr = smem_u32(smem + L.zero_off);
+  // Per-lane ldmatrix row addresses.
+  const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
+  const int a_col = 8 * (lane >> 4);
+  const int b_tok = lane & 7;
+  const int b_col = 8 * ((lane >> 3) & 1);
+  const bool b_valid = b_tok < a.T;
+  const uint32_t xs_base = smem_u32(xs + b_tok * XROW + b_col * 2);
+
+  bool ok = true;
+  for (int tile = 0; tile < n_tiles && ok; ++tile) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kc = 0; kc < n_kc; ++kc) {
+      const int u = tile * n_kc + kc;
+      const int s = u % kGemvStages;
+      if (!mbar_wait(&full_bar[s], (u / kGemvStages) & 1)) {
+        if (lane == 0) set_status(a.status, PL_ERR_TIMEOUT);
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      const int k0 = kc * kKC;
+      const int ksteps = min(kKC, K - k0) / 16;
+      const uint32_t stage = smem_u32(smem + s * kGemvStageBytes);
+      for (int ks = cw; ks < ksteps; ks += kGemvConsumers) {
+        uint32_t af[4], bfr2[2];
+        ldsm_x4(stage + a_row * kRowBytes + (ks * 16 + a_col) * 2, af[0], af[1], af[2], af[3]);
+        ldsm_x2(b_valid ? xs_base + (k0 + ks * 16) * 2 : zero_addr, bfr2[0], bfr2[1]);
+        mma_bf16_16816(acc, af, bfr2);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+    }
+    if (!ok) break;
+    // Cross-warp reduction of the 16 x 8 tile, then the epilogue.
+    float* rb = red + (tile & 1) * (kGemvConsumers * kTileRows * kMaxTok);
+    float* mine = rb + cw * kTileRows * kMaxTok;
+    mine[g * kMaxTok + 2 * tq] = acc[0];
+    mine[g * kMaxTok + 2 * tq + 1] = acc[1];
+    mine[(g + 8) * kMaxTok + 2 * tq] = acc[2];
+    mine[(g + 8) * kMaxTok + 2 * tq + 1] = acc[3];
+    named_barrier(1, NC);
+    {
+      const int row = ctid / kMaxTok, tok = ctid % kMaxTok;
+      const int64_t o = r0 + (int64_t)tile * kTileRows + row;
+      if (tok < a.T && o < r1) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvConsumers; ++w) v += rb[(w * kTileRows + row) * kMaxTok + tok];
+        if (o >= a.n_out) {
+          a.shrink_out[tok * a.shrink_stride + (o - a.n_out)] = v;
+        } else {
+          if (a.bias != nullptr) v += bf2f(a.bias[o]);
+          if (a.lora_b != nullptr) {
+            const int ad = a.tok_adapter != nullptr ? a.tok_adapter[tok] : 0;
+            float vb = bfr(v);
+            if (ad >= 0) {
+              int sl = 0;
+              while (sl < a.num_slices - 1 && o >= a.slice_end[sl]) ++sl;
+              const bf16* brow = a.lora_b + ((int64_t)ad * a.n_out + o) * a.rank;
+              const float* drow = a.lora_down + tok * a.down_stride + sl * a.rank;
+              float d = 0.f;
+              for (int j = 0; j < a.rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
+              vb = bfr(vb + bfr(d));
+            }
+            v = vb;
+          }
+          if (a.residual != nullptr) v = bf2f(a.residual[tok * a.res_stride + o]) + bfr(v);
+          a.y[tok * a.y_stride + o] = f2bf(v);
+        }
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------- shrink
+// One CTA per (rank row j, segment); down[t, j] = x[t] . A[adapter][j].
+__global__ void __launch_bounds__(256) lora_shrink_kernel(const bf16* __restrict__ x, int64_t x_stride,
+                                                         const bf16* __restrict__ A, int num_adapters, int rank,
+                                                         int K, const int32_t* __restrict__ seg_indptr,
+                                                         const int32_t* __restrict__ seg_adapter,
+                                                         float* __restrict__ down, int64_t down_stride) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int j = blockIdx.x, sg = blockIdx.y;
+  const int t0 = seg_indptr[sg], t1 = seg_indptr[sg + 1];
+  const int ad = seg_adapter[sg];
+  __shared__ float part[8][kMaxTok];
+  if (ad < 0 || ad >= num_adapters) {
+    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) down[t * down_stride + j] = 0.f;
+    return;
+  }
+  const bf16* arow = A + ((int64_t)ad * rank + j) * K;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int tb = t0; tb < t1; tb += kMaxTok) {
+    const int nt = min(kMaxTok, t1 - tb);
+    float acc[kMaxTok];
+#pragma unroll
+    for (int i = 0; i < kMaxTok; ++i) acc[i] = 0.f;
+    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+      uint4 av = *reinterpret_cast<const uint4*>(arow + k);
+      const uint32_t* ua = reinterpret_cast<const uint32_t*>(&av);
+      float af[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f = unpack_bf16x2(ua[i]);
+        af[2 * i] = f.x;
+        af[2 * i + 1] = f.y;
+      }
+#pragma unroll
+      for (int i = 0; i < kMaxTok; ++i) {
+        if (i < nt) {
+          uint4 xv = *reinterpret_cast<const uint4*>(x + (int64_t)(tb + i) * x_stride + k);
+          const uint32_t* ux = reinterpret_cast<const uint32_t*>(&xv);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float2 f = unpack_bf16x2(ux[q]);
+            acc[i] += af[2 * q] * f.x + af[2 * q + 1] * f.y;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxTok; ++i) {
+      float v = warp_sum(acc[i]);
+      if (lane == 0) part[warp][i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < nt) {
+      float v = 0.f;
+      for (int w = 0; w < (int)(blockDim.x / 32); ++w) v += part[w][threadIdx.x];
+      down[(int64_t)(tb + threadIdx.x) * down_stride + j] = v;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------ merge weight
+__global__ void lora_merge_weight_kernel(const bf16* __restrict__ w_in, bf16* __restrict__ w_out,
+                                         const bf16* __restrict__ A, const bf16* __restrict__ B, int N, int K,
+                                         int R, float scale, float sign, int mode) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t chunks = (int64_t)N * (K / 8);
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks; c += (int64_t)gridDim.x * blockDim.x) {
+    const int o = (int)(c / (K / 8));
+    const int col = (int)(c % (K / 8)) * 8;
+    float d[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = 0.f;
+    for (int j = 0; j < R; ++j) {
+      const float bj = bf2f(B[(int64_t)o * R + j]);
+      uint4 av = *reinterpret_cast<const uint4*>(A + (int64_t)j * K + col);
+      const uint32_t* ua = reinterpret_cast<const uint32_t*>(&av);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = unpack_bf16x2(ua[q]);
+        d[2 * q] += bj * f.x;
+        d[2 * q + 1] += bj * f.y;
+      }
+    }
+    uint4 wv = *reinterpret_cast<const uint4*>(w_in + (int64_t)o * K + col);
+    const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 out;
+    uint32_t* uo = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float2 wf = unpack_bf16x2(uw[q]);
+      float r[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float wi = h ? wf.y : wf.x;
+        const float dm = bfr(d[2 * q + h]);  // the bf16 matmul output B @ A
+        if (mode == 0) {
+          r[h] = wi + sign * bfr(dm * scale);
+        } else {
+          r[h] = wi + sign * scale * dm;
+        }
+      }
+      uo[q] = pack_bf16x2(r[0], r[1]);
+    }
+    *reinterpret_cast<uint4*>(w_out + (int64_t)o * K + col) = out;
+  }
+}
+
+}  // namespace pl
+
+// =================================================================== host
+extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
+                                               int32_t prologue, const void* norm_w, float norm_eps, const void* w,
+                                               int32_t n_out, const void* bias, const float* lora_down,
+                                               int64_t down_stride, const void* lora_b, int32_t lora_rank,
+                                               const int32_t* slice_end, int32_t num_slices,
+                                               const int32_t* tok_adapter, const void* residual, int64_t res_stride,
+                                               void* y, int64_t y_stride, const void* shrink_a, int32_t n_shrink,
+                                               float* shrink_out, int64_t shrink_stride, int32_t flags,
+                                               int32_t* status_dev, void* stream) {
+  if (num_tokens == 0 || (n_out == 0 && n_shrink == 0)) return PL_OK;
+  if (x == nullptr || w == nullptr || num_tokens < 0 || num_tokens > pl::kMaxTok || k_in <= 0 || n_out < 0 ||
+      n_shrink < 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (k_in % 16 != 0) return PL_ERR_UNSUPPORTED;
+  if (n_out > 0 && y == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  if (n_shrink > 0 && (shrink_a == nullptr || shrink_out == nullptr)) return PL_ERR_INVALID_ARGUMENT;
+  if (prologue == PL_PROLOGUE_RMSNORM && norm_w == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  if (prologue < 0 || prologue > 2) return PL_ERR_INVALID_ARGUMENT;
+  if (lora_b != nullptr && (lora_down == nullptr || lora_rank <= 0 || num_slices < 1 || num_slices > 4 ||
+                            (num_slices > 1 && slice_end == nullptr)))
+    return PL_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) || (x_stride % 8) ||
+      (shrink_a != nullptr && (reinterpret_cast<uintptr_t>(shrink_a) & 15)) ||
+      (norm_w != nullptr && (reinterpret_cast<uintptr_t>(norm_w) & 15)))
+    return PL_ERR_INVALID_ARGUMENT;
+
+  pl::GemvArgs a = {};
+  a.x = static_cast<const pl::bf16*>(x);
+  a.x_stride = x_stride;
+  a.T = num_tokens;
+  a.K = k_in;
+  a.prologue = prologue;
+  a.norm_w = static_cast<const pl::bf16*>(norm_w);
+  a.eps = norm_eps;
+  a.w = static_cast<const pl::bf16*>(w);
+  a.n_out = n_out;
+  a.bias = static_cast<const pl::bf16*>(bias);
+  a.lora_down = lora_down;
+  a.down_stride = down_stride;
+  a.lora_b = static_cast<const pl::bf16*>(lora_b);
+  a.rank = lora_rank;
+  a.num_slices = num_slices < 1 ? 1 : num_slices;
+  for (int i = 0; i < 4; ++i) a.slice_end[i] = n_out;
+  for (int i = 0; i < num_slices - 1 && slice_end != nullptr; ++i) a.slice_end[i] = slice_end[i];
+  a.tok_adapter = tok_adapter;
+  a.residual = static_cast<const pl::bf16*>(residual);
+  a.res_stride = res_stride;
+  a.y = static_cast<pl::bf16*>(y);
+  a.y_stride = y_stride;
+  a.shrink_a = static_cast<const pl::bf16*>(shrink_a);
+  a.n_shrink = n_shrink;
+  a.shrink_out = shrink_out;
+  a.shrink_stride = shrink_stride;
+  a.early_weights = (flags & 1) ? 1 : 0;
+  a.status = status_dev;
+
+  const pl::GemvSmem L = pl::gemv_smem_layout(num_tokens, k_in);
+  if (L.total > 227 * 1024) return PL_ERR_UNSUPPORTED;
+  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel), L.total);
+  if (st != PL_OK) return st;
+  int sms = pl_host::sm_count();
+  if (sms <= 0) sms = 148;
+  const int64_t rows = (int64_t)n_out + n_shrink;
+  const int64_t tiles = (rows + pl::kTileRows - 1) / pl::kTileRows;
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  return pl_host::launch_pdl(pl::linear_lora_kernel, dim3(grid), dim3(pl::kGemvThreads), L.total, stream, a);
+}
+
+extern "C" int32_t pl_lora_shrink_seg(const void* x, int64_t x_stride, const void* a, int32_t num_adapters,
+                                      int32_t rank, int32_t in_features, const int32_t* seg_indptr,
+                                      const int32_t* seg_adapter, int32_t num_segments, int32_t num_tokens,
+                                      float* down, int64_t down_stride, void* stream) {
+  if (num_tokens == 0 || num_segments == 0 || rank == 0) return PL_OK;
+  if (x == nullptr || a == nullptr || seg_indptr == nullptr || seg_adapter == nullptr || down == nullptr ||
+      rank < 0 || in_features <= 0 || num_segments < 0 || num_adapters <= 0 || num_segments > 65535)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (in_features % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(a) & 15) ||
+      (x_stride % 8))
+    return PL_ERR_UNSUPPORTED;
+  return pl_host::launch_pdl(pl::lora_shrink_kernel, dim3(rank, num_segments), dim3(256), 0, stream,
+                             static_cast<const pl::bf16*>(x), x_stride, static_cast<const pl::bf16*>(a),
+                             (int)num_adapters, (int)rank, (int)in_features, seg_indptr, seg_adapter, down,
+                             down_stride);
+}
+
+extern "C" int32_t pl_lora_merge_weight(const void* w_in, void* w_out, const void* a, const void* b, int32_t n_out,
+                                        int32_t k_in, int32_t rank, float scale, int32_t sign, int32_t mode,
+                                        void* stream) {
+  if (n_out == 0 || k_in == 0) return PL_OK;
+  if (w_in == nullptr || w_out == nullptr || a == nullptr || b == nullptr || n_out < 0 || k_in < 0 || rank <= 0 ||
+      (sign != 1 && sign != -1) || (mode != 0 && mode != 1))
+    return PL_ERR_INVALID_ARGUMENT;
+  if (k_in % 8 != 0 || (reinterpret_cast<uintptr_t>(w_in) & 15) || (reinterpret_cast<uintptr_t>(w_out) & 15) ||
+      (reinterpret_cast<uintptr_t>(a) & 15))
+    return PL_ERR_UNSUPPORTED;
+  int sms = pl_host::sm_count();
+  if (sms <= 0) sms = 148;
+  const int64_t chunks = (int64_t)n_out * (k_in / 8);
+  int64_t blocks = (chunks + 255) / 256;
+  if (blocks > 8LL * sms) blocks = 8LL * sms;
+  return pl_host::launch_pdl(pl::lora_merge_weight_kernel, dim3((unsigned)blocks), dim3(256), 0, stream,
+                             static_cast<const pl::bf16*>(w_in), static_cast<pl::bf16*>(w_out),
+                             static_cast<const pl::bf16*>(a), static_cast<const pl::bf16*>(b), (int)n_out, (int)k_in,
+                             (int)rank, scale, (float)sign, (int)mode);
+}

@@ -1,0 +1,332 @@
+"""Torch-tensor wrappers over the C ABI (``include/pagelora_b200.h``).
+
+Each function validates dtype / device / layout on the host, passes raw
+device pointers and the current CUDA stream to the library and raises on a
+non-zero status.  None of them allocates unless it creates its own output
+(``out=None``), and none synchronises, so every call is capturable in a
+CUDA graph when its outputs are preallocated.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from pagelora_b200 import _capi
+from pagelora_b200._capi import DecodePlan, call, ptr, stream_handle
+
+
+def _need_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise RuntimeError("pagelora_b200 kernels run on CUDA tensors only (no CPU path)")
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _row_stride(t: torch.Tensor, name: str) -> int:
+    if t.dim() < 2:
+        return t.shape[-1] if t.dim() == 1 else 0
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must be contiguous in its last dimension")
+    return t.stride(-2)
+
+
+# ------------------------------------------------------------ page tables
+def page_table_build(
+    span_block_id: torch.Tensor,
+    span_start: torch.Tensor,
+    span_length: torch.Tensor,
+    row_indptr: torch.Tensor,
+    page_size: int,
+    out_indptr: torch.Tensor,
+    out_indices: torch.Tensor,
+    out_last_page_len: torch.Tensor,
+    status: torch.Tensor,
+    err_row: torch.Tensor | None = None,
+) -> None:
+    """Device CSR page-table build from spans (see pl_page_table_build)."""
+
+    _need_cuda(span_block_id, out_indptr, status)
+    for name, t in (("span_block_id", span_block_id), ("span_start", span_start), ("span_length", span_length),
+                    ("row_indptr", row_indptr), ("out_indptr", out_indptr), ("out_indices", out_indices),
+                    ("out_last_page_len", out_last_page_len), ("status", status)):
+        _need(t, torch.int32, name)
+    num_rows = row_indptr.numel() - 1
+    call("pl_page_table_build", ptr(span_block_id), ptr(span_start), ptr(span_length), ptr(row_indptr),
+         num_rows, int(page_size), ptr(out_indptr), ptr(out_indices), ptr(out_last_page_len), ptr(status),
+         ptr(err_row), stream_handle())
+
+
+def page_table_advance(
+    row_num_pages: torch.Tensor,
+    last_page_len: torch.Tensor,
+    row_pages: torch.Tensor,
+    new_page_ids: torch.Tensor,
+    page_size: int,
+    out_indptr: torch.Tensor,
+    out_indices: torch.Tensor,
+    slot_page_id: torch.Tensor,
+    slot_offset: torch.Tensor,
+    positions: torch.Tensor | None,
+    status: torch.Tensor,
+) -> None:
+    """Advance a device page table by one token per row (pl_page_table_advance)."""
+
+    _need_cuda(row_pages, status)
+    num_rows, cap = row_pages.shape
+    call("pl_page_table_advance", ptr(row_num_pages), ptr(last_page_len), ptr(row_pages), ptr(new_page_ids),
+         int(num_rows), int(cap), int(page_size), ptr(out_indptr), ptr(out_indices), ptr(slot_page_id),
+         ptr(slot_offset), ptr(positions), ptr(status), stream_handle())
+
+
+# ------------------------------------------------------- decode attention
+def decode_plan(batch: int, num_qo_heads: int, num_kv_heads: int, head_dim: int, page_size: int,
+                total_pages: int, max_splits: int = 0) -> DecodePlan:
+    plan = DecodePlan()
+    lib = _capi.load_library()
+    _capi.check("pl_decode_plan", lib.pl_decode_plan(int(batch), int(num_qo_heads), int(num_kv_heads),
+                                                     int(head_dim), int(page_size), int(total_pages),
+                                                     int(max_splits), plan))
+    return plan
+
+
+def paged_decode(
+    q: torch.Tensor,
+    kv_cache: torch.Tensor,
+    indptr: torch.Tensor,
+    indices: torch.Tensor,
+    last_page_len: torch.Tensor,
+    *,
+    num_splits: int,
+    workspace: torch.Tensor | None,
+    status: torch.Tensor | None = None,
+    sm_scale: float | None = None,
+    out: torch.Tensor | None = None,
+    out_lse: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Paged decode attention: q [B, Hq, D] bf16, kv_cache [P, 2, PS, Hkv, D] bf16."""
+
+    _need_cuda(q, kv_cache, indptr, indices, last_page_len)
+    _need(q, torch.bfloat16, "q")
+    _need(kv_cache, torch.bfloat16, "kv_cache")
+    if kv_cache.dim() != 5 or kv_cache.size(1) != 2 or not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous [pages, 2, page_size, kv_heads, head_dim] tensor")
+    if q.dim() != 3 or q.stride(-1) != 1:
+        raise ValueError("q must be [batch, qo_heads, head_dim] with unit last stride")
+    for name, t in (("indptr", indptr), ("indices", indices), ("last_page_len", last_page_len)):
+        _need(t, torch.int32, name)
+    batch, hq, d = q.shape
+    num_pages, _, page_size, hkv, d2 = kv_cache.shape
+    if d2 != d:
+        raise ValueError("q and kv_cache head_dim differ")
+    if out is None:
+        out = torch.empty_like(q)
+    scale = (1.0 / math.sqrt(d)) if sm_scale is None else float(sm_scale)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    call("pl_paged_decode", ptr(q), q.stride(0), q.stride(1), ptr(kv_cache), int(num_pages), ptr(indptr),
+         ptr(indices), ptr(last_page_len), int(batch), int(hq), int(hkv), int(d), int(page_size), scale,
+         int(num_splits), ptr(out), out.stride(0), out.stride(1), ptr(out_lse), ptr(workspace), int(ws_bytes),
+         ptr(status), stream_handle())
+    return out
+
+
+def merge_states(v_partial: torch.Tensor, lse_partial: torch.Tensor, out: torch.Tensor | None = None,
+                 out_lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge [rows, S, D] fp32 partial states with natural-log LSE [rows, S]."""
+
+    _need_cuda(v_partial, lse_partial)
+    _need(v_partial, torch.float32, "v_partial")
+    _need(lse_partial, torch.float32, "lse_partial")
+    rows, states, d = v_partial.shape
+    if not v_partial.is_contiguous() or not lse_partial.is_contiguous():
+        raise ValueError("partial states must be contiguous")
+    if out is None:
+        out = torch.empty(rows, d, dtype=torch.bfloat16, device=v_partial.device)
+    call("pl_merge_states", ptr(v_partial), ptr(lse_partial), int(rows), int(states), int(d), ptr(out),
+         _row_stride(out, "out"), ptr(out_lse), stream_handle())
+    return out
+
+
+# --------------------------------------------------------------- LoRA path
+def lora_shrink_seg(x: torch.Tensor, a_stack: torch.Tensor, seg_indptr: torch.Tensor,
+                    seg_adapter: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """down[t] = x[t] . A[adapter(seg(t))]^T (fp32), a_stack [n_adapters, rank, in]."""
+
+    _need_cuda(x, a_stack, seg_indptr, seg_adapter)
+    _need(x, torch.bfloat16, "x")
+    _need(a_stack, torch.bfloat16, "a_stack")
+    _need(seg_indptr, torch.int32, "seg_indptr")
+    _need(seg_adapter, torch.int32, "seg_adapter")
+    n_ad, rank, k = a_stack.shape
+    t = x.shape[0]
+    if out is None:
+        out = torch.empty(t, rank, dtype=torch.float32, device=x.device)
+    call("pl_lora_shrink_seg", ptr(x), _row_stride(x, "x"), ptr(a_stack), int(n_ad), int(rank), int(k),
+         ptr(seg_indptr), ptr(seg_adapter), int(seg_adapter.numel()), int(t), ptr(out), _row_stride(out, "down"),
+         stream_handle())
+    return out
+
+
+def linear_lora_fused(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    prologue: int = _capi.PL_PROLOGUE_NONE,
+    norm_weight: torch.Tensor | None = None,
+    norm_eps: float = 1e-6,
+    lora_down: torch.Tensor | None = None,
+    lora_b: torch.Tensor | None = None,
+    slice_ends: tuple[int, ...] = (),
+    tok_adapter: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    shrink_a: torch.Tensor | None = None,
+    shrink_out: torch.Tensor | None = None,
+    weights_static: bool = False,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """y = x . W^T (+bias) (+ LoRA expand) (+ residual) for <= 8 tokens.
+
+    ``x`` is [T, K] (or [T, 2K] for the SiLU-and-mul prologue), ``weight``
+    [N, K], ``lora_b`` [n_adapters, N, rank] with scale folded in,
+    ``lora_down`` [T, >= num_slices*rank] fp32, ``shrink_a`` [n_shrink, K]
+    whose fp32 products go to ``shrink_out`` [T, n_shrink].
+    """
+
+    _need_cuda(x, weight)
+    _need(x, torch.bfloat16, "x")
+    _need(weight, torch.bfloat16, "weight")
+    if not weight.is_contiguous():
+        raise ValueError("weight must be contiguous [out, in]")
+    t = x.shape[0]
+    n, k = weight.shape
+    if out is None and n > 0:
+        out = torch.empty(t, n, dtype=torch.bfloat16, device=x.device)
+    rank = 0
+    num_slices = 1
+    slice_ptr, slice_keepalive = None, None
+    if lora_b is not None:
+        if lora_b.dim() == 2:
+            lora_b = lora_b.unsqueeze(0)
+        rank = lora_b.shape[-1]
+        num_slices = len(slice_ends) + 1 if slice_ends else 1
+        if slice_ends:
+            slice_ptr, slice_keepalive = ctypes_int32_array(slice_ends)
+    n_shrink = 0 if shrink_a is None else shrink_a.shape[0]
+    if shrink_a is not None and shrink_out is None:
+        shrink_out = torch.empty(t, n_shrink, dtype=torch.float32, device=x.device)
+    flags = _capi.PL_FLAG_WEIGHTS_STATIC if weights_static else 0
+    call("pl_linear_lora_expand_fused", ptr(x), _row_stride(x, "x"), int(t), int(k), int(prologue),
+         ptr(norm_weight), float(norm_eps), ptr(weight), int(n), ptr(bias), ptr(lora_down),
+         0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
+         slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
+         0 if residual is None else _row_stride(residual, "residual"), ptr(out),
+         0 if out is None else _row_stride(out, "out"), ptr(shrink_a), int(n_shrink), ptr(shrink_out),
+         0 if shrink_out is None else _row_stride(shrink_out, "shrink_out"), int(flags), ptr(status),
+         stream_handle())
+    del slice_keepalive
+    return out
+
+
+def ctypes_int32_array(values):
+    """A host int32 array and its address (keep the array alive across the call)."""
+
+    import ctypes
+
+    arr = (ctypes.c_int32 * len(values))(*[int(v) for v in values])
+    return ctypes.cast(arr, ctypes.c_void_p).value, arr
+
+
+def lora_merge_weight(w_in: torch.Tensor, a: torch.Tensor, b: torch.Tensor, scale: float, *, sign: int = 1,
+                      mode: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """w_out = w_in + sign * scale * (B @ A) with the reference's rounding (mode 0/1)."""
+
+    _need_cuda(w_in, a, b)
+    for name, t in (("w", w_in), ("a", a), ("b", b)):
+        _need(t, torch.bfloat16, name)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    n, k = w_in.shape
+    r = a.shape[0]
+    if out is None:
+        out = torch.empty_like(w_in)
+    call("pl_lora_merge_weight", ptr(w_in), ptr(out), ptr(a), ptr(b), int(n), int(k), int(r), float(scale),
+         int(sign), int(mode), stream_handle())
+    return out
+
+
+# ---------------------------------------------------- decode-step glue ops
+def kv_append(k: torch.Tensor, v: torch.Tensor, kv_cache: torch.Tensor, page_id: torch.Tensor,
+              page_offset: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """Scatter k, v [T, Hkv, D] into the pool at (page_id[t], page_offset[t])."""
+
+    _need_cuda(k, v, kv_cache, page_id, page_offset)
+    _need(page_id, torch.int32, "page_id")
+    _need(page_offset, torch.int32, "page_offset")
+    t, hkv, d = k.shape
+    if not (k.stride(-1) == 1 and k.stride(-2) == d and v.stride(-1) == 1 and v.stride(-2) == d):
+        raise ValueError("k/v must be [T, Hkv, D] with contiguous heads")
+    num_pages, _, page_size, _, _ = kv_cache.shape
+    call("pl_kv_append", ptr(k), k.stride(0), ptr(v), v.stride(0), ptr(kv_cache), int(num_pages), ptr(page_id),
+         ptr(page_offset), int(t), int(hkv), int(d), int(page_size), ptr(status), stream_handle())
+
+
+def qkv_rope_append(
+    qkv: torch.Tensor,
+    *,
+    num_qo_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    positions: torch.Tensor,
+    rope_theta: float,
+    kv_cache: torch.Tensor,
+    page_id: torch.Tensor,
+    page_offset: torch.Tensor,
+    q_out: torch.Tensor,
+    lora_down: torch.Tensor | None = None,
+    lora_b: torch.Tensor | None = None,
+    tok_adapter: torch.Tensor | None = None,
+    q_norm_weight: torch.Tensor | None = None,
+    k_norm_weight: torch.Tensor | None = None,
+    norm_eps: float = 1e-6,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    _need_cuda(qkv, positions, kv_cache, q_out)
+    t = qkv.shape[0]
+    num_pages, _, page_size, _, _ = kv_cache.shape
+    rank = 0
+    if lora_b is not None:
+        if lora_b.dim() == 2:
+            lora_b = lora_b.unsqueeze(0)
+        rank = lora_b.shape[-1]
+    call("pl_qkv_rope_append", ptr(qkv), _row_stride(qkv, "qkv"), ptr(lora_down),
+         0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank), ptr(tok_adapter),
+         ptr(q_norm_weight), ptr(k_norm_weight), float(norm_eps), ptr(positions), float(rope_theta), ptr(q_out),
+         ptr(kv_cache), int(num_pages), ptr(page_id), ptr(page_offset), int(t), int(num_qo_heads),
+         int(num_kv_heads), int(head_dim), int(page_size), ptr(status), stream_handle())
+    return q_out
+
+
+def embed(token_ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor,
+          status: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(token_ids, table, out)
+    _need(token_ids, torch.int64, "token_ids")
+    vocab, dim = table.shape
+    call("pl_embed", ptr(token_ids), ptr(table), int(vocab), int(dim), int(token_ids.numel()), ptr(out),
+         ptr(status), stream_handle())
+    return out
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    _need_cuda(logits, out)
+    _need(logits, torch.bfloat16, "logits")
+    _need(out, torch.int64, "out")
+    t, vocab = logits.shape
+    call("pl_argmax", ptr(logits), _row_stride(logits, "logits"), int(vocab), int(t), ptr(out), stream_handle())
+    return out

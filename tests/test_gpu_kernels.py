@@ -1,0 +1,387 @@
+"""Parity of every CUDA kernel (called through the C ABI) with the CPU oracle.
+
+Integer work (page tables) must be bit-exact; bf16 attention / LoRA outputs
+must be within max |err| <= 2e-2 of the fp64 oracle (the tolerance stated
+for this path), and LoRA outputs that mimic the reference's rounding points
+must match the reference's own bf16 outputs to within 2 bf16 ulps.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lora as olora
+from oracle import page_table as opt
+from oracle.numerics import apply_rope, bf16, rmsnorm_fused, rmsnorm_hf, silu
+from oracle.paged_decode import merge_states as o_merge
+from oracle.paged_decode import paged_decode as o_decode
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def K(cuda_device):
+    from pagelora_b200 import kernels
+
+    return kernels
+
+
+def _t(a, dtype=torch.bfloat16, dev="cuda"):
+    return torch.as_tensor(np.asarray(a, dtype=np.float32)).to(device=dev, dtype=dtype)
+
+
+def _i32(a, dev="cuda"):
+    return torch.as_tensor(np.asarray(a, dtype=np.int32)).to(dev)
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _ulps_close(actual, expected, ulps=2):
+    actual = np.asarray(actual, np.float32)
+    expected = np.asarray(expected, np.float32)
+    tol = ulps * np.maximum(np.abs(expected), 1e-3) * 2.0 ** -8 + 1e-6
+    bad = np.abs(actual - expected) > tol
+    assert not bad.any(), f"{bad.sum()} elements off; worst {float(np.max(np.abs(actual - expected) / tol)):.2f} tol"
+
+
+# ------------------------------------------------------------ page tables
+def _build_dev(K, rows, page_size):
+    flat = [s for row in rows for s in row]
+    row_indptr = np.cumsum([0] + [len(r) for r in rows])
+    blk = _i32([s[0] for s in flat] or [0])
+    st = _i32([s[1] for s in flat] or [0])
+    ln = _i32([s[2] for s in flat] or [0])
+    n_rows = len(rows)
+    out_indptr = torch.full((n_rows + 1,), -7, dtype=torch.int32, device="cuda")
+    out_indices = torch.full((max(1, len(flat)),), -7, dtype=torch.int32, device="cuda")
+    out_last = torch.full((max(1, n_rows),), -7, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    err_row = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    K.page_table_build(blk, st, ln, _i32(row_indptr), page_size, out_indptr, out_indices, out_last, status, err_row)
+    torch.cuda.synchronize()
+    return out_indptr.cpu().tolist(), out_indices.cpu().tolist(), out_last.cpu().tolist(), int(status.item())
+
+
+def test_page_table_build_bit_exact_vs_reference_fixture(K, golden_dir):
+    from pagelora_b200._capi import SPAN_ERROR_MESSAGES
+
+    cases = json.loads((golden_dir / "page_tables.json").read_text())
+    for case in cases:
+        indptr, indices, last, status = _build_dev(K, case["rows"], case["page_size"])
+        if "error" in case:
+            assert status != 0 and SPAN_ERROR_MESSAGES[status] == case["error"], case
+            assert indptr == [-7] * len(indptr)  # nothing written on error
+        else:
+            assert status == 0
+            assert indptr == case["indptr"]
+            n = case["indptr"][-1]
+            assert indices[:n] == case["indices"]
+            assert last[: len(case["rows"])] == case["last_page_len"]
+
+
+def test_page_table_build_large_rows_vs_oracle(K):
+    rng = np.random.default_rng(11)
+    rows = []
+    for _ in range(40):
+        n = int(rng.integers(0, 300))
+        pages = rng.permutation(5000)[:n]
+        row = []
+        for j, p in enumerate(pages):
+            ln = 16 if j < n - 1 else int(rng.integers(1, 17))
+            if rng.random() < 0.2 and ln > 1:
+                c = int(rng.integers(1, ln))
+                row += [[int(p), 0, c], [int(p), c, 0], [int(p), c, ln - c]]
+            else:
+                row.append([int(p), 0, ln])
+        rows.append(row)
+    got = _build_dev(K, rows, 16)
+    want = opt.build_batch(rows, 16)
+    assert got[3] == 0
+    assert got[0] == want[0] and got[1][: want[0][-1]] == want[1] and got[2] == want[2]
+
+
+def test_page_table_advance_vs_oracle(K):
+    rows, cap, ps = 5, 8, 4
+    row_pages = [[], [3], [5, 6], [7], [9, 10, 11]]
+    last = [0, 4, 2, 1, 4]
+    dev_pages = torch.zeros(rows, cap, dtype=torch.int32, device="cuda")
+    for r, pg in enumerate(row_pages):
+        if pg:
+            dev_pages[r, : len(pg)] = torch.tensor(pg, dtype=torch.int32)
+    n = _i32([len(p) for p in row_pages])
+    dl = _i32(last)
+    indptr = torch.zeros(rows + 1, dtype=torch.int32, device="cuda")
+    indices = torch.zeros(rows * cap, dtype=torch.int32, device="cuda")
+    sp, so, pos = (torch.zeros(rows, dtype=torch.int32, device="cuda") for _ in range(3))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for step in range(9):
+        new = [100 + 10 * step + r for r in range(rows)]
+        K.page_table_advance(n, dl, dev_pages, _i32(new), ps, indptr, indices, sp, so, pos, status)
+        want = opt.advance(row_pages, last, new, ps)
+        assert (sp.tolist(), so.tolist(), pos.tolist()) == tuple(list(x) for x in want)
+        ip, idx, ll = opt.build_batch([[(p, 0, ps) for p in pg[:-1]] + [(pg[-1], 0, last[r])]
+                                       for r, pg in enumerate(row_pages)], ps)
+        assert indptr.tolist() == ip and indices.tolist()[: ip[-1]] == idx and dl.tolist() == ll
+    assert int(status.item()) == 0
+
+
+# ------------------------------------------------------- decode attention
+def _decode_case(K, *, batch, hq, hkv, d, ps, lens, num_splits, seed, n_pages_pool=None, ws_mb=8):
+    rng = np.random.default_rng(seed)
+    pages_per_row = [-(-L // ps) for L in lens]
+    total = sum(pages_per_row)
+    pool = n_pages_pool or total + 3
+    cache = bf16(rng.normal(size=(pool, 2, ps, hkv, d)))
+    perm = rng.permutation(pool)[:total]
+    indptr = np.cumsum([0] + pages_per_row).tolist()
+    indices = perm.tolist()
+    last = [L - (n - 1) * ps if n else 0 for L, n in zip(lens, pages_per_row)]
+    q = bf16(rng.normal(size=(batch, hq, d)) * 1.5)
+    ws = torch.zeros(ws_mb << 20, dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    lse = torch.zeros(batch, hq, dtype=torch.float32, device="cuda")
+    out = K.paged_decode(_t(q), _t(cache), _i32(indptr), _i32(indices or [0]), _i32(last),
+                         num_splits=num_splits, workspace=ws, status=status, out_lse=lse)
+    torch.cuda.synchronize()
+    ref, ref_lse = o_decode(q, cache, indptr, indices, last)
+    assert int(status.item()) == 0
+    # counters are left at zero for the next call
+    assert int(ws[: 4 * batch * hkv].view(torch.int32).abs().sum().item()) == 0
+    return _np(out), _np(lse), ref, ref_lse
+
+
+@pytest.mark.parametrize("d,ps", [(128, 16), (64, 16), (128, 32), (64, 32)])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 8), (16, 2), (16, 1)])
+def test_paged_decode_vs_oracle(K, d, ps, hq, hkv):
+    lens = [1, ps, ps + 1, 5 * ps - 3, 300]
+    for splits in (1, 3, 16):
+        out, lse, ref, ref_lse = _decode_case(K, batch=len(lens), hq=hq, hkv=hkv, d=d, ps=ps, lens=lens,
+                                              num_splits=splits, seed=hq * 7 + d + ps + splits)
+        assert np.max(np.abs(out - ref)) <= ATOL
+        np.testing.assert_allclose(lse, ref_lse, rtol=1e-3, atol=1e-3)
+
+
+def test_paged_decode_empty_row_and_long_context(K):
+    out, lse, ref, ref_lse = _decode_case(K, batch=3, hq=32, hkv=8, d=128, ps=16, lens=[0, 2112, 7],
+                                          num_splits=37, seed=5)
+    assert np.all(out[0] == 0) and np.all(np.isneginf(lse[0]))
+    assert np.max(np.abs(out - ref)) <= ATOL
+    np.testing.assert_allclose(lse[1:], ref_lse[1:], rtol=1e-3, atol=1e-3)
+
+
+def test_paged_decode_reports_out_of_range_page(K):
+    cache = torch.zeros(4, 2, 16, 2, 64, dtype=torch.bfloat16, device="cuda")
+    q = torch.ones(1, 4, 64, dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    K.paged_decode(q, cache, _i32([0, 2]), _i32([1, 99]), _i32([16]), num_splits=1, workspace=ws, status=status)
+    torch.cuda.synchronize()
+    from pagelora_b200._capi import PL_ERR_PAGE_OUT_OF_RANGE
+
+    assert int(status.item()) == PL_ERR_PAGE_OUT_OF_RANGE
+
+
+def test_merge_states_vs_oracle(K):
+    rng = np.random.default_rng(2)
+    v = rng.normal(size=(37, 6, 128)).astype(np.float32)
+    lse = rng.normal(size=(37, 6)).astype(np.float32) * 3
+    lse[3, :] = -np.inf
+    lse[5, 2] = -np.inf
+    out_lse = torch.zeros(37, dtype=torch.float32, device="cuda")
+    out = K.merge_states(_t(v, torch.float32), _t(lse, torch.float32), out_lse=out_lse)
+    ref, ref_lse = o_merge(np.moveaxis(v, 1, 0), lse.T)
+    assert np.max(np.abs(_np(out) - ref)) <= ATOL
+    np.testing.assert_allclose(_np(out_lse)[np.isfinite(ref_lse)], ref_lse[np.isfinite(ref_lse)], rtol=1e-5)
+    assert np.all(np.isneginf(_np(out_lse)[3]))
+
+
+# ------------------------------------------------------------ LoRA kernels
+def test_lora_shrink_seg_vs_oracle(K):
+    rng = np.random.default_rng(4)
+    x = bf16(rng.normal(size=(13, 512)))
+    a = bf16(rng.normal(size=(3, 16, 512)) * 0.02)
+    seg_indptr, seg_adapter = [0, 2, 2, 9, 13], [1, 0, 2, -1]
+    out = K.lora_shrink_seg(_t(x), _t(a), _i32(seg_indptr), _i32(seg_adapter))
+    torch.cuda.synchronize()
+    ref = olora.shrink_seg(x, a, seg_indptr, seg_adapter)
+    np.testing.assert_allclose(_np(out), ref, rtol=1e-4, atol=1e-4)
+
+
+def test_linear_lora_matches_reference_lora_linear(K, golden_dir):
+    """The fused kernel reproduces multilora/linear.py LoRALinear.forward (bf16)."""
+
+    z = np.load(golden_dir / "lora_cases.npz")
+    for case in range(3):
+        pre = f"lora_linear_bf16_{case}_"
+        x, w, a, b = z[pre + "x"], z[pre + "w"], z[pre + "a"], z[pre + "b"]
+        sc = float(z[pre + "scale"][0])
+        bias = _t(z[pre + "bias"]) if z[pre + "bias"].size else None
+        t = x.shape[0]
+        down = K.lora_shrink_seg(_t(x), _t(a)[None], _i32([0, t]), _i32([0]))
+        y = K.linear_lora_fused(_t(x), _t(w), bias=bias, lora_down=down, lora_b=_t(bf16(b * sc))[None])
+        torch.cuda.synchronize()
+        _ulps_close(_np(y), z[pre + "y"])
+
+
+def test_packed_qkv_matches_reference(K, golden_dir):
+    """Packed q/k/v + packed LoRA delta (packed_ops.py) via the shrink rows
+    of the fused kernel and the expand of qkv_rope_append's LoRA step."""
+
+    z = np.load(golden_dir / "lora_cases.npz")
+    for case in range(2):
+        pre = f"packed_{case}_"
+        sc = float(z[pre + "scale"][0])
+        x = z[pre + "x"]
+        w = np.concatenate([z[f"{pre}{m}_w"] for m in "qkv"])
+        a = np.concatenate([z[f"{pre}{m}_a"] for m in "qkv"])
+        b = np.concatenate([bf16(z[f"{pre}{m}_b"] * sc) for m in "qkv"])
+        dq, dk = z[pre + "q"].shape[-1], z[pre + "k"].shape[-1]
+        down = torch.zeros(x.shape[0], a.shape[0], dtype=torch.float32, device="cuda")
+        base = K.linear_lora_fused(_t(x), _t(w), shrink_a=_t(a), shrink_out=down)
+        # expand exactly as the decode path does: slices q | k | v with rank r
+        y = K.linear_lora_fused(_t(x), _t(w), lora_down=down, lora_b=_t(b)[None], slice_ends=(dq, dq + dk))
+        torch.cuda.synchronize()
+        ref = np.concatenate([z[pre + "q"], z[pre + "k"], z[pre + "v"]], -1)
+        _ulps_close(_np(y), ref)
+        _ulps_close(_np(base), olora.linear(x, w, bf16=True))
+
+
+@pytest.mark.parametrize("t", [1, 2, 5, 8])
+def test_linear_lora_fused_prologues_and_epilogues_vs_oracle(K, t):
+    rng = np.random.default_rng(100 + t)
+    k_in, n, r, n_ad = 1024, 700, 16, 3
+    x = bf16(rng.normal(size=(t, k_in)))
+    res = bf16(rng.normal(size=(t, n)))
+    w = bf16(rng.normal(size=(n, k_in)) * 0.02)
+    bias = bf16(rng.normal(size=n) * 0.1)
+    nw = bf16(1 + rng.normal(size=k_in) * 0.1)
+    down = rng.normal(size=(t, 2 * r)).astype(np.float32)
+    bmat = bf16(rng.normal(size=(n_ad, n, r)) * 0.05)
+    tok_ad = rng.integers(-1, n_ad, size=t)
+    a_rows = bf16(rng.normal(size=(24, k_in)) * 0.02)
+    shrink = torch.zeros(t, 24, dtype=torch.float32, device="cuda")
+    y = K.linear_lora_fused(_t(x), _t(w), bias=_t(bias), prologue=1, norm_weight=_t(nw), norm_eps=1e-6,
+                            lora_down=_t(down, torch.float32), lora_b=_t(bmat), slice_ends=(300,),
+                            tok_adapter=_i32(tok_ad), residual=_t(res), shrink_a=_t(a_rows), shrink_out=shrink)
+    torch.cuda.synchronize()
+    xn = rmsnorm_fused(x, nw, 1e-6)
+    base = bf16(xn.astype(np.float64) @ w.T.astype(np.float64) + bias)
+    want = np.zeros((t, n), np.float32)
+    for i in range(t):
+        yi = base[i]
+        if tok_ad[i] >= 0:
+            d = np.concatenate([bmat[tok_ad[i], :300] @ bf16(down[i, :r]), bmat[tok_ad[i], 300:] @ bf16(down[i, r:])])
+            yi = bf16(yi + bf16(d))
+        want[i] = bf16(res[i] + yi)
+    _ulps_close(_np(y), want, ulps=3)
+    np.testing.assert_allclose(_np(shrink), xn.astype(np.float64) @ a_rows.T.astype(np.float64), rtol=1e-3, atol=1e-3)
+    # SiLU-and-mul prologue
+    gu = bf16(rng.normal(size=(t, 2 * k_in)))
+    y2 = K.linear_lora_fused(_t(gu), _t(w))
+    y3 = K.linear_lora_fused(_t(gu), _t(w), prologue=2)
+    torch.cuda.synchronize()
+    act = bf16(silu(gu[:, :k_in]) * gu[:, k_in:])
+    _ulps_close(_np(y3), bf16(act.astype(np.float64) @ w.T.astype(np.float64)), ulps=3)
+    _ulps_close(_np(y2), bf16(gu[:, :k_in].astype(np.float64) @ w.T.astype(np.float64)), ulps=3)
+
+
+def test_linear_lora_fused_large_shapes(K):
+    """Decode shapes of Qwen3-8B (qkv, o, gate_up, down) at one token."""
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for n, k in ((6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288)):
+        w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+        x = torch.randn(1, k, generator=g, device="cuda").bfloat16()
+        y = K.linear_lora_fused(x, w, weights_static=True)
+        ref = (x.double() @ w.double().T)
+        assert torch.max(torch.abs(y.double() - ref)).item() <= ATOL
+
+
+def test_lora_merge_weight_matches_reference(K, golden_dir):
+    z = np.load(golden_dir / "lora_cases.npz")
+    w, a, b, sc = _t(z["merge_w"]), _t(z["merge_a"]), _t(z["merge_b"]), float(z["merge_scale"][0])
+    m0 = K.lora_merge_weight(w, a, b, sc, mode=0)
+    m1 = K.lora_merge_weight(w, a, b, sc, mode=1)
+    un = K.lora_merge_weight(m0, a, b, sc, mode=0, sign=-1)
+    torch.cuda.synchronize()
+    _ulps_close(_np(m0), z["merge_serve_merged"])
+    _ulps_close(_np(m0), z["merge_effective_linear"])
+    _ulps_close(_np(m1), z["merge_effective_packed"])
+    _ulps_close(_np(un), z["merge_serve_unmerged"])
+
+
+# ------------------------------------------------------------- glue kernels
+def test_kv_append_matches_index_put(K):
+    cache = torch.zeros(6, 2, 16, 4, 128, dtype=torch.bfloat16, device="cuda")
+    ref = cache.clone()
+    k = torch.randn(5, 4, 128, device="cuda").bfloat16()
+    v = torch.randn(5, 4, 128, device="cuda").bfloat16()
+    pid = _i32([3, 0, 5, 3, 1])
+    off = _i32([0, 15, 7, 1, 9])
+    K.kv_append(k, v, cache, pid, off)
+    ref.index_put_((pid.long(), torch.zeros_like(pid).long(), off.long()), k)
+    ref.index_put_((pid.long(), torch.ones_like(pid).long(), off.long()), v)
+    torch.cuda.synchronize()
+    assert torch.equal(cache, ref)
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_qkv_rope_append_vs_oracle(K, qk_norm):
+    rng = np.random.default_rng(9)
+    t, hq, hkv, d, r, ps = 3, 8, 2, 128, 16, 16
+    n_all = (hq + 2 * hkv) * d
+    qkv = bf16(rng.normal(size=(t, n_all)))
+    down = rng.normal(size=(t, 3 * r)).astype(np.float32)
+    bmat = bf16(rng.normal(size=(1, n_all, r)) * 0.05)
+    qn = bf16(1 + rng.normal(size=d) * 0.1)
+    kn = bf16(1 + rng.normal(size=d) * 0.1)
+    pos = np.array([0, 17, 2047], np.int32)
+    pid, off = np.array([2, 0, 3], np.int32), np.array([0, 5, 15], np.int32)
+    cache = torch.zeros(4, 2, ps, hkv, d, dtype=torch.bfloat16, device="cuda")
+    q_out = torch.zeros(t, hq, d, dtype=torch.bfloat16, device="cuda")
+    K.qkv_rope_append(_t(qkv), num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, positions=_i32(pos),
+                      rope_theta=1e6, kv_cache=cache, page_id=_i32(pid), page_offset=_i32(off), q_out=q_out,
+                      lora_down=_t(down, torch.float32), lora_b=_t(bmat),
+                      q_norm_weight=_t(qn) if qk_norm else None, k_norm_weight=_t(kn) if qk_norm else None)
+    torch.cuda.synchronize()
+    full = np.zeros_like(qkv)
+    for i in range(t):
+        for sl, (c0, c1) in enumerate(((0, hq * d), (hq * d, (hq + hkv) * d), ((hq + hkv) * d, n_all))):
+            dl = bmat[0, c0:c1] @ bf16(down[i, sl * r:(sl + 1) * r])
+            full[i, c0:c1] = bf16(qkv[i, c0:c1] + bf16(dl))
+    q = full[:, : hq * d].reshape(t, hq, d)
+    k = full[:, hq * d:(hq + hkv) * d].reshape(t, hkv, d)
+    v = full[:, (hq + hkv) * d:].reshape(t, hkv, d)
+    if qk_norm:
+        q, k = rmsnorm_hf(q, qn, 1e-6), rmsnorm_hf(k, kn, 1e-6)
+    q, k = bf16(apply_rope(q, pos, 1e6)), bf16(apply_rope(k, pos, 1e6))
+    assert np.max(np.abs(_np(q_out) - q)) <= ATOL
+    c = _np(cache)
+    for i in range(t):
+        assert np.max(np.abs(c[pid[i], 0, off[i]] - k[i])) <= ATOL
+        assert np.array_equal(c[pid[i], 1, off[i]], v[i])
+
+
+def test_embed_and_argmax(K):
+    table = torch.randn(1000, 256, device="cuda").bfloat16()
+    ids = torch.tensor([5, 999, 0], device="cuda")
+    out = torch.zeros(3, 256, dtype=torch.bfloat16, device="cuda")
+    K.embed(ids, table, out)
+    logits = torch.randn(4, 151936, device="cuda").bfloat16()
+    logits[2, 77] = 50.0
+    logits[2, 78] = 50.0  # tie: first index wins (torch.argmax)
+    am = torch.zeros(4, dtype=torch.int64, device="cuda")
+    K.argmax(logits, am)
+    torch.cuda.synchronize()
+    assert torch.equal(out, table[ids])
+    assert torch.equal(am, torch.argmax(logits, -1))
+    assert am[2].item() == 77
