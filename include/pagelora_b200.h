@@ -204,14 +204,17 @@ int32_t pl_lora_shrink_seg(const void *x, int64_t x_stride,
 /*
  * Base projection with the LoRA expand and residual fused into its epilogue:
  *   base   = x . W^T (+ bias)                              (W bf16 [n_out, K])
- *   delta  = bf16( B_s[adapter(t)][o, :] . bf16(down[t, roff(o) : roff(o)+rank]) )
+ *   delta  = bf16( bf16( B[adapter(t)][o, :] . bf16(down[t, roff(o) : roff(o)+rank]) ) * lora_scale )
  *   y      = bf16( bf16(base) + delta )                     (lora_b != NULL)
  *   y      = bf16( residual + bf16(y) )                     (residual != NULL)
  * roff(o) = rank * (slice of o), slices are [0, slice_end[0]), [slice_end[0],
  * slice_end[1]), ... (up to 4, e.g. q/k/v) -- the packed block-diagonal B of
- * packed_ops.py:328-384 without its zero blocks.  B_s holds B * scale
- * (bf16, [num_adapters, n_out, rank]); adapter(t) = tok_adapter[t] (device,
- * -1 = none) or 0 when tok_adapter is NULL.
+ * packed_ops.py:328-384 without its zero blocks.  B is bf16
+ * [num_adapters, n_out, rank]; pass B * scale with lora_scale = 1 for the
+ * packed path (packed_ops.py:371-373 folds the scale into B) or the plain B
+ * with lora_scale = alpha/rank for LoRALinear.forward (linear.py:230-231
+ * scales the rounded product).  adapter(t) = tok_adapter[t] (device, -1 =
+ * none) or 0 when tok_adapter is NULL.
  * Optionally extra "shrink rows": rows n_out .. n_out+n_shrink of the
  * weight stream are taken from shrink_a (bf16 [n_shrink, K]) and their
  * fp32 results x . shrink_a^T are written to shrink_out[t, :] (row stride
@@ -232,7 +235,8 @@ int32_t pl_linear_lora_expand_fused(
     int32_t prologue, const void *norm_w, float norm_eps,
     const void *w, int32_t n_out, const void *bias,
     const float *lora_down, int64_t down_stride, const void *lora_b,
-    int32_t lora_rank, const int32_t *slice_end, int32_t num_slices,
+    int32_t lora_rank, float lora_scale, const int32_t *slice_end,
+    int32_t num_slices,
     const int32_t *tok_adapter,
     const void *residual, int64_t res_stride,
     void *y, int64_t y_stride,
@@ -271,8 +275,9 @@ int32_t pl_kv_append(const void *k, int64_t k_stride, const void *v,
                      int32_t *status_dev, void *stream);
 
 /*
- * Post-projection step of one decode token: optional packed-LoRA expand
- * (when lora_down != NULL, same rounding as pl_linear_lora_expand_fused),
+ * Post-projection step of one decode token: optional LoRA expand (when
+ * lora_down != NULL, same rounding and lora_scale rule as
+ * pl_linear_lora_expand_fused; a module without LoRA has zero B rows),
  * optional per-head RMSNorm of q and k (Qwen3 q_norm / k_norm with the HF
  * module's rounding), RoPE (non-interleaved, theta, positions) on q and k,
  * then K/V appended to the paged pool and q written for attention.
@@ -285,6 +290,7 @@ int32_t pl_kv_append(const void *k, int64_t k_stride, const void *v,
 int32_t pl_qkv_rope_append(const void *qkv, int64_t qkv_stride,
                            const float *lora_down, int64_t down_stride,
                            const void *lora_b, int32_t lora_rank,
+                           float lora_scale,
                            const int32_t *tok_adapter,
                            const void *q_norm_w, const void *k_norm_w,
                            float norm_eps, const int32_t *positions,

@@ -69,15 +69,15 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pl_lora_shrink_seg": (_I32, [_P, _I64, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _I64, _P]),
     "pl_linear_lora_expand_fused": (
         _I32,
-        [_P, _I64, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _I64, _P, _I32, _P, _I32, _P, _P, _I64, _P, _I64,
-         _P, _I32, _P, _I64, _I32, _P, _P],
+        [_P, _I64, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _I64, _P, _I32, _F, _P, _I32, _P, _P, _I64, _P,
+         _I64, _P, _I32, _P, _I64, _I32, _P, _P],
     ),
     "pl_lora_merge_weight": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _F, _I32, _I32, _P]),
     "pl_kv_append": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),
     "pl_qkv_rope_append": (
         _I32,
-        [_P, _I64, _P, _I64, _P, _I32, _P, _P, _P, _F, _P, _F, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32,
-         _I32, _P, _P],
+        [_P, _I64, _P, _I64, _P, _I32, _F, _P, _P, _P, _F, _P, _F, _P, _P, _I64, _P, _P, _I32, _I32, _I32,
+         _I32, _I32, _P, _P],
     ),
     "pl_embed": (_I32, [_P, _P, _I64, _I32, _I32, _P, _P, _P]),
     "pl_argmax": (_I32, [_P, _I64, _I32, _I32, _P, _P]),

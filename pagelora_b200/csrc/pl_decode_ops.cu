@@ -318,7 +318,7 @@ __global__ void kv_append_kernel(const bf16* __restrict__ k, int64_t k_stride, c
 template <int D>
 __global__ void __launch_bounds__(128) qkv_rope_append_kernel(
     const bf16* __restrict__ qkv, int64_t qkv_stride, const float* __restrict__ down, int64_t down_stride,
-    const bf16* __restrict__ lora_b, int rank, const int32_t* __restrict__ tok_adapter,
+    const bf16* __restrict__ lora_b, int rank, float lora_scale, const int32_t* __restrict__ tok_adapter,
     const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w, float eps,
     const int32_t* __restrict__ positions, float rope_theta, bf16* __restrict__ q_out, bf16* __restrict__ cache,
     int64_t num_pages, const int32_t* __restrict__ page_id, const int32_t* __restrict__ page_off, int T, int Hq,
@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(128) qkv_rope_append_kernel(
         const bf16* brow = lora_b + ((int64_t)ad * n_out + col + d0 + e) * rank;
         float d = 0.f;
         for (int j = 0; j < rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
-        v[e] = bfr(v[e] + bfr(d));
+        v[e] = bfr(v[e] + bfr(bfr(d) * lora_scale));
       }
     }
   }
@@ -521,6 +521,7 @@ extern "C" int32_t pl_kv_append(const void* k, int64_t k_stride, const void* v, 
 
 extern "C" int32_t pl_qkv_rope_append(const void* qkv, int64_t qkv_stride, const float* lora_down,
                                       int64_t down_stride, const void* lora_b, int32_t lora_rank,
+                                      float lora_scale,
                                       const int32_t* tok_adapter, const void* q_norm_w, const void* k_norm_w,
                                       float norm_eps, const int32_t* positions, float rope_theta, void* q_out,
                                       void* kv_cache, int64_t num_pages, const int32_t* page_id,
@@ -537,7 +538,7 @@ extern "C" int32_t pl_qkv_rope_append(const void* qkv, int64_t qkv_stride, const
   if (head_dim == 128)
     return pl_host::launch_pdl(pl::qkv_rope_append_kernel<128>, dim3(blocks), dim3(128), 0, stream,
                                static_cast<const pl::bf16*>(qkv), qkv_stride, lora_down, down_stride,
-                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, tok_adapter,
+                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, lora_scale, tok_adapter,
                                static_cast<const pl::bf16*>(q_norm_w), static_cast<const pl::bf16*>(k_norm_w),
                                norm_eps, positions, rope_theta, static_cast<pl::bf16*>(q_out),
                                static_cast<pl::bf16*>(kv_cache), num_pages, page_id, page_offset, (int)num_tokens,
@@ -545,7 +546,7 @@ extern "C" int32_t pl_qkv_rope_append(const void* qkv, int64_t qkv_stride, const
   if (head_dim == 64)
     return pl_host::launch_pdl(pl::qkv_rope_append_kernel<64>, dim3(blocks), dim3(128), 0, stream,
                                static_cast<const pl::bf16*>(qkv), qkv_stride, lora_down, down_stride,
-                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, tok_adapter,
+                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, lora_scale, tok_adapter,
                                static_cast<const pl::bf16*>(q_norm_w), static_cast<const pl::bf16*>(k_norm_w),
                                norm_eps, positions, rope_theta, static_cast<pl::bf16*>(q_out),
                                static_cast<pl::bf16*>(kv_cache), num_pages, page_id, page_offset, (int)num_tokens,

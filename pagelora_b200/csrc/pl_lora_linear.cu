@@ -40,6 +40,7 @@ struct GemvArgs {
   int64_t down_stride;
   const bf16* lora_b;
   int32_t rank;
+  float lora_scale;
   int32_t slice_end[4];
   int32_t num_slices;
   const int32_t* tok_adapter;
@@ -286,7 +287,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const Gemv
               const float* drow = a.lora_down + tok * a.down_stride + sl * a.rank;
               float d = 0.f;
               for (int j = 0; j < a.rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
-              vb = bfr(vb + bfr(d));
+              vb = bfr(vb + bfr(bfr(d) * a.lora_scale));
             }
             v = vb;
           }
@@ -415,6 +416,7 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
                                                int32_t prologue, const void* norm_w, float norm_eps, const void* w,
                                                int32_t n_out, const void* bias, const float* lora_down,
                                                int64_t down_stride, const void* lora_b, int32_t lora_rank,
+                                               float lora_scale,
                                                const int32_t* slice_end, int32_t num_slices,
                                                const int32_t* tok_adapter, const void* residual, int64_t res_stride,
                                                void* y, int64_t y_stride, const void* shrink_a, int32_t n_shrink,
@@ -452,6 +454,7 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   a.down_stride = down_stride;
   a.lora_b = static_cast<const pl::bf16*>(lora_b);
   a.rank = lora_rank;
+  a.lora_scale = lora_scale;
   a.num_slices = num_slices < 1 ? 1 : num_slices;
   for (int i = 0; i < 4; ++i) a.slice_end[i] = n_out;
   for (int i = 0; i < num_slices - 1 && slice_end != nullptr; ++i) a.slice_end[i] = slice_end[i];

@@ -85,6 +85,8 @@ class DecodeEngine:
         self.device = torch.device(device)
         self.page_size = page_size
         self.lora_rank = lora_spec.rank if (lora and lora_spec) else 0
+        self.lora_scale = lora_spec.scale if (lora and lora_spec) else 1.0
+        self.qkv_lora_scale = 1.0
         dev, bf = self.device, torch.bfloat16
         H, D = spec.hidden, spec.head_dim
 
@@ -101,6 +103,11 @@ class DecodeEngine:
             a_qkv = b_qkv = a_o = b_o = None
             if self.lora_rank:
                 r, sc = lora_spec.rank, lora_spec.scale
+                # With LoRA on all of q/k/v the reference packs B * scale into one
+                # block-diagonal matrix (packed_ops.py:363-375); otherwise each
+                # module's delta is bf16(bf16(down . B^T) * scale) (:534-553).
+                packed = all(f"layers.{i}.{t}" in lora for t in "qkv")
+                self.qkv_lora_scale = 1.0 if packed else sc
                 a_parts, b_parts = [], []
                 for t, od in (("q", spec.q_dim), ("k", spec.kv_dim), ("v", spec.kv_dim)):
                     ab = lora.get(f"layers.{i}.{t}")
@@ -109,13 +116,13 @@ class DecodeEngine:
                         b_parts.append(torch.zeros(od, r, device=dev, dtype=bf))
                     else:
                         a_parts.append(ab[0].to(dev, bf))
-                        b_parts.append((ab[1].to(dev, bf) * sc).to(bf))
+                        b_parts.append((ab[1].to(dev, bf) * sc).to(bf) if packed else ab[1].to(dev, bf))
                 a_qkv = torch.cat(a_parts, 0).contiguous()
                 b_qkv = torch.cat(b_parts, 0).unsqueeze(0).contiguous()
                 ab = lora.get(f"layers.{i}.o")
-                if ab is not None:
+                if ab is not None:  # LoRALinear.forward: scale applied to the rounded product
                     a_o = ab[0].to(dev, bf).unsqueeze(0).contiguous()
-                    b_o = (ab[1].to(dev, bf) * sc).to(bf).unsqueeze(0).contiguous()
+                    b_o = ab[1].to(dev, bf).unsqueeze(0).contiguous()
             wg, wu = take(p + "mlp.gate_proj.weight"), take(p + "mlp.up_proj.weight")
             w_gu = torch.cat([wg, wu], 0).contiguous()
             del wg, wu
@@ -218,7 +225,8 @@ class DecodeEngine:
                 deltas = []
                 off = 0
                 for j, od in enumerate((s.q_dim, s.kv_dim, s.kv_dim)):
-                    deltas.append(F.linear(down[:, j * r:(j + 1) * r], L.b_qkv[0, off:off + od]))
+                    dj = F.linear(down[:, j * r:(j + 1) * r], L.b_qkv[0, off:off + od])
+                    deltas.append(dj if self.qkv_lora_scale == 1.0 else dj * self.qkv_lora_scale)
                     off += od
                 qkv = qkv + torch.cat(deltas, -1)
             q = qkv[:, : s.q_dim].view(n, s.num_qo_heads, s.head_dim)
@@ -235,7 +243,7 @@ class DecodeEngine:
             attn = attn[0].transpose(0, 1).reshape(n, s.q_dim)
             o = F.linear(attn, L.w_o)
             if L.a_o is not None:
-                o = o + F.linear(F.linear(attn, L.a_o[0]), L.b_o[0])
+                o = o + F.linear(F.linear(attn, L.a_o[0]), L.b_o[0]) * self.lora_scale
             x = x + o
             h2 = _rmsnorm_fused(x, L.post_norm, s.rms_eps)
             gu = F.linear(h2, L.w_gate_up)
@@ -286,13 +294,13 @@ class DecodeEngine:
                               head_dim=s.head_dim, positions=self.positions, rope_theta=s.rope_theta,
                               kv_cache=self.kv[li], page_id=self.slot_page, page_offset=self.slot_off, q_out=self.q,
                               lora_down=self.down_qkv if L.b_qkv is not None else None, lora_b=L.b_qkv,
-                              q_norm_weight=L.q_norm, k_norm_weight=L.k_norm, norm_eps=s.rms_eps, status=st)
+                              lora_scale=self.qkv_lora_scale, q_norm_weight=L.q_norm, k_norm_weight=L.k_norm, norm_eps=s.rms_eps, status=st)
             K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
                            num_splits=self.num_splits, workspace=self.workspace, status=st, out=self.attn)
             if L.a_o is not None:
                 K.lora_shrink_seg(attn2d, L.a_o, self.seg_indptr, self.seg_adapter, out=self.down_o)
             K.linear_lora_fused(attn2d, L.w_o, lora_down=self.down_o if L.b_o is not None else None, lora_b=L.b_o,
-                                residual=self.x, out=self.x, weights_static=True, status=st)
+                                lora_scale=self.lora_scale, residual=self.x, out=self.x, weights_static=True, status=st)
             K.linear_lora_fused(self.x, L.w_gate_up, prologue=PL_PROLOGUE_RMSNORM, norm_weight=L.post_norm,
                                 norm_eps=s.rms_eps, out=self.gate_up, weights_static=True, status=st)
             K.linear_lora_fused(self.gate_up, L.w_down, prologue=PL_PROLOGUE_SILU_MUL, residual=self.x,

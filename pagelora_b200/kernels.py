@@ -182,6 +182,7 @@ def linear_lora_fused(
     norm_eps: float = 1e-6,
     lora_down: torch.Tensor | None = None,
     lora_b: torch.Tensor | None = None,
+    lora_scale: float = 1.0,
     slice_ends: tuple[int, ...] = (),
     tok_adapter: torch.Tensor | None = None,
     residual: torch.Tensor | None = None,
@@ -225,7 +226,7 @@ def linear_lora_fused(
     call("pl_linear_lora_expand_fused", ptr(x), _row_stride(x, "x"), int(t), int(k), int(prologue),
          ptr(norm_weight), float(norm_eps), ptr(weight), int(n), ptr(bias), ptr(lora_down),
          0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
-         slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
+         float(lora_scale), slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
          0 if residual is None else _row_stride(residual, "residual"), ptr(out),
          0 if out is None else _row_stride(out, "out"), ptr(shrink_a), int(n_shrink), ptr(shrink_out),
          0 if shrink_out is None else _row_stride(shrink_out, "shrink_out"), int(flags), ptr(status),
@@ -291,6 +292,7 @@ def qkv_rope_append(
     q_out: torch.Tensor,
     lora_down: torch.Tensor | None = None,
     lora_b: torch.Tensor | None = None,
+    lora_scale: float = 1.0,
     tok_adapter: torch.Tensor | None = None,
     q_norm_weight: torch.Tensor | None = None,
     k_norm_weight: torch.Tensor | None = None,
@@ -306,7 +308,8 @@ def qkv_rope_append(
             lora_b = lora_b.unsqueeze(0)
         rank = lora_b.shape[-1]
     call("pl_qkv_rope_append", ptr(qkv), _row_stride(qkv, "qkv"), ptr(lora_down),
-         0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank), ptr(tok_adapter),
+         0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
+         float(lora_scale), ptr(tok_adapter),
          ptr(q_norm_weight), ptr(k_norm_weight), float(norm_eps), ptr(positions), float(rope_theta), ptr(q_out),
          ptr(kv_cache), int(num_pages), ptr(page_id), ptr(page_offset), int(t), int(num_qo_heads),
          int(num_kv_heads), int(head_dim), int(page_size), ptr(status), stream_handle())
