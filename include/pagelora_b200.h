@@ -245,6 +245,16 @@ int32_t pl_linear_lora_expand_fused(
     int32_t *status_dev, void *stream);
 
 /*
+ * Pipeline shape of pl_linear_lora_expand_fused for this process: shared-
+ * memory ring depth (stages), columns per 16-row stage, consumer warps
+ * (4 or 8) and CTAs per SM.  No reference counterpart (a tuning knob);
+ * defaults 8 / 512 / 4 / 1.  The ring is made shallower automatically when
+ * tokens x K does not fit in shared memory.
+ */
+int32_t pl_linear_set_tuning(int32_t stages, int32_t cols_per_stage,
+                             int32_t consumer_warps, int32_t ctas_per_sm);
+
+/*
  * Merged ("effective") weight builder: w_out = w_in + sign * scale * (B @ A)
  * with the reference's rounding points (bf16 tensors):
  *   mode 0: bf16(w + bf16(bf16(B@A) * scale))  -- linear.py:143-146,166-172

@@ -18,8 +18,9 @@ namespace pl {
 
 using bf16 = __nv_bfloat16;
 
-// Bound of every device-side wait (ns).  A healthy wait lasts microseconds.
-constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
+// Bound of every device-side wait in SM cycles (~2 s at 2 GHz).  A healthy
+// wait lasts microseconds.
+constexpr long long kWaitTimeoutCycles = 4000000000ll;
 
 // ------------------------------------------------------------------ status
 __device__ __forceinline__ void set_status(int32_t* status, int32_t code) {
@@ -82,13 +83,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase with the given parity to complete; false on timeout.
+// The bound is checked against the SM cycle counter every 1024 polls: a
+// %globaltimer read costs a few hundred ns and would throttle every stage
+// hand-off of the TMA pipelines.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+  const long long c0 = clock64();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 0 && clock64() - c0 > kWaitTimeoutCycles) return false;
   }
-  return true;
 }
 
 // ------------------------------------------------------------------- TMA

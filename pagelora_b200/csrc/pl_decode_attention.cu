@@ -53,7 +53,11 @@ struct DecodeCfg {
   static constexpr int kHalfBytes = PS * 128;         // one box: PS rows x 128 B
   static constexpr int kTileBytes = kHalves * kHalfBytes;  // K (or V) of one page/head
   static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kStages = (65536 / kStageBytes) < 4 ? 4 : ((65536 / kStageBytes) > 8 ? 8 : 65536 / kStageBytes);
+  static constexpr int kBoxesPerPage = 2 * kHalves;            // K and V, per 64-dim half
+  static constexpr int kPagesPerBatch = 32 / kBoxesPerPage;    // pages per producer instruction
+  // Two producer batches in flight, at most 128 KB of stages.
+  static constexpr int kStages = (2 * kPagesPerBatch * kStageBytes <= 131072) ? 2 * kPagesPerBatch
+                                                                              : 131072 / kStageBytes;
   static constexpr int kQRowBytes = D * 2 + 16;       // padded rows: conflict-free ldmatrix
   static constexpr int kNT = PS / 8;                  // score n-tiles per page
   static constexpr int kDT = D / 8;                   // output n-tiles
@@ -66,6 +70,7 @@ struct DecodeCfg {
   static constexpr int kFlagOff = kNtokOff + kStages * 4;
   static constexpr int kSmemBytes = kFlagOff + 16 + 1024;  // + alignment slack
   static_assert(kConsumerWarps * 16 * D * 4 <= kStages * kStageBytes, "merge scratch must fit the stage ring");
+  static_assert(kStages >= kPagesPerBatch, "one producer batch must map to distinct stages");
 };
 
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128B-swizzled box.
@@ -114,42 +119,48 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && n > 0) {
+    // A TMA instruction costs ~0.3 us of issue time however many lanes issue
+    // it, so the warp loads a batch of pages per instruction: one lane per
+    // (page, K/V, 64-dim half) box.
+    if (n > 0) {
       int32_t last_len = args.last_page_len[b];
       last_len = last_len < 0 ? 0 : (last_len > PS ? PS : last_len);
+      const int box = lane % C::kBoxesPerPage;
       int issued = 0;
-      for (int i = 0; i < n; ++i) {
+      for (int i0 = 0; i0 < n; i0 += C::kPagesPerBatch) {
+        const int i = i0 + lane / C::kBoxesPerPage;
+        const bool active = lane < C::kBoxesPerPage * C::kPagesPerBatch && i < n;
         const int s = i % C::kStages;
-        if (i >= C::kStages) {
-          if (!mbar_wait(&empty_bar[s], ((i / C::kStages) - 1) & 1)) {
-            set_status(args.status, PL_ERR_TIMEOUT);
-            flags[0] = 1;
-            break;
+        bool ok = true;
+        if (active && i >= C::kStages) ok = mbar_wait(&empty_bar[s], ((i / C::kStages) - 1) & 1);
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) set_status(args.status, PL_ERR_TIMEOUT);
+          flags[0] = 1;
+          break;
+        }
+        const int32_t page_idx = p0 + i;
+        const int32_t pid = active ? args.indices[row_begin + page_idx] : 0;
+        const int32_t ntok = (page_idx == n_pages - 1) ? last_len : PS;
+        const bool valid = active && pid >= 0 && static_cast<int64_t>(pid) < args.num_pages && ntok > 0;
+        if (active && box == 0) {
+          if (!valid) {
+            if (ntok != 0) set_status(args.status, PL_ERR_PAGE_OUT_OF_RANGE);
+            stage_ntok[s] = 0;
+            mbar_arrive(&full_bar[s]);  // nothing to load: consumers skip the page
+          } else {
+            stage_ntok[s] = ntok;
+            mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
           }
         }
-        if (flags[0]) break;
-        const int32_t page_idx = p0 + i;
-        const int32_t pid = args.indices[row_begin + page_idx];
-        const int32_t ntok = (page_idx == n_pages - 1) ? last_len : PS;
-        if (pid < 0 || static_cast<int64_t>(pid) >= args.num_pages || ntok == 0) {
-          if (ntok != 0) set_status(args.status, PL_ERR_PAGE_OUT_OF_RANGE);
-          stage_ntok[s] = 0;
-          mbar_arrive(&full_bar[s]);  // nothing to load: consumers skip the page
-          ++issued;
-          continue;
+        __syncwarp();
+        if (valid) {
+          const int kv = box / C::kHalves, hh = box % C::kHalves;
+          uint8_t* dst = smem + C::kStageOff + s * C::kStageBytes + kv * C::kTileBytes + hh * C::kHalfBytes;
+          tma_load_4d(dst, &kv_map, hh * 64, kvh, 0, 2 * pid + kv, &full_bar[s]);
         }
-        stage_ntok[s] = ntok;
-        mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
-        uint8_t* kdst = smem + C::kStageOff + s * C::kStageBytes;
-        uint8_t* vdst = kdst + C::kTileBytes;
-#pragma unroll
-        for (int hh = 0; hh < C::kHalves; ++hh) {
-          tma_load_4d(kdst + hh * C::kHalfBytes, &kv_map, hh * 64, kvh, 0, 2 * pid + 0, &full_bar[s]);
-          tma_load_4d(vdst + hh * C::kHalfBytes, &kv_map, hh * 64, kvh, 0, 2 * pid + 1, &full_bar[s]);
-        }
-        ++issued;
+        issued = min(n, i0 + C::kPagesPerBatch);
       }
-      if (flags[0]) {
+      if (flags[0] && lane == 0) {
         // Abort: wait (bounded) for the loads still in flight before the CTA exits.
         for (int i = issued - C::kStages < 0 ? 0 : issued - C::kStages; i < issued; ++i)
           (void)mbar_wait(&full_bar[i % C::kStages], (i / C::kStages) & 1);
@@ -352,26 +363,48 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
       }
       named_barrier(1, 32 * kConsumerWarps);
       if (flags[1]) {
+        // Last CTA of this (row, kv head): merge the S partial states.  The
+        // split weights are computed once per query head into shared memory,
+        // then every thread reduces float4 columns with independent loads.
         __threadfence();
         const int S = args.num_splits;
-        for (int idx = ctid; idx < group * D; idx += 32 * kConsumerWarps) {
-          const int r = idx / D, d = idx % D;
-          const int64_t rowid = (int64_t)b * args.num_qo_heads + hq0 + r;
-          const float* lse = args.partial_lse + rowid * S;
+        const int64_t row0 = (int64_t)b * args.num_qo_heads + hq0;
+        float* wts = scratch;              // [group][S] weights, then [group] 1/L
+        float* inv_l = scratch + group * S;
+        for (int idx = ctid; idx < group * S; idx += 32 * kConsumerWarps)
+          wts[idx] = __ldcg(args.partial_lse + row0 * S + idx);
+        named_barrier(1, 32 * kConsumerWarps);
+        if (ctid < group) {
           float M = -INFINITY;
-          for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(lse + s));
-          float L = 0.f, acc = 0.f;
-          if (M != -INFINITY) {
-            for (int s = 0; s < S; ++s) {
-              const float wt = exp2f(__ldcg(lse + s) - M);
-              L += wt;
-              acc += wt * __ldcg(args.partial_o + (rowid * S + s) * D + d);
-            }
+          for (int s = 0; s < S; ++s) M = fmaxf(M, wts[ctid * S + s]);
+          float L = 0.f;
+          for (int s = 0; s < S; ++s) {
+            const float wt = (M == -INFINITY) ? 0.f : exp2f(wts[ctid * S + s] - M);
+            wts[ctid * S + s] = wt;
+            L += wt;
           }
-          const float val = (L > 0.f) ? acc / L : 0.f;
-          args.out[b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d] = f2bf(val);
-          if (args.out_lse != nullptr && d == 0)
-            args.out_lse[rowid] = (L > 0.f) ? (M + log2f(L)) * kLn2 : -INFINITY;
+          inv_l[ctid] = L > 0.f ? 1.f / L : 0.f;
+          if (args.out_lse != nullptr) args.out_lse[row0 + ctid] = (L > 0.f) ? (M + log2f(L)) * kLn2 : -INFINITY;
+        }
+        named_barrier(1, 32 * kConsumerWarps);
+        for (int idx = ctid; idx < group * (D / 4); idx += 32 * kConsumerWarps) {
+          const int r = idx / (D / 4), d = 4 * (idx % (D / 4));
+          const float4* src = reinterpret_cast<const float4*>(args.partial_o + ((row0 + r) * S) * D + d);
+          const float* wr = wts + r * S;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+          for (int s = 0; s < S; ++s) {
+            const float wt = wr[s];
+            const float4 o = __ldcg(src + (int64_t)s * (D / 4));
+            acc.x += wt * o.x;
+            acc.y += wt * o.y;
+            acc.z += wt * o.z;
+            acc.w += wt * o.w;
+          }
+          const float il = inv_l[r];
+          bf16* dst = args.out + b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
+          reinterpret_cast<uint2*>(dst)[0] = make_uint2(pack_bf16x2(acc.x * il, acc.y * il),
+                                                        pack_bf16x2(acc.z * il, acc.w * il));
         }
         if (ctid == 0) args.counters[b * args.num_kv_heads + kvh] = 0;
       }
@@ -508,11 +541,14 @@ extern "C" int32_t pl_decode_plan(int32_t batch, int32_t num_qo_heads, int32_t n
   const int64_t base = (int64_t)batch * num_kv_heads;
   int splits = 1;
   if (base > 0) {
-    const int64_t target = 2LL * sms;  // two resident CTAs per SM
+    // One wave of CTAs, one per SM; each split keeps >= 4 pages so the
+    // merge (proportional to the split count) stays small next to the scan.
+    const int64_t target = sms;
     const int64_t avg_pages = (total_pages + batch - 1) / (batch > 0 ? batch : 1);
     int64_t by_fill = (target + base - 1) / base;
-    int64_t by_len = avg_pages / 2;  // at least ~2 pages of work per split
+    int64_t by_len = avg_pages / 4;
     int64_t s = by_fill < by_len ? by_fill : by_len;
+    if (s > 64) s = 64;
     if (max_splits > 0 && s > max_splits) s = max_splits;
     splits = s < 1 ? 1 : static_cast<int>(s);
   }
@@ -538,7 +574,8 @@ extern "C" int32_t pl_paged_decode(const void* q, int64_t q_stride_b, int64_t q_
   if (group > 16 || (head_dim != 64 && head_dim != 128) || (page_size != 16 && page_size != 32))
     return PL_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(kv_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(q) & 15) != 0 ||
-      (q_stride_b % 8) != 0 || (q_stride_h % 8) != 0)
+      (q_stride_b % 8) != 0 || (q_stride_h % 8) != 0 || (reinterpret_cast<uintptr_t>(out) & 7) != 0 ||
+      (o_stride_b % 4) != 0 || (o_stride_h % 4) != 0)
     return PL_ERR_INVALID_ARGUMENT;
   const int64_t need = decode_workspace_bytes(batch, num_qo_heads, num_kv_heads, head_dim, num_splits);
   if (num_splits > 1 && (workspace == nullptr || workspace_bytes < need)) return PL_ERR_WORKSPACE_TOO_SMALL;

@@ -17,14 +17,8 @@
 
 namespace pl {
 
-constexpr int kGemvConsumers = 4;
-constexpr int kGemvThreads = 32 * (1 + kGemvConsumers);
-constexpr int kKC = 512;                      // columns per tile
-constexpr int kTileRows = 16;                 // rows per tile (mma M)
-constexpr int kRowBytes = kKC * 2 + 16;       // padded smem row: conflict-free ldmatrix
-constexpr int kGemvStageBytes = kTileRows * kRowBytes;
-constexpr int kGemvStages = 5;
-constexpr int kMaxTok = 8;                    // mma N
+constexpr int kTileRows = 16;  // rows per tile (mma M)
+constexpr int kMaxTok = 8;     // mma N
 
 struct GemvArgs {
   const bf16* x;
@@ -53,26 +47,34 @@ struct GemvArgs {
   float* shrink_out;
   int64_t shrink_stride;
   int32_t early_weights;  // weights are not produced upstream: stream them before the dependency resolves
+  int32_t stages;         // depth of the shared-memory ring
+  int32_t kc;             // columns per stage (multiple of 16)
   int32_t* status;
 };
 
 struct GemvSmem {
   // offsets from a 128-aligned base
-  int x_off, zero_off, red_off, bar_off, misc_off, total;
+  int row_bytes, stage_bytes, nbuf, x_off, zero_off, acc_off, cnt_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline GemvSmem gemv_smem_layout(int T, int K) {
+__host__ __device__ inline GemvSmem gemv_smem_layout(int T, int K, int stages, int kc) {
   GemvSmem L;
-  int off = kGemvStages * kGemvStageBytes;
+  L.row_bytes = kc * 2 + 16;  // padded rows: conflict-free ldmatrix
+  L.stage_bytes = kTileRows * L.row_bytes;
+  L.nbuf = stages + 2;        // tile accumulators in flight (see the epilogue)
+  int off = stages * L.stage_bytes;
   L.x_off = off;
   off += T * (K * 2 + 16);
   off = (off + 15) & ~15;
   L.zero_off = off;
   off += 16;
-  L.red_off = off;
-  off += 2 * kGemvConsumers * kTileRows * kMaxTok * 4;
+  L.acc_off = off;
+  off += L.nbuf * 8 * kTileRows * T * 4;  // [nbuf][warp (<= 8)][16][T] partial tiles
+  L.cnt_off = off;
+  off += L.nbuf * 4;
+  off = (off + 7) & ~7;
   L.bar_off = off;
-  off += 2 * kGemvStages * 8;
+  off += 2 * stages * 8;
   L.misc_off = off;
   off += 64;
   L.total = off + 128;
@@ -81,16 +83,54 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int T, int K) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
-__global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const GemvArgs a) {
+// Epilogue of one output element (row o, token tok) from its fp32 dot product.
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int tok, float v) {
+  if (o >= a.n_out) {
+    a.shrink_out[tok * a.shrink_stride + (o - a.n_out)] = v;
+    return;
+  }
+  if (a.bias != nullptr) v += bf2f(a.bias[o]);
+  if (a.lora_b != nullptr) {
+    const int ad = a.tok_adapter != nullptr ? a.tok_adapter[tok] : 0;
+    float vb = bfr(v);
+    if (ad >= 0) {
+      int sl = 0;
+      while (sl < a.num_slices - 1 && o >= a.slice_end[sl]) ++sl;
+      const bf16* brow = a.lora_b + ((int64_t)ad * a.n_out + o) * a.rank;
+      const float* drow = a.lora_down + tok * a.down_stride + sl * a.rank;
+      float d = 0.f;
+      for (int j = 0; j < a.rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
+      vb = bfr(vb + bfr(bfr(d) * a.lora_scale));
+    }
+    v = vb;
+  }
+  if (a.residual != nullptr) v = bf2f(a.residual[tok * a.res_stride + o]) + bfr(v);
+  a.y[tok * a.y_stride + o] = f2bf(v);
+}
+
+// One CTA per SM streams the weight rows [r0, r1) of its balanced share as
+// 16-row x kc-column tiles.  The producer warp loads a stage with one
+// instruction: lane r issues the bulk copy of row r's kc columns (4 KB at
+// kc = 2048), because a TMA instruction costs ~0.3 us of issue time however
+// many lanes take part.  Consumer warps split the k-steps of each stage and
+// run mma.sync m16n8k16 (weight rows = M, tokens = N); at the end of a tile
+// each warp adds its partial tile into a shared accumulator with shared-
+// memory atomics and the last warp to arrive applies the epilogue, so no
+// CTA-wide barrier ever stalls the stream.
+template <int NCW>
+__global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const GemvSmem L = gemv_smem_layout(a.T, a.K);
+  const int S = a.stages, KC = a.kc;
+  const GemvSmem L = gemv_smem_layout(a.T, a.K, S, KC);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-  uint64_t* empty_bar = full_bar + kGemvStages;
+  uint64_t* empty_bar = full_bar + S;
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + L.misc_off);
-  float* red = reinterpret_cast<float*>(smem + L.red_off);  // [2][warps][16][8]
+  float* tacc = reinterpret_cast<float*>(smem + L.acc_off);      // [nbuf][NCW][16][T]
+  int32_t* tcnt = reinterpret_cast<int32_t*>(smem + L.cnt_off);  // [nbuf]
   uint8_t* xs = smem + L.x_off;
   const int XROW = a.K * 2 + 16;
+  const int RB = L.row_bytes;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int K = a.K;
@@ -98,17 +138,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const Gemv
   const int64_t r0 = rows_total * blockIdx.x / gridDim.x;
   const int64_t r1 = rows_total * (blockIdx.x + 1) / gridDim.x;
   const int n_tiles = (int)((r1 - r0 + kTileRows - 1) / kTileRows);
-  const int n_kc = (K + kKC - 1) / kKC;
+  const int n_kc = (K + KC - 1) / KC;
   const int n_units = n_tiles * n_kc;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemvStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kGemvConsumers);
+      mbar_init(&empty_bar[s], NCW);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
+  for (int i = threadIdx.x; i < L.nbuf; i += blockDim.x) tcnt[i] = 0;
   if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(smem + L.zero_off)[threadIdx.x] = 0u;
   __syncthreads();
   pdl_launch_dependents();
@@ -119,9 +160,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const Gemv
     const uint64_t pol = l2_evict_first_policy();
     int issued = 0;
     for (int u = 0; u < n_units; ++u) {
-      const int s = u % kGemvStages;
-      if (u >= kGemvStages) {
-        if (!mbar_wait(&empty_bar[s], ((u / kGemvStages) - 1) & 1)) {
+      const int s = u % S;
+      if (u >= S) {
+        if (!mbar_wait(&empty_bar[s], ((u / S) - 1) & 1)) {
           if (lane == 0) {
             set_status(a.status, PL_ERR_TIMEOUT);
             *abort_flag = 1;
@@ -133,20 +174,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const Gemv
       const int tile = u / n_kc, kc = u % n_kc;
       const int64_t row0 = r0 + (int64_t)tile * kTileRows;
       const int rows = (int)((r1 - row0) < kTileRows ? (r1 - row0) : kTileRows);
-      const int k0 = kc * kKC;
-      const int kw = min(kKC, K - k0);
+      const int k0 = kc * KC;
+      const int kw = min(KC, K - k0);
       if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(rows * kw * 2));
       __syncwarp();
       if (lane < rows) {
         const int64_t row = row0 + lane;
         const bf16* src = row < a.n_out ? a.w + row * K : a.shrink_a + (row - a.n_out) * K;
-        bulk_g2s(smem + s * kGemvStageBytes + lane * kRowBytes, src + k0, (uint32_t)(kw * 2), &full_bar[s], pol);
+        bulk_g2s(smem + s * L.stage_bytes + lane * RB, src + k0, (uint32_t)(kw * 2), &full_bar[s], pol);
       }
       ++issued;
     }
     if (lane == 0 && *abort_flag) {
-      for (int u = issued - kGemvStages < 0 ? 0 : issued - kGemvStages; u < issued; ++u)
-        (void)mbar_wait(&full_bar[u % kGemvStages], (u / kGemvStages) & 1);
+      for (int u = issued - S < 0 ? 0 : issued - S; u < issued; ++u)
+        (void)mbar_wait(&full_bar[u % S], (u / S) & 1);
     }
     return;
   }
@@ -154,7 +195,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const Gemv
   // ------------------------------------------------------------- consumers
   const int cw = warp - 1;
   const int ctid = threadIdx.x - 32;
-  constexpr int NC = 32 * kGemvConsumers;
+  constexpr int NC = 32 * NCW;
   pdl_wait();
 
   // Prologue: activations -> bf16 rows in shared memory.
@@ -173,12 +214,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const Gemv
         }
       }
       ss = warp_sum(ss);
-      float* part = red;  // reuse the reduction scratch
+      float* part = reinterpret_cast<float*>(smem + L.misc_off + 16);  // NCW <= 8 partials
       if (lane == 0) part[cw] = ss;
       named_barrier(1, NC);
       float tot = 0.f;
 #pragma unroll
-      for (int w = 0; w < kGemvConsumers; ++w) tot += part[w];
+      for (int w = 0; w < NCW; ++w) tot += part[w];
       const float rstd = rsqrtf(tot / (float)K + a.eps);
       named_barrier(1, NC);
       for (int k = ctid * 8; k < K; k += NC * 8) {
@@ -229,71 +270,75 @@ __global__ void __launch_bounds__(kGemvThreads, 1) linear_lora_kernel(const Gemv
   const bool b_valid = b_tok < a.T;
   const uint32_t xs_base = smem_u32(xs + b_tok * XROW + b_col * 2);
 
-  bool ok = true;
-  for (int tile = 0; tile < n_tiles && ok; ++tile) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    // two independent accumulators so consecutive mma's do not serialise
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
     for (int kc = 0; kc < n_kc; ++kc) {
       const int u = tile * n_kc + kc;
-      const int s = u % kGemvStages;
-      if (!mbar_wait(&full_bar[s], (u / kGemvStages) & 1)) {
+      const int s = u % S;
+      if (!mbar_wait(&full_bar[s], (u / S) & 1)) {
         if (lane == 0) set_status(a.status, PL_ERR_TIMEOUT);
         *abort_flag = 1;
-        ok = false;
-        break;
       }
       if (*abort_flag) {
         ok = false;
         break;
       }
-      const int k0 = kc * kKC;
-      const int ksteps = min(kKC, K - k0) / 16;
-      const uint32_t stage = smem_u32(smem + s * kGemvStageBytes);
-      for (int ks = cw; ks < ksteps; ks += kGemvConsumers) {
-        uint32_t af[4], bfr2[2];
-        ldsm_x4(stage + a_row * kRowBytes + (ks * 16 + a_col) * 2, af[0], af[1], af[2], af[3]);
-        ldsm_x2(b_valid ? xs_base + (k0 + ks * 16) * 2 : zero_addr, bfr2[0], bfr2[1]);
-        mma_bf16_16816(acc, af, bfr2);
+      const int k0 = kc * KC;
+      const int ksteps = min(KC, K - k0) / 16;
+      const uint32_t stage = smem_u32(smem + s * L.stage_bytes) + a_row * RB + a_col * 2;
+      const uint32_t xcol = xs_base + k0 * 2;
+      for (int ks = cw; ks < ksteps; ks += 2 * NCW) {
+        const bool two = ks + NCW < ksteps;
+        uint32_t a0[4], b0[2], a1[4], b1[2];
+        ldsm_x4(stage + ks * 32, a0[0], a0[1], a0[2], a0[3]);
+        ldsm_x2(b_valid ? xcol + ks * 32 : zero_addr, b0[0], b0[1]);
+        if (two) {
+          ldsm_x4(stage + (ks + NCW) * 32, a1[0], a1[1], a1[2], a1[3]);
+          ldsm_x2(b_valid ? xcol + (ks + NCW) * 32 : zero_addr, b1[0], b1[1]);
+        }
+        mma_bf16_16816(acc0, a0, b0);
+        if (two) mma_bf16_16816(acc1, a1, b1);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
     if (!ok) break;
-    // Cross-warp reduction of the 16 x 8 tile, then the epilogue.
-    float* rb = red + (tile & 1) * (kGemvConsumers * kTileRows * kMaxTok);
-    float* mine = rb + cw * kTileRows * kMaxTok;
-    mine[g * kMaxTok + 2 * tq] = acc[0];
-    mine[g * kMaxTok + 2 * tq + 1] = acc[1];
-    mine[(g + 8) * kMaxTok + 2 * tq] = acc[2];
-    mine[(g + 8) * kMaxTok + 2 * tq + 1] = acc[3];
-    named_barrier(1, NC);
-    {
-      const int row = ctid / kMaxTok, tok = ctid % kMaxTok;
-      const int64_t o = r0 + (int64_t)tile * kTileRows + row;
-      if (tok < a.T && o < r1) {
+    // Store this warp's 16 x T partial in its slot; the last warp to arrive
+    // sums the slots in warp order (deterministic) and runs the epilogue.
+    const int T = a.T;
+    const int buf = tile % L.nbuf;
+    float* slots = tacc + buf * (NCW * kTileRows * T);
+    float* mine = slots + cw * (kTileRows * T);
+    if (2 * tq < T) {
+      mine[g * T + 2 * tq] = acc0[0] + acc1[0];
+      mine[(g + 8) * T + 2 * tq] = acc0[2] + acc1[2];
+    }
+    if (2 * tq + 1 < T) {
+      mine[g * T + 2 * tq + 1] = acc0[1] + acc1[1];
+      mine[(g + 8) * T + 2 * tq + 1] = acc0[3] + acc1[3];
+    }
+    __threadfence_block();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = (atomicAdd(&tcnt[buf], 1) == NCW - 1);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence_block();
+      for (int e = lane; e < kTileRows * T; e += 32) {
+        const int row = e / T, tok = e % T;
+        const int64_t o = r0 + (int64_t)tile * kTileRows + row;
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kGemvConsumers; ++w) v += rb[(w * kTileRows + row) * kMaxTok + tok];
-        if (o >= a.n_out) {
-          a.shrink_out[tok * a.shrink_stride + (o - a.n_out)] = v;
-        } else {
-          if (a.bias != nullptr) v += bf2f(a.bias[o]);
-          if (a.lora_b != nullptr) {
-            const int ad = a.tok_adapter != nullptr ? a.tok_adapter[tok] : 0;
-            float vb = bfr(v);
-            if (ad >= 0) {
-              int sl = 0;
-              while (sl < a.num_slices - 1 && o >= a.slice_end[sl]) ++sl;
-              const bf16* brow = a.lora_b + ((int64_t)ad * a.n_out + o) * a.rank;
-              const float* drow = a.lora_down + tok * a.down_stride + sl * a.rank;
-              float d = 0.f;
-              for (int j = 0; j < a.rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
-              vb = bfr(vb + bfr(bfr(d) * a.lora_scale));
-            }
-            v = vb;
-          }
-          if (a.residual != nullptr) v = bf2f(a.residual[tok * a.res_stride + o]) + bfr(v);
-          a.y[tok * a.y_stride + o] = f2bf(v);
-        }
+        for (int w = 0; w < NCW; ++w) v += *reinterpret_cast<volatile float*>(&slots[w * kTileRows * T + e]);
+        if (o < r1) gemv_epilogue(a, o, tok, v);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        tcnt[buf] = 0;
       }
     }
   }
@@ -412,6 +457,15 @@ __global__ void lora_merge_weight_kernel(const bf16* __restrict__ w_in, bf16* __
 }  // namespace pl
 
 // =================================================================== host
+namespace {
+// Pipeline shape of linear_lora_kernel (pl_linear_set_tuning): ring depth,
+// columns per 16-row stage, consumer warps, CTAs per SM.
+int g_gemv_stages = 3;
+int g_gemv_kc = 2048;
+int g_gemv_consumers = 8;
+int g_gemv_ctas_per_sm = 1;
+}  // namespace
+
 extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
                                                int32_t prologue, const void* norm_w, float norm_eps, const void* w,
                                                int32_t n_out, const void* bias, const float* lora_down,
@@ -470,16 +524,47 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   a.early_weights = (flags & 1) ? 1 : 0;
   a.status = status_dev;
 
-  const pl::GemvSmem L = pl::gemv_smem_layout(num_tokens, k_in);
-  if (L.total > 227 * 1024) return PL_ERR_UNSUPPORTED;
-  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel), L.total);
-  if (st != PL_OK) return st;
   int sms = pl_host::sm_count();
   if (sms <= 0) sms = 148;
   const int64_t rows = (int64_t)n_out + n_shrink;
   const int64_t tiles = (rows + pl::kTileRows - 1) / pl::kTileRows;
-  const int grid = (int)(tiles < sms ? tiles : sms);
-  return pl_host::launch_pdl(pl::linear_lora_kernel, dim3(grid), dim3(pl::kGemvThreads), L.total, stream, a);
+  const int64_t max_ctas = (int64_t)sms * g_gemv_ctas_per_sm;
+  const int grid = (int)(tiles < max_ctas ? tiles : max_ctas);
+  // Largest ring that fits: the tuned shape, then shallower / narrower stages.
+  int stages = g_gemv_stages, kc = g_gemv_kc;
+  pl::GemvSmem L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc);
+  while (L.total > 227 * 1024 && (stages > 2 || kc > 256)) {
+    if (stages > 2) {
+      --stages;
+    } else {
+      kc /= 2;
+      stages = g_gemv_stages;
+    }
+    L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc);
+  }
+  if (L.total > 227 * 1024) return PL_ERR_UNSUPPORTED;
+  a.stages = stages;
+  a.kc = kc;
+  if (g_gemv_consumers == 8) {
+    int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<8>), L.total);
+    if (st != PL_OK) return st;
+    return pl_host::launch_pdl(pl::linear_lora_kernel<8>, dim3(grid), dim3(32 * 9), L.total, stream, a);
+  }
+  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<4>), L.total);
+  if (st != PL_OK) return st;
+  return pl_host::launch_pdl(pl::linear_lora_kernel<4>, dim3(grid), dim3(32 * 5), L.total, stream, a);
+}
+
+extern "C" int32_t pl_linear_set_tuning(int32_t stages, int32_t cols_per_stage, int32_t consumer_warps,
+                                        int32_t ctas_per_sm) {
+  if (stages < 2 || stages > 16 || cols_per_stage < 256 || cols_per_stage > 4096 || cols_per_stage % 256 ||
+      (consumer_warps != 4 && consumer_warps != 8) || ctas_per_sm < 1 || ctas_per_sm > 4)
+    return PL_ERR_INVALID_ARGUMENT;
+  g_gemv_stages = stages;
+  g_gemv_kc = cols_per_stage;
+  g_gemv_consumers = consumer_warps;
+  g_gemv_ctas_per_sm = ctas_per_sm;
+  return PL_OK;
 }
 
 extern "C" int32_t pl_lora_shrink_seg(const void* x, int64_t x_stride, const void* a, int32_t num_adapters,

@@ -309,7 +309,9 @@ def test_linear_lora_fused_large_shapes(K):
         x = torch.randn(1, k, generator=g, device="cuda").bfloat16()
         y = K.linear_lora_fused(x, w, weights_static=True)
         ref = (x.double() @ w.double().T)
-        assert torch.max(torch.abs(y.double() - ref)).item() <= ATOL
+        # one bf16 rounding of the fp32 accumulation: within 1 ulp of |ref| (+ fp32 sum noise)
+        tol = torch.abs(ref) * 2.0 ** -8 + 1e-3
+        assert bool(torch.all(torch.abs(y.double() - ref) <= tol))
 
 
 def test_lora_merge_weight_matches_reference(K, golden_dir):
