@@ -66,7 +66,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._thread = threading.Thread(target=self._read, daemon=True)
             self._thread.start()
@@ -186,33 +186,39 @@ def run_reference(args) -> None:
 
 
 # --------------------------------------------------------------- GPU arm
-def kernel_roofline(engine, peak_gbs: float) -> dict:
-    """Per-launch CUDA-event timing of every launch of one decode step
-    (eager, each launch bracketed by events on the launching stream), grouped
-    by kernel; achieved GB/s = algorithmic bytes / measured duration."""
+def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
+    """Per-launch device time of every kernel of one decode step.
+
+    The decode step is captured a second time with a timing event recorded
+    before and after every launch (external event nodes of the graph, on the
+    launching stream); the graph is replayed ``replays`` times and each
+    launch's event pair gives its duration.  The event nodes serialise the
+    launches, so this is each kernel timed alone (the programmatic overlap
+    of the production graph is off).  achieved GB/s = algorithmic bytes of
+    the launch / its duration.
+    """
 
     import torch
 
     from pagelora_b200 import kernels as K
 
     s = engine.spec
-    stream = torch.cuda.current_stream()
+    bf = 2
     records: list[tuple[str, float, object, object]] = []
 
     def timed(name: str, nbytes: float, fn, *a, **kw):
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        e0 = torch.cuda.Event(enable_timing=True, external=True)
+        e1 = torch.cuda.Event(enable_timing=True, external=True)
+        e0.record()
         fn(*a, **kw)
-        e1.record(stream)
+        e1.record()
         records.append((name, nbytes, e0, e1))
 
-    bf = 2
-    r = engine.lora_rank
     ctx_tokens = (len(engine.host_pages) - 1) * engine.page_size + engine.host_last + 1
-    kv_bytes = ctx_tokens * s.num_kv_heads * s.head_dim * 2 * bf
-    attn_bytes = kv_bytes + 2 * s.q_dim * bf + (engine.indices.numel() * 0)
-    orig = (K.linear_lora_fused, K.paged_decode, K.lora_shrink_seg, K.qkv_rope_append)
+    attn_bytes = ctx_tokens * s.num_kv_heads * s.head_dim * 2 * bf + 2 * s.q_dim * bf
+    names = ("linear_lora_fused", "paged_decode", "lora_shrink_seg", "qkv_rope_append", "page_table_advance",
+             "embed", "argmax")
+    orig = {n: getattr(K, n) for n in names}
 
     def gemv_bytes(x, weight, kw):
         t = x.shape[0]
@@ -226,46 +232,51 @@ def kernel_roofline(engine, peak_gbs: float) -> dict:
             nb += kw["shrink_a"].numel() * bf + t * kw["shrink_a"].shape[0] * 4
         return nb
 
-    def w_gemv(x, weight, **kw):
-        timed("linear_lora_fused", gemv_bytes(x, weight, kw), orig[0], x, weight, **kw)
-
-    def w_attn(*a, **kw):
-        timed("paged_decode", attn_bytes, orig[1], *a, **kw)
-
-    def w_shrink(x, a_stack, *rest, **kw):
-        timed("lora_shrink_seg", a_stack.numel() * bf + x.numel() * bf + x.shape[0] * a_stack.shape[1] * 4,
-              orig[2], x, a_stack, *rest, **kw)
-
-    def w_rope(qkv, **kw):
-        nb = qkv.numel() * bf + s.q_dim * bf + 2 * s.kv_dim * bf
-        if kw.get("lora_b") is not None:
-            nb += kw["lora_b"].numel() * bf
-        timed("qkv_rope_append", nb, orig[3], qkv, **kw)
-
-    K.linear_lora_fused, K.paged_decode, K.lora_shrink_seg, K.qkv_rope_append = w_gemv, w_attn, w_shrink, w_rope
+    wrap = {
+        "linear_lora_fused": lambda x, w, **kw: timed("linear_lora_fused", gemv_bytes(x, w, kw),
+                                                      orig["linear_lora_fused"], x, w, **kw),
+        "paged_decode": lambda *a, **kw: timed("paged_decode", attn_bytes, orig["paged_decode"], *a, **kw),
+        "lora_shrink_seg": lambda x, a_st, *r, **kw: timed(
+            "lora_shrink_seg", a_st.numel() * bf + x.numel() * bf + x.shape[0] * a_st.shape[1] * 4,
+            orig["lora_shrink_seg"], x, a_st, *r, **kw),
+        "qkv_rope_append": lambda qkv, **kw: timed(
+            "qkv_rope_append", qkv.numel() * bf + s.q_dim * bf + 2 * s.kv_dim * bf
+            + (kw["lora_b"].numel() * bf if kw.get("lora_b") is not None else 0), orig["qkv_rope_append"], qkv, **kw),
+        "page_table_advance": lambda *a, **kw: timed("page_table_advance", 64, orig["page_table_advance"], *a, **kw),
+        "embed": lambda *a, **kw: timed("embed", 2 * s.hidden * bf, orig["embed"], *a, **kw),
+        "argmax": lambda *a, **kw: timed("argmax", s.vocab * bf, orig["argmax"], *a, **kw),
+    }
+    saved = [t.clone() for t in (engine.row_num_pages, engine.last_page_len, engine.row_pages, engine.token_buf)]
+    for n in names:
+        setattr(K, n, wrap[n])
     try:
-        saved = [t.clone() for t in (engine.row_num_pages, engine.last_page_len, engine.row_pages, engine.token_buf)]
-        engine.new_page_ids.fill_(engine.free_pages[-1] if engine.free_pages else 0)
-        for _ in range(2):  # the second pass is the measured one
-            records.clear()
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
             engine._decode_body()
-            for dst, src in zip((engine.row_num_pages, engine.last_page_len, engine.row_pages, engine.token_buf),
-                                saved):
-                dst.copy_(src)
-        torch.cuda.synchronize()
     finally:
-        K.linear_lora_fused, K.paged_decode, K.lora_shrink_seg, K.qkv_rope_append = orig
+        for n in names:
+            setattr(K, n, orig[n])
     agg: dict[str, list[float]] = {}
-    for name, nb, e0, e1 in records:
-        ms = e0.elapsed_time(e1)
-        a = agg.setdefault(name, [0, 0.0, 0.0])
-        a[0] += 1
-        a[1] += nb
-        a[2] += ms
+    engine.new_page_ids.fill_(engine.free_pages[-1] if engine.free_pages else 0)
+    for _ in range(replays):
+        g.replay()
+        torch.cuda.synchronize()
+        for name, nb, e0, e1 in records:
+            a = agg.setdefault(name, [0, 0.0, 0.0])
+            a[0] += 1
+            a[1] += nb
+            a[2] += e0.elapsed_time(e1)
+        for dst, src in zip((engine.row_num_pages, engine.last_page_len, engine.row_pages, engine.token_buf),
+                            saved):
+            dst.copy_(src)
+    torch.cuda.synchronize()
+    del g
     out = {}
     for name, (n, nb, ms) in agg.items():
         gbs = nb / (ms * 1e-3) / 1e9
-        out[name] = {"launches": n, "bytes_per_launch": nb / n, "us_per_launch": 1000.0 * ms / n,
+        out[name] = {"launches_per_step": n // replays, "bytes_per_launch": nb / n, "us_per_launch": 1000.0 * ms / n,
                      "achieved_gbs": gbs, "frac_of_peak": gbs / peak_gbs}
     return out
 
@@ -291,6 +302,10 @@ def run_ours(args) -> None:
     load_library()
     wl = WORKLOADS[WORKLOAD]
     spec = wl.model
+    if args.layers:
+        from dataclasses import replace
+
+        spec = replace(spec, num_layers=args.layers, name=f"{spec.name}-{args.layers}layers")
     steps, warmup = args.steps, max(3, args.warmup)
     weights = make_model_weights(spec, seed=0, device=device)
     loras = make_lora_weights(spec, wl.lora, device=device)
@@ -321,6 +336,13 @@ def run_ours(args) -> None:
         barrier()
     ms = e0.elapsed_time(e1)
     engine._check_status()
+    if args.profile:  # profiling runs stop after the graph-replayed steps
+        if rank == 0:
+            print(json.dumps({"profile": True, "layers": spec.num_layers, "steps": steps,
+                              "ms_per_step": ms / steps}), flush=True)
+        if ws > 1:
+            dist.destroy_process_group()
+        return
 
     # ---- e2e: through the public step API from pinned host memory
     first = engine.prefill(prompt)
@@ -349,6 +371,8 @@ def run_ours(args) -> None:
         value = ws * steps / (ms * 1e-3)
         e2e = ws * steps / (ms_e2e * 1e-3)
         dom = kern["linear_lora_fused"]
+        if args.layers:
+            raise SystemExit("--layers is for profiling runs only (use it with --profile)")
         cpu = cpu_decode_sample(wl.prompt_len, 3, 1) if ws == 1 else None
         # attention + LoRA bytes of one step over its measured kernel time
         att = kern.get("paged_decode", {})
@@ -382,6 +406,10 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling run: prefill, capture and the timed graph replays only")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling run on the first L layers (same per-layer shapes)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

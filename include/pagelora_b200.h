@@ -245,14 +245,18 @@ int32_t pl_linear_lora_expand_fused(
     int32_t *status_dev, void *stream);
 
 /*
- * Pipeline shape of pl_linear_lora_expand_fused for this process: shared-
- * memory ring depth (stages), columns per 16-row stage, consumer warps
- * (4 or 8) and CTAs per SM.  No reference counterpart (a tuning knob);
- * defaults 8 / 512 / 4 / 1.  The ring is made shallower automatically when
- * tokens x K does not fit in shared memory.
+ * Kernel variant and pipeline shape of pl_linear_lora_expand_fused for this
+ * process.  No reference counterpart (a tuning knob).
+ *   mode 1: TMA ring -- stages x (16 rows x cols_per_stage) bulk copies,
+ *           consumer_warps (4 or 8) mma warps, ctas_per_sm (1..4) CTAs per SM;
+ *           the ring is made shallower when tokens x K does not fit.
+ *   mode 2: register-direct loads -- consumer_warps (4 or 8) warps per CTA,
+ *           grid of ctas_per_sm (1..16) CTAs per SM (stages / cols_per_stage
+ *           are checked but unused).
  */
-int32_t pl_linear_set_tuning(int32_t stages, int32_t cols_per_stage,
-                             int32_t consumer_warps, int32_t ctas_per_sm);
+int32_t pl_linear_set_tuning(int32_t mode, int32_t stages,
+                             int32_t cols_per_stage, int32_t consumer_warps,
+                             int32_t ctas_per_sm);
 
 /*
  * Merged ("effective") weight builder: w_out = w_in + sign * scale * (B @ A)
@@ -316,10 +320,16 @@ int32_t pl_embed(const int64_t *token_ids, const void *table, int64_t vocab,
                  int32_t dim, int32_t num_tokens, void *out,
                  int32_t *status_dev, void *stream);
 
-/* First-index argmax over bf16 rows: out_ids[t] = argmax(logits[t, :vocab]).
- * Replaces model/flashinfer/sampling.py:8-15 (greedy_argmax_token). */
+/* First-index argmax over bf16 rows: out_ids[t] = argmax(logits[t, :vocab])
+ * (torch.argmax order: NaN wins, ties to the smaller index).
+ * Replaces model/flashinfer/sampling.py:8-15 (greedy_argmax_token).  Up to one
+ * CTA per SM scans each row; the workspace (16-byte aligned, >= 4*num_tokens +
+ * 8*num_tokens*148 bytes) holds the candidates and per-row arrival tickets,
+ * whose first 4*num_tokens bytes must be zero before the first call (every
+ * call leaves them zero). */
 int32_t pl_argmax(const void *logits, int64_t stride, int32_t vocab,
-                  int32_t num_tokens, int64_t *out_ids, void *stream);
+                  int32_t num_tokens, int64_t *out_ids, void *workspace,
+                  int64_t workspace_bytes, void *stream);
 
 #ifdef __cplusplus
 }

@@ -84,3 +84,4 @@ extern "C" const char* pl_status_string(int32_t status) {
 extern "C" const char* pl_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
 
 extern "C" int32_t pl_device_sm_count(void) { return pl_host::sm_count(); }
+

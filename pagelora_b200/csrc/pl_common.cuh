@@ -27,6 +27,46 @@ __device__ __forceinline__ void set_status(int32_t* status, int32_t code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// ------------------------------------------------------- optional tracing
+// Built only with -DPL_TRACE (a development build): records %globaltimer at
+// named points of CTA `blockIdx.x` of the traced launch into a device array.
+#ifdef PL_TRACE
+constexpr int kTraceCtas = 160, kTracePoints = 16;
+static __device__ unsigned long long g_pl_trace[kTraceCtas * kTracePoints];  // one per translation unit
+__device__ __forceinline__ void trace_point(int point) {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  if (blockIdx.x < kTraceCtas && blockIdx.y == 0 && blockIdx.z == 0) g_pl_trace[blockIdx.x * kTracePoints + point] = t;
+}
+__device__ __forceinline__ void trace_max(int point) {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  if (blockIdx.x < kTraceCtas && blockIdx.y == 0 && blockIdx.z == 0)
+    atomicMax(&g_pl_trace[blockIdx.x * kTracePoints + point], t);
+}
+#define PL_TRACE_POINT(p) ::pl::trace_point(p)
+#define PL_TRACE_MAX(p) ::pl::trace_max(p)
+// Reader of this translation unit's trace array (defined once per .cu).
+#define PL_TRACE_READER(name)                                                                           \
+  extern "C" int32_t name(unsigned long long* host_out, int32_t clear) {                                \
+    if (cudaMemcpyFromSymbol(host_out, ::pl::g_pl_trace, sizeof(::pl::g_pl_trace)) != cudaSuccess)      \
+      return PL_ERR_CUDA;                                                                               \
+    if (clear) {                                                                                        \
+      static unsigned long long zeros[::pl::kTraceCtas * ::pl::kTracePoints] = {0};                     \
+      if (cudaMemcpyToSymbol(::pl::g_pl_trace, zeros, sizeof(zeros)) != cudaSuccess) return PL_ERR_CUDA; \
+    }                                                                                                   \
+    return PL_OK;                                                                                       \
+  }
+#else
+#define PL_TRACE_POINT(p) \
+  do {                    \
+  } while (0)
+#define PL_TRACE_MAX(p) \
+  do {                  \
+  } while (0)
+#define PL_TRACE_READER(name)
+#endif
+
 // ------------------------------------------------------------ conversions
 __device__ __forceinline__ float bf2f(bf16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ bf16 f2bf(float v) { return __float2bfloat16_rn(v); }
@@ -160,6 +200,35 @@ __device__ __forceinline__ void mma_bf16_16816(float* d, const uint32_t* a, cons
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// LoRA expand dot product sum_j B[j] * bf16(down[j]) over one rank row, in j
+// order.  Vector loads (one 16-byte B load + two float4 down loads per 8
+// ranks) keep the loads independent; scalar fallback for odd ranks / alignment.
+__device__ __forceinline__ float lora_dot(const bf16* brow, const float* drow, int rank) {
+  float d = 0.f;
+  if ((rank & 7) == 0 && ((reinterpret_cast<uintptr_t>(brow) | reinterpret_cast<uintptr_t>(drow)) & 15) == 0) {
+#pragma unroll 4
+    for (int j = 0; j < rank; j += 8) {
+      const uint4 bv = *reinterpret_cast<const uint4*>(brow + j);
+      const float4 d0 = *reinterpret_cast<const float4*>(drow + j);
+      const float4 d1 = *reinterpret_cast<const float4*>(drow + j + 4);
+      const float2 b0 = unpack_bf16x2(bv.x), b1 = unpack_bf16x2(bv.y), b2 = unpack_bf16x2(bv.z),
+                   b3 = unpack_bf16x2(bv.w);
+      d = fmaf(b0.x, bfr(d0.x), d);
+      d = fmaf(b0.y, bfr(d0.y), d);
+      d = fmaf(b1.x, bfr(d0.z), d);
+      d = fmaf(b1.y, bfr(d0.w), d);
+      d = fmaf(b2.x, bfr(d1.x), d);
+      d = fmaf(b2.y, bfr(d1.y), d);
+      d = fmaf(b3.x, bfr(d1.z), d);
+      d = fmaf(b3.y, bfr(d1.w), d);
+    }
+  } else {
+#pragma unroll 8
+    for (int j = 0; j < rank; ++j) d = fmaf(bf2f(brow[j]), bfr(drow[j]), d);
+  }
+  return d;
 }
 
 // Named barrier among `count` threads (multiple of 32) of the CTA.

@@ -545,7 +545,7 @@ extern "C" int32_t pl_decode_plan(int32_t batch, int32_t num_qo_heads, int32_t n
     // merge (proportional to the split count) stays small next to the scan.
     const int64_t target = sms;
     const int64_t avg_pages = (total_pages + batch - 1) / (batch > 0 ? batch : 1);
-    int64_t by_fill = (target + base - 1) / base;
+    int64_t by_fill = target / base;  // never more CTAs than SMs: the ring needs a whole SM
     int64_t by_len = avg_pages / 4;
     int64_t s = by_fill < by_len ? by_fill : by_len;
     if (s > 64) s = 64;

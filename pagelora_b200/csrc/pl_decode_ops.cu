@@ -348,8 +348,7 @@ __global__ void __launch_bounds__(128) qkv_rope_append_kernel(
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         const bf16* brow = lora_b + ((int64_t)ad * n_out + col + d0 + e) * rank;
-        float d = 0.f;
-        for (int j = 0; j < rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
+        const float d = lora_dot(brow, drow, rank);
         v[e] = bfr(v[e] + bfr(bfr(d) * lora_scale));
       }
     }
@@ -412,29 +411,21 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const bf16* __rest
 }
 
 // ---------------------------------------------------------------- argmax
-__global__ void __launch_bounds__(1024) argmax_kernel(const bf16* __restrict__ logits, int64_t stride, int vocab,
-                                                      int64_t* __restrict__ out) {
-  pdl_launch_dependents();
-  pdl_wait();
-  const int t = blockIdx.x;
-  const bf16* row = logits + (int64_t)t * stride;
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = bf2f(row[i]);
-    if (v > best || (v == best && i < bi) || (v != v && best == best)) {
-      best = v;
-      bi = i;
-    }
-  }
-  __shared__ float sv[32];
-  __shared__ int si[32];
+// (value, index) ordering of torch.argmax: larger value wins, NaN beats any
+// number, ties go to the smaller index.
+__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn || bn) return vn && (!bn || i < bi);
+  return v > bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ void am_block_reduce(float& best, int& bi, float* sv, int* si) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi) || (ov != ov && best == best) || (ov != ov && best != best && oi < bi)) {
+    if (am_better(ov, oi, best, bi)) {
       best = ov;
       bi = oi;
     }
@@ -445,19 +436,84 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const bf16* __restrict__ l
   }
   __syncthreads();
   if (warp == 0) {
-    best = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
-    bi = lane < (int)(blockDim.x / 32) ? si[lane] : 0x7fffffff;
+    const int nw = blockDim.x / 32;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi) || (ov != ov && best == best) ||
-          (ov != ov && best != best && oi < bi)) {
+      if (am_better(ov, oi, best, bi)) {
         best = ov;
         bi = oi;
       }
     }
-    if (lane == 0) out[t] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+// grid (chunks, tokens): each CTA scans one vocab chunk and leaves a
+// candidate; the last CTA of a token (arrival ticket) reduces the
+// candidates in chunk order and resets the ticket.
+__global__ void __launch_bounds__(256) argmax_kernel(const bf16* __restrict__ logits, int64_t stride, int vocab,
+                                                     int chunk, int64_t* __restrict__ out, float* cand_v,
+                                                     int* cand_i, int* tickets) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int c = blockIdx.x, t = blockIdx.y, nc = gridDim.x;
+  const bf16* row = logits + (int64_t)t * stride;
+  const int i0 = c * chunk, i1 = min(vocab, i0 + chunk);
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const bool vec = ((reinterpret_cast<uintptr_t>(row) | (uintptr_t)(i0 * 2)) & 15) == 0;
+  if (vec) {
+    for (int i = i0 + threadIdx.x * 8; i < i1; i += blockDim.x * 8) {
+      if (i + 8 <= i1) {
+        const uint4 u = *reinterpret_cast<const uint4*>(row + i);
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(w[q]);
+          if (am_better(f.x, i + 2 * q, best, bi)) { best = f.x; bi = i + 2 * q; }
+          if (am_better(f.y, i + 2 * q + 1, best, bi)) { best = f.y; bi = i + 2 * q + 1; }
+        }
+      } else {
+        for (int j = i; j < i1; ++j) {
+          const float v = bf2f(row[j]);
+          if (am_better(v, j, best, bi)) { best = v; bi = j; }
+        }
+      }
+    }
+  } else {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+      const float v = bf2f(row[i]);
+      if (am_better(v, i, best, bi)) { best = v; bi = i; }
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ int is_last;
+  am_block_reduce(best, bi, sv, si);
+  if (threadIdx.x == 0) {
+    cand_v[t * nc + c] = best;
+    cand_i[t * nc + c] = bi;
+    __threadfence();
+    is_last = atomicAdd(&tickets[t], 1) == nc - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  best = -INFINITY;
+  bi = 0x7fffffff;
+  for (int k = threadIdx.x; k < nc; k += blockDim.x) {
+    const float v = __ldcg(cand_v + t * nc + k);
+    const int i = __ldcg(cand_i + t * nc + k);
+    if (am_better(v, i, best, bi)) { best = v; bi = i; }
+  }
+  __syncthreads();
+  am_block_reduce(best, bi, sv, si);
+  if (threadIdx.x == 0) {
+    out[t] = bi == 0x7fffffff ? 0 : bi;
+    tickets[t] = 0;
   }
 }
 
@@ -567,9 +623,24 @@ extern "C" int32_t pl_embed(const int64_t* token_ids, const void* table, int64_t
 }
 
 extern "C" int32_t pl_argmax(const void* logits, int64_t stride, int32_t vocab, int32_t num_tokens,
-                             int64_t* out_ids, void* stream) {
+                             int64_t* out_ids, void* workspace, int64_t workspace_bytes, void* stream) {
   if (num_tokens == 0) return PL_OK;
-  if (logits == nullptr || out_ids == nullptr || num_tokens < 0 || vocab <= 0) return PL_ERR_INVALID_ARGUMENT;
-  return pl_host::launch_pdl(pl::argmax_kernel, dim3(num_tokens), dim3(1024), 0, stream,
-                             static_cast<const pl::bf16*>(logits), stride, (int)vocab, out_ids);
+  if (logits == nullptr || out_ids == nullptr || num_tokens < 0 || vocab <= 0 || num_tokens > 65535)
+    return PL_ERR_INVALID_ARGUMENT;
+  int sms = pl_host::sm_count();
+  if (sms <= 0) sms = 148;
+  int chunks = (int)((vocab + 2047) / 2048);
+  if (chunks > sms) chunks = sms;
+  if (chunks < 1) chunks = 1;
+  const int chunk = (int)(((vocab + chunks - 1) / chunks + 7) / 8 * 8);
+  chunks = (vocab + chunk - 1) / chunk;
+  const int64_t need = (int64_t)num_tokens * 4 + (int64_t)num_tokens * chunks * 8;
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return PL_ERR_WORKSPACE_TOO_SMALL;
+  int* tickets = static_cast<int*>(workspace);
+  float* cand_v = reinterpret_cast<float*>(tickets + num_tokens);
+  int* cand_i = reinterpret_cast<int*>(cand_v + (int64_t)num_tokens * chunks);
+  return pl_host::launch_pdl(pl::argmax_kernel, dim3(chunks, num_tokens), dim3(256), 0, stream,
+                             static_cast<const pl::bf16*>(logits), stride, (int)vocab, chunk, out_ids, cand_v, cand_i,
+                             tickets);
 }

@@ -98,14 +98,121 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int 
       while (sl < a.num_slices - 1 && o >= a.slice_end[sl]) ++sl;
       const bf16* brow = a.lora_b + ((int64_t)ad * a.n_out + o) * a.rank;
       const float* drow = a.lora_down + tok * a.down_stride + sl * a.rank;
-      float d = 0.f;
-      for (int j = 0; j < a.rank; ++j) d += bf2f(brow[j]) * bfr(drow[j]);
+      const float d = lora_dot(brow, drow, a.rank);
       vb = bfr(vb + bfr(bfr(d) * a.lora_scale));
     }
     v = vb;
   }
   if (a.residual != nullptr) v = bf2f(a.residual[tok * a.res_stride + o]) + bfr(v);
   a.y[tok * a.y_stride + o] = f2bf(v);
+}
+
+// Stage the activations of all tokens as bf16 rows (stride xrow bytes) in
+// shared memory, applying the input prologue.  Loads are issued four chunks
+// at a time per thread so each pass costs one or two memory round trips.
+// `part` holds one float per warp; `bar` is a named barrier over `nthreads`.
+__device__ __forceinline__ void stage_activations(const GemvArgs& a, uint8_t* xs, int xrow, int tid, int nthreads,
+                                                  float* part, int bar) {
+  const int K = a.K;
+  const int lane = tid & 31, wid = tid >> 5;
+  const int step = nthreads * 8;
+  for (int t = 0; t < a.T; ++t) {
+    const bf16* xr = a.x + (int64_t)t * a.x_stride;
+    uint8_t* dst = xs + t * xrow;
+    if (a.prologue == PL_PROLOGUE_RMSNORM) {
+      float ss = 0.f;
+      for (int k0 = tid * 8; k0 < K; k0 += 4 * step) {
+        uint4 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = k0 + i * step;
+          v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = unpack_bf16x2(u[q]);
+            ss += f.x * f.x + f.y * f.y;
+          }
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) part[wid] = ss;
+      named_barrier(bar, nthreads);
+      float tot = 0.f;
+      for (int w = 0; w < nthreads / 32; ++w) tot += part[w];
+      const float rstd = rsqrtf(tot / (float)K + a.eps);
+      named_barrier(bar, nthreads);
+      for (int k0 = tid * 8; k0 < K; k0 += 4 * step) {
+        uint4 v[4], wv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = k0 + i * step;
+          v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+          wv[i] = k < K ? *reinterpret_cast<const uint4*>(a.norm_w + k) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = k0 + i * step;
+          if (k >= K) break;
+          const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+          const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv[i]);
+          uint4 o;
+          uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = unpack_bf16x2(u[q]);
+            const float2 g = unpack_bf16x2(uw[q]);
+            uo[q] = pack_bf16x2(f.x * rstd * g.x, f.y * rstd * g.y);
+          }
+          *reinterpret_cast<uint4*>(dst + k * 2) = o;
+        }
+      }
+    } else if (a.prologue == PL_PROLOGUE_SILU_MUL) {
+      for (int k0 = tid * 8; k0 < K; k0 += 4 * step) {
+        uint4 gv[4], uv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = k0 + i * step;
+          gv[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+          uv[i] = k < K ? *reinterpret_cast<const uint4*>(xr + K + k) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = k0 + i * step;
+          if (k >= K) break;
+          const uint32_t* ug = reinterpret_cast<const uint32_t*>(&gv[i]);
+          const uint32_t* uu = reinterpret_cast<const uint32_t*>(&uv[i]);
+          uint4 o;
+          uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 g = unpack_bf16x2(ug[q]);
+            const float2 up = unpack_bf16x2(uu[q]);
+            uo[q] = pack_bf16x2(silu_mul(g.x, up.x), silu_mul(g.y, up.y));
+          }
+          *reinterpret_cast<uint4*>(dst + k * 2) = o;
+        }
+      }
+    } else {
+      for (int k0 = tid * 8; k0 < K; k0 += 4 * step) {
+        uint4 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = k0 + i * step;
+          v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = k0 + i * step;
+          if (k < K) *reinterpret_cast<uint4*>(dst + k * 2) = v[i];
+        }
+      }
+    }
+  }
+  named_barrier(bar, nthreads);
 }
 
 // One CTA per SM streams the weight rows [r0, r1) of its balanced share as
@@ -142,6 +249,7 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
   const int n_units = n_tiles * n_kc;
 
   if (threadIdx.x == 0) {
+    PL_TRACE_POINT(0);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], NCW);
@@ -183,8 +291,11 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
         const bf16* src = row < a.n_out ? a.w + row * K : a.shrink_a + (row - a.n_out) * K;
         bulk_g2s(smem + s * L.stage_bytes + lane * RB, src + k0, (uint32_t)(kw * 2), &full_bar[s], pol);
       }
+      if (lane == 0 && u == 0) PL_TRACE_POINT(1);
+      if (lane == 0 && u == S) PL_TRACE_POINT(2);
       ++issued;
     }
+    if (lane == 0) PL_TRACE_POINT(3);
     if (lane == 0 && *abort_flag) {
       for (int u = issued - S < 0 ? 0 : issued - S; u < issued; ++u)
         (void)mbar_wait(&full_bar[u % S], (u / S) & 1);
@@ -197,68 +308,10 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
   const int ctid = threadIdx.x - 32;
   constexpr int NC = 32 * NCW;
   pdl_wait();
+  if (ctid == 0) PL_TRACE_POINT(4);
 
-  // Prologue: activations -> bf16 rows in shared memory.
-  for (int t = 0; t < a.T; ++t) {
-    const bf16* xr = a.x + (int64_t)t * a.x_stride;
-    uint8_t* dst = xs + t * XROW;
-    if (a.prologue == PL_PROLOGUE_RMSNORM) {
-      float ss = 0.f;
-      for (int k = ctid * 8; k < K; k += NC * 8) {
-        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 f = unpack_bf16x2(u[i]);
-          ss += f.x * f.x + f.y * f.y;
-        }
-      }
-      ss = warp_sum(ss);
-      float* part = reinterpret_cast<float*>(smem + L.misc_off + 16);  // NCW <= 8 partials
-      if (lane == 0) part[cw] = ss;
-      named_barrier(1, NC);
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < NCW; ++w) tot += part[w];
-      const float rstd = rsqrtf(tot / (float)K + a.eps);
-      named_barrier(1, NC);
-      for (int k = ctid * 8; k < K; k += NC * 8) {
-        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + k);
-        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
-        const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
-        uint4 o;
-        uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 f = unpack_bf16x2(u[i]);
-          float2 g = unpack_bf16x2(uw[i]);
-          uo[i] = pack_bf16x2(f.x * rstd * g.x, f.y * rstd * g.y);
-        }
-        *reinterpret_cast<uint4*>(dst + k * 2) = o;
-      }
-    } else if (a.prologue == PL_PROLOGUE_SILU_MUL) {
-      for (int k = ctid * 8; k < K; k += NC * 8) {
-        uint4 gv = *reinterpret_cast<const uint4*>(xr + k);
-        uint4 uv = *reinterpret_cast<const uint4*>(xr + K + k);
-        const uint32_t* ug = reinterpret_cast<const uint32_t*>(&gv);
-        const uint32_t* uu = reinterpret_cast<const uint32_t*>(&uv);
-        uint4 o;
-        uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 g = unpack_bf16x2(ug[i]);
-          float2 up = unpack_bf16x2(uu[i]);
-          uo[i] = pack_bf16x2(silu_mul(g.x, up.x), silu_mul(g.y, up.y));
-        }
-        *reinterpret_cast<uint4*>(dst + k * 2) = o;
-      }
-    } else {
-      for (int k = ctid * 8; k < K; k += NC * 8)
-        *reinterpret_cast<uint4*>(dst + k * 2) = *reinterpret_cast<const uint4*>(xr + k);
-    }
-  }
-  named_barrier(1, NC);
+  stage_activations(a, xs, XROW, ctid, NC, reinterpret_cast<float*>(smem + L.misc_off + 16), 1);
+  if (ctid == 0) PL_TRACE_POINT(5);
 
   const int g = lane >> 2, tq = lane & 3;
   const uint32_t zero_addr = smem_u32(smem + L.zero_off);
@@ -286,6 +339,8 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
         ok = false;
         break;
       }
+      if (ctid == 0 && u == 0) PL_TRACE_POINT(6);
+      if (ctid == 0 && u == n_units - 1) PL_TRACE_POINT(7);
       const int k0 = kc * KC;
       const int ksteps = min(KC, K - k0) / 16;
       const uint32_t stage = smem_u32(smem + s * L.stage_bytes) + a_row * RB + a_col * 2;
@@ -342,6 +397,140 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
       }
     }
   }
+  if (lane == 0) PL_TRACE_MAX(8);
+}
+
+// ------------------------------------------------- register-direct variant
+// Each CTA owns 16-row tiles (strided over the grid); its warps split K into
+// 32-column blocks.  A thread loads 16 bytes of weight row g and of row g+8
+// per block straight into registers (no shared-memory staging, no TMA issue
+// cost) and feeds them to mma.sync as A fragments with the 32 columns of the
+// block permuted: the k-step pairs {2t, 2t+1, 2t+8, 2t+9} map to columns
+// {8t .. 8t+3} and the second k-step to {8t+4 .. 8t+7}.  The activations use
+// the same mapping (one 16-byte shared load per block); a dot product does
+// not depend on the order of its k terms, so the permutation is free.  Loads run
+// one batch of kLdgUnroll blocks ahead of the math; the first batch of the
+// first tile is requested before the upstream grid has finished (static
+// weights).  Partial tiles of the warps are combined in shared memory.
+constexpr int kLdgUnroll = 4;
+
+struct LdgSmem {
+  int xrow, red_off, part_off, zero_off, total;
+};
+__host__ __device__ inline LdgSmem ldg_smem_layout(int T, int K, int nw) {
+  LdgSmem L;
+  L.xrow = K * 2 + 16;
+  int off = T * L.xrow;
+  off = (off + 15) & ~15;
+  L.red_off = off;
+  off += 2 * nw * kTileRows * kMaxTok * 4;
+  L.part_off = off;
+  off += 64;
+  L.zero_off = off;
+  off += 16;
+  L.total = off + 128;
+  return L;
+}
+
+template <int NW>
+__global__ void __launch_bounds__(32 * NW) linear_ldg_kernel(const GemvArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int K = a.K, T = a.T;
+  const LdgSmem L = ldg_smem_layout(T, K, NW);
+  uint8_t* xs = smem;
+  float* red = reinterpret_cast<float*>(smem + L.red_off);  // [2][NW][16][8]
+  float* part = reinterpret_cast<float*>(smem + L.part_off);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int g = lane >> 2, tq = lane & 3;
+  const int64_t rows_total = (int64_t)a.n_out + a.n_shrink;
+  const int n_tiles = (int)((rows_total + kTileRows - 1) / kTileRows);
+  const int nblk = K / 32;
+  const int b0 = warp * nblk / NW, b1 = (warp + 1) * nblk / NW;
+  if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(smem + L.zero_off)[threadIdx.x] = 0u;
+  if (threadIdx.x == 0) PL_TRACE_POINT(0);
+  pdl_launch_dependents();
+
+  auto row_ptr = [&](int64_t row) -> const uint4* {
+    const bf16* p = row < a.n_out ? a.w + row * K : a.shrink_a + (row - a.n_out) * K;
+    return reinterpret_cast<const uint4*>(p) + tq;  // this lane's 16 bytes of each 32-column block
+  };
+  // Weight registers of one batch of blocks: rows g and g + 8.
+  uint4 wa[kLdgUnroll], wb[kLdgUnroll];
+  auto load_batch = [&](int tile, int bb) {
+    const int64_t ra = (int64_t)tile * kTileRows + g, rb = ra + 8;
+    const bool va = ra < rows_total, vb = rb < rows_total;
+    const uint4* pa = row_ptr(va ? ra : 0);
+    const uint4* pb = row_ptr(vb ? rb : 0);
+#pragma unroll
+    for (int u = 0; u < kLdgUnroll; ++u) {
+      const int blk = bb + u;
+      const bool in = blk < b1;
+      wa[u] = (in && va) ? __ldcs(pa + blk * 4) : make_uint4(0, 0, 0, 0);
+      wb[u] = (in && vb) ? __ldcs(pb + blk * 4) : make_uint4(0, 0, 0, 0);
+    }
+  };
+
+  int tile = blockIdx.x;
+  if (a.early_weights && tile < n_tiles && b0 < b1) load_batch(tile, b0);
+  pdl_wait();
+  if (!a.early_weights && tile < n_tiles && b0 < b1) load_batch(tile, b0);
+  stage_activations(a, xs, L.xrow, threadIdx.x, 32 * NW, part, 1);
+  if (threadIdx.x == 0) PL_TRACE_POINT(5);
+
+  const uint32_t zero_addr = smem_u32(smem + L.zero_off);
+  const uint32_t xbase = g < T ? smem_u32(xs + g * L.xrow) + tq * 16 : 0u;
+  for (int it = 0; tile < n_tiles; tile += gridDim.x, ++it) {
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int bb = b0; bb < b1; bb += kLdgUnroll) {
+      uint4 ca[kLdgUnroll], cb[kLdgUnroll];
+#pragma unroll
+      for (int u = 0; u < kLdgUnroll; ++u) {
+        ca[u] = wa[u];
+        cb[u] = wb[u];
+      }
+      // request the next batch (this tile's next blocks, or the next tile's first)
+      if (bb + kLdgUnroll < b1)
+        load_batch(tile, bb + kLdgUnroll);
+      else if (tile + (int)gridDim.x < n_tiles)
+        load_batch(tile + gridDim.x, b0);
+#pragma unroll
+      for (int u = 0; u < kLdgUnroll; ++u) {
+        const int blk = bb + u;
+        if (blk < b1) {
+          uint32_t xv[4];
+          const uint32_t xaddr = g < T ? xbase + blk * 64 : zero_addr;
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(xv[0]), "=r"(xv[1]), "=r"(xv[2]), "=r"(xv[3])
+                       : "r"(xaddr));
+          const uint32_t a0[4] = {ca[u].x, cb[u].x, ca[u].y, cb[u].y};
+          const uint32_t a1[4] = {ca[u].z, cb[u].z, ca[u].w, cb[u].w};
+          mma_bf16_16816(acc0, a0, &xv[0]);
+          mma_bf16_16816(acc1, a1, &xv[2]);
+        }
+      }
+    }
+    // combine the warps' partial tiles, then the epilogue of the tile
+    float* rb = red + (it & 1) * (NW * kTileRows * kMaxTok);
+    float* mine = rb + warp * (kTileRows * kMaxTok);
+    mine[g * kMaxTok + 2 * tq] = acc0[0] + acc1[0];
+    mine[g * kMaxTok + 2 * tq + 1] = acc0[1] + acc1[1];
+    mine[(g + 8) * kMaxTok + 2 * tq] = acc0[2] + acc1[2];
+    mine[(g + 8) * kMaxTok + 2 * tq + 1] = acc0[3] + acc1[3];
+    __syncthreads();
+    for (int e = threadIdx.x; e < kTileRows * T; e += 32 * NW) {
+      const int row = e / T, tok = e % T;
+      const int64_t o = (int64_t)tile * kTileRows + row;
+      if (o < rows_total) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) v += rb[(w * kTileRows + row) * kMaxTok + tok];
+        gemv_epilogue(a, o, tok, v);
+      }
+    }
+  }
+  if (threadIdx.x == 0) PL_TRACE_MAX(8);
 }
 
 // ----------------------------------------------------------------- shrink
@@ -457,6 +646,8 @@ __global__ void lora_merge_weight_kernel(const bf16* __restrict__ w_in, bf16* __
 }  // namespace pl
 
 // =================================================================== host
+PL_TRACE_READER(pl_trace_read_gemv)
+
 namespace {
 // Pipeline shape of linear_lora_kernel (pl_linear_set_tuning): ring depth,
 // columns per 16-row stage, consumer warps, CTAs per SM.
@@ -464,6 +655,8 @@ int g_gemv_stages = 3;
 int g_gemv_kc = 2048;
 int g_gemv_consumers = 8;
 int g_gemv_ctas_per_sm = 1;
+int g_gemv_mode = 1;          // 1: TMA ring, 2: register-direct loads
+int g_ldg_ctas_per_sm = 4;
 }  // namespace
 
 extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
@@ -528,6 +721,21 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   if (sms <= 0) sms = 148;
   const int64_t rows = (int64_t)n_out + n_shrink;
   const int64_t tiles = (rows + pl::kTileRows - 1) / pl::kTileRows;
+  if (g_gemv_mode == 2 && k_in % 32 == 0) {
+    // register-direct variant: several CTAs per SM, tiles strided over the grid
+    const pl::LdgSmem Ld = pl::ldg_smem_layout(num_tokens, k_in, g_gemv_consumers);
+    if (Ld.total > 227 * 1024) return PL_ERR_UNSUPPORTED;
+    const int64_t cap = (int64_t)sms * g_ldg_ctas_per_sm;
+    const int grid_l = (int)(tiles < cap ? tiles : cap);
+    if (g_gemv_consumers == 8) {
+      int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_ldg_kernel<8>), Ld.total);
+      if (st != PL_OK) return st;
+      return pl_host::launch_pdl(pl::linear_ldg_kernel<8>, dim3(grid_l), dim3(256), Ld.total, stream, a);
+    }
+    int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_ldg_kernel<4>), Ld.total);
+    if (st != PL_OK) return st;
+    return pl_host::launch_pdl(pl::linear_ldg_kernel<4>, dim3(grid_l), dim3(128), Ld.total, stream, a);
+  }
   const int64_t max_ctas = (int64_t)sms * g_gemv_ctas_per_sm;
   const int grid = (int)(tiles < max_ctas ? tiles : max_ctas);
   // Largest ring that fits: the tuned shape, then shallower / narrower stages.
@@ -555,11 +763,18 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   return pl_host::launch_pdl(pl::linear_lora_kernel<4>, dim3(grid), dim3(32 * 5), L.total, stream, a);
 }
 
-extern "C" int32_t pl_linear_set_tuning(int32_t stages, int32_t cols_per_stage, int32_t consumer_warps,
-                                        int32_t ctas_per_sm) {
-  if (stages < 2 || stages > 16 || cols_per_stage < 256 || cols_per_stage > 4096 || cols_per_stage % 256 ||
-      (consumer_warps != 4 && consumer_warps != 8) || ctas_per_sm < 1 || ctas_per_sm > 4)
+extern "C" int32_t pl_linear_set_tuning(int32_t mode, int32_t stages, int32_t cols_per_stage,
+                                        int32_t consumer_warps, int32_t ctas_per_sm) {
+  if ((mode != 1 && mode != 2) || stages < 2 || stages > 16 || cols_per_stage < 256 || cols_per_stage > 4096 ||
+      cols_per_stage % 256 || (consumer_warps != 4 && consumer_warps != 8) || ctas_per_sm < 1 || ctas_per_sm > 16)
     return PL_ERR_INVALID_ARGUMENT;
+  g_gemv_mode = mode;
+  if (mode == 2) {
+    g_ldg_ctas_per_sm = ctas_per_sm;
+    g_gemv_consumers = consumer_warps;
+    return PL_OK;
+  }
+  if (ctas_per_sm > 4) return PL_ERR_INVALID_ARGUMENT;
   g_gemv_stages = stages;
   g_gemv_kc = cols_per_stage;
   g_gemv_consumers = consumer_warps;

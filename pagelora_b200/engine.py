@@ -166,6 +166,7 @@ class DecodeEngine:
         self.down_o = torch.zeros(1, max(self.lora_rank, 1), device=dev, dtype=torch.float32)
         self.gate_up = torch.zeros(1, 2 * spec.intermediate, device=dev, dtype=bf)
         self.logits = torch.zeros(1, spec.vocab, device=dev, dtype=bf)
+        self.argmax_ws = torch.zeros(K.argmax_workspace_bytes(1), device=dev, dtype=torch.uint8)
         self.num_splits = 1
         self.workspace = torch.zeros(1 << 20, device=dev, dtype=torch.uint8)
         # Host mirror of the row state (decides when a new page is needed).
@@ -307,7 +308,7 @@ class DecodeEngine:
                                 out=self.x, weights_static=True, status=st)
         K.linear_lora_fused(self.x, self.lm_head, prologue=PL_PROLOGUE_RMSNORM, norm_weight=self.final_norm,
                             norm_eps=s.rms_eps, out=self.logits, weights_static=True, status=st)
-        K.argmax(self.logits, self.token_buf)
+        K.argmax(self.logits, self.token_buf, self.argmax_ws)
 
     def launches_per_step(self) -> int:
         per_layer = 6 + sum(1 for L in self.layers[:1] if L.a_o is not None)

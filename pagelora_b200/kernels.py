@@ -326,10 +326,23 @@ def embed(token_ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor,
     return out
 
 
-def argmax(logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+def argmax_workspace_bytes(num_tokens: int, max_chunks: int = 1024) -> int:
+    return 4 * num_tokens + 8 * num_tokens * max_chunks
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """First-index argmax per row (torch.argmax semantics) on up to one CTA per SM.
+
+    ``workspace`` (uint8, zero-initialised once, reusable) holds the per-row
+    candidates and arrival tickets; a fresh zeroed one is made if omitted.
+    """
+
     _need_cuda(logits, out)
     _need(logits, torch.bfloat16, "logits")
     _need(out, torch.int64, "out")
     t, vocab = logits.shape
-    call("pl_argmax", ptr(logits), _row_stride(logits, "logits"), int(vocab), int(t), ptr(out), stream_handle())
+    if workspace is None:
+        workspace = torch.zeros(argmax_workspace_bytes(t), dtype=torch.uint8, device=logits.device)
+    call("pl_argmax", ptr(logits), _row_stride(logits, "logits"), int(vocab), int(t), ptr(out), ptr(workspace),
+         int(workspace.numel()), stream_handle())
     return out
