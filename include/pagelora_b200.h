@@ -162,6 +162,36 @@ int32_t pl_paged_decode(const void *q, int64_t q_stride_b, int64_t q_stride_h,
                         int32_t *status_dev, void *stream);
 
 /*
+ * pl_paged_decode without a caller workspace.  No counterpart in the
+ * reference: FlashInfer's wrapper takes a caller-allocated workspace.
+ * The split partials and arrival counters live in a fixed device array of
+ * PL_FIXED_SCRATCH_BYTES per device, inside the library; nothing is
+ * allocated.  Arguments and results are those of pl_paged_decode.
+ *   - Returns PL_ERR_WORKSPACE_TOO_SMALL, launching nothing, when
+ *     pl_decode_plan's workspace_bytes for the shape exceeds
+ *     PL_FIXED_SCRATCH_BYTES (e.g. batch * num_qo_heads * num_splits
+ *     * head_dim * 4 beyond ~4 MiB).
+ *   - The first call on each device (that device current) looks up the
+ *     array's address and clears it on `stream`; make that first call
+ *     before any stream capture.
+ *   - One array per device: calls that overlap on a device (two streams,
+ *     two host threads) race on it.  Serialise them.
+ */
+#define PL_FIXED_SCRATCH_BYTES (4 * 1024 * 1024)
+int32_t pl_paged_decode_fixed_scratch(const void *q, int64_t q_stride_b,
+                                      int64_t q_stride_h, const void *kv_cache,
+                                      int64_t num_pages, const int32_t *indptr,
+                                      const int32_t *indices,
+                                      const int32_t *last_page_len,
+                                      int32_t batch, int32_t num_qo_heads,
+                                      int32_t num_kv_heads, int32_t head_dim,
+                                      int32_t page_size, float sm_scale,
+                                      int32_t num_splits, void *out,
+                                      int64_t o_stride_b, int64_t o_stride_h,
+                                      float *out_lse, int32_t *status_dev,
+                                      void *stream);
+
+/*
  * Merge S partial attention states per (row, head) by log-sum-exp.
  * No reference counterpart in the project (FlashInfer merges internally);
  * it is the merge step of split-KV decode and of the cross-GPU split-KV

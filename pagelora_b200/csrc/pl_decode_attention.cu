@@ -630,3 +630,60 @@ extern "C" int32_t pl_merge_states(const float* v_partial, const float* lse_part
                              (int)num_rows, (int)num_states, (int)head_dim, static_cast<pl::bf16*>(out), out_stride,
                              out_lse);
 }
+
+// ------------------------------------------------- fixed-scratch variant
+// pl_paged_decode_fixed_scratch: the same kernel, with its split partials
+// and arrival counters in a file-scope device array instead of a caller
+// workspace, for callers that cannot allocate device memory.  One array per
+// device (a __device__ variable exists once in every context); its address
+// is looked up, and the whole array cleared on the caller's stream, by the
+// first call on each device.
+
+static __device__ __align__(256) uint8_t g_decode_fixed_scratch[PL_FIXED_SCRATCH_BYTES];
+
+namespace {
+constexpr int kScratchDevices = 64;
+std::mutex g_fixed_scratch_mu;
+void* g_fixed_scratch_ptr[kScratchDevices] = {};
+
+int32_t fixed_scratch(void* stream, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return pl_host::record_cuda_error(e);
+  if (dev < 0 || dev >= kScratchDevices) return PL_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_fixed_scratch_mu);
+  if (g_fixed_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_fixed_scratch);
+    if (e != cudaSuccess) return pl_host::record_cuda_error(e);
+    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255)) return PL_ERR_CUDA;
+    // The counters at the front must start at zero; every call leaves them so.
+    e = cudaMemsetAsync(p, 0, PL_FIXED_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return pl_host::record_cuda_error(e);
+    g_fixed_scratch_ptr[dev] = p;
+  }
+  *out = g_fixed_scratch_ptr[dev];
+  return PL_OK;
+}
+}  // namespace
+
+extern "C" int32_t pl_paged_decode_fixed_scratch(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                                 const void* kv_cache, int64_t num_pages, const int32_t* indptr,
+                                                 const int32_t* indices, const int32_t* last_page_len,
+                                                 int32_t batch, int32_t num_qo_heads, int32_t num_kv_heads,
+                                                 int32_t head_dim, int32_t page_size, float sm_scale,
+                                                 int32_t num_splits, void* out, int64_t o_stride_b,
+                                                 int64_t o_stride_h, float* out_lse, int32_t* status_dev,
+                                                 void* stream) {
+  if (batch == 0) return PL_OK;
+  if (batch < 0 || num_kv_heads <= 0 || num_qo_heads <= 0 || head_dim <= 0 || num_splits < 1)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (decode_workspace_bytes(batch, num_qo_heads, num_kv_heads, head_dim, num_splits) > PL_FIXED_SCRATCH_BYTES)
+    return PL_ERR_WORKSPACE_TOO_SMALL;
+  void* scratch = nullptr;
+  int32_t st = fixed_scratch(stream, &scratch);
+  if (st != PL_OK) return st;
+  return pl_paged_decode(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
+                         num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, o_stride_b,
+                         o_stride_h, out_lse, scratch, PL_FIXED_SCRATCH_BYTES, status_dev, stream);
+}
