@@ -277,6 +277,10 @@ int32_t pl_linear_lora_expand_fused(
 /*
  * Kernel variant and pipeline shape of pl_linear_lora_expand_fused for this
  * process.  No reference counterpart (a tuning knob).
+ *   mode -1: restore the built-in defaults (tuning and L2 prefetch).
+ *   mode 0: by size -- register-direct for launches of <= 64 MiB of weights
+ *           (shapes as last set for mode 2), TMA ring above (as last set for
+ *           mode 1); the other arguments are checked but unused.
  *   mode 1: TMA ring -- stages x (16 rows x cols_per_stage) bulk copies,
  *           consumer_warps (4 or 8) mma warps, ctas_per_sm (1..4) CTAs per SM;
  *           the ring is made shallower when tokens x K does not fit.
@@ -287,6 +291,14 @@ int32_t pl_linear_lora_expand_fused(
 int32_t pl_linear_set_tuning(int32_t mode, int32_t stages,
                              int32_t cols_per_stage, int32_t consumer_warps,
                              int32_t ctas_per_sm);
+
+/*
+ * Register-direct variant (tuning mode 2) with PL_FLAG_WEIGHTS_STATIC: bytes
+ * of weights per launch (whole 16-row tiles, the first ones of each CTA)
+ * that are prefetched into L2 before the upstream grid completes.  0 (the
+ * default) disables it; at most 1 GiB.  No reference counterpart.
+ */
+int32_t pl_linear_set_l2_prefetch(int64_t max_bytes);
 
 /*
  * Merged ("effective") weight builder: w_out = w_in + sign * scale * (B @ A)

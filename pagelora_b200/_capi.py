@@ -77,6 +77,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _I64, _P, _I32, _P, _I64, _I32, _P, _P],
     ),
     "pl_linear_set_tuning": (_I32, [_I32, _I32, _I32, _I32, _I32]),
+    "pl_linear_set_l2_prefetch": (_I32, [_I64]),
     "pl_lora_merge_weight": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _F, _I32, _I32, _P]),
     "pl_kv_append": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),
     "pl_qkv_rope_append": (

@@ -105,10 +105,12 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
     fence_barrier_init();
   }
   if (threadIdx.x == 32) prefetch_tensormap(&kv_map);
+  if (threadIdx.x == 0 && kvh == 0) PL_TRACE_POINT(0);
   __syncthreads();
 
   pdl_launch_dependents();
   pdl_wait();  // q, the page table and the freshly appended KV come from upstream kernels
+  if (threadIdx.x == 0 && kvh == 0) PL_TRACE_POINT(1);
 
   const int32_t row_begin = args.indptr[b];
   const int32_t n_pages = args.indptr[b + 1] - row_begin;
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
           }
         }
         __syncwarp();
+        if (lane == 0 && i0 == 0 && kvh == 0) PL_TRACE_POINT(2);
         if (valid) {
           const int kv = box / C::kHalves, hh = box % C::kHalves;
           uint8_t* dst = smem + C::kStageOff + s * C::kStageBytes + kv * C::kTileBytes + hh * C::kHalfBytes;
@@ -211,6 +214,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
         break;
       }
       if (flags[0]) break;
+      if (i == 0 && lane == 0 && kvh == 0) PL_TRACE_POINT(3);
       const int ntok = stage_ntok[s];
       if (ntok > 0) {
         const uint8_t* kbase = smem + C::kStageOff + s * C::kStageBytes;
@@ -300,6 +304,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
     }
 
     // ---- merge the consumer warps' states (scratch aliases the drained stage ring)
+    if (lane == 0 && kvh == 0) PL_TRACE_MAX(4);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
@@ -362,6 +367,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
         flags[1] = (ticket == args.num_splits - 1) ? 1 : 0;
       }
       named_barrier(1, 32 * kConsumerWarps);
+      if (ctid == 0 && kvh == 0) PL_TRACE_POINT(5);
       if (flags[1]) {
         // Last CTA of this (row, kv head): merge the S partial states.  The
         // split weights are computed once per query head into shared memory,
@@ -407,6 +413,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
                                                         pack_bf16x2(acc.z * il, acc.w * il));
         }
         if (ctid == 0) args.counters[b * args.num_kv_heads + kvh] = 0;
+        if (ctid == 0 && kvh == 0) PL_TRACE_POINT(6);
       }
     }
   }
@@ -437,6 +444,8 @@ __global__ void merge_states_kernel(const float* __restrict__ v, const float* __
 }  // namespace pl
 
 // =================================================================== host
+PL_TRACE_READER(pl_trace_read_attn)
+
 namespace {
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -324,8 +324,10 @@ __global__ void __launch_bounds__(128) qkv_rope_append_kernel(
     int64_t num_pages, const int32_t* __restrict__ page_id, const int32_t* __restrict__ page_off, int T, int Hq,
     int Hkv, int PS, int32_t* status) {
   constexpr int E = D / 32;  // elements per lane; lanes 0..15 hold [0, D/2), 16..31 hold [D/2, D)
+  if (threadIdx.x == 0) PL_TRACE_POINT(0);
   pdl_launch_dependents();
   pdl_wait();
+  if (threadIdx.x == 0) PL_TRACE_POINT(1);
   const int heads = Hq + 2 * Hkv;
   const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (gw >= T * heads) return;
@@ -378,6 +380,7 @@ __global__ void __launch_bounds__(128) qkv_rope_append_kernel(
 #pragma unroll
     for (int e = 0; e < E; ++e) v[e] = out[e];
   }
+  if (lane == 0) PL_TRACE_MAX(2);
   if (kind == 0) {
     bf16* dst = q_out + ((int64_t)t * Hq + hh) * D + d0;
 #pragma unroll
@@ -520,6 +523,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const bf16* __restrict__ lo
 }  // namespace pl
 
 // =================================================================== host
+PL_TRACE_READER(pl_trace_read_ops)
 extern "C" int32_t pl_page_table_build(const int32_t* span_block_id, const int32_t* span_start,
                                        const int32_t* span_length, const int32_t* row_indptr, int32_t num_rows,
                                        int32_t page_size, int32_t* out_indptr, int32_t* out_indices,

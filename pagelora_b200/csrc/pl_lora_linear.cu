@@ -49,6 +49,7 @@ struct GemvArgs {
   int32_t early_weights;  // weights are not produced upstream: stream them before the dependency resolves
   int32_t stages;         // depth of the shared-memory ring
   int32_t kc;             // columns per stage (multiple of 16)
+  int32_t prefetch_tiles; // tiles per CTA whose weights are pulled into L2 before the dependency resolves
   int32_t* status;
 };
 
@@ -472,6 +473,28 @@ __global__ void __launch_bounds__(32 * NW) linear_ldg_kernel(const GemvArgs a) {
   };
 
   int tile = blockIdx.x;
+  if (a.early_weights && warp == 0) {
+    // Pull the weights of this CTA's first tiles into L2 while the upstream
+    // grid is still running (16 KB per lane request; a tile is contiguous).
+    for (int j = 0; j < a.prefetch_tiles; ++j) {
+      const int t = blockIdx.x + j * (int)gridDim.x;
+      if (t >= n_tiles) break;
+      int64_t r0 = (int64_t)t * kTileRows, r1 = r0 + kTileRows;
+      if (r1 > rows_total) r1 = rows_total;
+      for (int part_i = 0; part_i < 2; ++part_i) {
+        const int64_t lo = part_i == 0 ? r0 : (r0 > a.n_out ? r0 : (int64_t)a.n_out);
+        const int64_t hi = part_i == 0 ? (r1 < a.n_out ? r1 : (int64_t)a.n_out) : r1;
+        if (hi <= lo) continue;
+        const char* base = part_i == 0 ? reinterpret_cast<const char*>(a.w + lo * K)
+                                       : reinterpret_cast<const char*>(a.shrink_a + (lo - a.n_out) * K);
+        const int64_t bytes = (hi - lo) * K * 2;
+        for (int64_t off = (int64_t)lane * 16384; off < bytes; off += 32 * 16384) {
+          const int64_t left = bytes - off;
+          prefetch_l2_bulk(base + off, (uint32_t)(left < 16384 ? left : 16384));
+        }
+      }
+    }
+  }
   if (a.early_weights && tile < n_tiles && b0 < b1) load_batch(tile, b0);
   pdl_wait();
   if (!a.early_weights && tile < n_tiles && b0 < b1) load_batch(tile, b0);
@@ -655,8 +678,11 @@ int g_gemv_stages = 3;
 int g_gemv_kc = 2048;
 int g_gemv_consumers = 8;
 int g_gemv_ctas_per_sm = 1;
-int g_gemv_mode = 1;          // 1: TMA ring, 2: register-direct loads
+int g_gemv_mode = 1;          // 0: by size, 1: TMA ring, 2: register-direct loads
+int g_ldg_warps = 4;
 int g_ldg_ctas_per_sm = 4;
+int64_t g_auto_ldg_max_bytes = int64_t(64) << 20;  // mode 0: register-direct up to this many weight bytes
+int64_t g_l2_prefetch_bytes = 0;  // register-direct variant: L2 prefetch budget per launch
 }  // namespace
 
 extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
@@ -721,13 +747,19 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   if (sms <= 0) sms = 148;
   const int64_t rows = (int64_t)n_out + n_shrink;
   const int64_t tiles = (rows + pl::kTileRows - 1) / pl::kTileRows;
-  if (g_gemv_mode == 2 && k_in % 32 == 0) {
+  const bool ldg = k_in % 32 == 0 &&
+                   (g_gemv_mode == 2 || (g_gemv_mode == 0 && rows * k_in * 2 <= g_auto_ldg_max_bytes));
+  if (ldg) {
     // register-direct variant: several CTAs per SM, tiles strided over the grid
-    const pl::LdgSmem Ld = pl::ldg_smem_layout(num_tokens, k_in, g_gemv_consumers);
+    const pl::LdgSmem Ld = pl::ldg_smem_layout(num_tokens, k_in, g_ldg_warps);
     if (Ld.total > 227 * 1024) return PL_ERR_UNSUPPORTED;
     const int64_t cap = (int64_t)sms * g_ldg_ctas_per_sm;
     const int grid_l = (int)(tiles < cap ? tiles : cap);
-    if (g_gemv_consumers == 8) {
+    const int64_t tile_bytes = (int64_t)pl::kTileRows * k_in * 2;
+    int64_t pf = g_l2_prefetch_bytes / ((int64_t)grid_l * tile_bytes);
+    const int64_t per_cta = (tiles + grid_l - 1) / grid_l;
+    a.prefetch_tiles = (int)(pf < per_cta ? pf : per_cta);
+    if (g_ldg_warps == 8) {
       int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_ldg_kernel<8>), Ld.total);
       if (st != PL_OK) return st;
       return pl_host::launch_pdl(pl::linear_ldg_kernel<8>, dim3(grid_l), dim3(256), Ld.total, stream, a);
@@ -765,13 +797,25 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
 
 extern "C" int32_t pl_linear_set_tuning(int32_t mode, int32_t stages, int32_t cols_per_stage,
                                         int32_t consumer_warps, int32_t ctas_per_sm) {
-  if ((mode != 1 && mode != 2) || stages < 2 || stages > 16 || cols_per_stage < 256 || cols_per_stage > 4096 ||
+  if (mode == -1) {  // built-in defaults
+    g_gemv_mode = 1;
+    g_gemv_stages = 3;
+    g_gemv_kc = 2048;
+    g_gemv_consumers = 8;
+    g_gemv_ctas_per_sm = 1;
+    g_ldg_warps = 4;
+    g_ldg_ctas_per_sm = 4;
+    g_l2_prefetch_bytes = 0;
+    return PL_OK;
+  }
+  if (mode < 0 || mode > 2 || stages < 2 || stages > 16 || cols_per_stage < 256 || cols_per_stage > 4096 ||
       cols_per_stage % 256 || (consumer_warps != 4 && consumer_warps != 8) || ctas_per_sm < 1 || ctas_per_sm > 16)
     return PL_ERR_INVALID_ARGUMENT;
   g_gemv_mode = mode;
+  if (mode == 0) return PL_OK;
   if (mode == 2) {
     g_ldg_ctas_per_sm = ctas_per_sm;
-    g_gemv_consumers = consumer_warps;
+    g_ldg_warps = consumer_warps;
     return PL_OK;
   }
   if (ctas_per_sm > 4) return PL_ERR_INVALID_ARGUMENT;
@@ -779,6 +823,12 @@ extern "C" int32_t pl_linear_set_tuning(int32_t mode, int32_t stages, int32_t co
   g_gemv_kc = cols_per_stage;
   g_gemv_consumers = consumer_warps;
   g_gemv_ctas_per_sm = ctas_per_sm;
+  return PL_OK;
+}
+
+extern "C" int32_t pl_linear_set_l2_prefetch(int64_t max_bytes) {
+  if (max_bytes < 0 || max_bytes > (int64_t(1) << 30)) return PL_ERR_INVALID_ARGUMENT;
+  g_l2_prefetch_bytes = max_bytes;
   return PL_OK;
 }
 

@@ -261,8 +261,33 @@ def test_packed_qkv_matches_reference(K, golden_dir):
         _ulps_close(_np(base), olora.linear(x, w, bf16=True))
 
 
+# GEMV variants: TMA ring (mode 1), register-direct loads with 4 or 8 warps
+# (mode 2, with and without the L2 prefetch of the first tiles), by size (mode 0).
+GEMV_TUNINGS = {
+    "tma": ((1, 3, 2048, 8, 1), 0),
+    "tma_4w2c": ((1, 4, 1024, 4, 2), 0),
+    "ldg_4w4c": ((2, 2, 256, 4, 4), 0),
+    "ldg_8w2c_pf": ((2, 2, 256, 8, 2), 64 << 20),
+    "auto_pf": ((0, 2, 256, 4, 1), 32 << 20),
+}
+
+
+@pytest.fixture(params=sorted(GEMV_TUNINGS))
+def gemv_tuning(request, K):
+    from pagelora_b200._capi import load_library
+
+    lib = load_library()
+    tune, pf = GEMV_TUNINGS[request.param]
+    if tune[0] == 0:
+        assert lib.pl_linear_set_tuning(2, 2, 256, 4, 4) == 0
+    assert lib.pl_linear_set_tuning(*tune) == 0
+    assert lib.pl_linear_set_l2_prefetch(pf) == 0
+    yield request.param
+    assert lib.pl_linear_set_tuning(-1, 0, 0, 0, 0) == 0
+
+
 @pytest.mark.parametrize("t", [1, 2, 5, 8])
-def test_linear_lora_fused_prologues_and_epilogues_vs_oracle(K, t):
+def test_linear_lora_fused_prologues_and_epilogues_vs_oracle(K, t, gemv_tuning):
     rng = np.random.default_rng(100 + t)
     k_in, n, r, n_ad = 1024, 700, 16, 3
     x = bf16(rng.normal(size=(t, k_in)))
@@ -300,7 +325,7 @@ def test_linear_lora_fused_prologues_and_epilogues_vs_oracle(K, t):
     _ulps_close(_np(y2), bf16(gu[:, :k_in].astype(np.float64) @ w.T.astype(np.float64)), ulps=3)
 
 
-def test_linear_lora_fused_large_shapes(K):
+def test_linear_lora_fused_large_shapes(K, gemv_tuning):
     """Decode shapes of Qwen3-8B (qkv, o, gate_up, down) at one token."""
 
     g = torch.Generator(device="cuda").manual_seed(0)
