@@ -186,6 +186,19 @@ def run_reference(args) -> None:
 
 
 # --------------------------------------------------------------- GPU arm
+def _ncu_traffic(kernel: str) -> float | None:
+    """DRAM bytes (read + write) per launch of ``kernel`` from the committed ncu
+    summary of the same workload (profiles/), or None when it has none."""
+
+    import re
+
+    for path in sorted((Path(__file__).resolve().parent / "profiles").glob("*.md")):
+        m = re.search(rf"traffic_bytes_per_launch\({re.escape(kernel)}\):\s*([0-9.eE+]+)", path.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
 def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
     """Per-launch device time of every kernel of one decode step.
 
@@ -388,7 +401,8 @@ def run_ours(args) -> None:
             "gpu_launches": engine.launches_per_step() * steps,
             "roofline": {"bound": "hbm", "kernel": "linear_lora_fused", "achieved": dom["achieved_gbs"],
                          "peak": peak, "unit": "GB/s", "frac": dom["achieved_gbs"] / peak, "peak_kind": peak_kind,
-                         "traffic": None},
+                         "traffic": _ncu_traffic("linear_lora_fused"),
+                         "algorithmic_bytes_per_launch": dom["bytes_per_launch"]},
             "kernels": kern,
             "attention_gbs": att.get("achieved_gbs"),
             "clocks": clk.summary(),
