@@ -300,6 +300,69 @@ int32_t pl_linear_set_tuning(int32_t mode, int32_t stages,
  */
 int32_t pl_linear_set_l2_prefetch(int64_t max_bytes);
 
+/* ------------------------------------------- multi-token linear (tcgen05) */
+
+typedef struct pl_gemm_plan_t {
+  int32_t num_splits;        /* K splits per 128-row weight tile               */
+  int32_t ctas;              /* grid size = ceil(n_out / 128) * num_splits     */
+  int64_t workspace_bytes;   /* bytes of workspace pl_linear_lora_gemm needs   */
+} pl_gemm_plan_t;
+
+/*
+ * Split-K plan of pl_linear_lora_gemm for T tokens (1..128), K inputs and
+ * n_out rows on the current device.
+ */
+int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t n_out,
+                            pl_gemm_plan_t *plan);
+
+/*
+ * Multi-token LoRA linear on the tcgen05 tensor cores (TMA-fed, accumulator
+ * in tensor memory): the batched-decode / prefill-chunk counterpart of
+ * pl_linear_lora_expand_fused for 1..128 tokens.  Replaces
+ * multilora/linear.py:200-231 (LoRALinear.forward: F.linear + the LoRA
+ * delta) and model/flashinfer/packed_ops.py:105-165, 251-265
+ * (project_qkv_packed / project_linear) for a multi-sequence batch.
+ *   x           bf16 [T, K] (row stride x_stride), already normalised
+ *               (pl_rmsnorm / pl_silu_mul); 16-byte aligned, K % 8 == 0
+ *   w           bf16 [n_out, K] row-major
+ *   epilogue    bias, LoRA expand and residual exactly as in
+ *               pl_linear_lora_expand_fused; tok_adapter[t] selects token
+ *               t's adapter (-1: none), so a batch mixes adapters
+ *               (segment-grouped shrink: pl_lora_shrink_seg)
+ *   num_splits  from pl_linear_gemm_plan; workspace (256-byte aligned) of
+ *               workspace_bytes whose first 4 * ceil(n_out / 128) bytes are
+ *               arrival counters: zero before the first call, left zero.
+ */
+int32_t pl_linear_lora_gemm(const void *x, int64_t x_stride, int32_t num_tokens,
+                            int32_t k_in, const void *w, int32_t n_out,
+                            const void *bias, const float *lora_down,
+                            int64_t down_stride, const void *lora_b,
+                            int32_t lora_rank, float lora_scale,
+                            const int32_t *slice_end, int32_t num_slices,
+                            const int32_t *tok_adapter, const void *residual,
+                            int64_t res_stride, void *y, int64_t y_stride,
+                            int32_t num_splits, void *workspace,
+                            int64_t workspace_bytes, int32_t flags,
+                            int32_t *status_dev, void *stream);
+
+/*
+ * FlashInfer RMSNorm over T rows (one bf16 rounding):
+ * y = bf16(x * rsqrt(mean(x^2) + eps) * w).  Replaces model/norm.py:51-54
+ * (flashinfer rmsnorm, called at model/norm.py:51-65) on the decode path.
+ * K % 8 == 0.
+ */
+int32_t pl_rmsnorm(const void *x, int64_t x_stride, int32_t num_tokens,
+                   int32_t k_in, const void *w, float eps, void *y,
+                   int64_t y_stride, void *stream);
+
+/*
+ * SwiGLU activation over packed [gate | up] rows: y[t, k] =
+ * bf16(silu(x[t, k]) * x[t, K + k]), k < K = k_out.  Replaces
+ * model/flashinfer/packed_ops.py:237 (flashinfer silu_and_mul).
+ */
+int32_t pl_silu_mul(const void *x, int64_t x_stride, int32_t num_tokens,
+                    int32_t k_out, void *y, int64_t y_stride, void *stream);
+
 /*
  * Merged ("effective") weight builder: w_out = w_in + sign * scale * (B @ A)
  * with the reference's rounding points (bf16 tensors):

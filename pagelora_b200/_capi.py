@@ -46,6 +46,10 @@ class DecodePlan(Structure):
     _fields_ = [("num_splits", c_int32), ("ctas", c_int32), ("workspace_bytes", c_int64)]
 
 
+class GemmPlan(Structure):
+    _fields_ = [("num_splits", c_int32), ("ctas", c_int32), ("workspace_bytes", c_int64)]
+
+
 _P = c_void_p
 _I32 = c_int32
 _I64 = c_int64
@@ -78,6 +82,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "pl_linear_set_tuning": (_I32, [_I32, _I32, _I32, _I32, _I32]),
     "pl_linear_set_l2_prefetch": (_I32, [_I64]),
+    "pl_linear_gemm_plan": (_I32, [_I32, _I32, _I32, POINTER(GemmPlan)]),
+    "pl_linear_lora_gemm": (
+        _I32,
+        [_P, _I64, _I32, _I32, _P, _I32, _P, _P, _I64, _P, _I32, _F, _P, _I32, _P, _P, _I64, _P, _I64, _I32, _P,
+         _I64, _I32, _P, _P],
+    ),
+    "pl_rmsnorm": (_I32, [_P, _I64, _I32, _I32, _P, _F, _P, _I64, _P]),
+    "pl_silu_mul": (_I32, [_P, _I64, _I32, _I32, _P, _I64, _P]),
     "pl_lora_merge_weight": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _F, _I32, _I32, _P]),
     "pl_kv_append": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),
     "pl_qkv_rope_append": (

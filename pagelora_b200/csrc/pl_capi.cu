@@ -39,6 +39,20 @@ int32_t sm_count() {
   return g_sm_count[dev];
 }
 
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
 int32_t ensure_smem_attr(const void* kernel, int bytes) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -448,24 +448,6 @@ PL_TRACE_READER(pl_trace_read_attn)
 
 namespace {
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
 struct MapKey {
   const void* ptr;
   int64_t pages;
@@ -496,7 +478,7 @@ int32_t kv_tensor_map(const void* cache, int64_t pages, int hkv, int d, int ps, 
       *out = g_maps.map[i];
       return PL_OK;
     }
-  EncodeTiledFn enc = get_encode_fn();
+  pl_host::EncodeTiledFn enc = pl_host::encode_tiled_fn();
   if (enc == nullptr) return PL_ERR_CUDA;
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)hkv, (cuuint64_t)ps, (cuuint64_t)(2 * pages)};
   cuuint64_t strides[3] = {(cuuint64_t)d * 2, (cuuint64_t)hkv * d * 2, (cuuint64_t)ps * hkv * d * 2};

@@ -1,0 +1,72 @@
+// Shared pieces of the linear-layer kernels: the argument block and the
+// per-element epilogue (bias, LoRA expand, residual) with the reference's
+// bf16 rounding points.
+#pragma once
+
+#include "pl_common.cuh"
+
+namespace pl {
+
+constexpr int kTileRows = 16;  // rows per tile (mma M)
+constexpr int kMaxTok = 8;     // mma N
+
+struct GemvArgs {
+  const bf16* x;
+  int64_t x_stride;
+  int32_t T, K;
+  int32_t prologue;
+  const bf16* norm_w;
+  float eps;
+  const bf16* w;
+  int32_t n_out;
+  const bf16* bias;
+  const float* lora_down;
+  int64_t down_stride;
+  const bf16* lora_b;
+  int32_t rank;
+  float lora_scale;
+  int32_t slice_end[4];
+  int32_t num_slices;
+  const int32_t* tok_adapter;
+  const bf16* residual;
+  int64_t res_stride;
+  bf16* y;
+  int64_t y_stride;
+  const bf16* shrink_a;
+  int32_t n_shrink;
+  float* shrink_out;
+  int64_t shrink_stride;
+  int32_t early_weights;  // weights are not produced upstream: stream them before the dependency resolves
+  int32_t stages;         // depth of the shared-memory ring
+  int32_t kc;             // columns per stage (multiple of 16)
+  int32_t prefetch_tiles; // tiles per CTA whose weights are pulled into L2 before the dependency resolves
+  int32_t* status;
+};
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+// Epilogue of one output element (row o, token tok) from its fp32 dot product.
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int tok, float v) {
+  if (o >= a.n_out) {
+    a.shrink_out[tok * a.shrink_stride + (o - a.n_out)] = v;
+    return;
+  }
+  if (a.bias != nullptr) v += bf2f(a.bias[o]);
+  if (a.lora_b != nullptr) {
+    const int ad = a.tok_adapter != nullptr ? a.tok_adapter[tok] : 0;
+    float vb = bfr(v);
+    if (ad >= 0) {
+      int sl = 0;
+      while (sl < a.num_slices - 1 && o >= a.slice_end[sl]) ++sl;
+      const bf16* brow = a.lora_b + ((int64_t)ad * a.n_out + o) * a.rank;
+      const float* drow = a.lora_down + tok * a.down_stride + sl * a.rank;
+      const float d = lora_dot(brow, drow, a.rank);
+      vb = bfr(vb + bfr(bfr(d) * a.lora_scale));
+    }
+    v = vb;
+  }
+  if (a.residual != nullptr) v = bf2f(a.residual[tok * a.res_stride + o]) + bfr(v);
+  a.y[tok * a.y_stride + o] = f2bf(v);
+}
+
+}  // namespace pl

@@ -235,6 +235,107 @@ def linear_lora_fused(
     return out
 
 
+def gemm_plan(num_tokens: int, k_in: int, n_out: int) -> _capi.GemmPlan:
+    """Split-K plan of :func:`linear_lora_gemm` on the current device."""
+
+    plan = _capi.GemmPlan()
+    call("pl_linear_gemm_plan", int(num_tokens), int(k_in), int(n_out), _capi.ctypes.byref(plan))
+    return plan
+
+
+def gemm_workspace_bytes(num_tokens: int, n_out: int, num_splits: int) -> int:
+    """Workspace of :func:`linear_lora_gemm` for an explicit split count
+    (counters, then fp32 split tiles [m_tiles, splits, N, 128])."""
+
+    m_tiles = -(-n_out // 128)
+    n_pad = 16 if num_tokens <= 16 else 32 if num_tokens <= 32 else 64 if num_tokens <= 64 else 128
+    nbytes = -(-m_tiles * 4 // 256) * 256
+    if num_splits > 1:
+        nbytes += m_tiles * num_splits * n_pad * 128 * 4
+    return nbytes
+
+
+def linear_lora_gemm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    lora_down: torch.Tensor | None = None,
+    lora_b: torch.Tensor | None = None,
+    lora_scale: float = 1.0,
+    slice_ends: tuple[int, ...] = (),
+    tok_adapter: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+    num_splits: int | None = None,
+    weights_static: bool = False,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """y = x . W^T (+bias) (+ per-token LoRA expand) (+ residual) for 1..128
+    tokens on the tcgen05 tensor cores.  ``x`` [T, K] is used as given (apply
+    :func:`rmsnorm` / :func:`silu_mul` first); the epilogue arguments are those
+    of :func:`linear_lora_fused`.  ``workspace`` (uint8, zeroed once) is sized
+    by :func:`gemm_plan`; one is allocated when omitted."""
+
+    _need_cuda(x, weight)
+    _need(x, torch.bfloat16, "x")
+    _need(weight, torch.bfloat16, "weight")
+    if not weight.is_contiguous():
+        raise ValueError("weight must be contiguous [out, in]")
+    t = x.shape[0]
+    n, k = weight.shape
+    if out is None:
+        out = torch.empty(t, n, dtype=torch.bfloat16, device=x.device)
+    splits = int(gemm_plan(t, k, n).num_splits) if num_splits is None else int(num_splits)
+    if workspace is None:
+        workspace = torch.zeros(gemm_workspace_bytes(t, n, splits), dtype=torch.uint8, device=x.device)
+    rank = 0
+    num_slices = 1
+    slice_ptr, slice_keepalive = None, None
+    if lora_b is not None:
+        if lora_b.dim() == 2:
+            lora_b = lora_b.unsqueeze(0)
+        rank = lora_b.shape[-1]
+        num_slices = len(slice_ends) + 1 if slice_ends else 1
+        if slice_ends:
+            slice_ptr, slice_keepalive = ctypes_int32_array(slice_ends)
+    flags = _capi.PL_FLAG_WEIGHTS_STATIC if weights_static else 0
+    call("pl_linear_lora_gemm", ptr(x), _row_stride(x, "x"), int(t), int(k), ptr(weight), int(n), ptr(bias),
+         ptr(lora_down), 0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
+         float(lora_scale), slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
+         0 if residual is None else _row_stride(residual, "residual"), ptr(out), _row_stride(out, "out"),
+         int(splits), ptr(workspace), int(workspace.numel()), int(flags), ptr(status), stream_handle())
+    del slice_keepalive
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """FlashInfer-style RMSNorm (one bf16 rounding) over rows of ``x`` [T, K]."""
+
+    _need_cuda(x, weight)
+    _need(x, torch.bfloat16, "x")
+    _need(weight, torch.bfloat16, "weight")
+    if out is None:
+        out = torch.empty_like(x)
+    call("pl_rmsnorm", ptr(x), _row_stride(x, "x"), int(x.shape[0]), int(x.shape[1]), ptr(weight), float(eps),
+         ptr(out), _row_stride(out, "out"), stream_handle())
+    return out
+
+
+def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(silu(gate) * up) over packed [T, 2K] rows -> [T, K]."""
+
+    _need_cuda(x)
+    _need(x, torch.bfloat16, "x")
+    t, k2 = x.shape
+    if out is None:
+        out = torch.empty(t, k2 // 2, dtype=torch.bfloat16, device=x.device)
+    call("pl_silu_mul", ptr(x), _row_stride(x, "x"), int(t), int(k2 // 2), ptr(out), _row_stride(out, "out"),
+         stream_handle())
+    return out
+
+
 def ctypes_int32_array(values):
     """A host int32 array and its address (keep the array alive across the call)."""
 

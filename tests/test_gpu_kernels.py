@@ -339,6 +339,84 @@ def test_linear_lora_fused_large_shapes(K, gemv_tuning):
         assert bool(torch.all(torch.abs(y.double() - ref) <= tol))
 
 
+def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
+    """fp64 restatement of the multi-token LoRA linear epilogue (per-token adapter)."""
+
+    t, n = x.shape[0], w.shape[0]
+    r = bmat.shape[-1]
+    base = bf16(x.astype(np.float64) @ w.T.astype(np.float64) + (0 if bias is None else bias))
+    want = np.zeros((t, n), np.float32)
+    mag = np.abs(base).astype(np.float32)  # size of the summands (cancellation bound)
+    for i in range(t):
+        yi = base[i]
+        if tok_ad[i] >= 0:
+            d = np.concatenate([bmat[tok_ad[i], :split_at] @ bf16(down[i, :r]),
+                                bmat[tok_ad[i], split_at:] @ bf16(down[i, r:2 * r])])
+            yi = bf16(yi + bf16(bf16(d) * scale))
+        mag[i] = np.maximum(mag[i], np.abs(yi))
+        if res is not None:
+            mag[i] = np.maximum(mag[i], np.abs(res[i]))
+        want[i] = bf16(res[i] + yi) if res is not None else yi
+    return mag, want
+
+
+@pytest.mark.parametrize("t", [1, 9, 16, 33, 64, 100, 128])
+def test_linear_lora_gemm_vs_oracle(K, t):
+    """tcgen05 multi-token linear: multi-adapter LoRA epilogue, partial tiles,
+    K tail, split-K 1 / planned / 5 (deterministic across splits)."""
+
+    rng = np.random.default_rng(300 + t)
+    k_in, n, r, n_ad = 600, 700, 16, 3   # K tail (600 = 9 chunks + 24), last row tile partial
+    x = bf16(rng.normal(size=(t, k_in)))
+    w = bf16(rng.normal(size=(n, k_in)) * 0.05)
+    bias = bf16(rng.normal(size=n) * 0.1)
+    res = bf16(rng.normal(size=(t, n)))
+    down = rng.normal(size=(t, 2 * r)).astype(np.float32)
+    bmat = bf16(rng.normal(size=(n_ad, n, r)) * 0.05)
+    tok_ad = rng.integers(-1, n_ad, size=t)
+    mag, want = _gemm_oracle(x, w, bias, down, bmat, tok_ad, 300, res, scale=2.0)
+    outs = []
+    for splits in (1, None, 5):
+        y = K.linear_lora_gemm(_t(x), _t(w), bias=_t(bias), lora_down=_t(down, torch.float32), lora_b=_t(bmat),
+                               lora_scale=2.0, slice_ends=(300,), tok_adapter=_i32(tok_ad), residual=_t(res),
+                               num_splits=splits)
+        torch.cuda.synchronize()
+        outs.append(_np(y))
+        _ulps_close(outs[-1], want, ulps=3, magnitude=mag)
+    # plain projection, no epilogue extras
+    y = K.linear_lora_gemm(_t(x), _t(w))
+    torch.cuda.synchronize()
+    _ulps_close(_np(y), bf16(x.astype(np.float64) @ w.T.astype(np.float64)), ulps=2)
+
+
+def test_linear_lora_gemm_llama2_shapes(K):
+    """Batched-decode shapes of Llama-2-7B (q/k/v, o, gate_up, down) at 64 tokens."""
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for n, k in ((12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008)):
+        w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+        x = torch.randn(64, k, generator=g, device="cuda").bfloat16()
+        y = K.linear_lora_gemm(x, w, weights_static=True)
+        ref = x.double() @ w.double().T
+        tol = torch.abs(ref) * 2.0 ** -8 + 1e-3
+        assert bool(torch.all(torch.abs(y.double() - ref) <= tol)), (n, k)
+        y2 = K.linear_lora_gemm(x, w, weights_static=True)  # counters were left at zero
+        assert torch.equal(y, y2)
+
+
+def test_rmsnorm_and_silu_mul_vs_oracle(K):
+    rng = np.random.default_rng(8)
+    x = bf16(rng.normal(size=(37, 4096)) * 3)
+    wn = bf16(1 + rng.normal(size=4096) * 0.1)
+    y = K.rmsnorm(_t(x), _t(wn), 1e-6)
+    gu = bf16(rng.normal(size=(37, 2 * 11008)))
+    z = K.silu_mul(_t(gu))
+    torch.cuda.synchronize()
+    # one bf16 rounding of an fp32 result: the fp32 sum order may move it by one ulp
+    _ulps_close(_np(y), rmsnorm_fused(x, wn, 1e-6), ulps=2)
+    _ulps_close(_np(z), bf16(silu(gu[:, :11008]) * gu[:, 11008:]), ulps=2)
+
+
 def test_lora_merge_weight_matches_reference(K, golden_dir):
     z = np.load(golden_dir / "lora_cases.npz")
     w, a, b, sc = _t(z["merge_w"]), _t(z["merge_a"]), _t(z["merge_b"]), float(z["merge_scale"][0])
