@@ -47,7 +47,7 @@ class DecodePlan(Structure):
 
 
 class GemmPlan(Structure):
-    _fields_ = [("num_splits", c_int32), ("ctas", c_int32), ("workspace_bytes", c_int64)]
+    _fields_ = [("ctas", c_int32), ("max_slots", c_int32), ("workspace_bytes", c_int64)]
 
 
 _P = c_void_p
@@ -82,7 +82,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "pl_linear_set_tuning": (_I32, [_I32, _I32, _I32, _I32, _I32]),
     "pl_linear_set_l2_prefetch": (_I32, [_I64]),
-    "pl_linear_gemm_plan": (_I32, [_I32, _I32, _I32, POINTER(GemmPlan)]),
+    "pl_linear_gemm_plan": (_I32, [_I32, _I32, _I32, _I32, POINTER(GemmPlan)]),
     "pl_linear_lora_gemm": (
         _I32,
         [_P, _I64, _I32, _I32, _P, _I32, _P, _P, _I64, _P, _I32, _F, _P, _I32, _P, _P, _I64, _P, _I64, _I32, _P,

@@ -177,6 +177,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 3-D tiled tensor copy global -> shared with an L2 cache policy (same
+// alignment rule on c0).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Ask L2 to fetch [src, src + bytes) from DRAM: no destination, no
 // completion to wait for.  src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {

@@ -45,12 +45,10 @@ struct GemvArgs {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
-// Epilogue of one output element (row o, token tok) from its fp32 dot product.
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int tok, float v) {
-  if (o >= a.n_out) {
-    a.shrink_out[tok * a.shrink_stride + (o - a.n_out)] = v;
-    return;
-  }
+// Epilogue value of one output element (row o < n_out, token tok) from its
+// fp32 dot product: bias, LoRA expand, residual, with the reference's bf16
+// rounding points (the caller rounds the result to bf16 once more).
+__device__ __forceinline__ float epilogue_value(const GemvArgs& a, int64_t o, int tok, float v) {
   if (a.bias != nullptr) v += bf2f(a.bias[o]);
   if (a.lora_b != nullptr) {
     const int ad = a.tok_adapter != nullptr ? a.tok_adapter[tok] : 0;
@@ -66,7 +64,32 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int 
     v = vb;
   }
   if (a.residual != nullptr) v = bf2f(a.residual[tok * a.res_stride + o]) + bfr(v);
-  a.y[tok * a.y_stride + o] = f2bf(v);
+  return v;
+}
+
+// Epilogue of one output element (row o, token tok): rows past n_out are
+// LoRA-A shrink rows whose fp32 products go to shrink_out.
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int tok, float v) {
+  if (o >= a.n_out) {
+    a.shrink_out[tok * a.shrink_stride + (o - a.n_out)] = v;
+    return;
+  }
+  a.y[tok * a.y_stride + o] = f2bf(epilogue_value(a, o, tok, v));
+}
+
+// Epilogue of rows o0..o0+3 (o0 % 4 == 0) of one token, stored as one 8-byte
+// vector when the four rows exist and the destination is 8-byte aligned.
+__device__ __forceinline__ void epilogue_rows4(const GemvArgs& a, int64_t o0, int tok, const float* v) {
+  if (o0 >= a.n_out) return;
+  bf16* dst = a.y + tok * a.y_stride + o0;
+  if (o0 + 4 <= a.n_out && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+    float r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = epilogue_value(a, o0 + i, tok, v[i]);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+  } else {
+    for (int i = 0; i < 4 && o0 + i < a.n_out; ++i) dst[i] = f2bf(epilogue_value(a, o0 + i, tok, v[i]));
+  }
 }
 
 }  // namespace pl

@@ -1,22 +1,28 @@
-// Multi-token LoRA linear (batched decode and prefill chunks, 9..128 tokens)
+// Multi-token LoRA linear (batched decode and prefill chunks, 1..128 tokens)
 // on the 5th-generation tensor cores, plus the small activation kernels that
 // feed it.
 //
-// pl_linear_lora_gemm computes y[t, n] = epilogue(sum_k x[t, k] * w[n, k])
-// for T <= 128 tokens.  A CTA owns a 128-row tile of the weight matrix and a
-// contiguous range of 64-column K chunks.  One thread streams the weight tile
-// (128 x 64 bf16, 16 KB) and the activation tile (N x 64) of each chunk into a
-// shared-memory ring with 2-D TMA (128-byte swizzle); one thread issues
-// tcgen05.mma (M = 128 weight rows, N = tokens padded to 16/32/64/128, K = 16)
-// with the accumulator in tensor memory; then all four warps read the
-// accumulator back with tcgen05.ld (warp w owns rows 32w..32w+31) and run the
-// same epilogue as the decode GEMV (bias, per-token LoRA expand with its
-// adapter, residual; the reference's bf16 rounding points).
-//
-// When the row tiles alone cannot fill the device, K is split across CTAs:
-// every split writes its fp32 tile to the workspace and the last split to
-// arrive (ticket per tile) adds the splits in split order -- deterministic --
-// and runs the epilogue.  No device-side wait depends on another CTA.
+// pl_linear_lora_gemm computes y[t, n] = epilogue(sum_k x[t, k] * w[n, k]).
+// Work is cut into units of one 128-row weight tile x one K block (4 chunks
+// of 64 columns, 2 when N = 128); the persistent grid has one CTA per SM and
+// CTA c takes the contiguous unit range [c*U/P, (c+1)*U/P) -- every SM
+// streams the same number of bytes whatever the tile count (per-SM copy
+// throughput, not HBM, is the limit when SMs idle).  Per CTA:
+//   warp 0     streams each unit's weight tile (128 rows x 256 columns, one
+//              3-D TMA copy reading 512 contiguous bytes per row) and the
+//              activation tile into a shared-memory ring, several units per
+//              issuing instruction;
+//   warp 1     (one lane) issues tcgen05.mma (M = 128, N = tokens padded to
+//              16/32/64/128, K = 16) into one of two tensor-memory
+//              accumulators, one per tile segment;
+//   warps 2-5  read a finished accumulator with tcgen05.ld (warp w owns
+//              lanes 32(w%4)..) while the next segment accumulates, and run
+//              the decode GEMV's epilogue (bias, per-token LoRA expand with
+//              the token's adapter, residual; the reference's bf16 rounding
+//              points), staged through shared memory into 8-byte stores.
+// A tile split between CTAs is finished by the last contributor (arrival
+// ticket per tile), which adds the contributors' fp32 partials in CTA order
+// -- deterministic -- and runs the epilogue.  No wait depends on another CTA.
 #include "pl_linear_common.cuh"
 
 #include <mutex>
@@ -24,57 +30,90 @@
 namespace pl {
 
 constexpr int kGemmM = 128;      // weight rows per tile (UMMA M)
-constexpr int kGemmKC = 64;      // K per stage: one 128-byte swizzled row of bf16
-constexpr int kGemmThreads = 128;
+constexpr int kGemmKC = 64;      // K per chunk: one 128-byte swizzled row of bf16
+constexpr int kGemmThreads = 192;
+constexpr int kGemmIssue = 4;    // units per producer TMA instruction
 
 struct GemmArgs {
   GemvArgs e;          // epilogue fields: n_out, bias, LoRA, residual, y, status; T, K
-  int32_t num_chunks;  // ceil(K / 64)
-  int32_t num_splits;
+  int32_t kblocks;     // K blocks per tile
+  int32_t units;       // m_tiles * kblocks
   int32_t stages;
-  float* partial;      // [m_tiles][splits][N][128] fp32 (num_splits > 1)
+  int32_t max_slots;   // partial slots per tile
+  float* partial;      // [m_tiles][max_slots][N][128] fp32
   int32_t* counters;   // [m_tiles] arrival tickets, zero between calls
 };
 
-template <int N>
+// N: tokens padded (UMMA N).  KCS: 64-column chunks per K block; with KCS > 1
+// the tiles come from 3-D tensor maps (64, rows, K / 64) so that one copy
+// reads KCS x 128 contiguous bytes of every weight row.
+template <int N, int KCS>
 struct GemmCfg {
-  static constexpr int kABytes = kGemmM * 128;  // 16 KB weight tile
-  static constexpr int kBBytes = N * 128;       // activation tile
+  static constexpr int kATile = kGemmM * 128;   // 16 KB weight tile per chunk
+  static constexpr int kBTile = N * 128;        // activation tile per chunk
+  static constexpr int kABytes = KCS * kATile;
+  static constexpr int kBBytes = KCS * kBTile;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = N < 32 ? 32 : N;
-  static_assert(kBBytes % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
+  static constexpr int kAccCols = N < 16 ? 16 : N;
+  static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;  // two accumulators
+  static constexpr int kStageTile = 16 * kGemmM * 4;                          // epilogue staging
+  static_assert(kBTile % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
 };
 
 __host__ __device__ inline int gemm_smem_bytes(int stage_bytes, int stages) {
-  return 1024 + stages * stage_bytes + (2 * stages + 1) * 8 + 32;
+  return 1024 + stages * stage_bytes + 16 * kGemmM * 4 + (2 * stages + 4) * 8 + 32;
 }
 
-template <int N>
+__host__ __device__ inline int unit_begin(int c, int units, int ctas) {
+  return (int)(((int64_t)c * units) / ctas);
+}
+// The CTA whose unit range holds unit u.
+__host__ __device__ inline int cta_of_unit(int u, int units, int ctas) {
+  int c = (int)(((int64_t)u * ctas) / units);
+  while (c + 1 < ctas && unit_begin(c + 1, units, ctas) <= u) ++c;
+  while (c > 0 && unit_begin(c, units, ctas) > u) --c;
+  return c;
+}
+
+template <int KCS>
+__device__ __forceinline__ void gemm_tile_load(void* dst, const CUtensorMap* map, int kb, int row0, uint64_t* bar,
+                                               uint64_t pol) {
+  if constexpr (KCS == 1)
+    tma_load_2d(dst, map, kb * kGemmKC, row0, bar, pol);
+  else
+    tma_load_3d(dst, map, 0, row0, kb * KCS, bar, pol);
+}
+
+template <int N, int KCS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                      const GemmArgs g) {
-  using C = GemmCfg<N>;
+  using C = GemmCfg<N, KCS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = g.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  float* stile = reinterpret_cast<float*>(smem + S * C::kStageBytes);  // [16 tokens][128 rows]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes + C::kStageTile);
   uint64_t* empty = full + S;
-  uint64_t* done = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* accf = empty + S;  // [2] accumulator ready
+  uint64_t* acce = accf + 2;   // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int32_t* flags = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);  // abort, last, issued, consumed
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int mt = blockIdx.x, split = blockIdx.y;
-  const int c0 = split * g.num_chunks / g.num_splits;
-  const int c1 = (split + 1) * g.num_chunks / g.num_splits;
-  const int nc = c1 - c0;  // >= 1: the host keeps num_splits <= num_chunks
+  const int P = gridDim.x, U = g.units, KB = g.kblocks;
+  const int u0 = unit_begin(blockIdx.x, U, P), u1 = unit_begin(blockIdx.x + 1, U, P);
+  const int n = u1 - u0;  // >= 1: the grid never exceeds the unit count
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);  // one arrival per epilogue warp
+    }
     flags[0] = flags[1] = flags[2] = flags[3] = 0;
     fence_barrier_init();
   }
@@ -90,133 +129,222 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) PL_TRACE_POINT(0);
   pdl_launch_dependents();
 
-  if (threadIdx.x == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // A TMA instruction costs a fixed issue time however many lanes issue
+    // it, so the warp issues up to kGemmIssue units per instruction: lane 2j
+    // loads unit j's weight tile (and arms its barrier), lane 2j+1 its
+    // activation tile.
     const uint64_t pol = l2_evict_first_policy();
-    const int pre = g.e.early_weights ? (nc < S ? nc : S) : 0;
-    for (int i = 0; i < pre; ++i) {  // weights are not produced upstream: start them now
+    const int pre = g.e.early_weights ? (n < S ? n : S) : 0;
+    for (int i = lane; i < pre; i += 32) {  // weights are not produced upstream: start them now
+      const int u = u0 + i;
       mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-      tma_load_2d(smem + i * C::kStageBytes, &wmap, (c0 + i) * kGemmKC, mt * kGemmM, &full[i], pol);
+      gemm_tile_load<KCS>(smem + i * C::kStageBytes, &wmap, u % KB, (u / KB) * kGemmM, &full[i], pol);
     }
     pdl_wait();
-    int i = 0;
-    for (; i < nc; ++i) {
+    if (lane == 0) PL_TRACE_POINT(1);
+    const int jb = lane >> 1, kind = lane & 1;
+    const int batch = S < kGemmIssue ? S : kGemmIssue;  // a batch never reuses its own stages
+    int i0 = 0;
+    for (; i0 < n; i0 += batch) {
+      const int i = i0 + jb;
+      const bool active = lane < 2 * batch && i < n;
       const int s = i % S;
-      if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1)) {
-        set_status(g.e.status, PL_ERR_TIMEOUT);
+      bool ok = true;
+      if (active && i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) set_status(g.e.status, PL_ERR_TIMEOUT);
         flags[0] = 1;
         break;
       }
+      const int u = u0 + i;
       uint8_t* st = smem + s * C::kStageBytes;
-      if (i >= pre) {
-        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-        tma_load_2d(st, &wmap, (c0 + i) * kGemmKC, mt * kGemmM, &full[s], pol);
+      if (active && kind == 0 && i >= pre) mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+      __syncwarp();
+      if (active) {
+        if (kind == 0) {
+          if (i >= pre) gemm_tile_load<KCS>(st, &wmap, u % KB, (u / KB) * kGemmM, &full[s], pol);
+        } else {
+          gemm_tile_load<KCS>(st + C::kABytes, &xmap, u % KB, 0, &full[s], 0ull);
+        }
       }
-      tma_load_2d(st + C::kABytes, &xmap, (c0 + i) * kGemmKC, 0, &full[s], 0ull);
     }
-    flags[2] = i > pre ? i : pre;
-  } else if (threadIdx.x == 32) {
+    if (lane == 0) flags[2] = i0 < n ? (i0 > pre ? i0 : pre) : n;
+  } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    constexpr uint32_t idesc = umma_idesc_bf16(kGemmM, N);
-    int i = 0;
-    for (; i < nc; ++i) {
-      const int s = i % S;
-      if (!mbar_wait(&full[s], (i / S) & 1)) {
-        set_status(g.e.status, PL_ERR_TIMEOUT);
-        flags[0] = 1;
-        break;
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kGemmM, N);
+      int i = 0, seg = 0;
+      bool ok = true;
+      for (; i < n; ++i) {
+        const int u = u0 + i, kb = u % KB;
+        const bool first = (i == 0 || kb == 0), last = (i == n - 1 || kb == KB - 1);
+        const int b = seg & 1;
+        if (first && seg >= 2) ok = mbar_wait(&acce[b], ((seg >> 1) - 1) & 1);
+        const int s = i % S;
+        if (ok) ok = mbar_wait(&full[s], (i / S) & 1);
+        if (!ok) {
+          set_status(g.e.status, PL_ERR_TIMEOUT);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * C::kStageBytes);
+        const uint32_t b0 = a0 + C::kABytes;
+        const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols);
+#pragma unroll
+        for (int j = 0; j < KCS; ++j) {
+#pragma unroll
+          for (int k = 0; k < kGemmKC / 16; ++k)
+            umma_bf16(acc, umma_desc_k_sw128(a0 + j * C::kATile + 32 * k),
+                      umma_desc_k_sw128(b0 + j * C::kBTile + 32 * k), idesc, (!first || j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        if (last) {
+          umma_commit(&accf[b]);
+          ++seg;
+        }
       }
-      tc_fence_after();
-      const uint32_t a0 = smem_u32(smem + s * C::kStageBytes);
-      const uint32_t b0 = a0 + C::kABytes;
-#pragma unroll
-      for (int k = 0; k < kGemmKC / 16; ++k)
-        umma_bf16(tmem, umma_desc_k_sw128(a0 + 32 * k), umma_desc_k_sw128(b0 + 32 * k), idesc,
-                  (i > 0 || k > 0) ? 1u : 0u);
-      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
-    }
-    flags[3] = i;
-    umma_commit(done);
-  }
-
-  // ------------------------------------------------------------ epilogue
-  pdl_wait();  // residual, LoRA down and adapter ids come from upstream kernels
-  if (!mbar_wait(done, 0)) {
-    set_status(g.e.status, PL_ERR_TIMEOUT);
-    flags[0] = 1;
-  }
-  tc_fence_after();
-  __syncthreads();
-  const bool abort = flags[0] != 0;
-  const int row = 32 * warp + lane;
-  const int64_t o = (int64_t)mt * kGemmM + row;
-  const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
-  const int T = g.e.T;
-  const bool row_ok = o < g.e.n_out;
-  if (g.num_splits == 1) {
-#pragma unroll 1
-    for (int c = 0; c < N / 16; ++c) {
-      float v[16];
-      tmem_ld16(lane_addr + 16 * c, v);  // whole warp, whatever the row
-      if (!abort && row_ok) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (16 * c + j < T) gemv_epilogue(g.e, o, 16 * c + j, v[j]);
+      flags[3] = i;
+      if (!ok) {
+        // Release the epilogue for the segments that will not be computed.
+        for (int i2 = i; i2 < n; ++i2) {
+          const int kb = (u0 + i2) % KB;
+          if (i2 == n - 1 || kb == KB - 1) {
+            umma_commit(&accf[seg & 1]);
+            ++seg;
+          }
+        }
       }
     }
   } else {
-    float* mine = g.partial + ((int64_t)mt * g.num_splits + split) * N * kGemmM;
-#pragma unroll 1
-    for (int c = 0; c < N / 16; ++c) {
-      float v[16];
-      tmem_ld16(lane_addr + 16 * c, v);
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (16 * c + j < T) __stcg(mine + (16 * c + j) * kGemmM + row, v[j]);
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const int32_t ticket = atomicAdd(&g.counters[mt], 1);
-      flags[1] = ticket == g.num_splits - 1 ? 1 : 0;
-    }
-    __syncthreads();
-    if (flags[1]) {
-      // Last split of this tile: add the splits in order, then the epilogue.
-      __threadfence();
-      const float* base = g.partial + (int64_t)mt * g.num_splits * N * kGemmM + row;
-      const int S2 = g.num_splits;
-#pragma unroll 1
-      for (int t0 = 0; t0 < T; t0 += 8) {
-        float acc[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-        for (int s = 0; s < S2; ++s) {
-          float p[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            p[j] = (t0 + j < T) ? __ldcg(base + ((int64_t)s * N + t0 + j) * kGemmM) : 0.f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] += p[j];
-        }
-        if (!abort && row_ok) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (t0 + j < T) gemv_epilogue(g.e, o, t0 + j, acc[j]);
-        }
+    // ------------------------------------------------------------ epilogue
+    pdl_wait();  // residual, LoRA down and adapter ids come from upstream kernels
+    const int ew = warp - 2;     // epilogue warp 0..3
+    const int q = warp & 3;      // TMEM lane quadrant this warp may read
+    const int row = 32 * q + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    const int T = g.e.T;
+    constexpr int kEpiThreads = 128;
+    int seg = 0;
+    for (int i = 0; i < n;) {
+      const int u = u0 + i, t = u / KB, ka = u % KB;
+      int len = KB - ka;
+      if (len > n - i) len = n - i;
+      const int b = seg & 1;
+      if (!mbar_wait(&accf[b], (seg >> 1) & 1)) {
+        set_status(g.e.status, PL_ERR_TIMEOUT);
+        flags[0] = 1;
       }
-      if (threadIdx.x == 0) g.counters[mt] = 0;
+      tc_fence_after();
+      const uint32_t acc = lane_base + (uint32_t)(b * C::kAccCols);
+      const int64_t o4 = (int64_t)t * kGemmM + 4 * lane;
+      const bool whole = (ka == 0 && len == KB);
+      if (whole) {
+        // The whole tile is here: stage [16 tokens][128 rows] through shared
+        // memory, then warp ew finishes tokens ew, ew+4, ... (4 rows a lane).
+#pragma unroll 1
+        for (int c = 0; c < N / 16 && 16 * c < T; ++c) {
+          float v[16];
+          tmem_ld16(acc + 16 * c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) stile[j * kGemmM + row] = v[j];
+          named_barrier(1, kEpiThreads);
+          if (!flags[0]) {
+            for (int j = ew; j < 16 && 16 * c + j < T; j += 4) {
+              const float4 r4 = *reinterpret_cast<const float4*>(stile + j * kGemmM + 4 * lane);
+              const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+              epilogue_rows4(g.e, o4, 16 * c + j, rv);
+            }
+          }
+          named_barrier(1, kEpiThreads);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[b]);
+      } else {
+        // Part of a tile: leave the fp32 partial in this CTA's slot; the last
+        // contributor adds the slots in order and runs the epilogue.
+        const int c_first = cta_of_unit(t * KB, U, P);
+        const int c_last = cta_of_unit(t * KB + KB - 1, U, P);
+        const int slot = blockIdx.x - c_first;
+        float* mine = g.partial + ((int64_t)t * g.max_slots + slot) * N * kGemmM;
+#pragma unroll 1
+        for (int c = 0; c < N / 16 && 16 * c < T; ++c) {
+          float v[16];
+          tmem_ld16(acc + 16 * c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (16 * c + j < T) __stcg(mine + (16 * c + j) * kGemmM + row, v[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[b]);
+        __threadfence();
+        named_barrier(1, kEpiThreads);
+        if (ew == 0 && lane == 0) {
+          const int32_t ticket = atomicAdd(&g.counters[t], 1);
+          flags[1] = ticket == c_last - c_first ? 1 : 0;
+        }
+        named_barrier(1, kEpiThreads);
+        if (flags[1]) {
+          __threadfence();
+          const int nslots = c_last - c_first + 1;
+          const float* base = g.partial + (int64_t)t * g.max_slots * N * kGemmM + 4 * lane;
+          // Two tokens x four slots of loads in flight per lane; slots are
+          // added in order, so the sum does not depend on timing.
+#pragma unroll 1
+          for (int tok = ew; tok < T; tok += 8) {
+            float a4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            const bool two = tok + 4 < T;
+#pragma unroll 1
+            for (int sl = 0; sl < nslots; sl += 4) {
+              float4 p[2][4];
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  p[h][k] = (sl + k < nslots && (h == 0 || two))
+                                ? __ldcg(reinterpret_cast<const float4*>(
+                                      base + ((int64_t)(sl + k) * N + tok + 4 * h) * kGemmM))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  a4[h][0] += p[h][k].x;
+                  a4[h][1] += p[h][k].y;
+                  a4[h][2] += p[h][k].z;
+                  a4[h][3] += p[h][k].w;
+                }
+            }
+            if (!flags[0]) {
+              epilogue_rows4(g.e, o4, tok, a4[0]);
+              if (two) epilogue_rows4(g.e, o4, tok + 4, a4[1]);
+            }
+          }
+          if (ew == 0 && lane == 0) g.counters[t] = 0;
+        }
+        named_barrier(1, kEpiThreads);  // flags[1] is reused by the next segment
+      }
+      i += len;
+      ++seg;
     }
+    if (threadIdx.x == 64) PL_TRACE_POINT(7);
   }
 
   // ------------------------------------------------------------ teardown
+  __syncthreads();
   if (threadIdx.x == 0) {
     // Loads issued but never consumed (abort only) must land before exit.
     const int issued = flags[2], consumed = flags[3];
     for (int i = consumed; i < issued; ++i) (void)mbar_wait(&full[i % S], (i / S) & 1);
   }
+  if (lane == 0) PL_TRACE_MAX(8);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -296,32 +424,39 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* __restrict__ 
 }  // namespace pl
 
 // =================================================================== host
+PL_TRACE_READER(pl_trace_read_gemm)
+
 namespace {
 
-struct Map2Key {
+struct MapKey2 {
   const void* ptr;
   int64_t inner, rows, stride;
-  int32_t box_rows, dev;
-  bool operator==(const Map2Key& o) const {
+  int32_t box_rows, kcs, dev;
+  bool operator==(const MapKey2& o) const {
     return ptr == o.ptr && inner == o.inner && rows == o.rows && stride == o.stride && box_rows == o.box_rows &&
-           dev == o.dev;
+           kcs == o.kcs && dev == o.dev;
   }
 };
 constexpr int kMap2Cache = 512;
 struct Map2Cache {
   std::mutex mu;
-  Map2Key key[kMap2Cache];
+  MapKey2 key[kMap2Cache];
   CUtensorMap map[kMap2Cache];
   int used = 0, next = 0;
 };
 Map2Cache g_map2;
 
-// bf16 matrix [rows][inner] with row stride `stride` elements; box 64 x box_rows,
-// 128-byte swizzle, out-of-range rows/columns read as zero.
-int32_t matrix_map(const void* ptr, int64_t inner, int64_t rows, int64_t stride, int box_rows, CUtensorMap* out) {
+// bf16 matrix [rows][inner] with a row stride of `stride` elements, read in
+// tiles of box_rows x (kcs x 64) with 128-byte swizzling; out-of-range rows
+// and chunks read as zero.  kcs == 1: 2-D map (inner, rows).  kcs > 1
+// (inner % 64 == 0): 3-D map (64, rows, inner / 64) whose chunk dimension
+// steps 128 bytes along the row, so one copy lands kcs consecutive
+// [box_rows][64] swizzled tiles.
+int32_t matrix_map(const void* ptr, int64_t inner, int64_t rows, int64_t stride, int box_rows, int kcs,
+                   CUtensorMap* out) {
   int dev = 0;
   cudaGetDevice(&dev);
-  Map2Key k{ptr, inner, rows, stride, box_rows, dev};
+  MapKey2 k{ptr, inner, rows, stride, box_rows, kcs, dev};
   std::lock_guard<std::mutex> lock(g_map2.mu);
   for (int i = 0; i < g_map2.used; ++i)
     if (g_map2.key[i] == k) {
@@ -330,15 +465,26 @@ int32_t matrix_map(const void* ptr, int64_t inner, int64_t rows, int64_t stride,
     }
   pl_host::EncodeTiledFn enc = pl_host::encode_tiled_fn();
   if (enc == nullptr) return PL_ERR_CUDA;
-  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)stride * 2};
-  cuuint32_t box[2] = {(cuuint32_t)pl::kGemmKC, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
   CUtensorMap m;
-  CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return PL_ERR_INVALID_ARGUMENT;
+  CUresult r;
+  if (kcs == 1) {
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)stride * 2};
+    cuuint32_t box[2] = {(cuuint32_t)pl::kGemmKC, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[3] = {(cuuint64_t)pl::kGemmKC, (cuuint64_t)rows, (cuuint64_t)(inner / pl::kGemmKC)};
+    cuuint64_t strides[2] = {(cuuint64_t)stride * 2, (cuuint64_t)pl::kGemmKC * 2};
+    cuuint32_t box[3] = {(cuuint32_t)pl::kGemmKC, (cuuint32_t)box_rows, (cuuint32_t)kcs};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return PL_ERR_UNSUPPORTED;
   int slot;
   if (g_map2.used < kMap2Cache) {
     slot = g_map2.used++;
@@ -356,55 +502,85 @@ int gemm_n(int tokens) { return tokens <= 16 ? 16 : tokens <= 32 ? 32 : tokens <
 
 int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
+constexpr int kGemmSmemBudget = 212 * 1024;
+
 struct GemmShape {
-  int n, stages, m_tiles, chunks, splits, stage_bytes;
+  int n, kcs, stages, m_tiles, kblocks, units, ctas, max_slots, stage_bytes;
 };
 
-GemmShape gemm_shape(int tokens, int k_in, int n_out, int sms) {
+// Tile geometry: K blocks of kcs x 64 columns (kcs 4, or 2 at N = 128, when
+// K % 64 == 0; else 1), as many ring stages as fit; `ctas` CTAs (one per SM
+// by default) share the m_tiles x kblocks units evenly.
+GemmShape gemm_shape(int tokens, int k_in, int n_out, int ctas, bool allow_3d) {
   GemmShape s;
   s.n = gemm_n(tokens);
-  s.stage_bytes = pl::kGemmM * 128 + s.n * 128;
+  s.kcs = (allow_3d && k_in % pl::kGemmKC == 0) ? (s.n == 128 ? 2 : 4) : 1;
+  s.stage_bytes = s.kcs * (pl::kGemmM * 128 + s.n * 128);
   s.m_tiles = (n_out + pl::kGemmM - 1) / pl::kGemmM;
-  s.chunks = (k_in + pl::kGemmKC - 1) / pl::kGemmKC;
-  // One CTA per SM; K is split only when the row tiles leave SMs idle, and
-  // every split keeps at least 4 chunks.
-  int splits = s.m_tiles >= sms ? 1 : sms / s.m_tiles;
-  const int max_by_k = s.chunks / 4 > 0 ? s.chunks / 4 : 1;
-  if (splits > max_by_k) splits = max_by_k;
-  if (splits > 16) splits = 16;
-  s.splits = splits < 1 ? 1 : splits;
-  int stages = (200 * 1024) / s.stage_bytes;
+  const int block_cols = pl::kGemmKC * s.kcs;
+  s.kblocks = (k_in + block_cols - 1) / block_cols;
+  s.units = s.m_tiles * s.kblocks;
+  s.ctas = ctas < s.units ? ctas : s.units;
+  int stages = kGemmSmemBudget / s.stage_bytes;
   if (stages > 8) stages = 8;
-  if (stages > s.chunks) stages = s.chunks < 2 ? 2 : s.chunks;
-  s.stages = stages;
+  s.stages = stages < 2 ? 2 : stages;
+  s.max_slots = 1;
+  for (int t = 0; t < s.m_tiles; ++t) {
+    const int c0 = pl::cta_of_unit(t * s.kblocks, s.units, s.ctas);
+    const int c1 = pl::cta_of_unit(t * s.kblocks + s.kblocks - 1, s.units, s.ctas);
+    if (c1 - c0 + 1 > s.max_slots) s.max_slots = c1 - c0 + 1;
+  }
   return s;
 }
 
 int64_t gemm_workspace_bytes(const GemmShape& s) {
   int64_t b = align256((int64_t)s.m_tiles * 4);
-  if (s.splits > 1) b += (int64_t)s.m_tiles * s.splits * s.n * pl::kGemmM * 4;
+  if (s.max_slots > 1) b += (int64_t)s.m_tiles * s.max_slots * s.n * pl::kGemmM * 4;
   return b;
 }
 
-template <int N>
-int32_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int m_tiles, int splits,
-                    int stage_bytes, int stages, void* stream) {
-  auto kern = pl::linear_tc_kernel<N>;
-  const int smem = pl::gemm_smem_bytes(stage_bytes, stages);
+template <int N, int KCS>
+int32_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int ctas, int stages,
+                    void* stream) {
+  auto kern = pl::linear_tc_kernel<N, KCS>;
+  const int smem = pl::gemm_smem_bytes(pl::GemmCfg<N, KCS>::kStageBytes, stages);
   int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (st != PL_OK) return st;
-  return pl_host::launch_pdl(kern, dim3(m_tiles, splits), dim3(pl::kGemmThreads), smem, stream, wm, xm, g);
+  return pl_host::launch_pdl(kern, dim3(ctas), dim3(pl::kGemmThreads), smem, stream, wm, xm, g);
+}
+
+template <int N>
+int32_t launch_gemm_n(int kcs, const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int ctas,
+                      int stages, void* stream) {
+  if (kcs == 1) return launch_gemm<N, 1>(wm, xm, g, ctas, stages, stream);
+  if constexpr (N == 128) return launch_gemm<N, 2>(wm, xm, g, ctas, stages, stream);
+  else return launch_gemm<N, 4>(wm, xm, g, ctas, stages, stream);
+}
+
+int sm_count_or_default() {
+  const int sms = pl_host::sm_count();
+  return sms > 0 ? sms : 148;
+}
+
+// One CTA per SM when the row tiles alone cover the device; otherwise 7/8 of
+// the SMs, which measured faster (fewer contributors per shared tile, less
+// partial traffic) on the 4096-row projections.
+int default_ctas(int n_out) {
+  const int sms = sm_count_or_default();
+  const int m_tiles = (n_out + pl::kGemmM - 1) / pl::kGemmM;
+  return m_tiles >= sms ? sms : (sms * 7) / 8;
 }
 
 }  // namespace
 
-extern "C" int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t n_out, pl_gemm_plan_t* plan) {
-  if (plan == nullptr || num_tokens < 1 || num_tokens > 128 || k_in <= 0 || n_out <= 0) return PL_ERR_INVALID_ARGUMENT;
-  int sms = pl_host::sm_count();
-  if (sms <= 0) sms = 148;
-  const GemmShape s = gemm_shape(num_tokens, k_in, n_out, sms);
-  plan->num_splits = s.splits;
-  plan->ctas = s.m_tiles * s.splits;
+extern "C" int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t n_out, int32_t num_ctas,
+                                       pl_gemm_plan_t* plan) {
+  if (plan == nullptr || num_tokens < 1 || num_tokens > 128 || k_in <= 0 || n_out <= 0 || num_ctas < 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  const GemmShape s = gemm_shape(num_tokens, k_in, n_out, num_ctas > 0 ? num_ctas : default_ctas(n_out),
+                                 k_in % pl::kGemmKC == 0);
+  plan->ctas = s.ctas;
+  plan->max_slots = s.max_slots;
   plan->workspace_bytes = gemm_workspace_bytes(s);
   return PL_OK;
 }
@@ -414,11 +590,11 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
                                        int64_t down_stride, const void* lora_b, int32_t lora_rank, float lora_scale,
                                        const int32_t* slice_end, int32_t num_slices, const int32_t* tok_adapter,
                                        const void* residual, int64_t res_stride, void* y, int64_t y_stride,
-                                       int32_t num_splits, void* workspace, int64_t workspace_bytes, int32_t flags,
+                                       int32_t num_ctas, void* workspace, int64_t workspace_bytes, int32_t flags,
                                        int32_t* status_dev, void* stream) {
   if (num_tokens == 0 || n_out == 0) return PL_OK;
   if (x == nullptr || w == nullptr || y == nullptr || num_tokens < 0 || num_tokens > 128 || k_in <= 0 ||
-      n_out < 0 || workspace == nullptr)
+      n_out < 0 || workspace == nullptr || num_ctas < 0)
     return PL_ERR_INVALID_ARGUMENT;
   if (k_in % 8 != 0 || x_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
       (reinterpret_cast<uintptr_t>(w) & 15))
@@ -426,20 +602,19 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   if (lora_b != nullptr && (lora_down == nullptr || lora_rank <= 0 || num_slices < 1 || num_slices > 4 ||
                             (num_slices > 1 && slice_end == nullptr)))
     return PL_ERR_INVALID_ARGUMENT;
-  int sms = pl_host::sm_count();
-  if (sms <= 0) sms = 148;
-  const GemmShape s = gemm_shape(num_tokens, k_in, n_out, sms);
-  if (num_splits < 1 || num_splits > s.chunks || num_splits > 16) return PL_ERR_INVALID_ARGUMENT;
-  GemmShape sh = s;
-  sh.splits = num_splits;
+  const int ctas = num_ctas > 0 ? num_ctas : default_ctas(n_out);
+  GemmShape sh = gemm_shape(num_tokens, k_in, n_out, ctas, true);
+  CUtensorMap wm, xm;
+  int32_t st = matrix_map(w, k_in, n_out, k_in, pl::kGemmM, sh.kcs, &wm);
+  if (st == PL_OK) st = matrix_map(x, k_in, num_tokens, x_stride, sh.n, sh.kcs, &xm);
+  if (st == PL_ERR_UNSUPPORTED && sh.kcs > 1) {  // no 3-D map: one chunk per K block
+    sh = gemm_shape(num_tokens, k_in, n_out, ctas, false);
+    st = matrix_map(w, k_in, n_out, k_in, pl::kGemmM, 1, &wm);
+    if (st == PL_OK) st = matrix_map(x, k_in, num_tokens, x_stride, sh.n, 1, &xm);
+  }
+  if (st != PL_OK) return st;
   if (workspace_bytes < gemm_workspace_bytes(sh) || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return PL_ERR_WORKSPACE_TOO_SMALL;
-
-  CUtensorMap wm, xm;
-  int32_t st = matrix_map(w, k_in, n_out, k_in, pl::kGemmM, &wm);
-  if (st != PL_OK) return st;
-  st = matrix_map(x, k_in, num_tokens, x_stride, sh.n, &xm);
-  if (st != PL_OK) return st;
 
   pl::GemmArgs g = {};
   pl::GemvArgs& a = g.e;
@@ -465,18 +640,19 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   a.y_stride = y_stride;
   a.early_weights = (flags & PL_FLAG_WEIGHTS_STATIC) ? 1 : 0;
   a.status = status_dev;
-  g.num_chunks = sh.chunks;
-  g.num_splits = num_splits;
+  g.kblocks = sh.kblocks;
+  g.units = sh.units;
   g.stages = sh.stages;
+  g.max_slots = sh.max_slots;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   g.counters = reinterpret_cast<int32_t*>(ws);
-  g.partial = num_splits > 1 ? reinterpret_cast<float*>(ws + align256((int64_t)sh.m_tiles * 4)) : nullptr;
+  g.partial = sh.max_slots > 1 ? reinterpret_cast<float*>(ws + align256((int64_t)sh.m_tiles * 4)) : nullptr;
 
   switch (sh.n) {
-    case 16: return launch_gemm<16>(wm, xm, g, sh.m_tiles, num_splits, sh.stage_bytes, sh.stages, stream);
-    case 32: return launch_gemm<32>(wm, xm, g, sh.m_tiles, num_splits, sh.stage_bytes, sh.stages, stream);
-    case 64: return launch_gemm<64>(wm, xm, g, sh.m_tiles, num_splits, sh.stage_bytes, sh.stages, stream);
-    default: return launch_gemm<128>(wm, xm, g, sh.m_tiles, num_splits, sh.stage_bytes, sh.stages, stream);
+    case 16: return launch_gemm_n<16>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
+    case 32: return launch_gemm_n<32>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
+    case 64: return launch_gemm_n<64>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
+    default: return launch_gemm_n<128>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
   }
 }
 

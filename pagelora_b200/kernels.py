@@ -235,24 +235,12 @@ def linear_lora_fused(
     return out
 
 
-def gemm_plan(num_tokens: int, k_in: int, n_out: int) -> _capi.GemmPlan:
-    """Split-K plan of :func:`linear_lora_gemm` on the current device."""
+def gemm_plan(num_tokens: int, k_in: int, n_out: int, num_ctas: int = 0) -> _capi.GemmPlan:
+    """Work split of :func:`linear_lora_gemm` (``num_ctas`` 0: one CTA per SM)."""
 
     plan = _capi.GemmPlan()
-    call("pl_linear_gemm_plan", int(num_tokens), int(k_in), int(n_out), _capi.ctypes.byref(plan))
+    call("pl_linear_gemm_plan", int(num_tokens), int(k_in), int(n_out), int(num_ctas), _capi.ctypes.byref(plan))
     return plan
-
-
-def gemm_workspace_bytes(num_tokens: int, n_out: int, num_splits: int) -> int:
-    """Workspace of :func:`linear_lora_gemm` for an explicit split count
-    (counters, then fp32 split tiles [m_tiles, splits, N, 128])."""
-
-    m_tiles = -(-n_out // 128)
-    n_pad = 16 if num_tokens <= 16 else 32 if num_tokens <= 32 else 64 if num_tokens <= 64 else 128
-    nbytes = -(-m_tiles * 4 // 256) * 256
-    if num_splits > 1:
-        nbytes += m_tiles * num_splits * n_pad * 128 * 4
-    return nbytes
 
 
 def linear_lora_gemm(
@@ -268,7 +256,7 @@ def linear_lora_gemm(
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
     workspace: torch.Tensor | None = None,
-    num_splits: int | None = None,
+    num_ctas: int = 0,
     weights_static: bool = False,
     status: torch.Tensor | None = None,
 ) -> torch.Tensor:
@@ -276,7 +264,8 @@ def linear_lora_gemm(
     tokens on the tcgen05 tensor cores.  ``x`` [T, K] is used as given (apply
     :func:`rmsnorm` / :func:`silu_mul` first); the epilogue arguments are those
     of :func:`linear_lora_fused`.  ``workspace`` (uint8, zeroed once) is sized
-    by :func:`gemm_plan`; one is allocated when omitted."""
+    by :func:`gemm_plan` for the same ``num_ctas``; one is allocated when
+    omitted."""
 
     _need_cuda(x, weight)
     _need(x, torch.bfloat16, "x")
@@ -287,9 +276,9 @@ def linear_lora_gemm(
     n, k = weight.shape
     if out is None:
         out = torch.empty(t, n, dtype=torch.bfloat16, device=x.device)
-    splits = int(gemm_plan(t, k, n).num_splits) if num_splits is None else int(num_splits)
     if workspace is None:
-        workspace = torch.zeros(gemm_workspace_bytes(t, n, splits), dtype=torch.uint8, device=x.device)
+        need = int(gemm_plan(t, k, n, num_ctas).workspace_bytes)
+        workspace = torch.zeros(need, dtype=torch.uint8, device=x.device)
     rank = 0
     num_slices = 1
     slice_ptr, slice_keepalive = None, None
@@ -305,7 +294,7 @@ def linear_lora_gemm(
          ptr(lora_down), 0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
          float(lora_scale), slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
          0 if residual is None else _row_stride(residual, "residual"), ptr(out), _row_stride(out, "out"),
-         int(splits), ptr(workspace), int(workspace.numel()), int(flags), ptr(status), stream_handle())
+         int(num_ctas), ptr(workspace), int(workspace.numel()), int(flags), ptr(status), stream_handle())
     del slice_keepalive
     return out
 

@@ -360,13 +360,16 @@ def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
     return mag, want
 
 
+@pytest.mark.parametrize("k_in", [600, 640])
 @pytest.mark.parametrize("t", [1, 9, 16, 33, 64, 100, 128])
-def test_linear_lora_gemm_vs_oracle(K, t):
-    """tcgen05 multi-token linear: multi-adapter LoRA epilogue, partial tiles,
-    K tail, split-K 1 / planned / 5 (deterministic across splits)."""
+def test_linear_lora_gemm_vs_oracle(K, t, k_in):
+    """tcgen05 multi-token linear: multi-adapter LoRA epilogue, partial row
+    tile, K tails (600: 2-D tiles with a partial 64-column chunk; 640: 3-D
+    tiles, last K block half empty), grids of 1 CTA (whole tiles), one per
+    SM and 7 CTAs (tiles shared between CTAs, partials merged in order)."""
 
-    rng = np.random.default_rng(300 + t)
-    k_in, n, r, n_ad = 600, 700, 16, 3   # K tail (600 = 9 chunks + 24), last row tile partial
+    rng = np.random.default_rng(300 + t + k_in)
+    n, r, n_ad = 700, 16, 3
     x = bf16(rng.normal(size=(t, k_in)))
     w = bf16(rng.normal(size=(n, k_in)) * 0.05)
     bias = bf16(rng.normal(size=n) * 0.1)
@@ -376,10 +379,10 @@ def test_linear_lora_gemm_vs_oracle(K, t):
     tok_ad = rng.integers(-1, n_ad, size=t)
     mag, want = _gemm_oracle(x, w, bias, down, bmat, tok_ad, 300, res, scale=2.0)
     outs = []
-    for splits in (1, None, 5):
+    for ctas in (1, 0, 7):
         y = K.linear_lora_gemm(_t(x), _t(w), bias=_t(bias), lora_down=_t(down, torch.float32), lora_b=_t(bmat),
                                lora_scale=2.0, slice_ends=(300,), tok_adapter=_i32(tok_ad), residual=_t(res),
-                               num_splits=splits)
+                               num_ctas=ctas)
         torch.cuda.synchronize()
         outs.append(_np(y))
         _ulps_close(outs[-1], want, ulps=3, magnitude=mag)
