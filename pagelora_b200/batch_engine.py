@@ -1,0 +1,419 @@
+"""Batched multi-adapter decode on the B200 kernels (many sequences, one step).
+
+The batched counterpart of :class:`pagelora_b200.engine.DecodeEngine`: B rows
+decode one token each per step, every row with its own context length, pages
+anywhere in the pool, and its own LoRA adapter.  It is the shape of the
+reference's batched graph runner (model/flashinfer/cuda_graph.py:118-543,
+``FlashInferBatchDecodeCudaGraphRunner``) over the batched layer
+(model/flashinfer/layer_runner.py:338-396) with the multi-adapter serving
+path of multilora (one adapter per row, segment-grouped shrink).
+
+One decode step (captured once into a CUDA graph, every launch PDL-chained):
+
+    page_table_advance (all rows) -> embed
+    per layer:  rmsnorm -> LoRA-A shrink (segments by adapter) -> q/k/v projection
+                -> q/k norm + RoPE + paged KV append (+ per-row LoRA-B expand)
+                -> paged decode -> o shrink -> o projection (+ per-row LoRA-B, residual)
+                -> rmsnorm -> gate_up projection -> SiLU-mul -> down projection (+ residual)
+    rmsnorm -> lm_head -> argmax (per row)
+
+Projections go to the tcgen05 GEMM (:func:`kernels.linear_lora_gemm`) for
+more than 8 rows and to the fused decode GEMV (norm / SiLU-mul prologue in
+the kernel) for up to 8.  Rows must be ordered by adapter so the shrink sees
+one segment per adapter.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from pagelora_b200 import kernels as K
+from pagelora_b200._capi import PL_PROLOGUE_RMSNORM, PL_PROLOGUE_SILU_MUL
+from pagelora_b200.engine import _rmsnorm_fused, _rmsnorm_hf, _rope
+from pagelora_b200.synthetic import LoRASpec, ModelSpec
+
+GEMV_MAX_ROWS = 8
+
+
+class BatchDecodeEngine:
+    """Greedy decoder for B rows with per-row adapters; weights in Hugging Face naming.
+
+    ``adapters`` is a list of LoRA weight dicts ({"layers.{i}.{q|k|v|o}": (A, B)}),
+    ``row_adapter[r]`` the adapter of row r (-1: base model only); rows are
+    grouped by adapter (non-decreasing ids, base rows first).
+    """
+
+    def __init__(self, spec: ModelSpec, weights: dict[str, torch.Tensor], *, adapters: list[dict] | None,
+                 lora_spec: LoRASpec | None, row_adapter: list[int], page_size: int = 16, max_context: int = 4096,
+                 num_pages: int | None = None, device: torch.device | str = "cuda") -> None:
+        self.spec = spec
+        self.device = torch.device(device)
+        self.page_size = page_size
+        self.rows = len(row_adapter)
+        if any(b < a for a, b in zip(row_adapter, row_adapter[1:])):
+            raise ValueError("rows must be grouped by adapter (non-decreasing adapter ids)")
+        n_ad = len(adapters) if adapters else 0
+        if any(a >= n_ad for a in row_adapter):
+            raise ValueError("row_adapter names an adapter that was not given")
+        self.row_adapter = list(row_adapter)
+        self.lora_rank = lora_spec.rank if (adapters and lora_spec) else 0
+        self.lora_scale = lora_spec.scale if (adapters and lora_spec) else 1.0
+        self.qkv_lora_scale = 1.0
+        dev, bf = self.device, torch.bfloat16
+        H, D, B = spec.hidden, spec.head_dim, self.rows
+
+        def take(name: str) -> torch.Tensor:
+            return weights.pop(name).to(device=dev, dtype=bf).contiguous()
+
+        self.layers = []
+        for i in range(spec.num_layers):
+            p = f"model.layers.{i}."
+            w_qkv = torch.cat([take(p + f"self_attn.{m}_proj.weight") for m in "qkv"], 0).contiguous()
+            L = dict(w_qkv=w_qkv, w_o=take(p + "self_attn.o_proj.weight"),
+                     w_gate_up=torch.cat([take(p + "mlp.gate_proj.weight"), take(p + "mlp.up_proj.weight")],
+                                         0).contiguous(),
+                     w_down=take(p + "mlp.down_proj.weight"), input_norm=take(p + "input_layernorm.weight"),
+                     post_norm=take(p + "post_attention_layernorm.weight"),
+                     q_norm=take(p + "self_attn.q_norm.weight") if spec.qk_norm else None,
+                     k_norm=take(p + "self_attn.k_norm.weight") if spec.qk_norm else None,
+                     a_qkv=None, b_qkv=None, a_o=None, b_o=None)
+            if self.lora_rank:
+                r, sc = lora_spec.rank, lora_spec.scale
+                packed = all(f"layers.{i}.{t}" in adapters[0] for t in "qkv")
+                self.qkv_lora_scale = 1.0 if packed else sc
+                a_st, b_st, ao_st, bo_st = [], [], [], []
+                for ad in adapters:
+                    a_parts, b_parts = [], []
+                    for t, od in (("q", spec.q_dim), ("k", spec.kv_dim), ("v", spec.kv_dim)):
+                        ab = ad.get(f"layers.{i}.{t}")
+                        if ab is None:
+                            a_parts.append(torch.zeros(r, H, device=dev, dtype=bf))
+                            b_parts.append(torch.zeros(od, r, device=dev, dtype=bf))
+                        else:
+                            a_parts.append(ab[0].to(dev, bf))
+                            b_parts.append((ab[1].to(dev, bf) * sc).to(bf) if packed else ab[1].to(dev, bf))
+                    a_st.append(torch.cat(a_parts, 0))
+                    b_st.append(torch.cat(b_parts, 0))
+                    ab = ad.get(f"layers.{i}.o")
+                    ao_st.append(ab[0].to(dev, bf) if ab is not None else torch.zeros(r, spec.q_dim, device=dev,
+                                                                                     dtype=bf))
+                    bo_st.append(ab[1].to(dev, bf) if ab is not None else torch.zeros(H, r, device=dev, dtype=bf))
+                L["a_qkv"] = torch.stack(a_st).contiguous()    # [n_ad, 3r, H]
+                L["b_qkv"] = torch.stack(b_st).contiguous()    # [n_ad, qkv_dim, r]
+                L["a_o"] = torch.stack(ao_st).contiguous()     # [n_ad, r, q_dim]
+                L["b_o"] = torch.stack(bo_st).contiguous()     # [n_ad, H, r]
+            self.layers.append(L)
+        self.embed = take("model.embed_tokens.weight")
+        self.final_norm = take("model.norm.weight")
+        self.lm_head = take("lm_head.weight") if "lm_head.weight" in weights else self.embed
+
+        # Paged KV pool [L, P, 2, PS, Hkv, D] and per-row device page tables.
+        self.max_pages_per_row = -(-max_context // page_size) + 1
+        self.num_pages = num_pages or B * self.max_pages_per_row + 4
+        self.kv = torch.zeros(spec.num_layers, self.num_pages, 2, page_size, spec.num_kv_heads, D, device=dev,
+                              dtype=bf)
+        self.free_pages = list(range(self.num_pages))
+        i32 = dict(device=dev, dtype=torch.int32)
+        self.row_pages = torch.zeros(B, self.max_pages_per_row, **i32)
+        self.row_num_pages = torch.zeros(B, **i32)
+        self.last_page_len = torch.zeros(B, **i32)
+        self.new_page_ids = torch.zeros(B, **i32)
+        self.indptr = torch.zeros(B + 1, **i32)
+        self.indices = torch.zeros(B * self.max_pages_per_row, **i32)
+        self.slot_page = torch.zeros(B, **i32)
+        self.slot_off = torch.zeros(B, **i32)
+        self.positions = torch.zeros(B, **i32)
+        self.status = torch.zeros(1, **i32)
+        self.tok_adapter = torch.tensor(self.row_adapter, **i32)
+        segs = [0]
+        seg_ad = []
+        for r in range(B):
+            if r == 0 or self.row_adapter[r] != self.row_adapter[r - 1]:
+                if r:
+                    segs.append(r)
+                seg_ad.append(self.row_adapter[r])
+        segs.append(B)
+        self.seg_indptr = torch.tensor(segs, **i32)
+        self.seg_adapter = torch.tensor(seg_ad, **i32)
+        self.token_buf = torch.zeros(B, device=dev, dtype=torch.int64)
+        r = max(self.lora_rank, 1)
+        self.x = torch.zeros(B, H, device=dev, dtype=bf)
+        self.xn = torch.zeros(B, H, device=dev, dtype=bf)
+        self.qkv = torch.zeros(B, spec.qkv_dim, device=dev, dtype=bf)
+        self.down_qkv = torch.zeros(B, 3 * r, device=dev, dtype=torch.float32)
+        self.q = torch.zeros(B, spec.num_qo_heads, D, device=dev, dtype=bf)
+        self.attn = torch.zeros(B, spec.num_qo_heads, D, device=dev, dtype=bf)
+        self.down_o = torch.zeros(B, r, device=dev, dtype=torch.float32)
+        self.gate_up = torch.zeros(B, 2 * spec.intermediate, device=dev, dtype=bf)
+        self.act = torch.zeros(B, spec.intermediate, device=dev, dtype=bf)
+        self.logits = torch.zeros(B, spec.vocab, device=dev, dtype=bf)
+        self.argmax_ws = torch.zeros(K.argmax_workspace_bytes(B), device=dev, dtype=torch.uint8)
+        ws = 256
+        if B > GEMV_MAX_ROWS:
+            for n, k in ((spec.qkv_dim, H), (H, spec.q_dim), (2 * spec.intermediate, H), (H, spec.intermediate),
+                         (spec.vocab, H)):
+                ws = max(ws, int(K.gemm_plan(B, k, n).workspace_bytes))
+        self.gemm_ws = torch.zeros(ws, device=dev, dtype=torch.uint8)
+        self.num_splits = 1
+        self.workspace = torch.zeros(1 << 20, device=dev, dtype=torch.uint8)
+        self.host_pages: list[list[int]] = [[] for _ in range(B)]
+        self.host_last = [0] * B
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.pinned_pages = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+        self.pinned_tokens = torch.zeros(B, dtype=torch.int64, pin_memory=True)
+
+    # ------------------------------------------------------------ planning
+    def plan(self) -> None:
+        """Split-KV plan for the current contexts (fixed in the captured graph)."""
+
+        s = self.spec
+        total = sum(len(p) for p in self.host_pages) + self.rows
+        p = K.decode_plan(self.rows, s.num_qo_heads, s.num_kv_heads, s.head_dim, self.page_size, total)
+        if p.workspace_bytes > self.workspace.numel():
+            self.workspace = torch.zeros(int(p.workspace_bytes), device=self.device, dtype=torch.uint8)
+            self.graph = None
+        if int(p.num_splits) != self.num_splits:
+            self.num_splits = int(p.num_splits)
+            self.graph = None
+
+    def _alloc_page(self) -> int:
+        if not self.free_pages:
+            raise RuntimeError("paged KV pool exhausted")
+        return self.free_pages.pop()
+
+    def shuffle_free_pages(self, seed: int) -> None:
+        """Randomly permute the free list (pages land anywhere in the pool)."""
+
+        g = torch.Generator().manual_seed(seed)
+        perm = torch.randperm(len(self.free_pages), generator=g).tolist()
+        self.free_pages = [self.free_pages[i] for i in perm]
+
+    # ------------------------------------------------------------- prefill
+    def _sync_rows(self) -> None:
+        self.row_pages.zero_()
+        for r in range(self.rows):
+            if self.host_pages[r]:
+                self.row_pages[r, : len(self.host_pages[r])] = torch.tensor(self.host_pages[r], dtype=torch.int32)
+        self.row_num_pages.copy_(torch.tensor([len(p) for p in self.host_pages], dtype=torch.int32))
+        self.last_page_len.copy_(torch.tensor(self.host_last, dtype=torch.int32))
+
+    @torch.no_grad()
+    def prefill(self, prompts: list[list[int]]) -> list[int]:
+        """Prefill every row's prompt (torch ops, each row with its adapter);
+        returns each row's first greedy token."""
+
+        if len(prompts) != self.rows:
+            raise ValueError("one prompt per row")
+        s = self.spec
+        firsts = []
+        self.prefill_logits = []
+        for r, prompt in enumerate(prompts):
+            n = len(prompt)
+            pages = [self._alloc_page() for _ in range(-(-n // self.page_size))]
+            self.host_pages[r], self.host_last[r] = list(pages), n - (len(pages) - 1) * self.page_size
+            ad = self.row_adapter[r]
+            ids = torch.tensor(prompt, device=self.device, dtype=torch.int64)
+            pos = torch.arange(n, device=self.device)
+            page_of = torch.tensor(pages, device=self.device, dtype=torch.int32)[pos // self.page_size]
+            off_of = (pos % self.page_size).to(torch.int32)
+            x = self.embed[ids]
+            for li, L in enumerate(self.layers):
+                h = _rmsnorm_fused(x, L["input_norm"], s.rms_eps)
+                qkv = F.linear(h, L["w_qkv"])
+                if ad >= 0 and L["a_qkv"] is not None:
+                    down = F.linear(h, L["a_qkv"][ad])
+                    rk = self.lora_rank
+                    deltas, off = [], 0
+                    for j, od in enumerate((s.q_dim, s.kv_dim, s.kv_dim)):
+                        dj = F.linear(down[:, j * rk:(j + 1) * rk], L["b_qkv"][ad, off:off + od])
+                        deltas.append(dj if self.qkv_lora_scale == 1.0 else dj * self.qkv_lora_scale)
+                        off += od
+                    qkv = qkv + torch.cat(deltas, -1)
+                q = qkv[:, : s.q_dim].view(n, s.num_qo_heads, s.head_dim)
+                k = qkv[:, s.q_dim: s.q_dim + s.kv_dim].view(n, s.num_kv_heads, s.head_dim)
+                v = qkv[:, s.q_dim + s.kv_dim:].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
+                if L["q_norm"] is not None:
+                    q = _rmsnorm_hf(q, L["q_norm"], s.rms_eps)
+                    k = _rmsnorm_hf(k, L["k_norm"], s.rms_eps)
+                q = _rope(q, pos, s.rope_theta)
+                k = _rope(k, pos, s.rope_theta).contiguous()
+                K.kv_append(k, v, self.kv[li], page_of, off_of, status=self.status)
+                attn = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                                      v.transpose(0, 1)[None], is_causal=True, enable_gqa=True)
+                attn = attn[0].transpose(0, 1).reshape(n, s.q_dim)
+                o = F.linear(attn, L["w_o"])
+                if ad >= 0 and L["a_o"] is not None:
+                    o = o + F.linear(F.linear(attn, L["a_o"][ad]), L["b_o"][ad]) * self.lora_scale
+                x = x + o
+                h2 = _rmsnorm_fused(x, L["post_norm"], s.rms_eps)
+                gu = F.linear(h2, L["w_gate_up"])
+                g, u = gu[:, : s.intermediate].float(), gu[:, s.intermediate:].float()
+                x = x + F.linear((g / (1.0 + torch.exp(-g)) * u).to(torch.bfloat16), L["w_down"])
+            logits = F.linear(_rmsnorm_fused(x[-1:], self.final_norm, s.rms_eps), self.lm_head)
+            self.prefill_logits.append(logits[0])
+            firsts.append(int(torch.argmax(logits[0]).item()))
+        self._sync_rows()
+        self.token_buf.copy_(torch.tensor(firsts, dtype=torch.int64))
+        self.plan()
+        self._check_status()
+        return firsts
+
+    @torch.no_grad()
+    def fill_random_context(self, lengths: list[int], *, seed: int = 0) -> None:
+        """Give row r a context of lengths[r] tokens whose K/V are random
+        N(0, 1) values (a stand-in for prefill when only the decode step is
+        measured); the first decode token of each row is random too."""
+
+        if len(lengths) != self.rows:
+            raise ValueError("one length per row")
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        for r, n in enumerate(lengths):
+            pages = [self._alloc_page() for _ in range(-(-n // self.page_size))]
+            self.host_pages[r], self.host_last[r] = list(pages), n - (len(pages) - 1) * self.page_size
+            idx = torch.tensor(pages, device=self.device, dtype=torch.int64)
+            for li in range(self.spec.num_layers):
+                vals = torch.randn((len(pages),) + tuple(self.kv.shape[2:]), generator=g, device=self.device)
+                self.kv[li].index_copy_(0, idx, vals.to(torch.bfloat16))
+        self._sync_rows()
+        self.token_buf.copy_(torch.randint(0, self.spec.vocab, (self.rows,), generator=g, device=self.device))
+        self.plan()
+
+    # --------------------------------------------------------- decode step
+    def _linear(self, x, w, *, prologue=0, norm_weight=None, **kw):
+        """Projection of all rows: fused GEMV (prologue inside) for <= 8 rows,
+        tcgen05 GEMM (after an explicit norm / SiLU-mul launch) above."""
+
+        s = self.spec
+        if self.rows <= GEMV_MAX_ROWS:
+            return K.linear_lora_fused(x, w, prologue=prologue, norm_weight=norm_weight, norm_eps=s.rms_eps,
+                                       weights_static=True, status=self.status, **kw)
+        if prologue == PL_PROLOGUE_RMSNORM:
+            x = K.rmsnorm(x, norm_weight, s.rms_eps, out=self.xn)
+        elif prologue == PL_PROLOGUE_SILU_MUL:
+            x = K.silu_mul(x, out=self.act)
+        return K.linear_lora_gemm(x, w, workspace=self.gemm_ws, weights_static=True, status=self.status, **kw)
+
+    def _decode_body(self) -> None:
+        s = self.spec
+        st = self.status
+        K.page_table_advance(self.row_num_pages, self.last_page_len, self.row_pages, self.new_page_ids,
+                             self.page_size, self.indptr, self.indices, self.slot_page, self.slot_off,
+                             self.positions, st)
+        K.embed(self.token_buf, self.embed, self.x, st)
+        attn2d = self.attn.view(self.rows, s.q_dim)
+        lora = self.lora_rank > 0
+        for li, L in enumerate(self.layers):
+            if lora:
+                # The shrink reads the normalised rows, so the norm is its own
+                # launch and the projection takes them as they are.
+                K.rmsnorm(self.x, L["input_norm"], s.rms_eps, out=self.xn)
+                K.lora_shrink_seg(self.xn, L["a_qkv"], self.seg_indptr, self.seg_adapter, out=self.down_qkv)
+                self._linear(self.xn, L["w_qkv"], out=self.qkv)
+            else:
+                self._linear(self.x, L["w_qkv"], prologue=PL_PROLOGUE_RMSNORM, norm_weight=L["input_norm"],
+                             out=self.qkv)
+            K.qkv_rope_append(self.qkv, num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads,
+                              head_dim=s.head_dim, positions=self.positions, rope_theta=s.rope_theta,
+                              kv_cache=self.kv[li], page_id=self.slot_page, page_offset=self.slot_off, q_out=self.q,
+                              lora_down=self.down_qkv if lora else None, lora_b=L["b_qkv"] if lora else None,
+                              lora_scale=self.qkv_lora_scale, tok_adapter=self.tok_adapter if lora else None,
+                              q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps, status=st)
+            K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
+                           num_splits=self.num_splits, workspace=self.workspace, status=st, out=self.attn)
+            if lora:
+                K.lora_shrink_seg(attn2d, L["a_o"], self.seg_indptr, self.seg_adapter, out=self.down_o)
+            self._linear(attn2d, L["w_o"], lora_down=self.down_o if lora else None, lora_b=L["b_o"] if lora else None,
+                         lora_scale=self.lora_scale, tok_adapter=self.tok_adapter if lora else None,
+                         residual=self.x, out=self.x)
+            self._linear(self.x, L["w_gate_up"], prologue=PL_PROLOGUE_RMSNORM, norm_weight=L["post_norm"],
+                         out=self.gate_up)
+            self._linear(self.gate_up, L["w_down"], prologue=PL_PROLOGUE_SILU_MUL, residual=self.x, out=self.x)
+        self._linear(self.x, self.lm_head, prologue=PL_PROLOGUE_RMSNORM, norm_weight=self.final_norm,
+                     out=self.logits)
+        K.argmax(self.logits, self.token_buf, self.argmax_ws)
+
+    def launches_per_step(self) -> int:
+        """Kernel launches of one step (all of them this library's kernels)."""
+
+        gemm = self.rows > GEMV_MAX_ROWS
+        if self.lora_rank > 0:
+            # norm, shrink, qkv, rope, attn, o shrink, o, gate_up, down (+ norm, SiLU-mul launches for the GEMM)
+            per_layer = 9 + (2 if gemm else 0)
+        else:
+            # qkv, rope, attn, o, gate_up, down (+ two norms and the SiLU-mul for the GEMM)
+            per_layer = 6 + (3 if gemm else 0)
+        head = 2 if gemm else 1  # (norm +) lm_head
+        return 2 + per_layer * self.spec.num_layers + head + 1
+
+    def capture(self) -> None:
+        """Capture one decode step into a CUDA graph (after an eager warm-up
+        on a copy of the row state)."""
+
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        saved = [t.clone() for t in (self.row_num_pages, self.last_page_len, self.row_pages, self.token_buf)]
+        with torch.cuda.stream(stream):
+            # Rows that need a page in the warm-up get a free one, so no live page is written.
+            self.new_page_ids.fill_(self.free_pages[-1] if self.free_pages else 0)
+            self._decode_body()
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        torch.cuda.synchronize(self.device)
+        for dst, src in zip((self.row_num_pages, self.last_page_len, self.row_pages, self.token_buf), saved):
+            dst.copy_(src)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            self._decode_body()
+        torch.cuda.synchronize(self.device)
+        self.graph = g
+
+    def _host_reserve(self) -> list[int]:
+        """Host side of one token's slot reservation per row: a new page id
+        where the row's last page is full (0 elsewhere, unused)."""
+
+        out = []
+        for r in range(self.rows):
+            if not self.host_pages[r] or self.host_last[r] >= self.page_size:
+                page = self._alloc_page()
+                self.host_pages[r].append(page)
+                self.host_last[r] = 1
+                out.append(page)
+            else:
+                self.host_last[r] += 1
+                out.append(0)
+        return out
+
+    def step_device(self) -> None:
+        """One decode step of all rows with inputs on the device (graph replay)."""
+
+        pages = self._host_reserve()
+        self.pinned_pages.copy_(torch.tensor(pages, dtype=torch.int32))
+        self.new_page_ids.copy_(self.pinned_pages, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._decode_body()
+
+    def step_host(self, tokens: list[int]) -> list[int]:
+        """One decode step driven from host memory: H2D of the rows' tokens and
+        page ids (pinned), replay, D2H of the next ids."""
+
+        pages = self._host_reserve()
+        self.pinned_pages.copy_(torch.tensor(pages, dtype=torch.int32))
+        self.pinned_tokens.copy_(torch.tensor(tokens, dtype=torch.int64))
+        self.new_page_ids.copy_(self.pinned_pages, non_blocking=True)
+        self.token_buf.copy_(self.pinned_tokens, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._decode_body()
+        self.pinned_tokens.copy_(self.token_buf, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return self.pinned_tokens.tolist()
+
+    def _check_status(self) -> None:
+        code = int(self.status.item())
+        if code != 0:
+            from pagelora_b200._capi import status_string
+
+            raise RuntimeError(f"device status {code}: {status_string(code)}")
