@@ -162,6 +162,25 @@ int32_t pl_paged_decode(const void *q, int64_t q_stride_b, int64_t q_stride_h,
                         int32_t *status_dev, void *stream);
 
 /*
+ * pl_paged_decode with the attention output in fp32 (`out` float, 16-byte
+ * aligned): the partial state of a split-KV shard, merged across GPUs with
+ * its LSE (pl_merge_states_strided).  No reference counterpart: the
+ * cross-GPU split-KV decode of long contexts is new on this path.
+ */
+int32_t pl_paged_decode_f32(const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                            const void *kv_cache, int64_t num_pages,
+                            const int32_t *indptr, const int32_t *indices,
+                            const int32_t *last_page_len,
+                            int32_t batch, int32_t num_qo_heads,
+                            int32_t num_kv_heads, int32_t head_dim,
+                            int32_t page_size, float sm_scale,
+                            int32_t num_splits,
+                            float *out, int64_t o_stride_b, int64_t o_stride_h,
+                            float *out_lse,
+                            void *workspace, int64_t workspace_bytes,
+                            int32_t *status_dev, void *stream);
+
+/*
  * pl_paged_decode without a caller workspace.  No counterpart in the
  * reference: FlashInfer's wrapper takes a caller-allocated workspace.
  * The split partials and arrival counters live in a fixed device array of
@@ -204,6 +223,19 @@ int32_t pl_merge_states(const float *v_partial, const float *lse_partial,
                         int32_t num_rows, int32_t num_states,
                         int32_t head_dim, void *out, int64_t out_stride,
                         float *out_lse, void *stream);
+
+/*
+ * pl_merge_states over partials with explicit element strides: state s of
+ * row r is v_partial[r * v_row_stride + s * v_state_stride + d] and
+ * lse_partial[r * lse_row_stride + s * lse_state_stride], e.g. the
+ * [gpus][rows][D] result of an all-gather.  No reference counterpart.
+ */
+int32_t pl_merge_states_strided(const float *v_partial, int64_t v_row_stride,
+                                int64_t v_state_stride, const float *lse_partial,
+                                int64_t lse_row_stride, int64_t lse_state_stride,
+                                int32_t num_rows, int32_t num_states,
+                                int32_t head_dim, void *out, int64_t out_stride,
+                                float *out_lse, void *stream);
 
 /* --------------------------------------------------------------- LoRA path */
 

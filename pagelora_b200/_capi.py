@@ -73,7 +73,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I32,
         [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _P, _P],
     ),
+    "pl_paged_decode_f32": (
+        _I32,
+        [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _P,
+         _I64, _P, _P],
+    ),
     "pl_merge_states": (_I32, [_P, _P, _I32, _I32, _I32, _P, _I64, _P, _P]),
+    "pl_merge_states_strided": (_I32, [_P, _I64, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _I64, _P, _P]),
     "pl_lora_shrink_seg": (_I32, [_P, _I64, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _I64, _P]),
     "pl_linear_lora_expand_fused": (
         _I32,

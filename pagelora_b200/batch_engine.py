@@ -31,6 +31,7 @@ import torch.nn.functional as F
 from pagelora_b200 import kernels as K
 from pagelora_b200._capi import PL_PROLOGUE_RMSNORM, PL_PROLOGUE_SILU_MUL
 from pagelora_b200.engine import _rmsnorm_fused, _rmsnorm_hf, _rope
+from pagelora_b200.split_kv import shard_row
 from pagelora_b200.synthetic import LoRASpec, ModelSpec
 
 GEMV_MAX_ROWS = 8
@@ -46,8 +47,16 @@ class BatchDecodeEngine:
 
     def __init__(self, spec: ModelSpec, weights: dict[str, torch.Tensor], *, adapters: list[dict] | None,
                  lora_spec: LoRASpec | None, row_adapter: list[int], page_size: int = 16, max_context: int = 4096,
-                 num_pages: int | None = None, device: torch.device | str = "cuda") -> None:
+                 num_pages: int | None = None, device: torch.device | str = "cuda",
+                 kv_shard: tuple[int, int] = (0, 1), group=None) -> None:
         self.spec = spec
+        # Split-KV: shard `rank` of `world` holds a contiguous page range of
+        # every row's context; the last shard owns the growing tail.
+        self.shard, self.world = int(kv_shard[0]), int(kv_shard[1])
+        if not 0 <= self.shard < self.world:
+            raise ValueError("kv_shard must be (rank, world) with 0 <= rank < world")
+        self.group = group
+        self.owner = self.shard == self.world - 1
         self.device = torch.device(device)
         self.page_size = page_size
         self.rows = len(row_adapter)
@@ -157,8 +166,15 @@ class BatchDecodeEngine:
         self.gemm_ws = torch.zeros(ws, device=dev, dtype=torch.uint8)
         self.num_splits = 1
         self.workspace = torch.zeros(1 << 20, device=dev, dtype=torch.uint8)
+        if self.world > 1:
+            # One packed [O fp32 | LSE] partial per shard, all-gathered each layer.
+            rows_h = B * spec.num_qo_heads
+            self.part = torch.zeros(rows_h * (D + 1), device=dev, dtype=torch.float32)
+            self.gathered = torch.zeros(self.world, rows_h * (D + 1), device=dev, dtype=torch.float32)
+            self.dummy_page = self._alloc_page()  # append target of the shards that do not own the tail
         self.host_pages: list[list[int]] = [[] for _ in range(B)]
         self.host_last = [0] * B
+        self.context_len = [0] * B
         self.graph: torch.cuda.CUDAGraph | None = None
         self.pinned_pages = torch.zeros(B, dtype=torch.int32, pin_memory=True)
         self.pinned_tokens = torch.zeros(B, dtype=torch.int64, pin_memory=True)
@@ -197,6 +213,27 @@ class BatchDecodeEngine:
                 self.row_pages[r, : len(self.host_pages[r])] = torch.tensor(self.host_pages[r], dtype=torch.int32)
         self.row_num_pages.copy_(torch.tensor([len(p) for p in self.host_pages], dtype=torch.int32))
         self.last_page_len.copy_(torch.tensor(self.host_last, dtype=torch.int32))
+        if self.world > 1:
+            # Global position of each row's next token (every shard applies RoPE to it).
+            self.positions.copy_(torch.tensor([n - 1 for n in self.context_len], dtype=torch.int32))
+            if not self.owner:
+                # Static page table of this shard; the new token's K/V go to the dummy page.
+                indptr = [0]
+                for pgs in self.host_pages:
+                    indptr.append(indptr[-1] + len(pgs))
+                self.indptr.copy_(torch.tensor(indptr, dtype=torch.int32))
+                flat = [p for pgs in self.host_pages for p in pgs]
+                if flat:
+                    self.indices[: len(flat)] = torch.tensor(flat, dtype=torch.int32)
+                self.slot_page.fill_(self.dummy_page)
+                self.slot_off.zero_()
+
+    def _own_pages(self, pages: list[int], n_tokens: int) -> tuple[list[int], list[int], int]:
+        """Split a row's pages between shards: (kept, released, tokens in the
+        kept last page)."""
+
+        p0, p1, last = shard_row(n_tokens, self.page_size, self.shard, self.world)
+        return pages[p0:p1], pages[:p0] + pages[p1:], last
 
     @torch.no_grad()
     def prefill(self, prompts: list[list[int]]) -> list[int]:
@@ -253,6 +290,12 @@ class BatchDecodeEngine:
             logits = F.linear(_rmsnorm_fused(x[-1:], self.final_norm, s.rms_eps), self.lm_head)
             self.prefill_logits.append(logits[0])
             firsts.append(int(torch.argmax(logits[0]).item()))
+        self.context_len = [len(p) for p in prompts]
+        if self.world > 1:
+            for r, n in enumerate(self.context_len):
+                kept, released, last = self._own_pages(self.host_pages[r], n)
+                self.host_pages[r], self.host_last[r] = kept, last
+                self.free_pages.extend(released)
         self._sync_rows()
         self.token_buf.copy_(torch.tensor(firsts, dtype=torch.int64))
         self.plan()
@@ -268,9 +311,13 @@ class BatchDecodeEngine:
         if len(lengths) != self.rows:
             raise ValueError("one length per row")
         g = torch.Generator(device=self.device).manual_seed(seed)
+        self.context_len = list(lengths)
         for r, n in enumerate(lengths):
-            pages = [self._alloc_page() for _ in range(-(-n // self.page_size))]
-            self.host_pages[r], self.host_last[r] = list(pages), n - (len(pages) - 1) * self.page_size
+            p0, p1, last = shard_row(n, self.page_size, self.shard, self.world)
+            pages = [self._alloc_page() for _ in range(p1 - p0)]
+            self.host_pages[r], self.host_last[r] = list(pages), last
+            if not pages:
+                continue
             idx = torch.tensor(pages, device=self.device, dtype=torch.int64)
             for li in range(self.spec.num_layers):
                 vals = torch.randn((len(pages),) + tuple(self.kv.shape[2:]), generator=g, device=self.device)
@@ -297,9 +344,16 @@ class BatchDecodeEngine:
     def _decode_body(self) -> None:
         s = self.spec
         st = self.status
-        K.page_table_advance(self.row_num_pages, self.last_page_len, self.row_pages, self.new_page_ids,
-                             self.page_size, self.indptr, self.indices, self.slot_page, self.slot_off,
-                             self.positions, st)
+        if self.world == 1:
+            K.page_table_advance(self.row_num_pages, self.last_page_len, self.row_pages, self.new_page_ids,
+                                 self.page_size, self.indptr, self.indices, self.slot_page, self.slot_off,
+                                 self.positions, st)
+        else:
+            self.positions.add_(1)
+            if self.owner:
+                K.page_table_advance(self.row_num_pages, self.last_page_len, self.row_pages, self.new_page_ids,
+                                     self.page_size, self.indptr, self.indices, self.slot_page, self.slot_off,
+                                     None, st)
         K.embed(self.token_buf, self.embed, self.x, st)
         attn2d = self.attn.view(self.rows, s.q_dim)
         lora = self.lora_rank > 0
@@ -319,8 +373,11 @@ class BatchDecodeEngine:
                               lora_down=self.down_qkv if lora else None, lora_b=L["b_qkv"] if lora else None,
                               lora_scale=self.qkv_lora_scale, tok_adapter=self.tok_adapter if lora else None,
                               q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps, status=st)
-            K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
-                           num_splits=self.num_splits, workspace=self.workspace, status=st, out=self.attn)
+            if self.world == 1:
+                K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
+                               num_splits=self.num_splits, workspace=self.workspace, status=st, out=self.attn)
+            else:
+                self._split_kv_attention(li)
             if lora:
                 K.lora_shrink_seg(attn2d, L["a_o"], self.seg_indptr, self.seg_adapter, out=self.down_o)
             self._linear(attn2d, L["w_o"], lora_down=self.down_o if lora else None, lora_b=L["b_o"] if lora else None,
@@ -332,6 +389,26 @@ class BatchDecodeEngine:
         self._linear(self.x, self.lm_head, prologue=PL_PROLOGUE_RMSNORM, norm_weight=self.final_norm,
                      out=self.logits)
         K.argmax(self.logits, self.token_buf, self.argmax_ws)
+
+    def _split_kv_attention(self, li: int) -> None:
+        """This shard's partial (O fp32, LSE) over its pages, one all-gather of
+        the packed partials over NCCL, then the LSE merge (same result on
+        every shard)."""
+
+        import torch.distributed as dist
+
+        s = self.spec
+        rows_h = self.rows * s.num_qo_heads
+        nd = rows_h * s.head_dim
+        o_part = self.part[:nd].view(self.rows, s.num_qo_heads, s.head_dim)
+        lse_part = self.part[nd:].view(self.rows, s.num_qo_heads)
+        K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
+                       num_splits=self.num_splits, workspace=self.workspace, status=self.status, out=o_part,
+                       out_lse=lse_part)
+        dist.all_gather_into_tensor(self.gathered, self.part, group=self.group)
+        v = self.gathered[:, :nd].view(self.world, rows_h, s.head_dim).permute(1, 0, 2)
+        lse = self.gathered[:, nd:].permute(1, 0)
+        K.merge_states_strided(v, lse, self.attn.view(rows_h, s.head_dim))
 
     def launches_per_step(self) -> int:
         """Kernel launches of one step (all of them this library's kernels)."""
@@ -352,14 +429,15 @@ class BatchDecodeEngine:
 
         stream = torch.cuda.Stream(device=self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
-        saved = [t.clone() for t in (self.row_num_pages, self.last_page_len, self.row_pages, self.token_buf)]
+        state = (self.row_num_pages, self.last_page_len, self.row_pages, self.token_buf, self.positions)
+        saved = [t.clone() for t in state]
         with torch.cuda.stream(stream):
             # Rows that need a page in the warm-up get a free one, so no live page is written.
             self.new_page_ids.fill_(self.free_pages[-1] if self.free_pages else 0)
             self._decode_body()
         torch.cuda.current_stream(self.device).wait_stream(stream)
         torch.cuda.synchronize(self.device)
-        for dst, src in zip((self.row_num_pages, self.last_page_len, self.row_pages, self.token_buf), saved):
+        for dst, src in zip(state, saved):
             dst.copy_(src)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
@@ -372,6 +450,8 @@ class BatchDecodeEngine:
         where the row's last page is full (0 elsewhere, unused)."""
 
         out = []
+        if self.world > 1 and not self.owner:
+            return [0] * self.rows  # the tail lives on the last shard
         for r in range(self.rows):
             if not self.host_pages[r] or self.host_last[r] >= self.page_size:
                 page = self._alloc_page()

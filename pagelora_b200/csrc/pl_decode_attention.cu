@@ -39,6 +39,7 @@ struct DecodeArgs {
   float scale_log2;  // sm_scale * log2(e)
   int32_t num_splits;
   bf16* out;
+  float* out_f32;       // when set, O is written here in fp32 instead of `out`
   int64_t o_stride_b, o_stride_h;
   float* out_lse;       // natural log, nullable
   int32_t* counters;    // [batch * Hkv], zero between calls
@@ -351,7 +352,11 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
       const float val = (L > 0.f) ? acc / L : 0.f;
       const float lse2 = (L > 0.f) ? M + log2f(L) : -INFINITY;
       if (single) {
-        args.out[b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d] = f2bf(val);
+        const int64_t oi = b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
+        if (args.out_f32 != nullptr)
+          args.out_f32[oi] = val;
+        else
+          args.out[oi] = f2bf(val);
         if (args.out_lse != nullptr && d == 0) args.out_lse[(int64_t)b * args.num_qo_heads + hq0 + r] = lse2 * kLn2;
       } else {
         const int64_t rowid = (int64_t)b * args.num_qo_heads + hq0 + r;
@@ -408,9 +413,13 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
             acc.w += wt * o.w;
           }
           const float il = inv_l[r];
-          bf16* dst = args.out + b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
-          reinterpret_cast<uint2*>(dst)[0] = make_uint2(pack_bf16x2(acc.x * il, acc.y * il),
-                                                        pack_bf16x2(acc.z * il, acc.w * il));
+          const int64_t oi = b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
+          if (args.out_f32 != nullptr) {
+            *reinterpret_cast<float4*>(args.out_f32 + oi) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
+          } else {
+            reinterpret_cast<uint2*>(args.out + oi)[0] = make_uint2(pack_bf16x2(acc.x * il, acc.y * il),
+                                                                     pack_bf16x2(acc.z * il, acc.w * il));
+          }
         }
         if (ctid == 0) args.counters[b * args.num_kv_heads + kvh] = 0;
         if (ctid == 0 && kvh == 0) PL_TRACE_POINT(6);
@@ -436,6 +445,32 @@ __global__ void merge_states_kernel(const float* __restrict__ v, const float* __
     float acc = 0.f;
     if (M != -INFINITY)
       for (int s = 0; s < num_states; ++s) acc += expf(l[s] - M) * v[((int64_t)row * num_states + s) * head_dim + d];
+    out[(int64_t)row * out_stride + d] = f2bf(L > 0.f ? acc / L : 0.f);
+  }
+  if (out_lse != nullptr && threadIdx.x == 0) out_lse[row] = L > 0.f ? M + logf(L) : -INFINITY;
+}
+
+// Same merge over partial states laid out with arbitrary row / state strides
+// (e.g. [states][rows][D] as gathered from several GPUs).
+__global__ void merge_states_strided_kernel(const float* __restrict__ v, int64_t v_row_stride, int64_t v_state_stride,
+                                            const float* __restrict__ lse, int64_t lse_row_stride,
+                                            int64_t lse_state_stride, int num_rows, int num_states, int head_dim,
+                                            bf16* __restrict__ out, int64_t out_stride, float* __restrict__ out_lse) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int row = blockIdx.x;
+  if (row >= num_rows) return;
+  const float* l = lse + (int64_t)row * lse_row_stride;
+  float M = -INFINITY;
+  for (int s = 0; s < num_states; ++s) M = fmaxf(M, l[s * lse_state_stride]);
+  float L = 0.f;
+  if (M != -INFINITY)
+    for (int s = 0; s < num_states; ++s) L += expf(l[s * lse_state_stride] - M);
+  const float* vr = v + (int64_t)row * v_row_stride;
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float acc = 0.f;
+    if (M != -INFINITY)
+      for (int s = 0; s < num_states; ++s) acc += expf(l[s * lse_state_stride] - M) * vr[s * v_state_stride + d];
     out[(int64_t)row * out_stride + d] = f2bf(L > 0.f ? acc / L : 0.f);
   }
   if (out_lse != nullptr && threadIdx.x == 0) out_lse[row] = L > 0.f ? M + logf(L) : -INFINITY;
@@ -549,13 +584,13 @@ extern "C" int32_t pl_decode_plan(int32_t batch, int32_t num_qo_heads, int32_t n
   return PL_OK;
 }
 
-extern "C" int32_t pl_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* kv_cache,
-                                   int64_t num_pages, const int32_t* indptr, const int32_t* indices,
-                                   const int32_t* last_page_len, int32_t batch, int32_t num_qo_heads,
-                                   int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float sm_scale,
-                                   int32_t num_splits, void* out, int64_t o_stride_b, int64_t o_stride_h,
-                                   float* out_lse, void* workspace, int64_t workspace_bytes, int32_t* status_dev,
-                                   void* stream) {
+namespace {
+int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* kv_cache,
+                          int64_t num_pages, const int32_t* indptr, const int32_t* indices,
+                          const int32_t* last_page_len, int32_t batch, int32_t num_qo_heads, int32_t num_kv_heads,
+                          int32_t head_dim, int32_t page_size, float sm_scale, int32_t num_splits, void* out,
+                          bool out_is_f32, int64_t o_stride_b, int64_t o_stride_h, float* out_lse, void* workspace,
+                          int64_t workspace_bytes, int32_t* status_dev, void* stream) {
   if (batch == 0) return PL_OK;
   if (q == nullptr || kv_cache == nullptr || indptr == nullptr || indices == nullptr || last_page_len == nullptr ||
       out == nullptr || batch < 0 || num_pages <= 0 || num_kv_heads <= 0 || num_qo_heads % num_kv_heads != 0 ||
@@ -565,8 +600,9 @@ extern "C" int32_t pl_paged_decode(const void* q, int64_t q_stride_b, int64_t q_
   if (group > 16 || (head_dim != 64 && head_dim != 128) || (page_size != 16 && page_size != 32))
     return PL_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(kv_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(q) & 15) != 0 ||
-      (q_stride_b % 8) != 0 || (q_stride_h % 8) != 0 || (reinterpret_cast<uintptr_t>(out) & 7) != 0 ||
-      (o_stride_b % 4) != 0 || (o_stride_h % 4) != 0)
+      (q_stride_b % 8) != 0 || (q_stride_h % 8) != 0 ||
+      (reinterpret_cast<uintptr_t>(out) & (out_is_f32 ? 15 : 7)) != 0 || (o_stride_b % 4) != 0 ||
+      (o_stride_h % 4) != 0)
     return PL_ERR_INVALID_ARGUMENT;
   const int64_t need = decode_workspace_bytes(batch, num_qo_heads, num_kv_heads, head_dim, num_splits);
   if (num_splits > 1 && (workspace == nullptr || workspace_bytes < need)) return PL_ERR_WORKSPACE_TOO_SMALL;
@@ -588,7 +624,8 @@ extern "C" int32_t pl_paged_decode(const void* q, int64_t q_stride_b, int64_t q_
   a.group = group;
   a.scale_log2 = sm_scale * pl::kLog2e;
   a.num_splits = num_splits;
-  a.out = static_cast<pl::bf16*>(out);
+  a.out = out_is_f32 ? nullptr : static_cast<pl::bf16*>(out);
+  a.out_f32 = out_is_f32 ? static_cast<float*>(out) : nullptr;
   a.o_stride_b = o_stride_b;
   a.o_stride_h = o_stride_h;
   a.out_lse = out_lse;
@@ -608,6 +645,46 @@ extern "C" int32_t pl_paged_decode(const void* q, int64_t q_stride_b, int64_t q_
   if (head_dim == 128 && page_size == 32) return launch_decode<128, 32>(map, a, batch, num_kv_heads, num_splits, stream);
   if (head_dim == 64 && page_size == 16) return launch_decode<64, 16>(map, a, batch, num_kv_heads, num_splits, stream);
   return launch_decode<64, 32>(map, a, batch, num_kv_heads, num_splits, stream);
+}
+}  // namespace
+
+extern "C" int32_t pl_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* kv_cache,
+                                   int64_t num_pages, const int32_t* indptr, const int32_t* indices,
+                                   const int32_t* last_page_len, int32_t batch, int32_t num_qo_heads,
+                                   int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float sm_scale,
+                                   int32_t num_splits, void* out, int64_t o_stride_b, int64_t o_stride_h,
+                                   float* out_lse, void* workspace, int64_t workspace_bytes, int32_t* status_dev,
+                                   void* stream) {
+  return paged_decode_impl(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
+                           num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, false,
+                           o_stride_b, o_stride_h, out_lse, workspace, workspace_bytes, status_dev, stream);
+}
+
+extern "C" int32_t pl_paged_decode_f32(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* kv_cache,
+                                       int64_t num_pages, const int32_t* indptr, const int32_t* indices,
+                                       const int32_t* last_page_len, int32_t batch, int32_t num_qo_heads,
+                                       int32_t num_kv_heads, int32_t head_dim, int32_t page_size, float sm_scale,
+                                       int32_t num_splits, float* out, int64_t o_stride_b, int64_t o_stride_h,
+                                       float* out_lse, void* workspace, int64_t workspace_bytes, int32_t* status_dev,
+                                       void* stream) {
+  return paged_decode_impl(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
+                           num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, true,
+                           o_stride_b, o_stride_h, out_lse, workspace, workspace_bytes, status_dev, stream);
+}
+
+extern "C" int32_t pl_merge_states_strided(const float* v_partial, int64_t v_row_stride, int64_t v_state_stride,
+                                           const float* lse_partial, int64_t lse_row_stride,
+                                           int64_t lse_state_stride, int32_t num_rows, int32_t num_states,
+                                           int32_t head_dim, void* out, int64_t out_stride, float* out_lse,
+                                           void* stream) {
+  if (num_rows == 0) return PL_OK;
+  if (v_partial == nullptr || lse_partial == nullptr || out == nullptr || num_rows < 0 || num_states < 1 ||
+      head_dim <= 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  return pl_host::launch_pdl(pl::merge_states_strided_kernel, dim3(num_rows), dim3(128), 0, stream, v_partial,
+                             v_row_stride, v_state_stride, lse_partial, lse_row_stride, lse_state_stride,
+                             (int)num_rows, (int)num_states, (int)head_dim, static_cast<pl::bf16*>(out), out_stride,
+                             out_lse);
 }
 
 extern "C" int32_t pl_merge_states(const float* v_partial, const float* lse_partial, int32_t num_rows,

@@ -109,7 +109,8 @@ def paged_decode(
     out: torch.Tensor | None = None,
     out_lse: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Paged decode attention: q [B, Hq, D] bf16, kv_cache [P, 2, PS, Hkv, D] bf16."""
+    """Paged decode attention: q [B, Hq, D] bf16, kv_cache [P, 2, PS, Hkv, D] bf16;
+    ``out`` bf16, or fp32 for a split-KV shard's partial state."""
 
     _need_cuda(q, kv_cache, indptr, indices, last_page_len)
     _need(q, torch.bfloat16, "q")
@@ -128,7 +129,8 @@ def paged_decode(
         out = torch.empty_like(q)
     scale = (1.0 / math.sqrt(d)) if sm_scale is None else float(sm_scale)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    call("pl_paged_decode", ptr(q), q.stride(0), q.stride(1), ptr(kv_cache), int(num_pages), ptr(indptr),
+    fn = "pl_paged_decode_f32" if out.dtype == torch.float32 else "pl_paged_decode"
+    call(fn, ptr(q), q.stride(0), q.stride(1), ptr(kv_cache), int(num_pages), ptr(indptr),
          ptr(indices), ptr(last_page_len), int(batch), int(hq), int(hkv), int(d), int(page_size), scale,
          int(num_splits), ptr(out), out.stride(0), out.stride(1), ptr(out_lse), ptr(workspace), int(ws_bytes),
          ptr(status), stream_handle())
@@ -148,6 +150,24 @@ def merge_states(v_partial: torch.Tensor, lse_partial: torch.Tensor, out: torch.
     if out is None:
         out = torch.empty(rows, d, dtype=torch.bfloat16, device=v_partial.device)
     call("pl_merge_states", ptr(v_partial), ptr(lse_partial), int(rows), int(states), int(d), ptr(out),
+         _row_stride(out, "out"), ptr(out_lse), stream_handle())
+    return out
+
+
+def merge_states_strided(v_partial: torch.Tensor, lse_partial: torch.Tensor, out: torch.Tensor,
+                         out_lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partial states given as views ``v_partial`` [rows, S, D] and
+    ``lse_partial`` [rows, S] with any strides (D unit-stride), e.g. a
+    permuted [S, rows, D] all-gather result."""
+
+    _need_cuda(v_partial, lse_partial, out)
+    _need(v_partial, torch.float32, "v_partial")
+    _need(lse_partial, torch.float32, "lse_partial")
+    rows, states, d = v_partial.shape
+    if v_partial.stride(2) != 1:
+        raise ValueError("partial states need unit stride along head_dim")
+    call("pl_merge_states_strided", ptr(v_partial), v_partial.stride(0), v_partial.stride(1), ptr(lse_partial),
+         lse_partial.stride(0), lse_partial.stride(1), int(rows), int(states), int(d), ptr(out),
          _row_stride(out, "out"), ptr(out_lse), stream_handle())
     return out
 

@@ -195,6 +195,54 @@ def test_paged_decode_reports_out_of_range_page(K):
     assert int(status.item()) == PL_ERR_PAGE_OUT_OF_RANGE
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_split_kv_shards_merge_to_full_decode(K, world):
+    """Split-KV across shards on one GPU: each shard's fp32 partial (O, LSE)
+    over its page range (pl_paged_decode_f32), stacked like an all-gather
+    [shard][rows][D] and merged with pl_merge_states_strided, equals the
+    full decode."""
+
+    from pagelora_b200.split_kv import shard_row
+
+    rng = np.random.default_rng(60 + world)
+    ps, hq, hkv, d = 16, 32, 8, 128
+    lengths = [1, 16, 17, 300, 2112, 45]
+    pages_per_row = [-(-n // ps) for n in lengths]
+    pool = sum(pages_per_row) + 5
+    cache = bf16(rng.normal(size=(pool, 2, ps, hkv, d)))
+    perm = rng.permutation(pool)
+    indptr = np.cumsum([0] + pages_per_row)
+    indices = perm[: indptr[-1]]
+    last = [n - (p - 1) * ps for n, p in zip(lengths, pages_per_row)]
+    q = bf16(rng.normal(size=(len(lengths), hq, d)) * 1.5)
+    qt, ct = _t(q), _t(cache)
+    rows = len(lengths)
+    gathered = torch.zeros(world, rows * hq * (d + 1), device="cuda")
+    ws = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+    for r in range(world):
+        sh_indptr, sh_indices, sh_last = [0], [], []
+        for b, n in enumerate(lengths):
+            p0, p1, kept_last = shard_row(n, ps, r, world)
+            sh_indices += indices[indptr[b] + p0: indptr[b] + p1].tolist()
+            sh_indptr.append(len(sh_indices))
+            sh_last.append(kept_last)
+        nd = rows * hq * d
+        o_part = gathered[r, :nd].view(rows, hq, d)
+        lse_part = gathered[r, nd:].view(rows, hq)
+        K.paged_decode(qt, ct, _i32(sh_indptr), _i32(sh_indices or [0]), _i32(sh_last), num_splits=3,
+                       workspace=ws, out=o_part, out_lse=lse_part)
+    nd = rows * hq * d
+    v = gathered[:, :nd].view(world, rows * hq, d).permute(1, 0, 2)
+    lse = gathered[:, nd:].permute(1, 0)
+    out = torch.empty(rows * hq, d, dtype=torch.bfloat16, device="cuda")
+    out_lse = torch.empty(rows * hq, dtype=torch.float32, device="cuda")
+    K.merge_states_strided(v, lse, out, out_lse)
+    torch.cuda.synchronize()
+    ref, ref_lse = o_decode(q, cache, indptr.tolist(), indices.tolist(), last)
+    assert np.max(np.abs(_np(out).reshape(rows, hq, d) - ref)) <= ATOL
+    np.testing.assert_allclose(_np(out_lse).reshape(rows, hq), ref_lse, rtol=1e-3, atol=1e-3)
+
+
 def test_merge_states_vs_oracle(K):
     rng = np.random.default_rng(2)
     v = rng.normal(size=(37, 6, 128)).astype(np.float32)
