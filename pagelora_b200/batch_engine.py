@@ -35,6 +35,15 @@ from pagelora_b200.split_kv import shard_row
 from pagelora_b200.synthetic import LoRASpec, ModelSpec
 
 GEMV_MAX_ROWS = 8
+GEMV_MAX_STAGED_BYTES = 96 * 1024  # activations the decode GEMV keeps in shared memory
+
+
+def uses_gemv(rows: int, k_in: int) -> bool:
+    """Whether a projection of `rows` tokens and K = k_in runs on the fused
+    decode GEMV (all rows' activations staged in shared memory) rather than
+    the tcgen05 GEMM."""
+
+    return rows <= GEMV_MAX_ROWS and rows * (2 * k_in + 16) <= GEMV_MAX_STAGED_BYTES
 
 
 class BatchDecodeEngine:
@@ -159,9 +168,9 @@ class BatchDecodeEngine:
         self.logits = torch.zeros(B, spec.vocab, device=dev, dtype=bf)
         self.argmax_ws = torch.zeros(K.argmax_workspace_bytes(B), device=dev, dtype=torch.uint8)
         ws = 256
-        if B > GEMV_MAX_ROWS:
-            for n, k in ((spec.qkv_dim, H), (H, spec.q_dim), (2 * spec.intermediate, H), (H, spec.intermediate),
-                         (spec.vocab, H)):
+        for n, k in ((spec.qkv_dim, H), (H, spec.q_dim), (2 * spec.intermediate, H), (H, spec.intermediate),
+                     (spec.vocab, H)):
+            if not uses_gemv(B, k):
                 ws = max(ws, int(K.gemm_plan(B, k, n).workspace_bytes))
         self.gemm_ws = torch.zeros(ws, device=dev, dtype=torch.uint8)
         self.num_splits = 1
@@ -328,11 +337,12 @@ class BatchDecodeEngine:
 
     # --------------------------------------------------------- decode step
     def _linear(self, x, w, *, prologue=0, norm_weight=None, **kw):
-        """Projection of all rows: fused GEMV (prologue inside) for <= 8 rows,
-        tcgen05 GEMM (after an explicit norm / SiLU-mul launch) above."""
+        """Projection of all rows: fused GEMV (prologue inside) when the rows'
+        activations fit in shared memory (uses_gemv), else tcgen05 GEMM after
+        an explicit norm / SiLU-mul launch."""
 
         s = self.spec
-        if self.rows <= GEMV_MAX_ROWS:
+        if uses_gemv(self.rows, w.shape[1]):
             return K.linear_lora_fused(x, w, prologue=prologue, norm_weight=norm_weight, norm_eps=s.rms_eps,
                                        weights_static=True, status=self.status, **kw)
         if prologue == PL_PROLOGUE_RMSNORM:
@@ -411,17 +421,22 @@ class BatchDecodeEngine:
         K.merge_states_strided(v, lse, self.attn.view(rows_h, s.head_dim))
 
     def launches_per_step(self) -> int:
-        """Kernel launches of one step (all of them this library's kernels)."""
+        """Kernel launches of one step (all of them this library's kernels;
+        the split-KV position increment and all-gather are not counted)."""
 
-        gemm = self.rows > GEMV_MAX_ROWS
-        if self.lora_rank > 0:
-            # norm, shrink, qkv, rope, attn, o shrink, o, gate_up, down (+ norm, SiLU-mul launches for the GEMM)
-            per_layer = 9 + (2 if gemm else 0)
-        else:
-            # qkv, rope, attn, o, gate_up, down (+ two norms and the SiLU-mul for the GEMM)
-            per_layer = 6 + (3 if gemm else 0)
-        head = 2 if gemm else 1  # (norm +) lm_head
-        return 2 + per_layer * self.spec.num_layers + head + 1
+        s, B = self.spec, self.rows
+        lora = self.lora_rank > 0
+        per_layer = 2  # q/k norm + RoPE + append, paged decode
+        if self.world > 1:
+            per_layer += 1  # partial-state merge
+        # q/k/v: with LoRA the norm is a launch of its own (the shrink reads it)
+        per_layer += 3 if lora else (1 if uses_gemv(B, s.hidden) else 2)
+        per_layer += 2 if lora else 1  # (o shrink +) o projection
+        per_layer += 1 if uses_gemv(B, s.hidden) else 2  # (norm +) gate_up
+        per_layer += 1 if uses_gemv(B, s.intermediate) else 2  # (SiLU-mul +) down
+        head = 1 if uses_gemv(B, s.hidden) else 2  # (norm +) lm_head
+        advance = 1 if (self.world == 1 or self.owner) else 0
+        return advance + 1 + per_layer * s.num_layers + head + 1
 
     def capture(self) -> None:
         """Capture one decode step into a CUDA graph (after an eager warm-up
