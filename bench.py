@@ -19,6 +19,14 @@ lm_head at the benchmark's context, scaled to 36 layers).
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 cuda.synchronize, timed with CUDA events on the stream the kernels run on.
 The weights (16 GB) exceed L2 (126 MB), so no flush is needed between steps.
+
+After the headline line's measurements the same run times two secondary
+workloads (``--no-extra`` skips them), reported under "workloads":
+  config3  Llama-2-7B arch, 64 rows, contexts U[512, 4096], 8 adapters,
+           rows sharded over the N ranks (strong scaling, no collective);
+  config5  Llama-3-8B arch, 8 x 32768-token contexts, split-KV over the N
+           ranks with an NCCL all-gather of the partial (O, LSE) per layer.
+Their contexts hold random K/V (their prefill is not part of a decode step).
 """
 
 from __future__ import annotations
@@ -294,6 +302,99 @@ def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
     return out
 
 
+def _timed_steps(engine, steps: int, warmup: int, device, barrier) -> float:
+    """ms per step of `steps` graph replays after `warmup` (CUDA events on the
+    launching stream; the caller takes the max over ranks)."""
+
+    import torch
+
+    for _ in range(warmup):
+        engine.step_device()
+    barrier()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        engine.step_device()
+    e1.record(stream)
+    barrier()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_config3(ws: int, rank: int, device, barrier, steps: int, warmup: int) -> dict:
+    """Llama-2-7B arch, 64 rows with contexts U[512, 4096]
+    (seed 0), 8 rank-16 adapters on q/k/v/o assigned round-robin, pages from
+    a shuffled pool.  Rows are sharded across ranks (64 / N each, no
+    collective).  The contexts' K/V are random values."""
+
+    import numpy as np
+    import torch
+
+    from pagelora_b200.batch_engine import BatchDecodeEngine
+    from pagelora_b200.synthetic import WORKLOADS, make_lora_weights, make_model_weights
+
+    wl = WORKLOADS["config3"]
+    spec, lspec = wl.model, wl.lora
+    total_rows = 64
+    lengths = np.random.default_rng(0).integers(512, 4097, size=total_rows).tolist()
+    r0, r1 = total_rows * rank // ws, total_rows * (rank + 1) // ws
+    mine = sorted(range(r0, r1), key=lambda i: i % 8)
+    row_adapter = [i % 8 for i in mine]
+    ctx = [lengths[i] for i in mine]
+    w = make_model_weights(spec, seed=0, device=device)
+    adapters = [make_lora_weights(spec, lspec, adapter=a, device=device) for a in range(8)]
+    pages = sum(-(-(n + steps + warmup + 40) // 16) for n in ctx) + 64
+    eng = BatchDecodeEngine(spec, w, adapters=adapters, lora_spec=lspec, row_adapter=row_adapter, page_size=16,
+                            max_context=4096 + steps + warmup + 40, num_pages=pages, device=device)
+    del w, adapters
+    eng.shuffle_free_pages(seed=1 + rank)
+    eng.fill_random_context(ctx, seed=2 + rank)
+    eng.capture()
+    ms = _timed_steps(eng, steps, warmup, device, barrier)
+    eng._check_status()
+    kv = sum(ctx) * spec.num_kv_heads * spec.head_dim * 4 * spec.num_layers
+    out = {"rows_per_gpu": len(ctx), "ms_per_step": ms, "launches_per_step": eng.launches_per_step(),
+           "kv_bytes_per_step": kv, "weight_bytes_per_step": spec.weight_bytes()}
+    eng.graph = None
+    del eng
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_config5(ws: int, rank: int, device, barrier, group, steps: int, warmup: int) -> dict:
+    """Llama-3-8B arch, 8 rows of 32768-token contexts,
+    rank-16 LoRA on q/v; split-KV across the ranks (each holds 1/N of every
+    row's pages; per layer one NCCL all-gather of the partial (O, LSE)).
+    The contexts' K/V are random values."""
+
+    import torch
+
+    from pagelora_b200.batch_engine import BatchDecodeEngine
+    from pagelora_b200.synthetic import WORKLOADS, make_lora_weights, make_model_weights
+
+    wl = WORKLOADS["config5"]
+    spec, lspec = wl.model, wl.lora
+    rows, ctx = 8, 32768
+    w = make_model_weights(spec, seed=0, device=device)
+    lo = make_lora_weights(spec, lspec, device=device)
+    pages = rows * (-(-ctx // 16) // ws + 2) + rows * (-(-(steps + warmup + 40) // 16)) + 64
+    eng = BatchDecodeEngine(spec, w, adapters=[lo], lora_spec=lspec, row_adapter=[0] * rows, page_size=16,
+                            max_context=ctx + steps + warmup + 40, num_pages=pages, device=device,
+                            kv_shard=(rank, ws), group=group)
+    del w, lo
+    eng.fill_random_context([ctx] * rows, seed=3)
+    eng.capture()
+    ms = _timed_steps(eng, steps, warmup, device, barrier)
+    eng._check_status()
+    out = {"rows": rows, "context": ctx, "ms_per_step": ms, "launches_per_step": eng.launches_per_step(),
+           "kv_bytes_per_step": rows * ctx * spec.num_kv_heads * spec.head_dim * 4 * spec.num_layers,
+           "weight_bytes_per_step_per_gpu": spec.weight_bytes()}
+    eng.graph = None
+    del eng
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -380,6 +481,45 @@ def run_ours(args) -> None:
     if ws > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e = float(t[0]), float(t[1])
+    launches = engine.launches_per_step()
+
+    # ---- secondary workloads (BASELINE configs 3 and 5), after freeing config 2
+    extra = {}
+    if not args.no_extra:
+        engine.graph = None
+        del engine
+        torch.cuda.empty_cache()
+        xs, xw = min(args.steps, 16), max(3, args.warmup)
+        c3 = run_config3(ws, rank, device, barrier, xs, xw)
+        c5 = run_config5(ws, rank, device, barrier, dist.group.WORLD if ws > 1 else None, xs, xw)
+        tt = torch.tensor([c3["ms_per_step"], c5["ms_per_step"], float(c3["kv_bytes_per_step"])], device=device,
+                          dtype=torch.float64)
+        if ws > 1:
+            mx = tt[:2].clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            kv3 = tt[2:].clone()
+            dist.all_reduce(kv3)
+            tt = torch.cat([mx, kv3])
+        c3["ms_per_step"], c5["ms_per_step"] = float(tt[0]), float(tt[1])
+        c3_bytes = float(tt[2]) + ws * c3["weight_bytes_per_step"]
+        c5_bytes = c5["kv_bytes_per_step"] + ws * c5["weight_bytes_per_step_per_gpu"]
+        extra["config3"] = {
+            "metric": "decode tok/s, 64 rows (Llama-2-7B arch, 8 adapters r16 q/k/v/o, ctx U[512,4096])",
+            "value": 64 * 1000.0 / c3["ms_per_step"], "unit": "tok/s", "ms_per_step": c3["ms_per_step"],
+            "rows_per_gpu": c3["rows_per_gpu"], "parallelism": f"request-sharded x{ws}", "scaling": "strong",
+            "steps": xs, "warmup": xw, "achieved_gbs_all_gpus": c3_bytes / (c3["ms_per_step"] * 1e-3) / 1e9,
+            "frac_of_peak_per_gpu": c3_bytes / ws / (c3["ms_per_step"] * 1e-3) / 1e9 / peak,
+            "gpu_launches_per_step_per_gpu": c3["launches_per_step"],
+            "data": "synthetic: random-init weights, random K/V contexts, shuffled page pool"}
+        extra["config5"] = {
+            "metric": "decode tok/s, 8 x 32768 ctx (Llama-3-8B arch, LoRA r16 q/v)",
+            "value": c5["rows"] * 1000.0 / c5["ms_per_step"], "unit": "tok/s", "ms_per_step": c5["ms_per_step"],
+            "parallelism": (f"split-KV x{ws} (NCCL all-gather of partial O/LSE per layer)" if ws > 1
+                            else "1 GPU"), "scaling": "strong",
+            "steps": xs, "warmup": xw, "achieved_gbs_all_gpus": c5_bytes / (c5["ms_per_step"] * 1e-3) / 1e9,
+            "frac_of_peak_per_gpu": c5_bytes / ws / (c5["ms_per_step"] * 1e-3) / 1e9 / peak,
+            "gpu_launches_per_step_per_gpu": c5["launches_per_step"],
+            "data": "synthetic: random-init weights, random K/V contexts"}
     if rank == 0:
         value = ws * steps / (ms * 1e-3)
         e2e = ws * steps / (ms_e2e * 1e-3)
@@ -398,7 +538,7 @@ def run_ours(args) -> None:
                        "lora": "r16 alpha32 q/k/v/o no-merge", "parallelism": f"request-sharded x{ws}",
                        "cuda_graph": True, "l2": "weights 16 GB > L2 126 MB; no flush"},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 8},
-            "gpu_launches": engine.launches_per_step() * steps,
+            "gpu_launches": launches * steps,
             "roofline": {"bound": "hbm", "kernel": "linear_lora_fused", "achieved": dom["achieved_gbs"],
                          "peak": peak, "unit": "GB/s", "frac": dom["achieved_gbs"] / peak, "peak_kind": peak_kind,
                          "traffic": _ncu_traffic("linear_lora_fused"),
@@ -407,6 +547,8 @@ def run_ours(args) -> None:
             "attention_gbs": att.get("achieved_gbs"),
             "clocks": clk.summary(),
         }
+        if extra:
+            line["workloads"] = extra
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
@@ -422,6 +564,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--profile", action="store_true",
                     help="profiling run: prefill, capture and the timed graph replays only")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the secondary workloads (configs 3 and 5) after the headline measurement")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling run on the first L layers (same per-layer shapes)")
     args = ap.parse_args()
