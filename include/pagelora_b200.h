@@ -162,6 +162,58 @@ int32_t pl_paged_decode(const void *q, int64_t q_stride_b, int64_t q_stride_h,
                         int32_t *status_dev, void *stream);
 
 /*
+ * One decoder layer's attention from the packed q/k/v projection row:
+ * per-head LoRA-B expand, Qwen3 q/k RMSNorm (HF rounding), RoPE, the paged
+ * append of the new token's K/V and the paged decode, in one launch.
+ * Replaces model/flashinfer/layer_runner.py:283-337 (projection split, head
+ * norms, RoPE via model/flashinfer/projection.py:34-190), :399-412
+ * (_append_decode_kv_static) and attention_backend.py:120-131 (run_decode).
+ *   qkv .. rope_theta  as pl_qkv_rope_append (rows = batch rows)
+ *   slot_page/offset   where row b's new token goes; it must be the last
+ *                      slot of the row's last page in the page table
+ *                      (pl_page_table_advance writes both); a row whose slot
+ *                      is elsewhere (a split-KV shard that does not hold the
+ *                      tail) appends nothing
+ *   q_out              nullable: the rotated q [batch, Hq, D] bf16
+ *   kv_cache .. out_lse, workspace  as pl_paged_decode; flags
+ *                      PL_DECODE_OUT_F32: `out` is fp32 (a split-KV partial)
+ */
+#define PL_DECODE_OUT_F32 1
+int32_t pl_paged_decode_qkv(const void *qkv, int64_t qkv_stride,
+                            const float *lora_down, int64_t down_stride,
+                            const void *lora_b, int32_t lora_rank,
+                            float lora_scale, const int32_t *tok_adapter,
+                            const void *q_norm_w, const void *k_norm_w,
+                            float norm_eps, const int32_t *positions,
+                            float rope_theta, const int32_t *slot_page,
+                            const int32_t *slot_offset, void *q_out,
+                            void *kv_cache, int64_t num_pages,
+                            const int32_t *indptr, const int32_t *indices,
+                            const int32_t *last_page_len, int32_t batch,
+                            int32_t num_qo_heads, int32_t num_kv_heads,
+                            int32_t head_dim, int32_t page_size, float sm_scale,
+                            int32_t num_splits, void *out, int64_t o_stride_b,
+                            int64_t o_stride_h, float *out_lse, int32_t flags,
+                            void *workspace, int64_t workspace_bytes,
+                            int32_t *status_dev, void *stream);
+
+/*
+ * Split merge of pl_paged_decode (and its variants): with `enable` (the
+ * default) the num_splits CTAs of one (row, kv head) run as a thread-block
+ * cluster and merge their states through distributed shared memory when
+ * num_splits <= 16 and every cluster of the launch fits on the device at
+ * once; otherwise, or with enable = 0, through the workspace.  The result is
+ * the same up to fp32 summation order.  No reference counterpart (a
+ * process-wide switch).
+ */
+int32_t pl_decode_set_cluster_merge(int32_t enable);
+
+/* Clusters of num_splits decode CTAs (2..16) the current device can hold at
+ * once for this head_dim / page_size (0: none); a diagnostic. */
+int32_t pl_decode_cluster_capacity(int32_t head_dim, int32_t page_size,
+                                   int32_t num_splits);
+
+/*
  * pl_paged_decode with the attention output in fp32 (`out` float, 16-byte
  * aligned): the partial state of a split-KV shard, merged across GPUs with
  * its LSE (pl_merge_states_strided).  No reference counterpart: the

@@ -32,6 +32,7 @@ PL_PROLOGUE_NONE = 0
 PL_PROLOGUE_RMSNORM = 1
 PL_PROLOGUE_SILU_MUL = 2
 PL_FLAG_WEIGHTS_STATIC = 1
+PL_DECODE_OUT_F32 = 1
 
 # Messages of the reference's ValueErrors for malformed spans
 # (model/kvcache/flashinfer_page_table.py:213-218).
@@ -78,6 +79,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _P,
          _I64, _P, _P],
     ),
+    "pl_paged_decode_qkv": (
+        _I32,
+        [_P, _I64, _P, _I64, _P, _I32, _F, _P, _P, _P, _F, _P, _F, _P, _P, _P, _P, _I64, _P, _P, _P, _I32, _I32,
+         _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _I32, _P, _I64, _P, _P],
+    ),
+    "pl_decode_set_cluster_merge": (_I32, [_I32]),
+    "pl_decode_cluster_capacity": (_I32, [_I32, _I32, _I32]),
     "pl_merge_states": (_I32, [_P, _P, _I32, _I32, _I32, _P, _I64, _P, _P]),
     "pl_merge_states_strided": (_I32, [_P, _I64, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _I64, _P, _P]),
     "pl_lora_shrink_seg": (_I32, [_P, _I64, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _I64, _P]),

@@ -377,17 +377,20 @@ class BatchDecodeEngine:
             else:
                 self._linear(self.x, L["w_qkv"], prologue=PL_PROLOGUE_RMSNORM, norm_weight=L["input_norm"],
                              out=self.qkv)
-            K.qkv_rope_append(self.qkv, num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads,
-                              head_dim=s.head_dim, positions=self.positions, rope_theta=s.rope_theta,
-                              kv_cache=self.kv[li], page_id=self.slot_page, page_offset=self.slot_off, q_out=self.q,
-                              lora_down=self.down_qkv if lora else None, lora_b=L["b_qkv"] if lora else None,
-                              lora_scale=self.qkv_lora_scale, tok_adapter=self.tok_adapter if lora else None,
-                              q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps, status=st)
+            # q/k head norm + RoPE + KV append + paged decode in one launch
+            # (on split-KV shards without the tail the slot is not in their
+            # page table, so they append nothing and return a partial state).
+            qkv_args = dict(num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads, positions=self.positions,
+                            rope_theta=s.rope_theta, slot_page=self.slot_page, slot_offset=self.slot_off,
+                            num_splits=self.num_splits, workspace=self.workspace,
+                            lora_down=self.down_qkv if lora else None, lora_b=L["b_qkv"] if lora else None,
+                            lora_scale=self.qkv_lora_scale, tok_adapter=self.tok_adapter if lora else None,
+                            q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps, status=st)
             if self.world == 1:
-                K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
-                               num_splits=self.num_splits, workspace=self.workspace, status=st, out=self.attn)
+                K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len,
+                                   out=self.attn, **qkv_args)
             else:
-                self._split_kv_attention(li)
+                self._split_kv_attention(li, qkv_args)
             if lora:
                 K.lora_shrink_seg(attn2d, L["a_o"], self.seg_indptr, self.seg_adapter, out=self.down_o)
             self._linear(attn2d, L["w_o"], lora_down=self.down_o if lora else None, lora_b=L["b_o"] if lora else None,
@@ -400,7 +403,7 @@ class BatchDecodeEngine:
                      out=self.logits)
         K.argmax(self.logits, self.token_buf, self.argmax_ws)
 
-    def _split_kv_attention(self, li: int) -> None:
+    def _split_kv_attention(self, li: int, qkv_args: dict) -> None:
         """This shard's partial (O fp32, LSE) over its pages, one all-gather of
         the packed partials over NCCL, then the LSE merge (same result on
         every shard)."""
@@ -412,9 +415,8 @@ class BatchDecodeEngine:
         nd = rows_h * s.head_dim
         o_part = self.part[:nd].view(self.rows, s.num_qo_heads, s.head_dim)
         lse_part = self.part[nd:].view(self.rows, s.num_qo_heads)
-        K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
-                       num_splits=self.num_splits, workspace=self.workspace, status=self.status, out=o_part,
-                       out_lse=lse_part)
+        K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len, out=o_part,
+                           out_lse=lse_part, **qkv_args)
         dist.all_gather_into_tensor(self.gathered, self.part, group=self.group)
         v = self.gathered[:, :nd].view(self.world, rows_h, s.head_dim).permute(1, 0, 2)
         lse = self.gathered[:, nd:].permute(1, 0)
@@ -426,7 +428,7 @@ class BatchDecodeEngine:
 
         s, B = self.spec, self.rows
         lora = self.lora_rank > 0
-        per_layer = 2  # q/k norm + RoPE + append, paged decode
+        per_layer = 1  # q/k norm + RoPE + append + paged decode
         if self.world > 1:
             per_layer += 1  # partial-state merge
         # q/k/v: with LoRA the norm is a launch of its own (the shrink reads it)

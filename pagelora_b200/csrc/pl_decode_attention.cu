@@ -18,12 +18,13 @@
 // over the pages indices[indptr[b] .. indptr[b+1]) of the NHD pool
 // [P, 2, page_size, Hkv, D]; the last page holds last_page_len[b] tokens.
 #include <mutex>
+#include <vector>
 
-#include "pl_common.cuh"
+#include "pl_qkv_head.cuh"
 
 namespace pl {
 
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = 6;
 constexpr int kDecodeThreads = 32 * (1 + kConsumerWarps);
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -38,6 +39,16 @@ struct DecodeArgs {
   int32_t num_qo_heads, num_kv_heads, group;
   float scale_log2;  // sm_scale * log2(e)
   int32_t num_splits;
+  int32_t cluster;      // 1: the splits of a (row, kv head) form one cluster and merge through DSMEM
+  // Fused q/k/v: q is computed from the projection row (qh) instead of read
+  // from `q`; the CTA that holds the row's last page appends the new token's
+  // K/V at (slot_page, slot_off) and uses them directly in this step.
+  int32_t fused;
+  QkvHeadArgs qh;
+  const int32_t* slot_page;
+  const int32_t* slot_off;
+  bf16* cache_w;        // the pool (writable) for the append
+  bf16* q_out;          // nullable: the rotated q is also written here [B, Hq, D]
   bf16* out;
   float* out_f32;       // when set, O is written here in fp32 instead of `out`
   int64_t o_stride_b, o_stride_h;
@@ -69,8 +80,15 @@ struct DecodeCfg {
   static constexpr int kBarOff = kMLOff + 2 * kConsumerWarps * 16 * 4;   // full[], empty[]
   static constexpr int kNtokOff = kBarOff + 2 * kStages * 8;
   static constexpr int kFlagOff = kNtokOff + kStages * 4;
-  static constexpr int kSmemBytes = kFlagOff + 16 + 1024;  // + alignment slack
-  static_assert(kConsumerWarps * 16 * D * 4 <= kStages * kStageBytes, "merge scratch must fit the stage ring");
+  // Cluster merge: what the other splits push here (this CTA reduces the
+  // float4 chunks j = split + S*i): O chunks [i][split] and LSE [split][row].
+  static constexpr int kClOff = (kFlagOff + 16 + 15) & ~15;
+  static constexpr int kClChunks = 16 * D / 4 + 16;                     // upper bound of i*S + s
+  static constexpr int kClLseOff = kClOff + kClChunks * 16;
+  static constexpr int kNewKvOff = kClLseOff + 16 * 16 * 4;             // fused: new K, V rows (bf16)
+  static constexpr int kSmemBytes = kNewKvOff + 2 * D * 2 + 1024;      // + alignment slack
+  static constexpr int kScratchRow = D + 4;                             // padded: conflict-free writes
+  static_assert(kConsumerWarps * 16 * kScratchRow * 4 <= kStages * kStageBytes, "merge scratch must fit the stage ring");
   static_assert(kStages >= kPagesPerBatch, "one producer batch must map to distinct stages");
 };
 
@@ -108,8 +126,19 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
   if (threadIdx.x == 32) prefetch_tensormap(&kv_map);
   if (threadIdx.x == 0 && kvh == 0) PL_TRACE_POINT(0);
   __syncthreads();
+  // Cluster merge: announce that this CTA runs (the others push into its
+  // shared memory after their matching wait).
+  if (args.cluster) cluster_arrive_relaxed();
 
   pdl_launch_dependents();
+  if (args.fused && warp >= 1) {
+    // static operands of this CTA's q heads (and of the K/V heads, which one
+    // CTA of the row will need) into L2 while the upstream grid finishes
+    const int cw = warp - 1;
+    for (int r = cw; r < group; r += kConsumerWarps) qkv_head_prefetch<D>(args.qh, kvh * group + r, lane);
+    const int kw = (cw + kConsumerWarps - group % kConsumerWarps) % kConsumerWarps;  // 0: K warp, 1: V warp
+    if (kw < 2) qkv_head_prefetch<D>(args.qh, args.num_qo_heads + kw * args.num_kv_heads + kvh, lane);
+  }
   pdl_wait();  // q, the page table and the freshly appended KV come from upstream kernels
   if (threadIdx.x == 0 && kvh == 0) PL_TRACE_POINT(1);
 
@@ -179,7 +208,9 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
 
     // Stage q rows (zero-padded to 16) into shared memory.
     uint8_t* qs = smem + C::kQOff;
-    {
+    bool appender = false;  // fused: this CTA holds the row's last page, where the new token goes
+    int new_off = 0;
+    if (!args.fused) {
       constexpr int kChunksPerRow = D / 8;
       for (int idx = ctid; idx < 16 * kChunksPerRow; idx += 32 * kConsumerWarps) {
         const int r = idx / kChunksPerRow, c = idx % kChunksPerRow;
@@ -190,8 +221,52 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
         }
         *reinterpret_cast<uint4*>(qs + r * C::kQRowBytes + c * 16) = v;
       }
+    } else {
+      constexpr int E = D / 32;
+      constexpr int kChunksPerRow = D / 8;
+      for (int idx = ctid; idx < (16 - group) * kChunksPerRow; idx += 32 * kConsumerWarps) {
+        const int r = group + idx / kChunksPerRow, c = idx % kChunksPerRow;
+        *reinterpret_cast<uint4*>(qs + r * C::kQRowBytes + c * 16) = make_uint4(0, 0, 0, 0);
+      }
+      // q heads of this group: normalised and rotated, one warp per head
+      for (int r = cw; r < group; r += kConsumerWarps) {
+        float v[E];
+        qkv_head_transform<D>(args.qh, b, kvh * group + r, lane, v);
+        bf16* dst = reinterpret_cast<bf16*>(qs + r * C::kQRowBytes) + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dst[e] = f2bf(v[e]);
+        if (args.q_out != nullptr && split == 0) {
+          bf16* g = args.q_out + ((int64_t)b * args.num_qo_heads + kvh * group + r) * D + lane * E;
+#pragma unroll
+          for (int e = 0; e < E; ++e) g[e] = f2bf(v[e]);
+        }
+      }
+      // The new token lands in the row's last page: the CTA holding that
+      // page computes its K/V, appends them and keeps them for this step.
+      if (n > 0 && p1 == n_pages) {
+        const int32_t last_pid = args.indices[row_begin + n_pages - 1];
+        const int32_t llen = args.last_page_len[b];
+        const int32_t spid = args.slot_page[b], soff = args.slot_off[b];
+        appender = spid == last_pid && soff == llen - 1 && soff >= 0 && soff < PS && spid >= 0 &&
+                   static_cast<int64_t>(spid) < args.num_pages;
+        new_off = soff;
+        // K and V go to the warps after the q heads' (idle ones when group < 5)
+        const int kw = (cw + kConsumerWarps - group % kConsumerWarps) % kConsumerWarps;
+        if (appender && kw < 2) {
+          float v[E];
+          qkv_head_transform<D>(args.qh, b, args.num_qo_heads + kw * args.num_kv_heads + kvh, lane, v);
+          bf16* sm = reinterpret_cast<bf16*>(smem + C::kNewKvOff) + kw * D + lane * E;
+          bf16* g = args.cache_w + ((((int64_t)spid * 2 + kw) * PS + soff) * args.num_kv_heads + kvh) * D + lane * E;
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            sm[e] = f2bf(v[e]);
+            g[e] = f2bf(v[e]);
+          }
+        }
+      }
     }
     named_barrier(1, 32 * kConsumerWarps);
+    if (ctid == 0 && kvh == 0) PL_TRACE_POINT(9);
 
     uint32_t qa[D / 16][4];
 #pragma unroll
@@ -216,6 +291,18 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
       }
       if (flags[0]) break;
       if (i == 0 && lane == 0 && kvh == 0) PL_TRACE_POINT(3);
+      if (appender && i == n - 1) {
+        // The copy of the last page may predate the append: put the new
+        // token's K and V rows into the staged tiles (16-byte chunks).
+        constexpr int kRowChunks = D / 8;
+        if (lane < 2 * kRowChunks) {
+          const int kv = lane / kRowChunks, c = lane % kRowChunks;
+          uint8_t* tile = smem + C::kStageOff + s * C::kStageBytes + kv * C::kTileBytes;
+          *reinterpret_cast<uint4*>(tile + (c / 8) * C::kHalfBytes + swz128(new_off, c % 8)) =
+              *reinterpret_cast<const uint4*>(smem + C::kNewKvOff + kv * D * 2 + c * 16);
+        }
+        __syncwarp();
+      }
       const int ntok = stage_ntok[s];
       if (ntok > 0) {
         const uint8_t* kbase = smem + C::kStageOff + s * C::kStageBytes;
@@ -311,18 +398,18 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     named_barrier(1, 32 * kConsumerWarps);  // every warp is done reading its stages
-    float* scratch = reinterpret_cast<float*>(smem + C::kStageOff);  // [warp][16][D]
+    if (ctid == 0 && kvh == 0) PL_TRACE_POINT(7);
+    float* scratch = reinterpret_cast<float*>(smem + C::kStageOff);  // [warp][16][kScratchRow]
     float* mw = ml;                                                   // [warp][16]
     float* lw = ml + kConsumerWarps * 16;
     {
-      float* ow = scratch + cw * 16 * D;
+      constexpr int SR = C::kScratchRow;
+      float* ow = scratch + cw * 16 * SR;
 #pragma unroll
       for (int j = 0; j < C::kDT; ++j) {
         const int d = 8 * j + 2 * t;
-        ow[g * D + d] = o[j][0];
-        ow[g * D + d + 1] = o[j][1];
-        ow[(g + 8) * D + d] = o[j][2];
-        ow[(g + 8) * D + d + 1] = o[j][3];
+        *reinterpret_cast<float2*>(ow + g * SR + d) = make_float2(o[j][0], o[j][1]);
+        *reinterpret_cast<float2*>(ow + (g + 8) * SR + d) = make_float2(o[j][2], o[j][3]);
       }
       if (t == 0) {
         mw[cw * 16 + g] = m0;
@@ -332,39 +419,61 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
       }
     }
     named_barrier(1, 32 * kConsumerWarps);
+    if (ctid == 0 && kvh == 0) PL_TRACE_POINT(8);
 
     const int hq0 = kvh * group;
     const bool single = args.num_splits == 1;
-    for (int idx = ctid; idx < group * D; idx += 32 * kConsumerWarps) {
-      const int r = idx / D, d = idx % D;
+    if (args.cluster) cluster_wait();  // every CTA of the cluster has started
+    // One float4 chunk (row r, columns d..d+3) per thread and pass: combine
+    // the consumer warps' states, then write the output (one split), push
+    // the chunk to the CTA of the cluster that reduces it, or leave it in
+    // the workspace for the last CTA to arrive.
+    for (int idx = ctid; idx < group * (D / 4); idx += 32 * kConsumerWarps) {
+      const int r = idx / (D / 4), d = 4 * (idx % (D / 4));
       float M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mw[w * 16 + r]);
-      float L = 0.f, acc = 0.f;
+      float L = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       if (M != -INFINITY) {
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) {
           const float wt = exp2f(mw[w * 16 + r] - M);
+          const float4 sv = *reinterpret_cast<const float4*>(scratch + (w * 16 + r) * C::kScratchRow + d);
           L += wt * lw[w * 16 + r];
-          acc += wt * scratch[(w * 16 + r) * D + d];
+          acc.x += wt * sv.x;
+          acc.y += wt * sv.y;
+          acc.z += wt * sv.z;
+          acc.w += wt * sv.w;
         }
       }
-      const float val = (L > 0.f) ? acc / L : 0.f;
+      const float il = (L > 0.f) ? 1.f / L : 0.f;
+      const float4 val = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
       const float lse2 = (L > 0.f) ? M + log2f(L) : -INFINITY;
       if (single) {
         const int64_t oi = b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
         if (args.out_f32 != nullptr)
-          args.out_f32[oi] = val;
+          *reinterpret_cast<float4*>(args.out_f32 + oi) = val;
         else
-          args.out[oi] = f2bf(val);
+          reinterpret_cast<uint2*>(args.out + oi)[0] =
+              make_uint2(pack_bf16x2(val.x, val.y), pack_bf16x2(val.z, val.w));
         if (args.out_lse != nullptr && d == 0) args.out_lse[(int64_t)b * args.num_qo_heads + hq0 + r] = lse2 * kLn2;
+      } else if (args.cluster) {
+        const int S = args.num_splits;
+        const uint32_t dst = (uint32_t)(idx % S);  // reducer CTA of this chunk
+        dsmem_st_f32x4(dsmem_map(smem_u32(smem + C::kClOff) + ((idx / S) * S + split) * 16, dst), val);
+        if (d == 0) {
+          const uint32_t lse_at = smem_u32(smem + C::kClLseOff) + (split * 16 + r) * 4;
+          for (int c = 0; c < S; ++c) dsmem_st_f32(dsmem_map(lse_at, c), lse2);  // every reducer needs it
+        }
       } else {
         const int64_t rowid = (int64_t)b * args.num_qo_heads + hq0 + r;
-        args.partial_o[(rowid * args.num_splits + split) * D + d] = val;
+        *reinterpret_cast<float4*>(args.partial_o + (rowid * args.num_splits + split) * D + d) = val;
         if (d == 0) args.partial_lse[rowid * args.num_splits + split] = lse2;
       }
     }
-    if (!single) {
+    if (ctid == 0 && kvh == 0) PL_TRACE_POINT(10);
+    if (!single && !args.cluster) {
       __threadfence();
       named_barrier(1, 32 * kConsumerWarps);
       if (ctid == 0) {
@@ -425,6 +534,58 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
         if (ctid == 0 && kvh == 0) PL_TRACE_POINT(6);
       }
     }
+  }
+
+  if (args.cluster) {
+    // The splits of this (row, kv head) are the CTAs of one cluster (rank =
+    // split).  Every CTA has pushed its chunk j to CTA j % S and its LSE to
+    // all CTAs (remote stores, made visible by the barrier); each CTA then
+    // reduces its chunks from its own shared memory.  Nothing is read
+    // remotely, so no CTA waits for another one after the barrier.
+    __syncwarp();
+    if (warp == 0) cluster_wait();  // the producer warp's half of the start barrier
+    if (threadIdx.x == 32 && kvh == 0) PL_TRACE_POINT(11);
+    cluster_sync_all();
+    if (threadIdx.x == 32 && kvh == 0) PL_TRACE_POINT(12);
+    const int S = args.num_splits;
+    const float4* recv = reinterpret_cast<const float4*>(smem + C::kClOff);
+    const float* recv_lse = reinterpret_cast<const float*>(smem + C::kClLseOff);
+    const int hq0 = kvh * group;
+    for (int i = threadIdx.x; i * S + split < group * (D / 4); i += kDecodeThreads) {
+      const int j = i * S + split;  // chunk reduced here
+      const int r = j / (D / 4), d = 4 * (j % (D / 4));
+      float M = -INFINITY;
+      for (int s = 0; s < S; ++s) M = fmaxf(M, recv_lse[s * 16 + r]);
+      float L = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (M != -INFINITY) {
+        for (int s = 0; s < S; ++s) {
+          const float l = recv_lse[s * 16 + r];
+          const float w = l == -INFINITY ? 0.f : exp2f(l - M);
+          const float4 o = recv[i * S + s];
+          L += w;
+          acc.x += w * o.x;
+          acc.y += w * o.y;
+          acc.z += w * o.z;
+          acc.w += w * o.w;
+        }
+      }
+      if (i == 0 && threadIdx.x == 0 && kvh == 0) {
+        asm volatile("" ::"f"(acc.x));
+        PL_TRACE_POINT(14);
+      }
+      const float il = L > 0.f ? 1.f / L : 0.f;
+      const int64_t oi = b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
+      if (args.out_f32 != nullptr) {
+        *reinterpret_cast<float4*>(args.out_f32 + oi) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
+      } else {
+        reinterpret_cast<uint2*>(args.out + oi)[0] =
+            make_uint2(pack_bf16x2(acc.x * il, acc.y * il), pack_bf16x2(acc.z * il, acc.w * il));
+      }
+      if (args.out_lse != nullptr && d == 0)
+        args.out_lse[(int64_t)b * args.num_qo_heads + hq0 + r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+    }
+    if (threadIdx.x == 0 && kvh == 0) PL_TRACE_POINT(15);
   }
 }
 
@@ -551,7 +712,70 @@ int32_t launch_decode(const CUtensorMap& map, const pl::DecodeArgs& a, int batch
   auto kern = pl::paged_decode_kernel<D, PS>;
   int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (st != PL_OK) return st;
+  if (a.cluster)
+    return pl_host::launch_pdl_cluster(kern, dim3(splits, hkv, batch), dim3(pl::kDecodeThreads), C::kSmemBytes,
+                                       stream, splits, map, a);
   return pl_host::launch_pdl(kern, dim3(splits, hkv, batch), dim3(pl::kDecodeThreads), C::kSmemBytes, stream, map, a);
+}
+
+// Split merge through a thread-block cluster (the splits of one (row, kv
+// head) as one cluster of up to 16 CTAs) when every cluster of the launch
+// can be resident at once; answers are cached per kernel, size and device.
+bool g_cluster_merge = true;
+constexpr int kMaxClusterSplits = 16;
+
+struct ClusterFit {
+  const void* kernel;
+  int dev, splits, active;
+};
+std::mutex g_fit_mu;
+std::vector<ClusterFit> g_fits;
+
+template <int D, int PS>
+int cluster_capacity(int splits) {
+  using C = pl::DecodeCfg<D, PS>;
+  auto kern = pl::paged_decode_kernel<D, PS>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  {
+    std::lock_guard<std::mutex> lock(g_fit_mu);
+    for (const auto& f : g_fits)
+      if (f.kernel == reinterpret_cast<const void*>(kern) && f.dev == dev && f.splits == splits) return f.active;
+  }
+  int active = 0;
+  if (pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes) == PL_OK &&
+      (splits <= 8 ||
+       cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(splits, 1, 1);
+    cfg.blockDim = dim3(pl::kDecodeThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess) active = 0;
+  }
+  cudaGetLastError();  // a refused query leaves no sticky error
+  std::lock_guard<std::mutex> lock(g_fit_mu);
+  g_fits.push_back({reinterpret_cast<const void*>(kern), dev, splits, active});
+  return active;
+}
+
+int cluster_capacity_for(int head_dim, int page_size, int splits) {
+  if (head_dim == 128 && page_size == 16) return cluster_capacity<128, 16>(splits);
+  if (head_dim == 128 && page_size == 32) return cluster_capacity<128, 32>(splits);
+  if (head_dim == 64 && page_size == 16) return cluster_capacity<64, 16>(splits);
+  if (head_dim == 64 && page_size == 32) return cluster_capacity<64, 32>(splits);
+  return 0;
+}
+
+bool use_cluster_merge(int head_dim, int page_size, int splits, int64_t clusters) {
+  return g_cluster_merge && splits >= 2 && splits <= kMaxClusterSplits &&
+         (int64_t)cluster_capacity_for(head_dim, page_size, splits) >= clusters;
 }
 
 }  // namespace
@@ -576,6 +800,17 @@ extern "C" int32_t pl_decode_plan(int32_t batch, int32_t num_qo_heads, int32_t n
     int64_t s = by_fill < by_len ? by_fill : by_len;
     if (s > 64) s = 64;
     if (max_splits > 0 && s > max_splits) s = max_splits;
+    // Fewer splits are worth a cluster merge (no round trip through global
+    // memory, no arrival ticket): take the largest split count whose clusters
+    // all fit on the device at once (measured on B200: 10 at 8 clusters of
+    // 137 KB CTAs, where 16-CTA clusters fit only 7 at a time).
+    if (s >= 2 && g_cluster_merge) {
+      for (int64_t c = s < kMaxClusterSplits ? s : kMaxClusterSplits; c >= 2; --c)
+        if (use_cluster_merge(head_dim, page_size, (int)c, base)) {
+          s = c;
+          break;
+        }
+    }
     splits = s < 1 ? 1 : static_cast<int>(s);
   }
   plan_out->num_splits = splits;
@@ -590,8 +825,18 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                           const int32_t* last_page_len, int32_t batch, int32_t num_qo_heads, int32_t num_kv_heads,
                           int32_t head_dim, int32_t page_size, float sm_scale, int32_t num_splits, void* out,
                           bool out_is_f32, int64_t o_stride_b, int64_t o_stride_h, float* out_lse, void* workspace,
-                          int64_t workspace_bytes, int32_t* status_dev, void* stream) {
+                          int64_t workspace_bytes, int32_t* status_dev, void* stream,
+                          const pl::QkvHeadArgs* fused = nullptr, const int32_t* slot_page = nullptr,
+                          const int32_t* slot_off = nullptr, void* q_out = nullptr) {
   if (batch == 0) return PL_OK;
+  if (fused != nullptr) {  // q comes from the projection row: validate that instead
+    if (fused->qkv == nullptr || fused->positions == nullptr || slot_page == nullptr || slot_off == nullptr ||
+        (fused->down != nullptr && fused->lora_b != nullptr && fused->rank <= 0) ||
+        fused->Hq != num_qo_heads || fused->Hkv != num_kv_heads)
+      return PL_ERR_INVALID_ARGUMENT;
+    q = kv_cache;  // any 16-byte aligned pointer: the q checks below do not apply
+    q_stride_b = q_stride_h = 0;
+  }
   if (q == nullptr || kv_cache == nullptr || indptr == nullptr || indices == nullptr || last_page_len == nullptr ||
       out == nullptr || batch < 0 || num_pages <= 0 || num_kv_heads <= 0 || num_qo_heads % num_kv_heads != 0 ||
       num_splits < 1)
@@ -624,6 +869,13 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
   a.group = group;
   a.scale_log2 = sm_scale * pl::kLog2e;
   a.num_splits = num_splits;
+  a.cluster = use_cluster_merge(head_dim, page_size, num_splits, (int64_t)batch * num_kv_heads) ? 1 : 0;
+  a.fused = fused != nullptr ? 1 : 0;
+  a.qh = fused != nullptr ? *fused : pl::QkvHeadArgs{};
+  a.slot_page = slot_page;
+  a.slot_off = slot_off;
+  a.cache_w = static_cast<pl::bf16*>(const_cast<void*>(kv_cache));
+  a.q_out = static_cast<pl::bf16*>(q_out);
   a.out = out_is_f32 ? nullptr : static_cast<pl::bf16*>(out);
   a.out_f32 = out_is_f32 ? static_cast<float*>(out) : nullptr;
   a.o_stride_b = o_stride_b;
@@ -670,6 +922,49 @@ extern "C" int32_t pl_paged_decode_f32(const void* q, int64_t q_stride_b, int64_
   return paged_decode_impl(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
                            num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, true,
                            o_stride_b, o_stride_h, out_lse, workspace, workspace_bytes, status_dev, stream);
+}
+
+extern "C" int32_t pl_paged_decode_qkv(const void* qkv, int64_t qkv_stride, const float* lora_down,
+                                       int64_t down_stride, const void* lora_b, int32_t lora_rank, float lora_scale,
+                                       const int32_t* tok_adapter, const void* q_norm_w, const void* k_norm_w,
+                                       float norm_eps, const int32_t* positions, float rope_theta,
+                                       const int32_t* slot_page, const int32_t* slot_offset, void* q_out,
+                                       void* kv_cache, int64_t num_pages, const int32_t* indptr,
+                                       const int32_t* indices, const int32_t* last_page_len, int32_t batch,
+                                       int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+                                       int32_t page_size, float sm_scale, int32_t num_splits, void* out,
+                                       int64_t o_stride_b, int64_t o_stride_h, float* out_lse, int32_t flags,
+                                       void* workspace, int64_t workspace_bytes, int32_t* status_dev, void* stream) {
+  pl::QkvHeadArgs h;
+  h.qkv = static_cast<const pl::bf16*>(qkv);
+  h.qkv_stride = qkv_stride;
+  h.down = lora_down;
+  h.down_stride = down_stride;
+  h.lora_b = static_cast<const pl::bf16*>(lora_b);
+  h.rank = lora_rank;
+  h.lora_scale = lora_scale;
+  h.tok_adapter = tok_adapter;
+  h.q_norm_w = static_cast<const pl::bf16*>(q_norm_w);
+  h.k_norm_w = static_cast<const pl::bf16*>(k_norm_w);
+  h.eps = norm_eps;
+  h.positions = positions;
+  h.theta = rope_theta;
+  h.Hq = num_qo_heads;
+  h.Hkv = num_kv_heads;
+  return paged_decode_impl(nullptr, 0, 0, kv_cache, num_pages, indptr, indices, last_page_len, batch, num_qo_heads,
+                           num_kv_heads, head_dim, page_size, sm_scale, num_splits, out,
+                           (flags & PL_DECODE_OUT_F32) != 0, o_stride_b, o_stride_h, out_lse, workspace,
+                           workspace_bytes, status_dev, stream, &h, slot_page, slot_offset, q_out);
+}
+
+extern "C" int32_t pl_decode_cluster_capacity(int32_t head_dim, int32_t page_size, int32_t num_splits) {
+  if (num_splits < 2 || num_splits > kMaxClusterSplits) return 0;
+  return cluster_capacity_for(head_dim, page_size, num_splits);
+}
+
+extern "C" int32_t pl_decode_set_cluster_merge(int32_t enable) {
+  g_cluster_merge = enable != 0;
+  return PL_OK;
 }
 
 extern "C" int32_t pl_merge_states_strided(const float* v_partial, int64_t v_row_stride, int64_t v_state_stride,

@@ -1,7 +1,7 @@
 // Page-table construction and the small per-token kernels of one decode
 // step: q/k head RMSNorm + RoPE + paged KV append, the plain KV append,
 // embedding gather and first-index argmax.
-#include "pl_common.cuh"
+#include "pl_qkv_head.cuh"
 
 namespace pl {
 
@@ -316,73 +316,28 @@ __global__ void kv_append_kernel(const bf16* __restrict__ k, int64_t k_stride, c
 // ------------------------------------------- q/k norm + RoPE + KV append
 // One warp per (token, head) over the packed [q | k | v] projection row.
 template <int D>
-__global__ void __launch_bounds__(128) qkv_rope_append_kernel(
-    const bf16* __restrict__ qkv, int64_t qkv_stride, const float* __restrict__ down, int64_t down_stride,
-    const bf16* __restrict__ lora_b, int rank, float lora_scale, const int32_t* __restrict__ tok_adapter,
-    const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w, float eps,
-    const int32_t* __restrict__ positions, float rope_theta, bf16* __restrict__ q_out, bf16* __restrict__ cache,
-    int64_t num_pages, const int32_t* __restrict__ page_id, const int32_t* __restrict__ page_off, int T, int Hq,
-    int Hkv, int PS, int32_t* status) {
-  constexpr int E = D / 32;  // elements per lane; lanes 0..15 hold [0, D/2), 16..31 hold [D/2, D)
+__global__ void __launch_bounds__(128) qkv_rope_append_kernel(const QkvHeadArgs a, bf16* __restrict__ q_out,
+                                                              bf16* __restrict__ cache, int64_t num_pages,
+                                                              const int32_t* __restrict__ page_id,
+                                                              const int32_t* __restrict__ page_off, int T, int PS,
+                                                              int32_t* status) {
+  constexpr int E = D / 32;
   if (threadIdx.x == 0) PL_TRACE_POINT(0);
   pdl_launch_dependents();
+  const int heads = a.Hq + 2 * a.Hkv;
+  const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (gw < T * heads) qkv_head_prefetch<D>(a, gw % heads, lane);
   pdl_wait();
   if (threadIdx.x == 0) PL_TRACE_POINT(1);
-  const int heads = Hq + 2 * Hkv;
-  const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (gw >= T * heads) return;
-  const int lane = threadIdx.x & 31;
   const int t = gw / heads, hh = gw % heads;
-  const int kind = hh < Hq ? 0 : (hh < Hq + Hkv ? 1 : 2);  // q, k, v
-  const int col = hh * D;                                     // packed column of this head
   const int d0 = lane * E;
   float v[E];
-  {
-    const bf16* src = qkv + (int64_t)t * qkv_stride + col + d0;
-#pragma unroll
-    for (int e = 0; e < E; ++e) v[e] = bf2f(src[e]);
-  }
-  if (down != nullptr && lora_b != nullptr) {
-    const int ad = tok_adapter != nullptr ? tok_adapter[t] : 0;
-    if (ad >= 0) {
-      const int n_out = heads * D;
-      const float* drow = down + (int64_t)t * down_stride + kind * rank;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const bf16* brow = lora_b + ((int64_t)ad * n_out + col + d0 + e) * rank;
-        const float d = lora_dot(brow, drow, rank);
-        v[e] = bfr(v[e] + bfr(bfr(d) * lora_scale));
-      }
-    }
-  }
-  if (kind < 2) {
-    const bf16* nw = kind == 0 ? q_norm_w : k_norm_w;
-    if (nw != nullptr) {  // HF RMSNorm module: fp32 normalise, round, scale, round
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) ss += v[e] * v[e];
-      ss = warp_sum(ss);
-      const float r = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-      for (int e = 0; e < E; ++e) v[e] = bfr(bf2f(nw[d0 + e]) * bfr(v[e] * r));
-    }
-    const float pos = (float)positions[t];
-    float out[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
-      const int i = (d0 + e) % (D / 2);
-      const float inv_freq = 1.0f / powf(rope_theta, (float)(2 * i) / (float)D);
-      float sn, cs;
-      sincosf(pos * inv_freq, &sn, &cs);
-      out[e] = lane < 16 ? v[e] * cs - partner * sn : v[e] * cs + partner * sn;
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) v[e] = out[e];
-  }
+  qkv_head_transform<D>(a, t, hh, lane, v);
   if (lane == 0) PL_TRACE_MAX(2);
-  if (kind == 0) {
-    bf16* dst = q_out + ((int64_t)t * Hq + hh) * D + d0;
+  if (hh < a.Hq) {
+    bf16* dst = q_out + ((int64_t)t * a.Hq + hh) * D + d0;
 #pragma unroll
     for (int e = 0; e < E; ++e) dst[e] = f2bf(v[e]);
   } else {
@@ -391,8 +346,9 @@ __global__ void __launch_bounds__(128) qkv_rope_append_kernel(
       if (lane == 0) set_status(status, PL_ERR_PAGE_OUT_OF_RANGE);
       return;
     }
-    const int h = kind == 1 ? hh - Hq : hh - Hq - Hkv;
-    bf16* dst = cache + ((((int64_t)pid * 2 + (kind - 1)) * PS + off) * Hkv + h) * D + d0;
+    const int kv = hh < a.Hq + a.Hkv ? 0 : 1;
+    const int h = hh - a.Hq - kv * a.Hkv;
+    bf16* dst = cache + ((((int64_t)pid * 2 + kv) * PS + off) * a.Hkv + h) * D + d0;
 #pragma unroll
     for (int e = 0; e < E; ++e) dst[e] = f2bf(v[e]);
   }
@@ -593,24 +549,32 @@ extern "C" int32_t pl_qkv_rope_append(const void* qkv, int64_t qkv_stride, const
       page_offset == nullptr || num_tokens < 0 || num_qo_heads <= 0 || num_kv_heads <= 0 || page_size <= 0)
     return PL_ERR_INVALID_ARGUMENT;
   if (lora_down != nullptr && lora_b != nullptr && lora_rank <= 0) return PL_ERR_INVALID_ARGUMENT;
+  pl::QkvHeadArgs a;
+  a.qkv = static_cast<const pl::bf16*>(qkv);
+  a.qkv_stride = qkv_stride;
+  a.down = lora_down;
+  a.down_stride = down_stride;
+  a.lora_b = static_cast<const pl::bf16*>(lora_b);
+  a.rank = lora_rank;
+  a.lora_scale = lora_scale;
+  a.tok_adapter = tok_adapter;
+  a.q_norm_w = static_cast<const pl::bf16*>(q_norm_w);
+  a.k_norm_w = static_cast<const pl::bf16*>(k_norm_w);
+  a.eps = norm_eps;
+  a.positions = positions;
+  a.theta = rope_theta;
+  a.Hq = num_qo_heads;
+  a.Hkv = num_kv_heads;
   const int warps = num_tokens * (num_qo_heads + 2 * num_kv_heads);
   const int blocks = (warps + 3) / 4;
   if (head_dim == 128)
-    return pl_host::launch_pdl(pl::qkv_rope_append_kernel<128>, dim3(blocks), dim3(128), 0, stream,
-                               static_cast<const pl::bf16*>(qkv), qkv_stride, lora_down, down_stride,
-                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, lora_scale, tok_adapter,
-                               static_cast<const pl::bf16*>(q_norm_w), static_cast<const pl::bf16*>(k_norm_w),
-                               norm_eps, positions, rope_theta, static_cast<pl::bf16*>(q_out),
-                               static_cast<pl::bf16*>(kv_cache), num_pages, page_id, page_offset, (int)num_tokens,
-                               (int)num_qo_heads, (int)num_kv_heads, (int)page_size, status_dev);
+    return pl_host::launch_pdl(pl::qkv_rope_append_kernel<128>, dim3(blocks), dim3(128), 0, stream, a,
+                               static_cast<pl::bf16*>(q_out), static_cast<pl::bf16*>(kv_cache), num_pages, page_id,
+                               page_offset, (int)num_tokens, (int)page_size, status_dev);
   if (head_dim == 64)
-    return pl_host::launch_pdl(pl::qkv_rope_append_kernel<64>, dim3(blocks), dim3(128), 0, stream,
-                               static_cast<const pl::bf16*>(qkv), qkv_stride, lora_down, down_stride,
-                               static_cast<const pl::bf16*>(lora_b), (int)lora_rank, lora_scale, tok_adapter,
-                               static_cast<const pl::bf16*>(q_norm_w), static_cast<const pl::bf16*>(k_norm_w),
-                               norm_eps, positions, rope_theta, static_cast<pl::bf16*>(q_out),
-                               static_cast<pl::bf16*>(kv_cache), num_pages, page_id, page_offset, (int)num_tokens,
-                               (int)num_qo_heads, (int)num_kv_heads, (int)page_size, status_dev);
+    return pl_host::launch_pdl(pl::qkv_rope_append_kernel<64>, dim3(blocks), dim3(128), 0, stream, a,
+                               static_cast<pl::bf16*>(q_out), static_cast<pl::bf16*>(kv_cache), num_pages, page_id,
+                               page_offset, (int)num_tokens, (int)page_size, status_dev);
   return PL_ERR_UNSUPPORTED;
 }
 

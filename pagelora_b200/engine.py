@@ -3,15 +3,16 @@
 ``DecodeEngine`` runs the decode layer of the reference
 (model/flashinfer/layer_runner.py:283-337, cuda_graph.py:245-263) with the
 no-merge LoRA delta (packed_ops.py:105-165, multilora/linear.py:200-231) on
-this package's kernels, seven launches per layer:
+this package's kernels, six launches per layer:
 
   1. linear_lora_fused   RMSNorm -> [W_q;W_k;W_v] and the packed LoRA A rows
-  2. qkv_rope_append     + B.down (packed expand), q/k head norm, RoPE, KV append
-  3. paged_decode        split-KV paged attention with in-kernel merge
-  4. lora_shrink_seg     attn . A_o^T
-  5. linear_lora_fused   W_o with the LoRA expand and the residual in the epilogue
-  6. linear_lora_fused   RMSNorm -> [W_gate;W_up]
-  7. linear_lora_fused   SiLU-and-mul -> W_down with the residual in the epilogue
+  2. paged_decode_qkv    + B.down (packed expand), q/k head norm, RoPE, KV append,
+                         then split-KV paged attention with the split merge
+                         (thread-block cluster or arrival ticket) in the kernel
+  3. lora_shrink_seg     attn . A_o^T
+  4. linear_lora_fused   W_o with the LoRA expand and the residual in the epilogue
+  5. linear_lora_fused   RMSNorm -> [W_gate;W_up]
+  6. linear_lora_fused   SiLU-and-mul -> W_down with the residual in the epilogue
 
 plus page-table advance + embedding in front and the final norm + lm_head +
 argmax behind.  The page table lives on the device and is advanced inside
@@ -291,13 +292,14 @@ class DecodeEngine:
                                 norm_eps=s.rms_eps, out=self.qkv, shrink_a=L.a_qkv,
                                 shrink_out=self.down_qkv if L.a_qkv is not None else None, weights_static=True,
                                 status=st)
-            K.qkv_rope_append(self.qkv, num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads,
-                              head_dim=s.head_dim, positions=self.positions, rope_theta=s.rope_theta,
-                              kv_cache=self.kv[li], page_id=self.slot_page, page_offset=self.slot_off, q_out=self.q,
-                              lora_down=self.down_qkv if L.b_qkv is not None else None, lora_b=L.b_qkv,
-                              lora_scale=self.qkv_lora_scale, q_norm_weight=L.q_norm, k_norm_weight=L.k_norm, norm_eps=s.rms_eps, status=st)
-            K.paged_decode(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len,
-                           num_splits=self.num_splits, workspace=self.workspace, status=st, out=self.attn)
+            # q/k head norm + RoPE + KV append + paged decode: one launch
+            K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len,
+                               num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads, positions=self.positions,
+                               rope_theta=s.rope_theta, slot_page=self.slot_page, slot_offset=self.slot_off,
+                               num_splits=self.num_splits, workspace=self.workspace,
+                               lora_down=self.down_qkv if L.b_qkv is not None else None, lora_b=L.b_qkv,
+                               lora_scale=self.qkv_lora_scale, q_norm_weight=L.q_norm, k_norm_weight=L.k_norm,
+                               norm_eps=s.rms_eps, out=self.attn, status=st)
             if L.a_o is not None:
                 K.lora_shrink_seg(attn2d, L.a_o, self.seg_indptr, self.seg_adapter, out=self.down_o)
             K.linear_lora_fused(attn2d, L.w_o, lora_down=self.down_o if L.b_o is not None else None, lora_b=L.b_o,
@@ -311,7 +313,7 @@ class DecodeEngine:
         K.argmax(self.logits, self.token_buf, self.argmax_ws)
 
     def launches_per_step(self) -> int:
-        per_layer = 6 + sum(1 for L in self.layers[:1] if L.a_o is not None)
+        per_layer = 5 + sum(1 for L in self.layers[:1] if L.a_o is not None)
         return 2 + per_layer * len(self.layers) + 2
 
     def capture(self) -> None:

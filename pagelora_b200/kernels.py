@@ -137,6 +137,67 @@ def paged_decode(
     return out
 
 
+def paged_decode_qkv(
+    qkv: torch.Tensor,
+    kv_cache: torch.Tensor,
+    indptr: torch.Tensor,
+    indices: torch.Tensor,
+    last_page_len: torch.Tensor,
+    *,
+    num_qo_heads: int,
+    num_kv_heads: int,
+    positions: torch.Tensor,
+    rope_theta: float,
+    slot_page: torch.Tensor,
+    slot_offset: torch.Tensor,
+    num_splits: int,
+    workspace: torch.Tensor | None,
+    lora_down: torch.Tensor | None = None,
+    lora_b: torch.Tensor | None = None,
+    lora_scale: float = 1.0,
+    tok_adapter: torch.Tensor | None = None,
+    q_norm_weight: torch.Tensor | None = None,
+    k_norm_weight: torch.Tensor | None = None,
+    norm_eps: float = 1e-6,
+    out: torch.Tensor | None = None,
+    out_lse: torch.Tensor | None = None,
+    q_out: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
+    sm_scale: float | None = None,
+) -> torch.Tensor:
+    """q/k head norm + RoPE + paged append + paged decode in one launch, from
+    the packed projection rows ``qkv`` [B, (Hq + 2 Hkv) * D] bf16; ``out`` is
+    [B, Hq, D] bf16, or fp32 for a split-KV partial."""
+
+    _need_cuda(qkv, kv_cache, indptr, indices, last_page_len, positions, slot_page, slot_offset)
+    _need(qkv, torch.bfloat16, "qkv")
+    _need(kv_cache, torch.bfloat16, "kv_cache")
+    if kv_cache.dim() != 5 or kv_cache.size(1) != 2 or not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous [pages, 2, page_size, kv_heads, head_dim] tensor")
+    batch = qkv.shape[0]
+    num_pages, _, page_size, hkv, d = kv_cache.shape
+    if hkv != num_kv_heads or qkv.shape[1] != (num_qo_heads + 2 * num_kv_heads) * d:
+        raise ValueError("qkv / kv_cache shapes do not match the head counts")
+    if out is None:
+        out = torch.empty(batch, num_qo_heads, d, dtype=torch.bfloat16, device=qkv.device)
+    rank = 0
+    if lora_b is not None:
+        if lora_b.dim() == 2:
+            lora_b = lora_b.unsqueeze(0)
+        rank = lora_b.shape[-1]
+    scale = (1.0 / math.sqrt(d)) if sm_scale is None else float(sm_scale)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    flags = _capi.PL_DECODE_OUT_F32 if out.dtype == torch.float32 else 0
+    call("pl_paged_decode_qkv", ptr(qkv), _row_stride(qkv, "qkv"), ptr(lora_down),
+         0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank), float(lora_scale),
+         ptr(tok_adapter), ptr(q_norm_weight), ptr(k_norm_weight), float(norm_eps), ptr(positions),
+         float(rope_theta), ptr(slot_page), ptr(slot_offset), ptr(q_out), ptr(kv_cache), int(num_pages), ptr(indptr),
+         ptr(indices), ptr(last_page_len), int(batch), int(num_qo_heads), int(num_kv_heads), int(d),
+         int(page_size), scale, int(num_splits), ptr(out), out.stride(0), out.stride(1), ptr(out_lse), int(flags),
+         ptr(workspace), int(ws_bytes), ptr(status), stream_handle())
+    return out
+
+
 def merge_states(v_partial: torch.Tensor, lse_partial: torch.Tensor, out: torch.Tensor | None = None,
                  out_lse: torch.Tensor | None = None) -> torch.Tensor:
     """Merge [rows, S, D] fp32 partial states with natural-log LSE [rows, S]."""

@@ -175,6 +175,101 @@ def test_paged_decode_vs_oracle(K, d, ps, hq, hkv):
         np.testing.assert_allclose(lse, ref_lse, rtol=1e-3, atol=1e-3)
 
 
+@pytest.mark.parametrize("batch,hq,hkv,lens_scale", [(1, 32, 8, 132), (3, 16, 2, 40), (2, 8, 8, 9)])
+def test_paged_decode_cluster_merge_matches_workspace_merge(K, batch, hq, hkv, lens_scale):
+    """The split merge through a thread-block cluster (DSMEM) and the one
+    through the workspace give the same output and LSE, both within the
+    oracle tolerance (splits 2..16, empty splits included)."""
+
+    from pagelora_b200._capi import load_library
+
+    lib = load_library()
+    rng = np.random.default_rng(batch * 100 + hkv)
+    lens = [int(lens_scale * 16 - rng.integers(0, 16)) for _ in range(batch)]
+    lens[0] = max(lens[0], 1)
+    for splits in (2, 5, 16):
+        res = []
+        for cluster in (1, 0):
+            assert lib.pl_decode_set_cluster_merge(cluster) == 0
+            try:
+                res.append(_decode_case(K, batch=batch, hq=hq, hkv=hkv, d=128, ps=16, lens=lens,
+                                        num_splits=splits, seed=splits))
+            finally:
+                lib.pl_decode_set_cluster_merge(1)
+        (o1, l1, ref, ref_lse), (o0, l0, _, _) = res
+        assert np.max(np.abs(o1 - ref)) <= ATOL and np.max(np.abs(o0 - ref)) <= ATOL
+        assert np.max(np.abs(o1 - o0)) <= 2 ** -7 * max(1.0, float(np.max(np.abs(o0))))
+        np.testing.assert_allclose(l1, l0, rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(l1, ref_lse, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("d,hq,hkv,qk_norm", [(128, 32, 8, True), (64, 8, 2, False), (128, 16, 16, False)])
+def test_paged_decode_qkv_matches_rope_then_decode(K, d, hq, hkv, qk_norm):
+    """The fused launch (head norm + RoPE + append + decode) equals the two
+    launches it replaces: same output, LSE, rotated q and appended K/V, for
+    new tokens mid-page and at a fresh page, with multi-adapter LoRA, split
+    counts 1 / 3 / 16; and a row whose slot is not its last page appends
+    nothing (a split-KV shard without the tail)."""
+
+    rng = np.random.default_rng(d + hq + hkv)
+    ps, r, n_ad = 16, 16, 2
+    lens = [1, 17, 40, 300]               # tokens including the new one
+    b = len(lens)
+    pages_per_row = [-(-n // ps) for n in lens]
+    pool = sum(pages_per_row) + 6
+    cache = _t(bf16(rng.normal(size=(pool, 2, ps, hkv, d))))
+    perm = rng.permutation(pool)
+    indptr = np.cumsum([0] + pages_per_row)
+    indices = perm[: indptr[-1]]
+    last = [n - (p - 1) * ps for n, p in zip(lens, pages_per_row)]
+    slot_page = [int(indices[indptr[i + 1] - 1]) for i in range(b)]
+    slot_off = [l - 1 for l in last]
+    slot_page[2] = int(perm[-1])          # row 2's slot is elsewhere: no append, no injection
+    n_heads = hq + 2 * hkv
+    qkv = _t(bf16(rng.normal(size=(b, n_heads * d))))
+    down = _t(rng.normal(size=(b, 3 * r)).astype(np.float32), torch.float32)
+    lb = _t(bf16(rng.normal(size=(n_ad, n_heads * d, r)) * 0.05))
+    tok_ad = _i32([0, 1, -1, 1])
+    qn = _t(bf16(1 + rng.normal(size=d) * 0.1)) if qk_norm else None
+    kn = _t(bf16(1 + rng.normal(size=d) * 0.1)) if qk_norm else None
+    pos = _i32([n - 1 for n in lens])
+    dev_ip, dev_idx, dev_last = _i32(indptr), _i32(indices), _i32(last)
+    sp, so = _i32(slot_page), _i32(slot_off)
+    ws = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+    common = dict(lora_down=down, lora_b=lb, lora_scale=1.0, tok_adapter=tok_ad, q_norm_weight=qn,
+                  k_norm_weight=kn, norm_eps=1e-6)
+    for splits in (1, 3, 16):
+        c_ref = cache.clone()
+        q_ref = torch.empty(b, hq, d, dtype=torch.bfloat16, device="cuda")
+        K.qkv_rope_append(qkv, num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, positions=pos, rope_theta=1e6,
+                          kv_cache=c_ref, page_id=sp, page_offset=so, q_out=q_ref, **common)
+        lse_ref = torch.empty(b, hq, device="cuda")
+        o_ref = K.paged_decode(q_ref, c_ref, dev_ip, dev_idx, dev_last, num_splits=splits, workspace=ws,
+                               out_lse=lse_ref)
+        c_f = cache.clone()
+        q_f = torch.zeros(b, hq, d, dtype=torch.bfloat16, device="cuda")
+        lse_f = torch.empty(b, hq, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        o_f = K.paged_decode_qkv(qkv, c_f, dev_ip, dev_idx, dev_last, num_qo_heads=hq, num_kv_heads=hkv,
+                                 positions=pos, rope_theta=1e6, slot_page=sp, slot_offset=so, num_splits=splits,
+                                 workspace=ws, out_lse=lse_f, q_out=q_f, status=status, **common)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert torch.equal(q_f, q_ref)
+        # appended K/V: identical where the row owns its slot; row 2's slot page untouched by the fused call
+        for i in (0, 1, 3):
+            assert torch.equal(c_f[slot_page[i], :, slot_off[i]], c_ref[slot_page[i], :, slot_off[i]])
+        assert torch.equal(c_f[slot_page[2]], cache[slot_page[2]])
+        keep = [0, 1, 3]
+        assert np.max(np.abs(_np(o_f)[keep] - _np(o_ref)[keep])) <= 2 ** -7 * 4
+        np.testing.assert_allclose(_np(lse_f)[keep], _np(lse_ref)[keep], rtol=1e-5, atol=1e-5)
+        # row 2: attention over its pages as they are (no new token)
+        np.testing.assert_allclose(_np(o_f)[2], _np(K.paged_decode(q_f[2:3], cache, _i32([0, pages_per_row[2]]),
+                                                                   _i32(indices[indptr[2]:indptr[3]]),
+                                                                   _i32([last[2]]), num_splits=1,
+                                                                   workspace=ws))[0], atol=2 ** -7 * 4)
+
+
 def test_paged_decode_empty_row_and_long_context(K):
     out, lse, ref, ref_lse = _decode_case(K, batch=3, hq=32, hkv=8, d=128, ps=16, lens=[0, 2112, 7],
                                           num_splits=37, seed=5)
