@@ -20,10 +20,12 @@ Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 cuda.synchronize, timed with CUDA events on the stream the kernels run on.
 The weights (16 GB) exceed L2 (126 MB), so no flush is needed between steps.
 
-After the headline line's measurements the same run times two secondary
+After the headline line's measurements the same run times three secondary
 workloads (``--no-extra`` skips them), reported under "workloads":
   config3  Llama-2-7B arch, 64 rows, contexts U[512, 4096], 8 adapters,
            rows sharded over the N ranks (strong scaling, no collective);
+  config4  Qwen3-8B arch, 16 branches sharing a 2048-token prefix stored
+           once (shared-prefix decode), rows sharded over the N ranks;
   config5  Llama-3-8B arch, 8 x 32768-token contexts, split-KV over the N
            ranks with an NCCL all-gather of the partial (O, LSE) per layer.
 Their contexts hold random K/V (their prefill is not part of a decode step).
@@ -361,6 +363,45 @@ def run_config3(ws: int, rank: int, device, barrier, steps: int, warmup: int) ->
     return out
 
 
+def run_config4(ws: int, rank: int, device, barrier, steps: int, warmup: int) -> dict:
+    """Qwen3-8B arch, 16 branches sharing a 2048-token
+    prefix, 64-token suffixes, one rank-16 LoRA on q/k/v/o.  The prefix is
+    stored once and read through the shared-prefix pass; rows are sharded
+    across ranks (16 / N each, every rank holds the prefix).  The K/V of the
+    prefix and suffixes are random values."""
+
+    import torch
+
+    from pagelora_b200.batch_engine import BatchDecodeEngine
+    from pagelora_b200.synthetic import WORKLOADS, make_lora_weights, make_model_weights
+
+    wl = WORKLOADS["config4"]
+    spec, lspec = wl.model, wl.lora
+    total_rows, prefix_len, suffix_len = 16, 2048, 64
+    rows = total_rows * (rank + 1) // ws - total_rows * rank // ws
+    w = make_model_weights(spec, seed=0, device=device)
+    lo = make_lora_weights(spec, lspec, device=device)
+    per_row = -(-(suffix_len + steps + warmup + 40) // 16)
+    pages = -(-prefix_len // 16) + rows * per_row + 64
+    eng = BatchDecodeEngine(spec, w, adapters=[lo], lora_spec=lspec, row_adapter=[0] * rows, page_size=16,
+                            max_context=suffix_len + steps + warmup + 40, num_pages=pages, device=device)
+    del w, lo
+    eng.fill_random_shared(prefix_len, [suffix_len] * rows, seed=4 + rank)
+    eng.capture()
+    ms = _timed_steps(eng, steps, warmup, device, barrier)
+    eng._check_status()
+    ctx_avg = suffix_len + (warmup + steps) / 2
+    kv_logical = rows * (prefix_len + ctx_avg) * spec.num_kv_heads * spec.head_dim * 4 * spec.num_layers
+    kv_unique = (eng.cascade.prefix_bytes_per_layer() + rows * ctx_avg * spec.num_kv_heads * spec.head_dim * 4) \
+        * spec.num_layers
+    out = {"rows_per_gpu": rows, "ms_per_step": ms, "launches_per_step": eng.launches_per_step(),
+           "kv_bytes_logical": kv_logical, "kv_bytes_read": kv_unique, "weight_bytes_per_step": spec.weight_bytes()}
+    eng.graph = None
+    del eng
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_config5(ws: int, rank: int, device, barrier, group, steps: int, warmup: int) -> dict:
     """Llama-3-8B arch, 8 rows of 32768-token contexts,
     rank-16 LoRA on q/v; split-KV across the ranks (each holds 1/N of every
@@ -491,17 +532,30 @@ def run_ours(args) -> None:
         torch.cuda.empty_cache()
         xs, xw = min(args.steps, 16), max(3, args.warmup)
         c3 = run_config3(ws, rank, device, barrier, xs, xw)
+        c4 = run_config4(ws, rank, device, barrier, xs, xw)
         c5 = run_config5(ws, rank, device, barrier, dist.group.WORLD if ws > 1 else None, xs, xw)
-        tt = torch.tensor([c3["ms_per_step"], c5["ms_per_step"], float(c3["kv_bytes_per_step"])], device=device,
+        tt = torch.tensor([c3["ms_per_step"], c4["ms_per_step"], c5["ms_per_step"], float(c3["kv_bytes_per_step"]),
+                           float(c4["kv_bytes_read"]), float(c4["kv_bytes_logical"])], device=device,
                           dtype=torch.float64)
         if ws > 1:
-            mx = tt[:2].clone()
+            mx = tt[:3].clone()
             dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            kv3 = tt[2:].clone()
-            dist.all_reduce(kv3)
-            tt = torch.cat([mx, kv3])
-        c3["ms_per_step"], c5["ms_per_step"] = float(tt[0]), float(tt[1])
-        c3_bytes = float(tt[2]) + ws * c3["weight_bytes_per_step"]
+            sm = tt[3:].clone()
+            dist.all_reduce(sm)
+            tt = torch.cat([mx, sm])
+        c3["ms_per_step"], c4["ms_per_step"], c5["ms_per_step"] = float(tt[0]), float(tt[1]), float(tt[2])
+        c3_bytes = float(tt[3]) + ws * c3["weight_bytes_per_step"]
+        c4_bytes = float(tt[4]) + ws * c4["weight_bytes_per_step"]
+        extra["config4"] = {
+            "metric": "decode tok/s, 16 branches sharing a 2048-token prefix (Qwen3-8B arch, LoRA r16 q/k/v/o)",
+            "value": 16 * 1000.0 / c4["ms_per_step"], "unit": "tok/s", "ms_per_step": c4["ms_per_step"],
+            "rows_per_gpu": c4["rows_per_gpu"], "parallelism": f"request-sharded x{ws}", "scaling": "strong",
+            "steps": xs, "warmup": xw, "kv_bytes_read_per_step": float(tt[4]),
+            "kv_bytes_logical_per_step": float(tt[5]),
+            "achieved_gbs_all_gpus": c4_bytes / (c4["ms_per_step"] * 1e-3) / 1e9,
+            "frac_of_peak_per_gpu": c4_bytes / ws / (c4["ms_per_step"] * 1e-3) / 1e9 / peak,
+            "gpu_launches_per_step_per_gpu": c4["launches_per_step"],
+            "data": "synthetic: random-init weights, random K/V for the prefix and the suffixes"}
         c5_bytes = c5["kv_bytes_per_step"] + ws * c5["weight_bytes_per_step_per_gpu"]
         extra["config3"] = {
             "metric": "decode tok/s, 64 rows (Llama-2-7B arch, 8 adapters r16 q/k/v/o, ctx U[512,4096])",

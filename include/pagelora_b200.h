@@ -144,7 +144,9 @@ int32_t pl_decode_plan(int32_t batch, int32_t num_qo_heads,
  *            go to `workspace` and the last CTA of each (row, kv head) merges
  *            them (no second launch).  The first 4*batch*num_kv_heads bytes of
  *            the workspace are arrival counters that must be zero before the
- *            first call; every call leaves them zero again.
+ *            first call; every call leaves them zero again.  The partials
+ *            follow the counters, so a workspace serves calls of one
+ *            batch x num_kv_heads; give calls of other shapes their own.
  * Supported: head_dim 64 or 128, page_size 16 or 32, group (qo/kv) <= 16.
  * A row with no pages yields O = 0 and LSE = -inf.
  */
@@ -198,6 +200,30 @@ int32_t pl_paged_decode_qkv(const void *qkv, int64_t qkv_stride,
                             int32_t *status_dev, void *stream);
 
 /*
+ * Paged decode of query rows that share page lists: row b attends to the
+ * pages of page-table row b / fold (the CSR has ceil(batch / fold) rows).
+ * The `fold` rows of a page-table row sit in one tensor-core tile (fold x
+ * group <= 16 query heads), so each shared page is read once per `fold`
+ * rows.  Used for the shared prefix of a branch batch (the reference repeats
+ * the prefix pages in every branch's table, model/flashinfer/generation.py
+ * :872-1132); otherwise as pl_paged_decode (flags PL_DECODE_OUT_F32: fp32
+ * out for a partial state merged with pl_merge_states_strided).
+ */
+int32_t pl_paged_decode_shared(const void *q, int64_t q_stride_b,
+                               int64_t q_stride_h, const void *kv_cache,
+                               int64_t num_pages, const int32_t *indptr,
+                               const int32_t *indices,
+                               const int32_t *last_page_len, int32_t batch,
+                               int32_t fold, int32_t num_qo_heads,
+                               int32_t num_kv_heads, int32_t head_dim,
+                               int32_t page_size, float sm_scale,
+                               int32_t num_splits, void *out,
+                               int64_t o_stride_b, int64_t o_stride_h,
+                               float *out_lse, int32_t flags, void *workspace,
+                               int64_t workspace_bytes, int32_t *status_dev,
+                               void *stream);
+
+/*
  * Split merge of pl_paged_decode (and its variants): with `enable` (the
  * default) the num_splits CTAs of one (row, kv head) run as a thread-block
  * cluster and merge their states through distributed shared memory when
@@ -238,10 +264,13 @@ int32_t pl_paged_decode_f32(const void *q, int64_t q_stride_b, int64_t q_stride_
  * The split partials and arrival counters live in a fixed device array of
  * PL_FIXED_SCRATCH_BYTES per device, inside the library; nothing is
  * allocated.  Arguments and results are those of pl_paged_decode.
+ *   - The array's first 64 KiB are arrival counters for up to 16384
+ *     (row, kv head) pairs whatever the shape, so calls of different shapes
+ *     may follow one another; the split partials use the rest.
  *   - Returns PL_ERR_WORKSPACE_TOO_SMALL, launching nothing, when
- *     pl_decode_plan's workspace_bytes for the shape exceeds
- *     PL_FIXED_SCRATCH_BYTES (e.g. batch * num_qo_heads * num_splits
- *     * head_dim * 4 beyond ~4 MiB).
+ *     batch * num_kv_heads exceeds 16384 or the partials (batch *
+ *     num_qo_heads * num_splits * (head_dim + 1) * 4 bytes) exceed the
+ *     remaining ~4 MiB.
  *   - The first call on each device (that device current) looks up the
  *     array's address and clears it on `stream`; make that first call
  *     before any stream capture.

@@ -84,6 +84,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _P, _I64, _P, _I32, _F, _P, _P, _P, _F, _P, _F, _P, _P, _P, _P, _I64, _P, _P, _P, _I32, _I32,
          _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _I32, _P, _I64, _P, _P],
     ),
+    "pl_paged_decode_shared": (
+        _I32,
+        [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P,
+         _I32, _P, _I64, _P, _P],
+    ),
     "pl_decode_set_cluster_merge": (_I32, [_I32]),
     "pl_decode_cluster_capacity": (_I32, [_I32, _I32, _I32]),
     "pl_merge_states": (_I32, [_P, _P, _I32, _I32, _I32, _P, _I64, _P, _P]),

@@ -184,6 +184,8 @@ class BatchDecodeEngine:
         self.host_pages: list[list[int]] = [[] for _ in range(B)]
         self.host_last = [0] * B
         self.context_len = [0] * B
+        self.cascade = None  # shared-prefix decode (branch batches)
+        self.prefix_len = 0
         self.graph: torch.cuda.CUDAGraph | None = None
         self.pinned_pages = torch.zeros(B, dtype=torch.int32, pin_memory=True)
         self.pinned_tokens = torch.zeros(B, dtype=torch.int64, pin_memory=True)
@@ -245,60 +247,74 @@ class BatchDecodeEngine:
         return pages[p0:p1], pages[:p0] + pages[p1:], last
 
     @torch.no_grad()
+    def _forward_prompt(self, prompt: list[int], ad: int, page_of: torch.Tensor, off_of: torch.Tensor,
+                        keep: torch.Tensor | None = None) -> torch.Tensor:
+        """Torch forward of one row's whole prompt with adapter `ad`; writes
+        the K/V of position i to (page_of[i], off_of[i]) for the positions in
+        `keep` (all when None) and returns the last position's logits."""
+
+        s = self.spec
+        n = len(prompt)
+        ids = torch.tensor(prompt, device=self.device, dtype=torch.int64)
+        pos = torch.arange(n, device=self.device)
+        x = self.embed[ids]
+        for li, L in enumerate(self.layers):
+            h = _rmsnorm_fused(x, L["input_norm"], s.rms_eps)
+            qkv = F.linear(h, L["w_qkv"])
+            if ad >= 0 and L["a_qkv"] is not None:
+                down = F.linear(h, L["a_qkv"][ad])
+                rk = self.lora_rank
+                deltas, off = [], 0
+                for j, od in enumerate((s.q_dim, s.kv_dim, s.kv_dim)):
+                    dj = F.linear(down[:, j * rk:(j + 1) * rk], L["b_qkv"][ad, off:off + od])
+                    deltas.append(dj if self.qkv_lora_scale == 1.0 else dj * self.qkv_lora_scale)
+                    off += od
+                qkv = qkv + torch.cat(deltas, -1)
+            q = qkv[:, : s.q_dim].view(n, s.num_qo_heads, s.head_dim)
+            k = qkv[:, s.q_dim: s.q_dim + s.kv_dim].view(n, s.num_kv_heads, s.head_dim)
+            v = qkv[:, s.q_dim + s.kv_dim:].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
+            if L["q_norm"] is not None:
+                q = _rmsnorm_hf(q, L["q_norm"], s.rms_eps)
+                k = _rmsnorm_hf(k, L["k_norm"], s.rms_eps)
+            q = _rope(q, pos, s.rope_theta)
+            k = _rope(k, pos, s.rope_theta).contiguous()
+            if keep is None:
+                K.kv_append(k, v, self.kv[li], page_of, off_of, status=self.status)
+            elif keep.numel():
+                K.kv_append(k[keep].contiguous(), v[keep].contiguous(), self.kv[li], page_of[keep].contiguous(),
+                            off_of[keep].contiguous(), status=self.status)
+            attn = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                                  v.transpose(0, 1)[None], is_causal=True, enable_gqa=True)
+            attn = attn[0].transpose(0, 1).reshape(n, s.q_dim)
+            o = F.linear(attn, L["w_o"])
+            if ad >= 0 and L["a_o"] is not None:
+                o = o + F.linear(F.linear(attn, L["a_o"][ad]), L["b_o"][ad]) * self.lora_scale
+            x = x + o
+            h2 = _rmsnorm_fused(x, L["post_norm"], s.rms_eps)
+            gu = F.linear(h2, L["w_gate_up"])
+            g, u = gu[:, : s.intermediate].float(), gu[:, s.intermediate:].float()
+            x = x + F.linear((g / (1.0 + torch.exp(-g)) * u).to(torch.bfloat16), L["w_down"])
+        return F.linear(_rmsnorm_fused(x[-1:], self.final_norm, s.rms_eps), self.lm_head)[0]
+
+    @torch.no_grad()
     def prefill(self, prompts: list[list[int]]) -> list[int]:
         """Prefill every row's prompt (torch ops, each row with its adapter);
         returns each row's first greedy token."""
 
         if len(prompts) != self.rows:
             raise ValueError("one prompt per row")
-        s = self.spec
         firsts = []
         self.prefill_logits = []
         for r, prompt in enumerate(prompts):
             n = len(prompt)
             pages = [self._alloc_page() for _ in range(-(-n // self.page_size))]
             self.host_pages[r], self.host_last[r] = list(pages), n - (len(pages) - 1) * self.page_size
-            ad = self.row_adapter[r]
-            ids = torch.tensor(prompt, device=self.device, dtype=torch.int64)
             pos = torch.arange(n, device=self.device)
             page_of = torch.tensor(pages, device=self.device, dtype=torch.int32)[pos // self.page_size]
             off_of = (pos % self.page_size).to(torch.int32)
-            x = self.embed[ids]
-            for li, L in enumerate(self.layers):
-                h = _rmsnorm_fused(x, L["input_norm"], s.rms_eps)
-                qkv = F.linear(h, L["w_qkv"])
-                if ad >= 0 and L["a_qkv"] is not None:
-                    down = F.linear(h, L["a_qkv"][ad])
-                    rk = self.lora_rank
-                    deltas, off = [], 0
-                    for j, od in enumerate((s.q_dim, s.kv_dim, s.kv_dim)):
-                        dj = F.linear(down[:, j * rk:(j + 1) * rk], L["b_qkv"][ad, off:off + od])
-                        deltas.append(dj if self.qkv_lora_scale == 1.0 else dj * self.qkv_lora_scale)
-                        off += od
-                    qkv = qkv + torch.cat(deltas, -1)
-                q = qkv[:, : s.q_dim].view(n, s.num_qo_heads, s.head_dim)
-                k = qkv[:, s.q_dim: s.q_dim + s.kv_dim].view(n, s.num_kv_heads, s.head_dim)
-                v = qkv[:, s.q_dim + s.kv_dim:].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
-                if L["q_norm"] is not None:
-                    q = _rmsnorm_hf(q, L["q_norm"], s.rms_eps)
-                    k = _rmsnorm_hf(k, L["k_norm"], s.rms_eps)
-                q = _rope(q, pos, s.rope_theta)
-                k = _rope(k, pos, s.rope_theta).contiguous()
-                K.kv_append(k, v, self.kv[li], page_of, off_of, status=self.status)
-                attn = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
-                                                      v.transpose(0, 1)[None], is_causal=True, enable_gqa=True)
-                attn = attn[0].transpose(0, 1).reshape(n, s.q_dim)
-                o = F.linear(attn, L["w_o"])
-                if ad >= 0 and L["a_o"] is not None:
-                    o = o + F.linear(F.linear(attn, L["a_o"][ad]), L["b_o"][ad]) * self.lora_scale
-                x = x + o
-                h2 = _rmsnorm_fused(x, L["post_norm"], s.rms_eps)
-                gu = F.linear(h2, L["w_gate_up"])
-                g, u = gu[:, : s.intermediate].float(), gu[:, s.intermediate:].float()
-                x = x + F.linear((g / (1.0 + torch.exp(-g)) * u).to(torch.bfloat16), L["w_down"])
-            logits = F.linear(_rmsnorm_fused(x[-1:], self.final_norm, s.rms_eps), self.lm_head)
-            self.prefill_logits.append(logits[0])
-            firsts.append(int(torch.argmax(logits[0]).item()))
+            logits = self._forward_prompt(prompt, self.row_adapter[r], page_of, off_of)
+            self.prefill_logits.append(logits)
+            firsts.append(int(torch.argmax(logits).item()))
         self.context_len = [len(p) for p in prompts]
         if self.world > 1:
             for r, n in enumerate(self.context_len):
@@ -335,6 +351,83 @@ class BatchDecodeEngine:
         self.token_buf.copy_(torch.randint(0, self.spec.vocab, (self.rows,), generator=g, device=self.device))
         self.plan()
 
+    # ------------------------------------------------------ shared prefix
+    def _set_shared_prefix(self, prefix_pages: list[int], prefix_len: int) -> None:
+        from pagelora_b200.cascade import SharedPrefixDecode
+
+        if self.world != 1:
+            raise ValueError("a shared prefix is not combined with split-KV")
+        s = self.spec
+        self.prefix_pages = list(prefix_pages)
+        self.prefix_len = int(prefix_len)
+        self.cascade = SharedPrefixDecode(num_rows=self.rows, num_qo_heads=s.num_qo_heads,
+                                          num_kv_heads=s.num_kv_heads, head_dim=s.head_dim,
+                                          page_size=self.page_size, prefix_pages=self.prefix_pages,
+                                          prefix_last_len=prefix_len - (len(prefix_pages) - 1) * self.page_size,
+                                          device=self.device, max_suffix_pages=self.max_pages_per_row)
+        self.graph = None
+
+    @torch.no_grad()
+    def prefill_shared(self, prefix: list[int], suffixes: list[list[int]]) -> list[int]:
+        """Branch batch (the reference's generation.py:872-1132 shape): every
+        row continues the same `prefix` with its own suffix.  The prefix K/V
+        are stored once in shared pages; each row's page table holds only its
+        suffix (and the tokens it decodes), and decode attends to the prefix
+        through the shared-prefix pass.  All rows must use the same adapter
+        (the prefix K/V depend on it).  Returns each row's first token."""
+
+        if len(suffixes) != self.rows:
+            raise ValueError("one suffix per row")
+        if len(set(self.row_adapter)) != 1:
+            raise ValueError("rows sharing a prefix must use the same adapter")
+        ps = self.page_size
+        n_pre = len(prefix)
+        prefix_pages = [self._alloc_page() for _ in range(-(-n_pre // ps))]
+        firsts = []
+        self.prefill_logits = []
+        for r, suf in enumerate(suffixes):
+            n = n_pre + len(suf)
+            pages = [self._alloc_page() for _ in range(-(-len(suf) // ps))]
+            self.host_pages[r], self.host_last[r] = list(pages), len(suf) - (len(pages) - 1) * ps
+            pos = torch.arange(n)
+            page_of = torch.tensor([prefix_pages[p // ps] if p < n_pre else pages[(p - n_pre) // ps]
+                                    for p in pos.tolist()], dtype=torch.int32, device=self.device)
+            off_of = torch.tensor([p % ps if p < n_pre else (p - n_pre) % ps for p in pos.tolist()],
+                                  dtype=torch.int32, device=self.device)
+            keep = torch.arange(0 if r == 0 else n_pre, n, device=self.device)  # the prefix K/V once
+            logits = self._forward_prompt(prefix + suf, self.row_adapter[r], page_of, off_of, keep)
+            self.prefill_logits.append(logits)
+            firsts.append(int(torch.argmax(logits).item()))
+        self.context_len = [n_pre + len(suf) for suf in suffixes]
+        self._set_shared_prefix(prefix_pages, n_pre)
+        self._sync_rows()
+        self.token_buf.copy_(torch.tensor(firsts, dtype=torch.int64))
+        self.plan()
+        self._check_status()
+        return firsts
+
+    @torch.no_grad()
+    def fill_random_shared(self, prefix_len: int, suffix_lens: list[int], *, seed: int = 0) -> None:
+        """fill_random_context for a branch batch: one shared prefix of random
+        K/V plus a random suffix per row."""
+
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        ps = self.page_size
+        prefix_pages = [self._alloc_page() for _ in range(-(-prefix_len // ps))]
+        groups = [prefix_pages] + [[self._alloc_page() for _ in range(-(-n // ps))] for n in suffix_lens]
+        for r, n in enumerate(suffix_lens):
+            self.host_pages[r], self.host_last[r] = groups[r + 1], n - (len(groups[r + 1]) - 1) * ps
+        for pages in groups:
+            idx = torch.tensor(pages, device=self.device, dtype=torch.int64)
+            for li in range(self.spec.num_layers):
+                vals = torch.randn((len(pages),) + tuple(self.kv.shape[2:]), generator=g, device=self.device)
+                self.kv[li].index_copy_(0, idx, vals.to(torch.bfloat16))
+        self.context_len = [prefix_len + n for n in suffix_lens]
+        self._set_shared_prefix(prefix_pages, prefix_len)
+        self._sync_rows()
+        self.token_buf.copy_(torch.randint(0, self.spec.vocab, (self.rows,), generator=g, device=self.device))
+        self.plan()
+
     # --------------------------------------------------------- decode step
     def _linear(self, x, w, *, prologue=0, norm_weight=None, **kw):
         """Projection of all rows: fused GEMV (prologue inside) when the rows'
@@ -358,6 +451,8 @@ class BatchDecodeEngine:
             K.page_table_advance(self.row_num_pages, self.last_page_len, self.row_pages, self.new_page_ids,
                                  self.page_size, self.indptr, self.indices, self.slot_page, self.slot_off,
                                  self.positions, st)
+            if self.cascade is not None:
+                self.positions.add_(self.prefix_len)  # the rows' tables hold only their suffixes
         else:
             self.positions.add_(1)
             if self.owner:
@@ -386,7 +481,17 @@ class BatchDecodeEngine:
                             lora_down=self.down_qkv if lora else None, lora_b=L["b_qkv"] if lora else None,
                             lora_scale=self.qkv_lora_scale, tok_adapter=self.tok_adapter if lora else None,
                             q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps, status=st)
-            if self.world == 1:
+            if self.cascade is not None:
+                # shared prefix: append + rotate, then prefix pass + suffix pass + merge
+                K.qkv_rope_append(self.qkv, num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads,
+                                  head_dim=s.head_dim, positions=self.positions, rope_theta=s.rope_theta,
+                                  kv_cache=self.kv[li], page_id=self.slot_page, page_offset=self.slot_off,
+                                  q_out=self.q, lora_down=qkv_args["lora_down"], lora_b=qkv_args["lora_b"],
+                                  lora_scale=self.qkv_lora_scale, tok_adapter=qkv_args["tok_adapter"],
+                                  q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps,
+                                  status=st)
+                self.cascade.run(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len, self.attn, st)
+            elif self.world == 1:
                 K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len,
                                    out=self.attn, **qkv_args)
             else:
@@ -428,7 +533,9 @@ class BatchDecodeEngine:
 
         s, B = self.spec, self.rows
         lora = self.lora_rank > 0
-        per_layer = 1  # q/k norm + RoPE + append + paged decode
+        # q/k norm + RoPE + append + paged decode; with a shared prefix:
+        # RoPE + append, prefix pass, suffix pass, merge
+        per_layer = 4 if self.cascade is not None else 1
         if self.world > 1:
             per_layer += 1  # partial-state merge
         # q/k/v: with LoRA the norm is a launch of its own (the shrink reads it)

@@ -39,6 +39,11 @@ struct DecodeArgs {
   int32_t num_qo_heads, num_kv_heads, group;
   float scale_log2;  // sm_scale * log2(e)
   int32_t num_splits;
+  // Row folding (shared page lists): blockIdx.z is a page-table row shared by
+  // `fold` consecutive query rows; tile row m is query row z*fold + m/group,
+  // head kvh*group + m%group.  Rows >= rows_real are padding.
+  int32_t fold;
+  int32_t rows_real;
   int32_t cluster;      // 1: the splits of a (row, kv head) form one cluster and merge through DSMEM
   // Fused q/k/v: q is computed from the projection row (qh) instead of read
   // from `q`; the CTA that holds the row's last page appends the new token's
@@ -113,6 +118,9 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int group = args.group;
+  const int mrows = group * args.fold;  // tile rows in use (<= 16)
+  auto row_of = [&](int m) { return (int)blockIdx.z * args.fold + m / group; };
+  auto head_of = [&](int m) { return kvh * group + m % group; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -215,8 +223,9 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
       for (int idx = ctid; idx < 16 * kChunksPerRow; idx += 32 * kConsumerWarps) {
         const int r = idx / kChunksPerRow, c = idx % kChunksPerRow;
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < group) {
-          const bf16* src = args.q + b * args.q_stride_b + (int64_t)(kvh * group + r) * args.q_stride_h + c * 8;
+        if (r < mrows && row_of(r) < args.rows_real) {
+          const bf16* src =
+              args.q + (int64_t)row_of(r) * args.q_stride_b + (int64_t)head_of(r) * args.q_stride_h + c * 8;
           v = *reinterpret_cast<const uint4*>(src);
         }
         *reinterpret_cast<uint4*>(qs + r * C::kQRowBytes + c * 16) = v;
@@ -421,15 +430,16 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
     named_barrier(1, 32 * kConsumerWarps);
     if (ctid == 0 && kvh == 0) PL_TRACE_POINT(8);
 
-    const int hq0 = kvh * group;
     const bool single = args.num_splits == 1;
     if (args.cluster) cluster_wait();  // every CTA of the cluster has started
     // One float4 chunk (row r, columns d..d+3) per thread and pass: combine
     // the consumer warps' states, then write the output (one split), push
     // the chunk to the CTA of the cluster that reduces it, or leave it in
     // the workspace for the last CTA to arrive.
-    for (int idx = ctid; idx < group * (D / 4); idx += 32 * kConsumerWarps) {
+    for (int idx = ctid; idx < mrows * (D / 4); idx += 32 * kConsumerWarps) {
       const int r = idx / (D / 4), d = 4 * (idx % (D / 4));
+      const int orow = row_of(r), ohead = head_of(r);
+      const bool live = orow < args.rows_real;
       float M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mw[w * 16 + r]);
@@ -451,13 +461,16 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
       const float4 val = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
       const float lse2 = (L > 0.f) ? M + log2f(L) : -INFINITY;
       if (single) {
-        const int64_t oi = b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
-        if (args.out_f32 != nullptr)
-          *reinterpret_cast<float4*>(args.out_f32 + oi) = val;
-        else
-          reinterpret_cast<uint2*>(args.out + oi)[0] =
-              make_uint2(pack_bf16x2(val.x, val.y), pack_bf16x2(val.z, val.w));
-        if (args.out_lse != nullptr && d == 0) args.out_lse[(int64_t)b * args.num_qo_heads + hq0 + r] = lse2 * kLn2;
+        if (live) {
+          const int64_t oi = (int64_t)orow * args.o_stride_b + (int64_t)ohead * args.o_stride_h + d;
+          if (args.out_f32 != nullptr)
+            *reinterpret_cast<float4*>(args.out_f32 + oi) = val;
+          else
+            reinterpret_cast<uint2*>(args.out + oi)[0] =
+                make_uint2(pack_bf16x2(val.x, val.y), pack_bf16x2(val.z, val.w));
+          if (args.out_lse != nullptr && d == 0)
+            args.out_lse[(int64_t)orow * args.num_qo_heads + ohead] = lse2 * kLn2;
+        }
       } else if (args.cluster) {
         const int S = args.num_splits;
         const uint32_t dst = (uint32_t)(idx % S);  // reducer CTA of this chunk
@@ -466,8 +479,8 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
           const uint32_t lse_at = smem_u32(smem + C::kClLseOff) + (split * 16 + r) * 4;
           for (int c = 0; c < S; ++c) dsmem_st_f32(dsmem_map(lse_at, c), lse2);  // every reducer needs it
         }
-      } else {
-        const int64_t rowid = (int64_t)b * args.num_qo_heads + hq0 + r;
+      } else if (live) {
+        const int64_t rowid = (int64_t)orow * args.num_qo_heads + ohead;
         *reinterpret_cast<float4*>(args.partial_o + (rowid * args.num_splits + split) * D + d) = val;
         if (d == 0) args.partial_lse[rowid * args.num_splits + split] = lse2;
       }
@@ -488,13 +501,17 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
         // then every thread reduces float4 columns with independent loads.
         __threadfence();
         const int S = args.num_splits;
-        const int64_t row0 = (int64_t)b * args.num_qo_heads + hq0;
-        float* wts = scratch;              // [group][S] weights, then [group] 1/L
-        float* inv_l = scratch + group * S;
-        for (int idx = ctid; idx < group * S; idx += 32 * kConsumerWarps)
-          wts[idx] = __ldcg(args.partial_lse + row0 * S + idx);
+        float* wts = scratch;              // [mrows][S] weights, then [mrows] 1/L
+        float* inv_l = scratch + mrows * S;
+        for (int idx = ctid; idx < mrows * S; idx += 32 * kConsumerWarps) {
+          const int m = idx / S;
+          wts[idx] = row_of(m) < args.rows_real
+                         ? __ldcg(args.partial_lse + ((int64_t)row_of(m) * args.num_qo_heads + head_of(m)) * S +
+                                  idx % S)
+                         : -INFINITY;
+        }
         named_barrier(1, 32 * kConsumerWarps);
-        if (ctid < group) {
+        if (ctid < mrows) {
           float M = -INFINITY;
           for (int s = 0; s < S; ++s) M = fmaxf(M, wts[ctid * S + s]);
           float L = 0.f;
@@ -504,12 +521,16 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
             L += wt;
           }
           inv_l[ctid] = L > 0.f ? 1.f / L : 0.f;
-          if (args.out_lse != nullptr) args.out_lse[row0 + ctid] = (L > 0.f) ? (M + log2f(L)) * kLn2 : -INFINITY;
+          if (args.out_lse != nullptr && row_of(ctid) < args.rows_real)
+            args.out_lse[(int64_t)row_of(ctid) * args.num_qo_heads + head_of(ctid)] =
+                (L > 0.f) ? (M + log2f(L)) * kLn2 : -INFINITY;
         }
         named_barrier(1, 32 * kConsumerWarps);
-        for (int idx = ctid; idx < group * (D / 4); idx += 32 * kConsumerWarps) {
+        for (int idx = ctid; idx < mrows * (D / 4); idx += 32 * kConsumerWarps) {
           const int r = idx / (D / 4), d = 4 * (idx % (D / 4));
-          const float4* src = reinterpret_cast<const float4*>(args.partial_o + ((row0 + r) * S) * D + d);
+          if (row_of(r) >= args.rows_real) continue;
+          const int64_t rowid = (int64_t)row_of(r) * args.num_qo_heads + head_of(r);
+          const float4* src = reinterpret_cast<const float4*>(args.partial_o + (rowid * S) * D + d);
           const float* wr = wts + r * S;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
@@ -522,7 +543,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
             acc.w += wt * o.w;
           }
           const float il = inv_l[r];
-          const int64_t oi = b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
+          const int64_t oi = (int64_t)row_of(r) * args.o_stride_b + (int64_t)head_of(r) * args.o_stride_h + d;
           if (args.out_f32 != nullptr) {
             *reinterpret_cast<float4*>(args.out_f32 + oi) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
           } else {
@@ -550,10 +571,10 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
     const int S = args.num_splits;
     const float4* recv = reinterpret_cast<const float4*>(smem + C::kClOff);
     const float* recv_lse = reinterpret_cast<const float*>(smem + C::kClLseOff);
-    const int hq0 = kvh * group;
-    for (int i = threadIdx.x; i * S + split < group * (D / 4); i += kDecodeThreads) {
+    for (int i = threadIdx.x; i * S + split < mrows * (D / 4); i += kDecodeThreads) {
       const int j = i * S + split;  // chunk reduced here
       const int r = j / (D / 4), d = 4 * (j % (D / 4));
+      if (row_of(r) >= args.rows_real) continue;
       float M = -INFINITY;
       for (int s = 0; s < S; ++s) M = fmaxf(M, recv_lse[s * 16 + r]);
       float L = 0.f;
@@ -575,7 +596,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
         PL_TRACE_POINT(14);
       }
       const float il = L > 0.f ? 1.f / L : 0.f;
-      const int64_t oi = b * args.o_stride_b + (int64_t)(hq0 + r) * args.o_stride_h + d;
+      const int64_t oi = (int64_t)row_of(r) * args.o_stride_b + (int64_t)head_of(r) * args.o_stride_h + d;
       if (args.out_f32 != nullptr) {
         *reinterpret_cast<float4*>(args.out_f32 + oi) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
       } else {
@@ -583,7 +604,8 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
             make_uint2(pack_bf16x2(acc.x * il, acc.y * il), pack_bf16x2(acc.z * il, acc.w * il));
       }
       if (args.out_lse != nullptr && d == 0)
-        args.out_lse[(int64_t)b * args.num_qo_heads + hq0 + r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+        args.out_lse[(int64_t)row_of(r) * args.num_qo_heads + head_of(r)] =
+            L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
     }
     if (threadIdx.x == 0 && kvh == 0) PL_TRACE_POINT(15);
   }
@@ -827,7 +849,8 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                           bool out_is_f32, int64_t o_stride_b, int64_t o_stride_h, float* out_lse, void* workspace,
                           int64_t workspace_bytes, int32_t* status_dev, void* stream,
                           const pl::QkvHeadArgs* fused = nullptr, const int32_t* slot_page = nullptr,
-                          const int32_t* slot_off = nullptr, void* q_out = nullptr) {
+                          const int32_t* slot_off = nullptr, void* q_out = nullptr, int fold = 1,
+                          int64_t counter_bytes = 0) {
   if (batch == 0) return PL_OK;
   if (fused != nullptr) {  // q comes from the projection row: validate that instead
     if (fused->qkv == nullptr || fused->positions == nullptr || slot_page == nullptr || slot_off == nullptr ||
@@ -842,14 +865,22 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
       num_splits < 1)
     return PL_ERR_INVALID_ARGUMENT;
   const int group = num_qo_heads / num_kv_heads;
-  if (group > 16 || (head_dim != 64 && head_dim != 128) || (page_size != 16 && page_size != 32))
+  if (fold < 1 || (fused != nullptr && fold != 1)) return PL_ERR_INVALID_ARGUMENT;
+  if (group * fold > 16 || (head_dim != 64 && head_dim != 128) || (page_size != 16 && page_size != 32))
     return PL_ERR_UNSUPPORTED;
+  const int vrows = (batch + fold - 1) / fold;  // page-table rows
   if ((reinterpret_cast<uintptr_t>(kv_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(q) & 15) != 0 ||
       (q_stride_b % 8) != 0 || (q_stride_h % 8) != 0 ||
       (reinterpret_cast<uintptr_t>(out) & (out_is_f32 ? 15 : 7)) != 0 || (o_stride_b % 4) != 0 ||
       (o_stride_h % 4) != 0)
     return PL_ERR_INVALID_ARGUMENT;
-  const int64_t need = decode_workspace_bytes(batch, num_qo_heads, num_kv_heads, head_dim, num_splits);
+  // counters per (page-table row, kv head), partial states per (query row, head);
+  // a caller may reserve a fixed counter region so that shapes can alternate
+  if (counter_bytes > 0 && counter_bytes < (int64_t)vrows * num_kv_heads * 4) return PL_ERR_WORKSPACE_TOO_SMALL;
+  const int64_t c_bytes = counter_bytes > 0 ? counter_bytes : align256((int64_t)vrows * num_kv_heads * 4);
+  const int64_t need = num_splits <= 1 ? c_bytes
+                                       : c_bytes + align256((int64_t)batch * num_qo_heads * num_splits * head_dim * 4) +
+                                             align256((int64_t)batch * num_qo_heads * num_splits * 4);
   if (num_splits > 1 && (workspace == nullptr || workspace_bytes < need)) return PL_ERR_WORKSPACE_TOO_SMALL;
 
   CUtensorMap map;
@@ -869,7 +900,9 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
   a.group = group;
   a.scale_log2 = sm_scale * pl::kLog2e;
   a.num_splits = num_splits;
-  a.cluster = use_cluster_merge(head_dim, page_size, num_splits, (int64_t)batch * num_kv_heads) ? 1 : 0;
+  a.fold = fold;
+  a.rows_real = batch;
+  a.cluster = use_cluster_merge(head_dim, page_size, num_splits, (int64_t)vrows * num_kv_heads) ? 1 : 0;
   a.fused = fused != nullptr ? 1 : 0;
   a.qh = fused != nullptr ? *fused : pl::QkvHeadArgs{};
   a.slot_page = slot_page;
@@ -886,17 +919,16 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
   a.partial_o = nullptr;
   a.partial_lse = nullptr;
   if (num_splits > 1) {
-    const int64_t c_bytes = align256((int64_t)batch * num_kv_heads * 4);
     const int64_t o_bytes = align256((int64_t)batch * num_qo_heads * num_splits * head_dim * 4);
     a.partial_o = reinterpret_cast<float*>(ws + c_bytes);
     a.partial_lse = reinterpret_cast<float*>(ws + c_bytes + o_bytes);
   }
   a.status = status_dev;
 
-  if (head_dim == 128 && page_size == 16) return launch_decode<128, 16>(map, a, batch, num_kv_heads, num_splits, stream);
-  if (head_dim == 128 && page_size == 32) return launch_decode<128, 32>(map, a, batch, num_kv_heads, num_splits, stream);
-  if (head_dim == 64 && page_size == 16) return launch_decode<64, 16>(map, a, batch, num_kv_heads, num_splits, stream);
-  return launch_decode<64, 32>(map, a, batch, num_kv_heads, num_splits, stream);
+  if (head_dim == 128 && page_size == 16) return launch_decode<128, 16>(map, a, vrows, num_kv_heads, num_splits, stream);
+  if (head_dim == 128 && page_size == 32) return launch_decode<128, 32>(map, a, vrows, num_kv_heads, num_splits, stream);
+  if (head_dim == 64 && page_size == 16) return launch_decode<64, 16>(map, a, vrows, num_kv_heads, num_splits, stream);
+  return launch_decode<64, 32>(map, a, vrows, num_kv_heads, num_splits, stream);
 }
 }  // namespace
 
@@ -922,6 +954,20 @@ extern "C" int32_t pl_paged_decode_f32(const void* q, int64_t q_stride_b, int64_
   return paged_decode_impl(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
                            num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, true,
                            o_stride_b, o_stride_h, out_lse, workspace, workspace_bytes, status_dev, stream);
+}
+
+extern "C" int32_t pl_paged_decode_shared(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                          const void* kv_cache, int64_t num_pages, const int32_t* indptr,
+                                          const int32_t* indices, const int32_t* last_page_len, int32_t batch,
+                                          int32_t fold, int32_t num_qo_heads, int32_t num_kv_heads,
+                                          int32_t head_dim, int32_t page_size, float sm_scale, int32_t num_splits,
+                                          void* out, int64_t o_stride_b, int64_t o_stride_h, float* out_lse,
+                                          int32_t flags, void* workspace, int64_t workspace_bytes,
+                                          int32_t* status_dev, void* stream) {
+  return paged_decode_impl(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
+                           num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out,
+                           (flags & PL_DECODE_OUT_F32) != 0, o_stride_b, o_stride_h, out_lse, workspace,
+                           workspace_bytes, status_dev, stream, nullptr, nullptr, nullptr, nullptr, fold);
 }
 
 extern "C" int32_t pl_paged_decode_qkv(const void* qkv, int64_t qkv_stride, const float* lora_down,
@@ -1000,9 +1046,13 @@ extern "C" int32_t pl_merge_states(const float* v_partial, const float* lse_part
 // workspace, for callers that cannot allocate device memory.  One array per
 // device (a __device__ variable exists once in every context); its address
 // is looked up, and the whole array cleared on the caller's stream, by the
-// first call on each device.
+// first call on each device.  Its first kFixedCounterBytes hold the arrival
+// counters whatever the shape, so that calls of different shapes may follow
+// one another (a shape-sized counter region would let one call's partials
+// land on another's counters).
 
 static __device__ __align__(256) uint8_t g_decode_fixed_scratch[PL_FIXED_SCRATCH_BYTES];
+constexpr int64_t kFixedCounterBytes = 64 * 1024;  // (row, kv head) pairs up to 16384
 
 namespace {
 constexpr int kScratchDevices = 64;
@@ -1041,12 +1091,18 @@ extern "C" int32_t pl_paged_decode_fixed_scratch(const void* q, int64_t q_stride
   if (batch == 0) return PL_OK;
   if (batch < 0 || num_kv_heads <= 0 || num_qo_heads <= 0 || head_dim <= 0 || num_splits < 1)
     return PL_ERR_INVALID_ARGUMENT;
-  if (decode_workspace_bytes(batch, num_qo_heads, num_kv_heads, head_dim, num_splits) > PL_FIXED_SCRATCH_BYTES)
+  const int64_t partial_bytes =
+      num_splits <= 1 ? 0
+                      : align256((int64_t)batch * num_qo_heads * num_splits * head_dim * 4) +
+                            align256((int64_t)batch * num_qo_heads * num_splits * 4);
+  if ((int64_t)batch * num_kv_heads * 4 > kFixedCounterBytes ||
+      kFixedCounterBytes + partial_bytes > PL_FIXED_SCRATCH_BYTES)
     return PL_ERR_WORKSPACE_TOO_SMALL;
   void* scratch = nullptr;
   int32_t st = fixed_scratch(stream, &scratch);
   if (st != PL_OK) return st;
-  return pl_paged_decode(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
-                         num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, o_stride_b,
-                         o_stride_h, out_lse, scratch, PL_FIXED_SCRATCH_BYTES, status_dev, stream);
+  return paged_decode_impl(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
+                           num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, false,
+                           o_stride_b, o_stride_h, out_lse, scratch, PL_FIXED_SCRATCH_BYTES, status_dev, stream,
+                           nullptr, nullptr, nullptr, nullptr, 1, kFixedCounterBytes);
 }

@@ -137,6 +137,42 @@ def paged_decode(
     return out
 
 
+def paged_decode_shared(
+    q: torch.Tensor,
+    kv_cache: torch.Tensor,
+    indptr: torch.Tensor,
+    indices: torch.Tensor,
+    last_page_len: torch.Tensor,
+    *,
+    fold: int,
+    num_splits: int,
+    workspace: torch.Tensor | None,
+    out: torch.Tensor,
+    out_lse: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
+    sm_scale: float | None = None,
+) -> torch.Tensor:
+    """Paged decode where query row b uses page-table row b // fold (rows
+    that share a page list read it once per `fold` rows); ``out`` bf16 or
+    fp32 [B, Hq, D]."""
+
+    _need_cuda(q, kv_cache, indptr, indices, last_page_len, out)
+    _need(q, torch.bfloat16, "q")
+    _need(kv_cache, torch.bfloat16, "kv_cache")
+    if kv_cache.dim() != 5 or kv_cache.size(1) != 2 or not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous [pages, 2, page_size, kv_heads, head_dim] tensor")
+    batch, hq, d = q.shape
+    num_pages, _, page_size, hkv, _ = kv_cache.shape
+    scale = (1.0 / math.sqrt(d)) if sm_scale is None else float(sm_scale)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    flags = _capi.PL_DECODE_OUT_F32 if out.dtype == torch.float32 else 0
+    call("pl_paged_decode_shared", ptr(q), q.stride(0), q.stride(1), ptr(kv_cache), int(num_pages), ptr(indptr),
+         ptr(indices), ptr(last_page_len), int(batch), int(fold), int(hq), int(hkv), int(d), int(page_size), scale,
+         int(num_splits), ptr(out), out.stride(0), out.stride(1), ptr(out_lse), int(flags), ptr(workspace),
+         int(ws_bytes), ptr(status), stream_handle())
+    return out
+
+
 def paged_decode_qkv(
     qkv: torch.Tensor,
     kv_cache: torch.Tensor,

@@ -96,3 +96,50 @@ def test_batch_decode_crosses_page_boundaries_and_random_pages(cuda_device):
             new.append(tok)
         nxt = new
     assert int(eng.status.item()) == 0
+
+
+SMALL_QWEN = ModelSpec("small-qwen3", 2, 512, 8, 2, 128, 1024, 4096, 1.0e6, 1e-6, qk_norm=True)
+
+
+@pytest.mark.parametrize("rows", [6, 10], ids=["6rows-gemv", "10rows-gemm"])
+def test_shared_prefix_branches_match_oracle(cuda_device, rows):
+    """Branch batch: rows continue one shared prefix (stored once) with their
+    own suffixes; decode runs the shared-prefix pass + suffix pass + merge.
+    Every row's logits equal an oracle decoder that ran prefix + suffix alone."""
+
+    from pagelora_b200.batch_engine import BatchDecodeEngine
+
+    spec, lspec = SMALL_QWEN, LoRASpec(16, 32.0, ("q", "k", "v", "o"))
+    w = make_model_weights(spec, seed=0, dtype=torch.float32, norm_jitter=0.1)
+    w = {k: v.bfloat16() for k, v in w.items()}
+    lo = make_lora_weights(spec, lspec, dtype=torch.bfloat16)
+    eng = BatchDecodeEngine(spec, dict(w), adapters=[lo], lora_spec=lspec, row_adapter=[0] * rows, page_size=16,
+                            max_context=160, device=cuda_device)
+    eng.shuffle_free_pages(seed=9)
+    prefix = random_prompt(spec.vocab, 48, seed=1)          # ends on a page boundary
+    rng = np.random.default_rng(rows)
+    suffixes = [random_prompt(spec.vocab, int(n), seed=20 + i) for i, n in enumerate(rng.integers(1, 30, size=rows))]
+    eng.prefill_shared(prefix, suffixes)
+    oracles, nxt = [], []
+    for suf in suffixes:
+        o = OracleDecoder(spec, {k: v.float() for k, v in w.items()},
+                          {k: (a.float(), b.float()) for k, (a, b) in lo.items()}, lspec.scale, page_size=16,
+                          num_pages=16, bf16=True)
+        tok = 0
+        for t in prefix + suf:
+            tok, _ = o.step(t)
+        oracles.append(o)
+        nxt.append(tok)
+    for step in range(4):
+        if step == 2:
+            eng.capture()
+        eng.step_host(nxt)
+        got = eng.logits.float().cpu().numpy()
+        new = []
+        for r, o in enumerate(oracles):
+            tok, lg = o.step(nxt[r])
+            err = float(np.max(np.abs(got[r] - lg)))
+            assert err < 0.1, (step, r, err)
+            new.append(tok)
+        nxt = new
+    assert int(eng.status.item()) == 0

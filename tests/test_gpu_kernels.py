@@ -270,6 +270,58 @@ def test_paged_decode_qkv_matches_rope_then_decode(K, d, hq, hkv, qk_norm):
                                                                    workspace=ws))[0], atol=2 ** -7 * 4)
 
 
+@pytest.mark.parametrize("rows,hq,hkv,fold", [(7, 32, 8, 4), (5, 16, 16, 16), (6, 8, 2, 3)])
+def test_paged_decode_shared_folded_rows(K, rows, hq, hkv, fold):
+    """Rows folded onto shared page-table rows (fold x group tile rows) equal
+    plain decode with the page lists repeated per row, for one split, the
+    cluster merge and the workspace merge; padding rows of the last fold are
+    not written."""
+
+    from pagelora_b200._capi import load_library
+
+    lib = load_library()
+    rng = np.random.default_rng(rows * 10 + fold)
+    ps, d = 16, 128
+    vrows = -(-rows // fold)
+    lens = rng.integers(1, 400, size=vrows).tolist()
+    pages = [-(-n // ps) for n in lens]
+    pool = sum(pages) + 4
+    cache = _t(bf16(rng.normal(size=(pool, 2, ps, hkv, d))))
+    perm = rng.permutation(pool).tolist()
+    lists, off = [], 0
+    for n in pages:
+        lists.append(perm[off:off + n])
+        off += n
+    last = [n - (p - 1) * ps for n, p in zip(lens, pages)]
+    q = _t(bf16(rng.normal(size=(rows, hq, d)) * 1.5))
+    v_indptr = _i32(np.cumsum([0] + pages))
+    v_idx = _i32([x for l in lists for x in l])
+    v_last = _i32(last)
+    row_lists = [lists[b // fold] for b in range(rows)]
+    r_indptr = _i32(np.cumsum([0] + [len(l) for l in row_lists]))
+    r_idx = _i32([x for l in row_lists for x in l])
+    r_last = _i32([last[b // fold] for b in range(rows)])
+    ws = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")      # one workspace per shape
+    ws_ref = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+    for splits in (1, 3, 16):
+        for cluster in (1, 0):
+            lib.pl_decode_set_cluster_merge(cluster)
+            try:
+                out = torch.full((rows, hq, d), float("nan"), device="cuda")
+                lse = torch.full((rows, hq), float("nan"), device="cuda")
+                K.paged_decode_shared(q, cache, v_indptr, v_idx, v_last, fold=fold, num_splits=splits, workspace=ws,
+                                      out=out, out_lse=lse)
+                ref_lse = torch.empty(rows, hq, device="cuda")
+                ref = K.paged_decode(q, cache, r_indptr, r_idx, r_last, num_splits=splits, workspace=ws_ref,
+                                     out=torch.empty(rows, hq, d, device="cuda"), out_lse=ref_lse)
+                torch.cuda.synchronize()
+            finally:
+                lib.pl_decode_set_cluster_merge(1)
+            assert torch.isfinite(out).all() and torch.isfinite(lse).all()
+            assert float((out - ref).abs().max()) <= 1e-4
+            assert float((lse - ref_lse).abs().max()) <= 1e-4
+
+
 def test_paged_decode_empty_row_and_long_context(K):
     out, lse, ref, ref_lse = _decode_case(K, batch=3, hq=32, hkv=8, d=128, ps=16, lens=[0, 2112, 7],
                                           num_splits=37, seed=5)

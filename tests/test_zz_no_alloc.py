@@ -82,6 +82,21 @@ def test_fixed_scratch_matches_workspace_entry_point(cuda_device, hq, hkv, d, ps
         np.testing.assert_allclose(lse, ref_lse, rtol=1e-3, atol=1e-3)
 
 
+def test_fixed_scratch_calls_of_different_shapes_in_a_row(cuda_device):
+    """The array is shared by every call: a call with few (row, kv head)
+    pairs followed by one with many must still find zeroed counters."""
+
+    small = _case(31, batch_lens=[300, 17], hq=32, hkv=8, d=128, ps=16)
+    large = _case(32, batch_lens=[40, 300, 1, 77, 500, 16, 33], hq=16, hkv=16, d=128, ps=16)
+    ws = {k: torch.zeros(8 << 20, dtype=torch.uint8, device="cuda") for k in ("s", "l")}
+    for _ in range(2):
+        for name, args in (("s", small), ("l", large)):
+            ref_o, ref_lse = _run("pl_paged_decode", *args, 7, workspace=ws[name])
+            o, lse = _run("pl_paged_decode_fixed_scratch", *args, 7)
+            assert np.max(np.abs(o - ref_o)) <= ATOL
+            np.testing.assert_allclose(lse, ref_lse, rtol=1e-3, atol=1e-3)
+
+
 def test_fixed_scratch_rejects_shapes_beyond_its_size(cuda_device):
     from pagelora_b200._capi import PL_ERR_WORKSPACE_TOO_SMALL, PageLoRAError
 
