@@ -318,6 +318,39 @@ int32_t pl_merge_states_strided(const float *v_partial, int64_t v_row_stride,
                                 int32_t head_dim, void *out, int64_t out_stride,
                                 float *out_lse, void *stream);
 
+/* ------------------------------------------------------ prefill attention */
+/*
+ * Ragged paged prefill attention on the tcgen05 tensor cores.  Replaces
+ * model/flashinfer/attention_backend.py:133-190 (plan_prefill + run_prefill:
+ * FlashInfer BatchPrefillWithPagedKVCacheWrapper, NHD, pos_encoding NONE,
+ * sm_scale = query_rescale / sqrt(D) applied to q / query_rescale, which is
+ * sm_scale = 1/sqrt(D) on q itself).  Nothing is planned on the host: the
+ * kernel finds each CTA's (request, query tile) from qo_indptr, so the call
+ * depends on the shapes only and can be captured once per total_q.
+ *   q           bf16, token t / head h at q + t*q_stride_t + h*q_stride_h
+ *               (strides in elements, multiples of 8; 16-byte aligned)
+ *   qo_indptr   int32 [batch+1]: request b owns tokens [qo_indptr[b], qo_indptr[b+1])
+ *   kv_*        the request's pages, as for pl_paged_decode; the queries are
+ *               the LAST qo_len positions of the kv_len keys (causal: query i
+ *               sees keys 0 .. kv_len - qo_len + i)
+ *   total_q     >= qo_indptr[batch]; sizes the grid and bounds every q/out access
+ *   out         bf16 like q; out_lse nullable fp32 [total_q, num_qo_heads], natural log
+ * head_dim 64 or 128, page_size 16/32/64/128, num_qo_heads / num_kv_heads
+ * <= 128.  Rows with no visible key get O = 0 (LSE -inf).  Device errors
+ * (PL_ERR_PAGE_OUT_OF_RANGE: the page reads as zeros; PL_ERR_INVALID_ARGUMENT:
+ * qo_indptr outside [0, total_q]) go to *status_dev.
+ */
+int32_t pl_paged_prefill(const void *q, int64_t q_stride_t, int64_t q_stride_h,
+                         const void *kv_cache, int64_t num_pages,
+                         const int32_t *qo_indptr, const int32_t *kv_indptr,
+                         const int32_t *kv_indices,
+                         const int32_t *kv_last_page_len, int32_t batch,
+                         int32_t total_q, int32_t num_qo_heads,
+                         int32_t num_kv_heads, int32_t head_dim,
+                         int32_t page_size, float sm_scale, int32_t causal,
+                         void *out, int64_t out_stride_t, int64_t out_stride_h,
+                         float *out_lse, int32_t *status_dev, void *stream);
+
 /* --------------------------------------------------------------- LoRA path */
 
 /*

@@ -93,6 +93,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pl_decode_cluster_capacity": (_I32, [_I32, _I32, _I32]),
     "pl_merge_states": (_I32, [_P, _P, _I32, _I32, _I32, _P, _I64, _P, _P]),
     "pl_merge_states_strided": (_I32, [_P, _I64, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _I64, _P, _P]),
+    "pl_paged_prefill": (
+        _I32,
+        [_P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64,
+         _P, _P, _P],
+    ),
     "pl_lora_shrink_seg": (_I32, [_P, _I64, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _I64, _P]),
     "pl_linear_lora_expand_fused": (
         _I32,

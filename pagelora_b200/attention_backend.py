@@ -16,8 +16,8 @@ creates its backend (model/flashinfer/generation.py:105-121, _make_backend):
 Decode runs the sm_100a paged decode kernel through the C ABI; the page
 table is copied into persistent, power-of-two sized device buffers at plan
 time (the reference's graph-safe buffers, :198-221), so a captured decode
-graph keeps valid pointers across replans.  Prefill is plain torch
-(gather the pages, causal SDPA): it is not on the decode hot path.
+graph keeps valid pointers across replans.  Prefill runs the sm_100a
+tcgen05 paged prefill kernel (ragged, causal) over the same page layout.
 There is no FlashInfer and no CPU path: a non-CUDA device raises.
 """
 
@@ -27,7 +27,6 @@ import math
 from collections import deque
 
 import torch
-import torch.nn.functional as F
 
 from pagelora_b200 import kernels as K
 
@@ -140,55 +139,44 @@ class B200AttentionBackend:
     def plan_prefill(self, *, qo_indptr: torch.Tensor, paged_kv_indptr: torch.Tensor,
                      paged_kv_indices: torch.Tensor, paged_kv_last_page_len: torch.Tensor, causal: bool = True,
                      q_data_type: torch.dtype | None = None, kv_data_type: torch.dtype | None = None) -> None:
-        """Record the ragged prefill layout (host lists; prefill is torch SDPA)."""
+        """Record the ragged prefill layout (:133-170).  Nothing is planned on
+        the host: the kernel finds each CTA's request and query tile from
+        qo_indptr, so only device copies of the four index arrays are kept."""
 
+        for dt in (q_data_type, kv_data_type):
+            if dt is not None and dt != torch.bfloat16:
+                raise NotImplementedError(f"B200 prefill kernel is bf16 only (got {dt})")
+        dev = dict(device=self.device, dtype=torch.int32)
         self._prefill_plan = {
-            "qo_indptr": [int(v) for v in qo_indptr.tolist()],
-            "kv_indptr": [int(v) for v in paged_kv_indptr.tolist()],
-            "kv_indices": paged_kv_indices.to(device=self.device, dtype=torch.long),
-            "last": [int(v) for v in paged_kv_last_page_len.tolist()],
+            "qo_indptr": qo_indptr.to(**dev).contiguous(),
+            "kv_indptr": paged_kv_indptr.to(**dev).contiguous(),
+            "kv_indices": paged_kv_indices.to(**dev).contiguous(),
+            "last": paged_kv_last_page_len.to(**dev).contiguous(),
             "causal": bool(causal),
         }
 
     def run_prefill(self, q: torch.Tensor, paged_kv_cache_layer: torch.Tensor) -> torch.Tensor:
-        """Paged prefill: q NHD [sum(qo), Hq, D] or BHSD [B, Hq, S, D] (:172-190)."""
+        """Paged prefill: q NHD [sum(qo), Hq, D] or BHSD [B, Hq, S, D] (:172-190).
+
+        The reference runs q / query_rescale with sm_scale = query_rescale /
+        sqrt(D); for the power-of-two rescale both scalings are exact, so the
+        kernel applies 1 / sqrt(D) to q itself."""
 
         if q.dim() == 4:
             bsz, num_heads, seqlen, head_dim = q.shape
             q_nhd = q.transpose(1, 2).reshape(bsz * seqlen, num_heads, head_dim)
-            out = self._prefill_nhd(q_nhd, paged_kv_cache_layer, default_rows=[seqlen] * bsz)
+            out = self._prefill_nhd(q_nhd, paged_kv_cache_layer)
             return out.reshape(bsz, seqlen, num_heads, head_dim).transpose(1, 2).contiguous()
-        return self._prefill_nhd(q, paged_kv_cache_layer, default_rows=[q.shape[0]])
+        return self._prefill_nhd(q, paged_kv_cache_layer)
 
-    def _prefill_nhd(self, q: torch.Tensor, cache: torch.Tensor, *, default_rows: list[int]) -> torch.Tensor:
+    def _prefill_nhd(self, q: torch.Tensor, cache: torch.Tensor) -> torch.Tensor:
         plan = self._prefill_plan
         if plan is None:
             raise RuntimeError("plan_prefill must be called before run_prefill")
-        ps = cache.shape[2]
-        out = torch.empty_like(q)
-        group = self.num_qo_heads // self.num_kv_heads
-        for b in range(len(plan["last"])):
-            q0, q1 = plan["qo_indptr"][b], plan["qo_indptr"][b + 1]
-            p0, p1 = plan["kv_indptr"][b], plan["kv_indptr"][b + 1]
-            if q1 <= q0:
-                continue
-            pages = plan["kv_indices"][p0:p1]
-            n_kv = (p1 - p0 - 1) * ps + plan["last"][b] if p1 > p0 else 0
-            k = cache[pages, 0].reshape(-1, self.num_kv_heads, self.head_dim)[:n_kv]
-            v = cache[pages, 1].reshape(-1, self.num_kv_heads, self.head_dim)[:n_kv]
-            qb = q[q0:q1].transpose(0, 1)[None]
-            kb = k.transpose(0, 1)[None].repeat_interleave(group, dim=1)
-            vb = v.transpose(0, 1)[None].repeat_interleave(group, dim=1)
-            n_q = q1 - q0
-            mask = None
-            if plan["causal"]:
-                # queries are the last n_q positions of the n_kv keys
-                i = torch.arange(n_q, device=q.device)[:, None] + (n_kv - n_q)
-                j = torch.arange(n_kv, device=q.device)[None, :]
-                mask = j <= i
-            o = F.scaled_dot_product_attention(qb, kb, vb, attn_mask=mask, scale=1.0 / math.sqrt(self.head_dim))
-            out[q0:q1] = o[0].transpose(0, 1).to(out.dtype)
-        return out
+        if q.stride(-1) != 1 or q.stride(0) % 8 or q.stride(1) % 8 or q.data_ptr() % 16:
+            q = q.contiguous()
+        return K.paged_prefill(q, cache, plan["qo_indptr"], plan["kv_indptr"], plan["kv_indices"], plan["last"],
+                               causal=plan["causal"], sm_scale=1.0 / math.sqrt(self.head_dim), status=self.status)
 
 
 # Name of the reference class, for injection by name.

@@ -26,8 +26,6 @@ namespace pl {
 
 constexpr int kConsumerWarps = 6;
 constexpr int kDecodeThreads = 32 * (1 + kConsumerWarps);
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
 
 struct DecodeArgs {
   const bf16* q;
@@ -313,6 +311,18 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
         __syncwarp();
       }
       const int ntok = stage_ntok[s];
+      if (ntok > 0 && ntok < PS) {
+        // Slots past the last token hold whatever the pool had there (the
+        // reference allocates it uninitialised): their p is 0, but 0 * NaN
+        // is NaN, so clear those V rows of the staged page.
+        constexpr int kRowUnits = 8 * C::kHalves;
+        uint8_t* vt = smem + C::kStageOff + s * C::kStageBytes + C::kTileBytes;
+        for (int idx = lane; idx < (PS - ntok) * kRowUnits; idx += 32) {
+          const int r = ntok + idx / kRowUnits, hh = (idx % kRowUnits) / 8, c = idx % 8;
+          *reinterpret_cast<uint4*>(vt + hh * C::kHalfBytes + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
       if (ntok > 0) {
         const uint8_t* kbase = smem + C::kStageOff + s * C::kStageBytes;
         const uint8_t* vbase = kbase + C::kTileBytes;
@@ -684,6 +694,9 @@ struct MapCache {
 };
 MapCache g_maps;
 
+}  // namespace
+
+namespace pl_host {
 // Tensor map over one layer's pool viewed as [2*P][PS][Hkv][D] (innermost last):
 // dims (inner->outer) {D, Hkv, PS, 2P}, box {64, 1, PS, 1}, 128B swizzle.
 int32_t kv_tensor_map(const void* cache, int64_t pages, int hkv, int d, int ps, CUtensorMap* out) {
@@ -719,6 +732,9 @@ int32_t kv_tensor_map(const void* cache, int64_t pages, int hkv, int d, int ps, 
   *out = m;
   return PL_OK;
 }
+}  // namespace pl_host
+
+namespace {
 
 int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
@@ -884,7 +900,7 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
   if (num_splits > 1 && (workspace == nullptr || workspace_bytes < need)) return PL_ERR_WORKSPACE_TOO_SMALL;
 
   CUtensorMap map;
-  int32_t st = kv_tensor_map(kv_cache, num_pages, num_kv_heads, head_dim, page_size, &map);
+  int32_t st = pl_host::kv_tensor_map(kv_cache, num_pages, num_kv_heads, head_dim, page_size, &map);
   if (st != PL_OK) return st;
 
   pl::DecodeArgs a;

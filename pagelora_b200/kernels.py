@@ -269,6 +269,49 @@ def merge_states_strided(v_partial: torch.Tensor, lse_partial: torch.Tensor, out
     return out
 
 
+# ------------------------------------------------------- prefill attention
+def paged_prefill(
+    q: torch.Tensor,
+    kv_cache: torch.Tensor,
+    qo_indptr: torch.Tensor,
+    kv_indptr: torch.Tensor,
+    kv_indices: torch.Tensor,
+    kv_last_page_len: torch.Tensor,
+    *,
+    causal: bool = True,
+    sm_scale: float | None = None,
+    out: torch.Tensor | None = None,
+    out_lse: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Ragged paged prefill attention: q [total_q, Hq, D] bf16 (NHD), request b
+    owns tokens qo_indptr[b]:qo_indptr[b+1], which are the last positions of
+    its kv_len keys; ``out`` bf16 like q, ``out_lse`` fp32 [total_q, Hq]."""
+
+    _need_cuda(q, kv_cache, qo_indptr, kv_indptr, kv_indices, kv_last_page_len)
+    _need(q, torch.bfloat16, "q")
+    _need(kv_cache, torch.bfloat16, "kv_cache")
+    if kv_cache.dim() != 5 or kv_cache.size(1) != 2 or not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous [pages, 2, page_size, kv_heads, head_dim] tensor")
+    if q.dim() != 3 or q.stride(-1) != 1:
+        raise ValueError("q must be [tokens, qo_heads, head_dim] with unit last stride")
+    for name, t in (("qo_indptr", qo_indptr), ("kv_indptr", kv_indptr), ("kv_indices", kv_indices),
+                    ("kv_last_page_len", kv_last_page_len)):
+        _need(t, torch.int32, name)
+    total_q, hq, d = q.shape
+    num_pages, _, page_size, hkv, d2 = kv_cache.shape
+    if d2 != d:
+        raise ValueError("q and kv_cache head_dim differ")
+    if out is None:
+        out = torch.empty_like(q)
+    scale = (1.0 / math.sqrt(d)) if sm_scale is None else float(sm_scale)
+    call("pl_paged_prefill", ptr(q), q.stride(0), q.stride(1), ptr(kv_cache), int(num_pages), ptr(qo_indptr),
+         ptr(kv_indptr), ptr(kv_indices), ptr(kv_last_page_len), int(qo_indptr.numel() - 1), int(total_q), int(hq),
+         int(hkv), int(d), int(page_size), scale, 1 if causal else 0, ptr(out), out.stride(0), out.stride(1),
+         ptr(out_lse), ptr(status), stream_handle())
+    return out
+
+
 # --------------------------------------------------------------- LoRA path
 def lora_shrink_seg(x: torch.Tensor, a_stack: torch.Tensor, seg_indptr: torch.Tensor,
                     seg_adapter: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -140,7 +140,7 @@ def test_page_table_advance_vs_oracle(K):
 
 
 # ------------------------------------------------------- decode attention
-def _decode_case(K, *, batch, hq, hkv, d, ps, lens, num_splits, seed, n_pages_pool=None, ws_mb=8):
+def _decode_case(K, *, batch, hq, hkv, d, ps, lens, num_splits, seed, n_pages_pool=None, ws_mb=8, poison=False):
     rng = np.random.default_rng(seed)
     pages_per_row = [-(-L // ps) for L in lens]
     total = sum(pages_per_row)
@@ -150,6 +150,13 @@ def _decode_case(K, *, batch, hq, hkv, d, ps, lens, num_splits, seed, n_pages_po
     indptr = np.cumsum([0] + pages_per_row).tolist()
     indices = perm.tolist()
     last = [L - (n - 1) * ps if n else 0 for L, n in zip(lens, pages_per_row)]
+    if poison:
+        # NaN in every slot no row owns (the reference's pool is uninitialised)
+        owned = np.zeros((pool, ps), dtype=bool)
+        for r in range(batch):
+            for j, pg in enumerate(indices[indptr[r]:indptr[r + 1]]):
+                owned[pg, : (ps if j < pages_per_row[r] - 1 else last[r])] = True
+        cache = np.where(owned[:, None, :, None, None], cache, np.float32(np.nan)).astype(np.float32)
     q = bf16(rng.normal(size=(batch, hq, d)) * 1.5)
     ws = torch.zeros(ws_mb << 20, dtype=torch.uint8, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -171,6 +178,20 @@ def test_paged_decode_vs_oracle(K, d, ps, hq, hkv):
     for splits in (1, 3, 16):
         out, lse, ref, ref_lse = _decode_case(K, batch=len(lens), hq=hq, hkv=hkv, d=d, ps=ps, lens=lens,
                                               num_splits=splits, seed=hq * 7 + d + ps + splits)
+        assert np.max(np.abs(out - ref)) <= ATOL
+        np.testing.assert_allclose(lse, ref_lse, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("d,ps", [(128, 16), (64, 32)])
+def test_paged_decode_ignores_nan_past_last_token(K, d, ps):
+    """Slots past a row's last token (and pages no row owns) hold NaN: p = 0
+    there must not turn into 0 * NaN."""
+
+    lens = [1, ps - 3, 3 * ps + 5, 200]
+    for splits in (1, 4):
+        out, lse, ref, ref_lse = _decode_case(K, batch=len(lens), hq=16, hkv=4, d=d, ps=ps, lens=lens,
+                                              num_splits=splits, seed=splits + d, poison=True)
+        assert np.isfinite(out).all() and np.isfinite(lse).all()
         assert np.max(np.abs(out - ref)) <= ATOL
         np.testing.assert_allclose(lse, ref_lse, rtol=1e-3, atol=1e-3)
 

@@ -20,6 +20,7 @@ from oracle import page_table as opt
 from oracle.decoder import OracleDecoder
 from oracle.numerics import bf16
 from oracle.paged_decode import merge_states, paged_decode, split_states
+from oracle.paged_prefill import paged_prefill
 
 
 def test_page_table_known_answers():
@@ -125,6 +126,44 @@ def test_decode_finite_mask_known_answer():
     assert out[0, 0, 0] == 1.0
     out, _ = paged_decode(np.full((1, 1, 1), 0.0, np.float32), cache, [0, 1], [0], [2])
     assert out[0, 0, 0] == pytest.approx(5.0)
+
+
+def test_prefill_finite_mask_known_answer():
+    """Restates test/test_flashinfer_backend.py:157-177 (the reference's
+    prefill test): causal query 0 sees key 0 only, query 1 sees both equal
+    scores."""
+
+    cache = np.zeros((1, 2, 2, 1, 1), np.float32)
+    cache[0, 0, :, 0, 0] = 100.0
+    cache[0, 1, :, 0, 0] = [1.0, 9.0]
+    q = np.full((2, 1, 1), -1000.0, np.float32)
+    out, _ = paged_prefill(q, cache, [0, 2], [0, 1], [0], [2])
+    assert out[:, 0, 0].tolist() == [1.0, 5.0]
+
+
+def test_prefill_rows_equal_decodes_over_visible_prefix():
+    """Causal prefill query i (of the last qo_len positions) equals a decode
+    over the first kv_len - qo_len + i + 1 keys; non-causal equals a decode
+    over all keys."""
+
+    rng = np.random.default_rng(4)
+    ps, n_pages = 16, 7
+    cache = bf16(rng.normal(size=(n_pages, 2, ps, 2, 64)))
+    pages = list(rng.permutation(n_pages)[:5])
+    kv_len, qo = 70, 9
+    q = bf16(rng.normal(size=(qo, 8, 64)))
+    last = kv_len - 4 * ps
+    out, lse = paged_prefill(q, cache, [0, qo], [0, 5], pages, [last])
+    for i in range(qo):
+        vis = kv_len - qo + i + 1
+        n = -(-vis // ps)
+        d_out, d_lse = paged_decode(q[i:i + 1], cache, [0, n], pages[:n], [vis - (n - 1) * ps])
+        np.testing.assert_allclose(out[i], d_out[0], rtol=1e-12, atol=1e-12)
+        np.testing.assert_allclose(lse[i], d_lse[0], rtol=1e-12)
+    out_nc, _ = paged_prefill(q, cache, [0, qo], [0, 5], pages, [last], causal=False)
+    for i in range(qo):
+        d_out, _ = paged_decode(q[i:i + 1], cache, [0, 5], pages, [last])
+        np.testing.assert_allclose(out_nc[i], d_out[0], rtol=1e-12, atol=1e-12)
 
 
 def test_split_merge_equals_full():
