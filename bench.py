@@ -449,6 +449,79 @@ def run_config5(ws: int, rank: int, device, barrier, group, steps: int, warmup: 
     return out
 
 
+def _bf16_peak() -> tuple[float, str]:
+    """Dense bf16 tensor peak (burst figure: the prefill launch is timed alone)."""
+
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def run_prefill(device, steps: int, warmup: int) -> dict:
+    """Paged prefill attention (pl_paged_prefill), one causal request per
+    launch: config 2's 2048-token prompt (Qwen3-8B heads) and config 5's
+    32768-token context (Llama-3-8B heads), page size 16, shuffled pages,
+    random q / K / V.  One launch is one layer's attention; FLOPs count the
+    causal visible keys only (4 * D * Hq per query-key pair).  L2 is flushed
+    (a 256 MB write) before every timed launch; the timing excludes it."""
+
+    import torch
+
+    from pagelora_b200 import kernels as K
+    from pagelora_b200.synthetic import WORKLOADS
+
+    peak, kind = _bf16_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    out = {}
+    for name, tokens in (("config2", 2048), ("config5", 32768)):
+        spec = WORKLOADS[name].model
+        hq, hkv, d, ps = spec.num_qo_heads, spec.num_kv_heads, spec.head_dim, 16
+        n_pages = -(-tokens // ps)
+        g = torch.Generator(device=device).manual_seed(tokens)
+        cache = torch.randn(n_pages + 7, 2, ps, hkv, d, generator=g, device=device).to(torch.bfloat16)
+        pages = torch.randperm(n_pages + 7, generator=g, device=device)[:n_pages].to(torch.int32)
+        q = torch.randn(tokens, hq, d, generator=g, device=device).to(torch.bfloat16)
+        i32 = dict(dtype=torch.int32, device=device)
+        qo = torch.tensor([0, tokens], **i32)
+        kvp = torch.tensor([0, n_pages], **i32)
+        last = torch.tensor([tokens - (n_pages - 1) * ps], **i32)
+        status = torch.zeros(1, **i32)
+        o = torch.empty_like(q)
+        for _ in range(warmup):
+            K.paged_prefill(q, cache, qo, kvp, pages, last, out=o, status=status)
+        torch.cuda.synchronize(device)
+        total = 0.0
+        for _ in range(steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            K.paged_prefill(q, cache, qo, kvp, pages, last, out=o, status=status)
+            e1.record()
+            torch.cuda.synchronize(device)
+            total += e0.elapsed_time(e1)
+        if int(status.item()) != 0:
+            raise RuntimeError(f"prefill status {int(status.item())}")
+        ms = total / steps
+        flops = 4.0 * d * hq * tokens * (tokens + 1) / 2
+        tf = flops / (ms * 1e-3) / 1e12
+        out[name] = {"metric": f"causal prefill attention, one {tokens}-token request ({spec.name} heads {hq}/{hkv}, "
+                               f"head_dim {d}, page 16)", "value": tf, "unit": "TFLOP/s", "ms_per_launch": ms,
+                     "flops_per_launch": flops, "tokens": tokens,
+                     "tokens_per_s_per_layer": tokens / (ms * 1e-3), "steps": steps, "warmup": warmup,
+                     "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                  "frac": tf / peak, "peak_kind": kind},
+                     "l2": "flushed (256 MB write) before every timed launch", "gpu_launches_per_step": 1,
+                     "data": "synthetic: random q/K/V, shuffled pages"}
+        del cache, q, o
+    del flush
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -468,6 +541,13 @@ def run_ours(args) -> None:
     if plbuild.is_stale():
         plbuild.build()
     load_library()
+    if args.prefill_only:  # profiling runs of the prefill kernel alone
+        pf = run_prefill(device, max(1, args.steps), max(3, args.warmup))
+        if rank == 0:
+            print(json.dumps({"profile": "prefill", **{k: v["value"] for k, v in pf.items()}}), flush=True)
+        if ws > 1:
+            dist.destroy_process_group()
+        return
     wl = WORKLOADS[WORKLOAD]
     spec = wl.model
     if args.layers:
@@ -588,6 +668,21 @@ def run_ours(args) -> None:
             "frac_of_peak_per_gpu": c5_bytes / ws / (c5["ms_per_step"] * 1e-3) / 1e9 / peak,
             "gpu_launches_per_step_per_gpu": c5["launches_per_step"],
             "data": "synthetic: random-init weights, random K/V contexts"}
+        # prefill attention (every rank runs the same launches; the slowest rank counts)
+        pf = run_prefill(device, xs, xw)
+        pt = torch.tensor([pf[k]["ms_per_launch"] for k in ("config2", "config5")], device=device,
+                          dtype=torch.float64)
+        if ws > 1:
+            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        for i, k in enumerate(("config2", "config5")):
+            r = pf[k]
+            r["ms_per_launch"] = float(pt[i])
+            r["value"] = r["flops_per_launch"] / (r["ms_per_launch"] * 1e-3) / 1e12
+            r["tokens_per_s_per_layer"] = r["tokens"] / (r["ms_per_launch"] * 1e-3)
+            r["roofline"]["achieved"] = r["value"]
+            r["roofline"]["frac"] = r["value"] / r["roofline"]["peak"]
+            r["scaling"] = f"replicas x{ws}" if ws > 1 else "1 GPU"
+            extra[f"prefill_{k}"] = r
     if rank == 0:
         value = ws * steps / (ms * 1e-3)
         e2e = ws * steps / (ms_e2e * 1e-3)
@@ -634,6 +729,8 @@ def main() -> None:
                     help="profiling run: prefill, capture and the timed graph replays only")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the secondary workloads (configs 3, 4 and 5) after the headline measurement")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="profiling run: the paged prefill attention workloads only")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling run on the first L layers (same per-layer shapes)")
     args = ap.parse_args()

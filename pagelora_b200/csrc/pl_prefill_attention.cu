@@ -4,35 +4,40 @@
 // model/flashinfer/attention_backend.py:133-190 (pos_encoding_mode NONE, NHD
 // layout, sm_scale = query_rescale / sqrt(D) on q / query_rescale).
 //
-// One CTA takes one (request, query tile, kv head).  A query tile is 128
-// tensor-core rows = TQ tokens x the `group` query heads that share the kv
-// head (TQ = 128 / group), so every K/V tile is read once for the group.
-// The request's kv tokens are visited in tiles of 128 (128 / page_size pages)
-// up to the last position the tile's queries may see.  Per CTA:
-//   warp 0     TMA producer: one lane per (page, K/V, 64-dim half) box, all
-//              boxes of a kv tile in one instruction, a 2-stage ring; pages
-//              past the request's end load from an out-of-range coordinate,
-//              which the copy fills with zeros;
-//   warp 1     one lane issues tcgen05.mma: S_j = Q.K_j^T into one of two
-//              TMEM score buffers, then O += P_{j-1}.V_{j-1} into the TMEM
-//              output accumulator (V as an MN-major operand, no transpose);
-//   warps 2-5  one thread per tile row: stage the row's q into shared memory,
-//              then per kv tile read the row's scores from TMEM, apply the
-//              causal / length mask, run the online softmax in the log2
-//              domain, write P (bf16) into a swizzled shared-memory tile for
-//              the P.V product, and at the end normalise O from TMEM and store
-//              it.  The output is rescaled only when a row's running maximum
-//              grows by more than 2^8 (P stays <= 256 otherwise), so most
-//              tiles never touch O.
+// One CTA takes one (request, pair of query tiles, kv head).  A query tile
+// is 128 tensor-core rows = TQ tokens x the `group` query heads that share
+// the kv head (TQ = 128 / group), so every K/V tile is read once for 2 x 128
+// rows.  The request's kv tokens are visited in tiles of 128 (128 / page_size
+// pages) up to the last position the pair's queries may see.  Per CTA:
+//   warp 0     TMA producer: K_0, V_0, K_1, V_1, ... through a 3-slot ring,
+//              one lane per (page, 64-dim half) box, one instruction per
+//              tile half; pages past the request's end load from an
+//              out-of-range coordinate, which the copy fills with zeros;
+//   warp 1     one lane issues tcgen05.mma in ping-pong order
+//                S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) ...
+//              (S_X = Q_X.K^T into tile X's TMEM score columns, PV_X = P_X.V
+//              accumulated into its TMEM output columns, V an MN-major
+//              operand), so each softmax group works while the tensor core
+//              runs the other tile's products;
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one thread per tile
+//              row stages the row's q, then per kv tile reads the row's
+//              scores from TMEM, masks (causal / length), runs the online
+//              softmax in the log2 domain and writes P (bf16) into the
+//              tile's swizzled shared-memory P operand; at the end it
+//              normalises O from TMEM and stores it.  Scores are
+//              exponentiated against the running row maximum in one pass;
+//              only a row whose maximum grows by more than 2^8 (and the
+//              first tile) takes a max pass first and rescales O.
 // Waits are bounded; on expiry the kernel records PL_ERR_TIMEOUT, lets its
 // copies and tensor-core work drain (bounded) and returns.
 #include "pl_common.cuh"
 
 namespace pl {
 
-constexpr int kPrefillThreads = 192;
-constexpr int kPrefillM = 128;  // tile rows
-constexpr int kPrefillN = 128;  // kv tokens per tile
+constexpr int kPrefillThreads = 320;
+constexpr int kPrefillM = 128;         // rows of one query tile
+constexpr int kPrefillN = 128;         // kv tokens per tile
+constexpr int kPrefillSlots = 3;       // K/V ring slots (one K or V tile each)
 constexpr float kRescaleSlack = 8.0f;  // log2 growth of the row max tolerated before rescaling O
 
 struct PrefillArgs {
@@ -53,28 +58,32 @@ struct PrefillArgs {
 
 template <int D>
 struct PrefillCfg {
-  static constexpr int kChunks = D / 64;                  // 64-dim (128-byte) column chunks
-  static constexpr int kChunkBytes = kPrefillM * 128;     // one chunk of a 128-row tile: 16 KB
-  static constexpr int kQBytes = kChunks * kChunkBytes;
-  static constexpr int kKVTileBytes = kChunks * kChunkBytes;  // K (or V) of 128 kv tokens
-  static constexpr int kStageBytes = 2 * kKVTileBytes;
-  static constexpr int kStages = 2;
-  static constexpr int kPBytes = 2 * kChunkBytes;         // P: 128 rows x 128 kv bf16
-  static constexpr int kQOff = 0;
-  static constexpr int kStageOff = kQOff + kQBytes;
-  static constexpr int kPOff = kStageOff + kStages * kStageBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
-  // full[2] empty[2] sready[2] pready[2] odone[2] qready fin
-  static constexpr int kNumBars = 12;
+  static constexpr int kChunks = D / 64;                   // 64-dim (128-byte) column chunks
+  static constexpr int kChunkBytes = kPrefillM * 128;      // one chunk of a 128-row tile: 16 KB
+  static constexpr int kQBytes = kChunks * kChunkBytes;    // one query tile
+  static constexpr int kKVBytes = kChunks * kChunkBytes;   // K (or V) of 128 kv tokens
+  static constexpr int kPBytes = 2 * kChunkBytes;          // P: 128 rows x 128 kv bf16
+  static constexpr int kQOff = 0;                          // Q_A, Q_B
+  static constexpr int kPOff = kQOff + 2 * kQBytes;        // P_A, P_B
+  static constexpr int kSlotOff = kPOff + 2 * kPBytes;     // K/V ring
+  static constexpr int kBarOff = kSlotOff + kPrefillSlots * kKVBytes;
+  // full[3] empty[3] s[2] p[2] o[2] q[2] fin
+  static constexpr int kNumBars = 2 * kPrefillSlots + 9;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, flags
   static constexpr int kSmemBytes = 1024 + kMiscOff + 64;
-  static constexpr int kTmemCols = 512;                    // S0 [0,128) S1 [128,256) O [256, 256+D)
-  static constexpr int kOCol = 256;
+  static constexpr int kTmemCols = 512;                    // S_A 0, S_B 128, O_A 256, O_B 384
   static_assert(kSmemBytes <= 232448, "prefill tiles exceed the shared-memory limit");
 };
 
 // Byte offset of 16-byte unit `u` of row `r` in a 128B-swizzled K-major chunk.
 __device__ __forceinline__ uint32_t pf_swz(int r, int u) { return r * 128 + ((u ^ (r & 7)) << 4); }
+
+// 2^x on the multi-function unit (PTX ex2.approx, flush-to-zero); x = -inf gives 0.
+__device__ __forceinline__ float pf_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int D>
 __global__ void __launch_bounds__(kPrefillThreads, 1)
@@ -83,27 +92,29 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-  uint64_t* full = bars;        // [2] kv tile landed
-  uint64_t* empty = bars + 2;   // [2] kv stage free (after P.V)
-  uint64_t* sready = bars + 4;  // [2] scores S_j in TMEM
-  uint64_t* pready = bars + 6;  // [2] P_j in shared memory (128 arrivals)
-  uint64_t* odone = bars + 8;   // [2] O += P_j.V_j finished
-  uint64_t* qready = bars + 10; // q tile staged (128 arrivals)
-  uint64_t* fin = bars + 11;    // every tensor-core op of the CTA finished
+  uint64_t* full = bars;                          // [3] ring slot landed
+  uint64_t* empty = bars + kPrefillSlots;         // [3] ring slot free
+  uint64_t* sready = bars + 2 * kPrefillSlots;    // [2] S_X in TMEM
+  uint64_t* pready = sready + 2;                  // [2] P_X in shared memory (128 arrivals)
+  uint64_t* odone = sready + 4;                   // [2] O_X += P_X.V finished
+  uint64_t* qready = sready + 6;                  // [2] Q_X staged (128 arrivals)
+  uint64_t* fin = sready + 8;                     // every tensor-core op of the CTA finished
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int32_t* flags = reinterpret_cast<volatile int32_t*>(smem + C::kMiscOff + 16);  // abort, issued, consumed
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int kvh = blockIdx.y;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kPrefillSlots; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
-      mbar_init(&sready[i], 1);
-      mbar_init(&pready[i], 128);
-      mbar_init(&odone[i], 1);
     }
-    mbar_init(qready, 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&sready[x], 1);
+      mbar_init(&pready[x], 128);
+      mbar_init(&odone[x], 1);
+      mbar_init(&qready[x], 128);
+    }
     mbar_init(fin, 1);
     flags[0] = flags[1] = flags[2] = 0;
     fence_barrier_init();
@@ -113,16 +124,17 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   pdl_launch_dependents();
   pdl_wait();  // q, the page table and the KV pages come from upstream kernels
 
-  // ---- this CTA's (request, query tile): heavier (later) tiles of a request first
-  int req = -1, tile = 0, qo_begin = 0, qlen = 0;
+  // ---- this CTA's (request, tile pair): heavier (later) pairs of a request first
+  const int tq2 = 2 * a.tq;
+  int req = -1, pair = 0, qo_begin = 0, qlen = 0;
   {
     int acc = 0;
     for (int b = 0; b < a.batch; ++b) {
       const int q0 = a.qo_indptr[b], q1 = a.qo_indptr[b + 1];
-      const int n = q1 > q0 ? (q1 - q0 + a.tq - 1) / a.tq : 0;
+      const int n = q1 > q0 ? (q1 - q0 + tq2 - 1) / tq2 : 0;
       if ((int)blockIdx.x < acc + n) {
         req = b;
-        tile = n - 1 - ((int)blockIdx.x - acc);
+        pair = n - 1 - ((int)blockIdx.x - acc);
         qo_begin = q0;
         qlen = q1 - q0;
         break;
@@ -133,7 +145,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   if (blockIdx.x == 0 && kvh == 0 && threadIdx.x == 0) {
     if (a.qo_indptr[0] < 0 || a.qo_indptr[a.batch] > a.total_q) set_status(a.status, PL_ERR_INVALID_ARGUMENT);
   }
-  if (req < 0) return;  // past the last tile: nothing allocated yet
+  if (req < 0) return;  // past the last pair: nothing allocated yet
   if (qo_begin < 0 || qo_begin + qlen > a.total_q) {
     if (threadIdx.x == 0) set_status(a.status, PL_ERR_INVALID_ARGUMENT);
     return;
@@ -144,11 +156,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   int last = a.kv_last[req];
   last = last < 0 ? 0 : (last > PS ? PS : last);
   const int kv_len = n_pages > 0 ? (n_pages - 1) * PS + last : 0;
-  const int t0 = tile * a.tq;
-  const int t1 = min(t0 + a.tq, qlen);
-  int n_vis = a.causal ? kv_len - qlen + t1 : kv_len;  // kv positions the tile's queries may see
+  const int t0 = pair * tq2;
+  const int t1 = min(t0 + tq2, qlen);
+  int n_vis = a.causal ? kv_len - qlen + t1 : kv_len;  // kv positions the pair's queries may see
   n_vis = n_vis < 0 ? 0 : (n_vis > kv_len ? kv_len : n_vis);
   const int ntiles = (n_vis + kPrefillN - 1) / kPrefillN;
+  // The CTAs resident at one time mostly share a kv head and would walk the
+  // same K/V tiles in lock-step, all hitting the same L2 lines; each starts
+  // at its own tile instead (online softmax is order-free).
+  const int rot = ntiles > 1 ? (int)(((unsigned)pair * 7u + (unsigned)kvh * 3u) % (unsigned)ntiles) : 0;
+  auto tile_of = [&](int it) { return it + rot < ntiles ? it + rot : it + rot - ntiles; };
 
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -161,23 +178,24 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    const int ppt = kPrefillN / PS;                 // pages per kv tile
-    const int boxes = ppt * 2 * C::kChunks;         // <= 32 (host checks)
-    const int p = lane / (2 * C::kChunks), kv = (lane / C::kChunks) & 1, hh = lane % C::kChunks;
-    int j = 0;
-    for (; j < ntiles; ++j) {
-      const int s = j & 1;
+    // item i: tile i / 2, K (even) or V (odd), ring slot i % 3
+    const int ppt = kPrefillN / PS;       // pages per kv tile
+    const int boxes = ppt * C::kChunks;   // <= 16 (host checks)
+    const int p = lane / C::kChunks, hh = lane % C::kChunks;
+    int i = 0;
+    for (; i < 2 * ntiles; ++i) {
+      const int s = i % kPrefillSlots;
       bool ok = true;
-      if (j >= 2) ok = mbar_wait(&empty[s], ((j >> 1) - 1) & 1);
+      if (i >= kPrefillSlots) ok = mbar_wait(&empty[s], ((i / kPrefillSlots) - 1) & 1);
       if (__any_sync(0xffffffffu, !ok || flags[0] != 0)) {  // one decision for the whole warp
         if (lane == 0 && !__all_sync(0xffffffffu, ok)) set_status(a.status, PL_ERR_TIMEOUT);
         flags[0] = 1;
         break;
       }
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], C::kKVBytes);
       __syncwarp();
       if (lane < boxes) {
-        const int page_idx = j * ppt + p;
+        const int kv = i & 1, page_idx = tile_of(i >> 1) * ppt + p;
         int32_t coord = (int32_t)(2 * a.num_pages);  // out of range: the copy writes zeros
         if (page_idx < n_pages) {
           const int32_t pid = a.kv_indices[kv_begin + page_idx];
@@ -186,51 +204,72 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           else
             set_status(a.status, PL_ERR_PAGE_OUT_OF_RANGE);
         }
-        uint8_t* dst = smem + C::kStageOff + s * C::kStageBytes + kv * C::kKVTileBytes + hh * C::kChunkBytes +
-                       p * PS * 128;
+        uint8_t* dst = smem + C::kSlotOff + s * C::kKVBytes + hh * C::kChunkBytes + p * PS * 128;
         tma_load_4d(dst, &kv_map, hh * 64, kvh, 0, coord, &full[s]);
       }
     }
-    if (lane == 0) flags[1] = j;
+    if (lane == 0) flags[1] = i;
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kPrefillM, kPrefillN);
       constexpr uint32_t idesc_o = umma_idesc_bf16(kPrefillM, D) | (1u << 16);  // B (V) MN-major
-      const uint32_t q_base = smem_u32(smem + C::kQOff);
-      bool ok = ntiles == 0 || mbar_wait(qready, 0);
-      int consumed = 0;
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int s = j & 1;
-          ok = mbar_wait(&full[s], (j >> 1) & 1) && !flags[0];
-          if (!ok) break;
-          consumed = j + 1;
-          tc_fence_after();
-          const uint32_t k_base = smem_u32(smem + C::kStageOff + s * C::kStageBytes);
-          const uint32_t d_s = tmem + (uint32_t)(s * kPrefillN);
+      int consumed = 0;  // ring items whose arrival was observed
+      bool ok = ntiles == 0 || (mbar_wait(&qready[0], 0) && mbar_wait(&qready[1], 0));
+      auto wait_item = [&](int item) -> bool {
+        const bool r = mbar_wait(&full[item % kPrefillSlots], (item / kPrefillSlots) & 1) && !flags[0];
+        if (r && item + 1 > consumed) consumed = item + 1;
+        if (r) tc_fence_after();
+        return r;
+      };
+      auto issue_s = [&](int x, int j) {  // S_X = Q_X . K_j^T
+        const uint32_t qb = smem_u32(smem + C::kQOff + x * C::kQBytes);
+        const uint32_t kb = smem_u32(smem + C::kSlotOff + ((2 * j) % kPrefillSlots) * C::kKVBytes);
 #pragma unroll
-          for (int c = 0; c < C::kChunks; ++c)
+        for (int c = 0; c < C::kChunks; ++c)
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              umma_bf16(d_s, umma_desc_k_sw128(q_base + c * C::kChunkBytes + 32 * k),
-                        umma_desc_k_sw128(k_base + c * C::kChunkBytes + 32 * k), idesc_s, (c | k) ? 1u : 0u);
-          umma_commit(&sready[s]);
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(tmem + (uint32_t)(x * kPrefillN), umma_desc_k_sw128(qb + c * C::kChunkBytes + 32 * k),
+                      umma_desc_k_sw128(kb + c * C::kChunkBytes + 32 * k), idesc_s, (c | k) ? 1u : 0u);
+        umma_commit(&sready[x]);
+      };
+      auto issue_pv = [&](int x, int j) {  // O_X += P_X . V_j
+        const uint32_t pb = smem_u32(smem + C::kPOff + x * C::kPBytes);
+        const uint32_t vb = smem_u32(smem + C::kSlotOff + ((2 * j + 1) % kPrefillSlots) * C::kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kPrefillN / 16; ++kk)
+          umma_bf16(tmem + (uint32_t)(256 + x * 128), umma_desc_k_sw128(pb + (kk >> 2) * C::kChunkBytes + 32 * (kk & 3)),
+                    umma_desc_mn_sw128(vb + kk * 16 * 128, C::kChunkBytes, 1024), idesc_o,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&odone[x]);
+      };
+      if (ok && ntiles > 0) {
+        ok = wait_item(0);
+        if (ok) {
+          issue_s(0, 0);
+          issue_s(1, 0);
+          umma_commit(&empty[0]);  // K_0 read by both products
         }
-        if (j >= 1) {
-          const int jp = j - 1, sp = jp & 1;
-          ok = mbar_wait(&pready[sp], (jp >> 1) & 1) && !flags[0];
+      }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const bool more = j + 1 < ntiles;
+        ok = mbar_wait(&pready[0], j & 1) && wait_item(2 * j + 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          ok = wait_item(2 * j + 2);
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t p_base = smem_u32(smem + C::kPOff + sp * C::kPBytes);
-          const uint32_t v_base = smem_u32(smem + C::kStageOff + sp * C::kStageBytes + C::kKVTileBytes);
-#pragma unroll
-          for (int kk = 0; kk < kPrefillN / 16; ++kk)
-            umma_bf16(tmem + C::kOCol, umma_desc_k_sw128(p_base + (kk >> 2) * C::kChunkBytes + 32 * (kk & 3)),
-                      umma_desc_mn_sw128(v_base + kk * 16 * 128, C::kChunkBytes, 1024), idesc_o,
-                      (jp > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&odone[sp]);
-          umma_commit(&empty[sp]);
+          issue_s(0, j + 1);
+        }
+        ok = mbar_wait(&pready[1], j & 1) && !flags[0];
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&empty[(2 * j + 1) % kPrefillSlots]);  // V_j done
+        if (more) {
+          issue_s(1, j + 1);
+          umma_commit(&empty[(2 * j + 2) % kPrefillSlots]);  // K_{j+1} done
         }
       }
       if (!ok) {
@@ -243,24 +282,27 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     }
   } else {
     // -------------------------------------------------- softmax / epilogue
+    const int x = warp < 6 ? 0 : 1;  // query tile A (warps 2-5) or B (warps 6-9)
     const int quad = warp & 3;
     const int m = 32 * quad + lane;  // tile row == TMEM lane
-    const int tok = t0 + m / a.group;
+    const int tok = t0 + x * a.tq + m / a.group;
     const int head = kvh * a.group + m % a.group;
     const bool row_ok = m < a.tq * a.group && tok < t1;
     const uint32_t row_tmem = tmem + ((uint32_t)(32 * quad) << 16);
+    const uint32_t s_tmem = row_tmem + (uint32_t)(x * kPrefillN);
+    const uint32_t o_tmem = row_tmem + (uint32_t)(256 + x * 128);
 
     // stage q (rows outside the tile are zero)
     {
       const bf16* src = a.q + (int64_t)(qo_begin + tok) * a.q_stride_t + (int64_t)head * a.q_stride_h;
-      uint8_t* qs = smem + C::kQOff;
+      uint8_t* qs = smem + C::kQOff + x * C::kQBytes;
 #pragma unroll
       for (int u = 0; u < D / 8; ++u) {
         const uint4 v = row_ok ? __ldg(reinterpret_cast<const uint4*>(src) + u) : make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(qs + (u >> 3) * C::kChunkBytes + pf_swz(m, u & 7)) = v;
       }
       fence_proxy_async_smem();
-      mbar_arrive(qready);
+      mbar_arrive(&qready[x]);
     }
 
     // last kv position this row may see (rows outside the tile see all)
@@ -269,79 +311,142 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int s = j & 1;
-      ok = mbar_wait(&sready[s], (j >> 1) & 1);
+      ok = mbar_wait(&sready[x], j & 1);
       if (__any_sync(0xffffffffu, !ok || flags[0] != 0)) {  // tcgen05.ld below is warp-wide
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t s_tmem = row_tmem + (uint32_t)(s * kPrefillN);
-      const int kv0 = j * kPrefillN;
-      // pass 1: row maximum of the masked, scaled scores
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kPrefillN / 32; ++c) {
-        float v[32];
-        tmem_ld32(s_tmem + 32 * c, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (kv0 + 32 * c + i <= lim) tmax = fmaxf(tmax, v[i] * sl2);
-      }
-      const float m_new = fmaxf(m_run, tmax);
-      const bool rescale = m_run != -INFINITY && m_new > m_run + kRescaleSlack;
-      const float m_use = (m_run == -INFINITY || rescale) ? m_new : m_run;
-      // P buffer s is free once P_{j-2}.V_{j-2} has run
-      if (j >= 2) ok = mbar_wait(&odone[s], ((j - 2) >> 1) & 1);
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O must hold P_{j-1}.V_{j-1} before it is scaled
-        ok = ok && mbar_wait(&odone[(j - 1) & 1], ((j - 1) >> 1) & 1);
-        tc_fence_after();
-        const float alpha = rescale ? exp2f(m_run - m_use) : 1.f;
-#pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          float v[16];
-          tmem_ld16(row_tmem + C::kOCol + 16 * c, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] *= alpha;
-          tmem_st16_wait(row_tmem + C::kOCol + 16 * c, v);
-        }
-        l_run *= alpha;
-      }
+      const int kv0 = tile_of(j) * kPrefillN;
+      const bool masked = kv0 + kPrefillN - 1 > lim;  // some column of this row is masked
+      // P_X and O_X are free once P_X(j-1).V_{j-1} has run (S_X(j) was issued
+      // after it, so this wait returns at once)
+      if (j >= 1) ok = mbar_wait(&odone[x], (j - 1) & 1);
       if (!__all_sync(0xffffffffu, ok)) {
         ok = false;
         break;
       }
-      m_run = m_use;
-      // pass 2: P = exp2(s - m), row sum, bf16 P into the swizzled tile
-      const float base = m_use == -INFINITY ? 0.f : m_use;
-      uint8_t* pt = smem + C::kPOff + s * C::kPBytes;
-      float sum = 0.f;
+      tc_fence_after();
+      uint8_t* pt = smem + C::kPOff + x * C::kPBytes;
+      // One pass against the running maximum; a row whose maximum grows by
+      // more than 2^kRescaleSlack (and the first tile) takes the two-pass path.
+      // Max and sum run as 8 independent chains each.
+      bool two_pass = __any_sync(0xffffffffu, m_run == -INFINITY);
+      if (!two_pass) {
+        const float nb = -m_run;
+        float sm[8], mx[8];
 #pragma unroll
-      for (int c = 0; c < kPrefillN / 32; ++c) {
-        float v[32];
-        tmem_ld32(s_tmem + 32 * c, v);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = kv0 + 32 * c + i <= lim ? exp2f(v[i] * sl2 - base) : 0.f;
-          const float p1 = kv0 + 32 * c + i + 1 <= lim ? exp2f(v[i + 1] * sl2 - base) : 0.f;
-          sum += p0 + p1;
-          pk[i / 2] = pack_bf16x2(p0, p1);
+        for (int k = 0; k < 8; ++k) {
+          sm[k] = 0.f;
+          mx[k] = -INFINITY;
         }
-        uint8_t* chunk = pt + (c >> 1) * C::kChunkBytes;
+#pragma unroll 1
+        for (int h = 0; h < kPrefillN / 64; ++h) {
+          float v[64];
+          tmem_ld64(s_tmem + 64 * h, v);
+          uint32_t pk[32];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(chunk + pf_swz(m, (c & 1) * 4 + u)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          for (int i = 0; i < 64; i += 2) {
+            const int col = kv0 + 64 * h + i;
+            float p0 = pf_exp2(fmaf(v[i], sl2, nb));
+            float p1 = pf_exp2(fmaf(v[i + 1], sl2, nb));
+            float s0 = v[i], s1 = v[i + 1];
+            if (masked) {
+              const bool k0 = col <= lim, k1 = col + 1 <= lim;
+              p0 = k0 ? p0 : 0.f;
+              p1 = k1 ? p1 : 0.f;
+              s0 = k0 ? s0 : -INFINITY;
+              s1 = k1 ? s1 : -INFINITY;
+            }
+            mx[(i >> 1) & 7] = fmaxf(mx[(i >> 1) & 7], fmaxf(s0, s1));
+            sm[(i >> 1) & 7] += p0 + p1;
+            pk[i / 2] = pack_bf16x2(p0, p1);
+          }
+          uint8_t* chunk = pt + h * C::kChunkBytes;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(chunk + pf_swz(m, u)) =
+                make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+        const float vmax =
+            fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        two_pass = __any_sync(0xffffffffu, vmax * sl2 > m_run + kRescaleSlack);
+        if (!two_pass) l_run += ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
       }
-      l_run += sum;
+      if (two_pass) {
+        // pass 1: row maximum of the masked scores
+        float mx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+#pragma unroll 1
+        for (int h = 0; h < kPrefillN / 64; ++h) {
+          float v[64];
+          tmem_ld64(s_tmem + 64 * h, v);
+          if (masked) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], kv0 + 64 * h + i <= lim ? v[i] : -INFINITY);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], v[i]);
+          }
+        }
+        float tmax =
+            fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        tmax *= sl2;  // sl2 > 0: the max commutes with the scaling
+        const float m_new = fmaxf(m_run, tmax);
+        const bool rescale = m_run != -INFINITY && m_new > m_run + kRescaleSlack;
+        const float m_use = (m_run == -INFINITY || rescale) ? m_new : m_run;
+        if (__any_sync(0xffffffffu, rescale)) {
+          const float alpha = rescale ? pf_exp2(m_run - m_use) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            float v[16];
+            tmem_ld16(o_tmem + 16 * c, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] *= alpha;
+            tmem_st16_wait(o_tmem + 16 * c, v);
+          }
+          l_run *= alpha;
+        }
+        m_run = m_use;
+        // pass 2: P = exp2(s * scale - m), row sum, bf16 P into the swizzled tile
+        const float nb = m_use == -INFINITY ? 0.f : -m_use;
+        float sm[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sm[k] = 0.f;
+#pragma unroll 1
+        for (int h = 0; h < kPrefillN / 64; ++h) {
+          float v[64];
+          tmem_ld64(s_tmem + 64 * h, v);
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const int col = kv0 + 64 * h + i;
+            float p0 = pf_exp2(fmaf(v[i], sl2, nb));
+            float p1 = pf_exp2(fmaf(v[i + 1], sl2, nb));
+            if (masked) {
+              p0 = col <= lim ? p0 : 0.f;
+              p1 = col + 1 <= lim ? p1 : 0.f;
+            }
+            sm[(i >> 1) & 7] += p0 + p1;
+            pk[i / 2] = pack_bf16x2(p0, p1);
+          }
+          uint8_t* chunk = pt + h * C::kChunkBytes;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(chunk + pf_swz(m, u)) =
+                make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+        l_run += ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+      }
       // Slots past the request's last token in its last page hold whatever
-      // the pool had there (0 * NaN is NaN): clear those V rows.
+      // the pool had there (0 * NaN is NaN): tile A's threads clear those V
+      // rows (P_A.V_j runs first, after this tile's arrival).
       const int tail0 = kv_len - kv0, tail1 = min(kPrefillN, n_pages * PS - kv0);
-      if (tail0 >= 0 && tail0 < tail1) {
-        if (mbar_wait(&full[s], (j >> 1) & 1)) {
-          uint8_t* vt = smem + C::kStageOff + s * C::kStageBytes + C::kKVTileBytes;
+      if (x == 0 && tail0 >= 0 && tail0 < tail1) {
+        const int item = 2 * j + 1;
+        if (mbar_wait(&full[item % kPrefillSlots], (item / kPrefillSlots) & 1)) {
+          uint8_t* vt = smem + C::kSlotOff + (item % kPrefillSlots) * C::kKVBytes;
           const int units = (tail1 - tail0) * C::kChunks * 8;
           for (int idx = m; idx < units; idx += 128) {
             const int r = tail0 + idx / (C::kChunks * 8), hh = (idx / 8) % C::kChunks, u = idx % 8;
@@ -351,7 +456,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&pready[s]);
+      mbar_arrive(&pready[x]);
     }
     if (!ok) {
       set_status(a.status, PL_ERR_TIMEOUT);
@@ -360,7 +465,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     // ---- epilogue: O / l  (ok is warp-uniform here)
     bool have_o = false;
     if (ok && ntiles > 0) {
-      have_o = __all_sync(0xffffffffu, mbar_wait(&odone[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1));
+      have_o = __all_sync(0xffffffffu, mbar_wait(&odone[x], (ntiles - 1) & 1));
       if (!have_o) {
         set_status(a.status, PL_ERR_TIMEOUT);
         flags[0] = 1;
@@ -373,7 +478,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     for (int c = 0; c < D / 32; ++c) {
       float v[32];
       if (have_o) {
-        tmem_ld32(row_tmem + C::kOCol + 32 * c, v);
+        tmem_ld32(o_tmem + 32 * c, v);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -397,7 +502,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   if (threadIdx.x == 0) {
     // copies issued but never consumed (abort only) must land before exit
     const int issued = flags[1], consumed = flags[2];
-    for (int i = consumed; i < issued; ++i) (void)mbar_wait(&full[i & 1], (i >> 1) & 1);
+    for (int i = consumed; i < issued; ++i) (void)mbar_wait(&full[i % kPrefillSlots], (i / kPrefillSlots) & 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -470,8 +575,8 @@ extern "C" int32_t pl_paged_prefill(const void* q, int64_t q_stride_t, int64_t q
   a.out_stride_h = out_stride_h;
   a.lse = out_lse;
   a.status = status_dev;
-  // every request contributes ceil(len / tq) <= len / tq + 1 tiles
-  const int64_t grid_x = ((int64_t)total_q + a.tq - 1) / a.tq + batch;
+  // every request contributes ceil(len / 2tq) <= len / 2tq + 1 tile pairs
+  const int64_t grid_x = ((int64_t)total_q + 2 * a.tq - 1) / (2 * a.tq) + batch;
   if (grid_x > 0x7FFFFFFF) return PL_ERR_INVALID_ARGUMENT;
   if (head_dim == 128) return launch_prefill<128>(map, a, (int)grid_x, num_kv_heads, stream);
   return launch_prefill<64>(map, a, (int)grid_x, num_kv_heads, stream);
