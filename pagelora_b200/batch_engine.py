@@ -249,7 +249,8 @@ class BatchDecodeEngine:
     @torch.no_grad()
     def _forward_prompt(self, prompt: list[int], ad: int, page_of: torch.Tensor, off_of: torch.Tensor,
                         keep: torch.Tensor | None = None) -> torch.Tensor:
-        """Torch forward of one row's whole prompt with adapter `ad`; writes
+        """Forward of one row's whole prompt with adapter `ad` (torch GEMMs,
+        the paged prefill attention kernel); writes
         the K/V of position i to (page_of[i], off_of[i]) for the positions in
         `keep` (all when None) and returns the last position's logits."""
 
@@ -258,6 +259,19 @@ class BatchDecodeEngine:
         ids = torch.tensor(prompt, device=self.device, dtype=torch.int64)
         pos = torch.arange(n, device=self.device)
         x = self.embed[ids]
+        # The row's K/V are not always one page list of this pool (a split-KV
+        # shard keeps its range only; a shared prefix may end mid-page), so
+        # each layer's K/V also go to a scratch pool of the row's own pages,
+        # over which the paged prefill kernel attends.
+        ps = self.page_size
+        npg = -(-n // ps)
+        i32 = dict(device=self.device, dtype=torch.int32)
+        scratch = torch.empty((npg, 2, ps) + tuple(self.kv.shape[-2:]), device=self.device, dtype=torch.bfloat16)
+        s_page, s_off = (pos // ps).to(torch.int32), (pos % ps).to(torch.int32)
+        pf_qo = torch.tensor([0, n], **i32)
+        pf_kvp = torch.tensor([0, npg], **i32)
+        pf_idx = torch.arange(npg, **i32)
+        pf_last = torch.tensor([n - (npg - 1) * ps], **i32)
         for li, L in enumerate(self.layers):
             h = _rmsnorm_fused(x, L["input_norm"], s.rms_eps)
             qkv = F.linear(h, L["w_qkv"])
@@ -283,9 +297,9 @@ class BatchDecodeEngine:
             elif keep.numel():
                 K.kv_append(k[keep].contiguous(), v[keep].contiguous(), self.kv[li], page_of[keep].contiguous(),
                             off_of[keep].contiguous(), status=self.status)
-            attn = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
-                                                  v.transpose(0, 1)[None], is_causal=True, enable_gqa=True)
-            attn = attn[0].transpose(0, 1).reshape(n, s.q_dim)
+            K.kv_append(k, v, scratch, s_page, s_off, status=self.status)
+            attn = K.paged_prefill(q, scratch, pf_qo, pf_kvp, pf_idx, pf_last, status=self.status)
+            attn = attn.reshape(n, s.q_dim)
             o = F.linear(attn, L["w_o"])
             if ad >= 0 and L["a_o"] is not None:
                 o = o + F.linear(F.linear(attn, L["a_o"][ad]), L["b_o"][ad]) * self.lora_scale

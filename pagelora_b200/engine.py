@@ -21,8 +21,8 @@ reference recaptures whenever the page count changes, cuda_graph.py:90).
 Consecutive kernels use programmatic dependent launch, so each weight
 stream starts while the previous kernel drains.
 
-The prompt is prefilled with torch (cuBLAS GEMMs + SDPA), which is outside
-the decode hot path this package accelerates.
+The prompt is prefilled with torch GEMMs around the sm_100a paged prefill
+attention kernel (pl_paged_prefill over the pool pages just written).
 """
 
 from __future__ import annotations
@@ -206,7 +206,8 @@ class DecodeEngine:
 
     @torch.no_grad()
     def prefill(self, prompt: list[int]) -> int:
-        """Prefill the prompt into fresh pages (torch ops); returns the first greedy token."""
+        """Prefill the prompt into fresh pages (torch GEMMs, the paged prefill
+        attention kernel over the pool); returns the first greedy token."""
 
         s = self.spec
         self.reset()
@@ -218,6 +219,11 @@ class DecodeEngine:
         page_of = torch.tensor(pages, device=self.device, dtype=torch.int32)[pos // self.page_size]
         off_of = (pos % self.page_size).to(torch.int32)
         x = self.embed[ids]
+        i32 = dict(device=self.device, dtype=torch.int32)
+        pf_qo = torch.tensor([0, n], **i32)
+        pf_kvp = torch.tensor([0, len(pages)], **i32)
+        pf_idx = torch.tensor(pages, **i32)
+        pf_last = torch.tensor([self.host_last], **i32)
         for li, L in enumerate(self.layers):
             h = _rmsnorm_fused(x, L.input_norm, s.rms_eps)
             qkv = F.linear(h, L.w_qkv)
@@ -240,9 +246,9 @@ class DecodeEngine:
             q = _rope(q, pos, s.rope_theta)
             k = _rope(k, pos, s.rope_theta).contiguous()
             K.kv_append(k, v, self.kv[li], page_of, off_of, status=self.status)
-            attn = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
-                                                  v.transpose(0, 1)[None], is_causal=True, enable_gqa=True)
-            attn = attn[0].transpose(0, 1).reshape(n, s.q_dim)
+            # causal paged prefill over the pages just written (tcgen05 kernel)
+            attn = K.paged_prefill(q, self.kv[li], pf_qo, pf_kvp, pf_idx, pf_last, status=self.status)
+            attn = attn.reshape(n, s.q_dim)
             o = F.linear(attn, L.w_o)
             if L.a_o is not None:
                 o = o + F.linear(F.linear(attn, L.a_o[0]), L.b_o[0]) * self.lora_scale
