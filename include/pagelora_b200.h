@@ -376,6 +376,11 @@ int32_t pl_lora_shrink_seg(const void *x, int64_t x_stride,
 #define PL_PROLOGUE_RMSNORM 1  /* x <- bf16(x * rsqrt(mean(x^2)+eps) * norm_w)       */
 #define PL_PROLOGUE_SILU_MUL 2 /* x[t] <- bf16(silu(x[t,:K]) * x[t,K:2K]) (gate_up)  */
 #define PL_FLAG_WEIGHTS_STATIC 1
+#define PL_FLAG_DOWN_FROM_X 2  /* lora_down unused: the kernel computes the LoRA   */
+                               /* down x . A^T itself; shrink_a = A stack          */
+                               /* [n_shrink adapters][lora_rank][k_in] (token t   */
+                               /* uses tok_adapter[t], or 0), lora_rank <= 64,    */
+                               /* one slice; no shrink rows are produced          */
 
 /*
  * Base projection with the LoRA expand and residual fused into its epilogue:
@@ -405,6 +410,9 @@ int32_t pl_lora_shrink_seg(const void *x, int64_t x_stride,
  * flags: PL_FLAG_WEIGHTS_STATIC lets the kernel stream w / shrink_a before
  * the preceding kernel on the stream has finished (programmatic dependent
  * launch); pass it only when no upstream kernel writes those weights.
+ * PL_FLAG_DOWN_FROM_X folds the LoRA shrink of multilora/linear.py:226-227
+ * (x . A^T, fp32) into the launch: every CTA computes the down values of
+ * its tokens from the staged x, so no separate pl_lora_shrink_seg runs.
  */
 int32_t pl_linear_lora_expand_fused(
     const void *x, int64_t x_stride, int32_t num_tokens, int32_t k_in,

@@ -34,6 +34,8 @@ struct GemvArgs {
   int64_t y_stride;
   const bf16* shrink_a;
   int32_t n_shrink;
+  const bf16* pro_a;      // LoRA A stack [adapters][rank][K]: down computed in the kernel from x (or null)
+  int32_t pro_a_adapters;
   float* shrink_out;
   int64_t shrink_stride;
   int32_t early_weights;  // weights are not produced upstream: stream them before the dependency resolves
@@ -48,7 +50,10 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + 
 // Epilogue value of one output element (row o < n_out, token tok) from its
 // fp32 dot product: bias, LoRA expand, residual, with the reference's bf16
 // rounding points (the caller rounds the result to bf16 once more).
-__device__ __forceinline__ float epilogue_value(const GemvArgs& a, int64_t o, int tok, float v) {
+// `down` / `dstride`: the LoRA down rows (a.lora_down, or the kernel's own
+// copy in shared memory).
+__device__ __forceinline__ float epilogue_value(const GemvArgs& a, int64_t o, int tok, float v, const float* down,
+                                                int64_t dstride) {
   if (a.bias != nullptr) v += bf2f(a.bias[o]);
   if (a.lora_b != nullptr) {
     const int ad = a.tok_adapter != nullptr ? a.tok_adapter[tok] : 0;
@@ -57,7 +62,7 @@ __device__ __forceinline__ float epilogue_value(const GemvArgs& a, int64_t o, in
       int sl = 0;
       while (sl < a.num_slices - 1 && o >= a.slice_end[sl]) ++sl;
       const bf16* brow = a.lora_b + ((int64_t)ad * a.n_out + o) * a.rank;
-      const float* drow = a.lora_down + tok * a.down_stride + sl * a.rank;
+      const float* drow = down + tok * dstride + sl * a.rank;
       const float d = lora_dot(brow, drow, a.rank);
       vb = bfr(vb + bfr(bfr(d) * a.lora_scale));
     }
@@ -67,14 +72,22 @@ __device__ __forceinline__ float epilogue_value(const GemvArgs& a, int64_t o, in
   return v;
 }
 
+__device__ __forceinline__ float epilogue_value(const GemvArgs& a, int64_t o, int tok, float v) {
+  return epilogue_value(a, o, tok, v, a.lora_down, a.down_stride);
+}
+
 // Epilogue of one output element (row o, token tok): rows past n_out are
 // LoRA-A shrink rows whose fp32 products go to shrink_out.
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int tok, float v) {
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int tok, float v, const float* down,
+                                              int64_t dstride) {
   if (o >= a.n_out) {
     a.shrink_out[tok * a.shrink_stride + (o - a.n_out)] = v;
     return;
   }
-  a.y[tok * a.y_stride + o] = f2bf(epilogue_value(a, o, tok, v));
+  a.y[tok * a.y_stride + o] = f2bf(epilogue_value(a, o, tok, v, down, dstride));
+}
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int tok, float v) {
+  gemv_epilogue(a, o, tok, v, a.lora_down, a.down_stride);
 }
 
 // Epilogue of rows o0..o0+3 (o0 % 4 == 0) of one token, stored as one 8-byte

@@ -19,10 +19,12 @@ namespace pl {
 
 struct GemvSmem {
   // offsets from a 128-aligned base
-  int row_bytes, stage_bytes, nbuf, x_off, zero_off, acc_off, cnt_off, bar_off, misc_off, total;
+  int row_bytes, stage_bytes, nbuf, x_off, zero_off, acc_off, cnt_off, bar_off, misc_off, down_off, total;
 };
 
-__host__ __device__ inline GemvSmem gemv_smem_layout(int T, int K, int stages, int kc) {
+// down_floats: fp32 LoRA down values the kernel computes itself (T * rank
+// with a LoRA A stack in the arguments, else 0).
+__host__ __device__ inline GemvSmem gemv_smem_layout(int T, int K, int stages, int kc, int down_floats) {
   GemvSmem L;
   L.row_bytes = kc * 2 + 16;  // padded rows: conflict-free ldmatrix
   L.stage_bytes = kTileRows * L.row_bytes;
@@ -42,8 +44,68 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int T, int K, int stages, i
   off += 2 * stages * 8;
   L.misc_off = off;
   off += 64;
+  L.down_off = off;
+  off += down_floats * 4;
   L.total = off + 128;
   return L;
+}
+
+// down[t][r] = x_staged[t] . A[adapter(t)][r] (fp32) for every token of the
+// launch, into shared memory; `scratch` holds [warps][T][rank] partials (the
+// tile-accumulator region, unused until the main loop).  rank <= 64.
+__device__ __forceinline__ void down_from_staged(const GemvArgs& a, const uint8_t* xs, int xrow, float* down,
+                                                 float* scratch, int tid, int nthreads, int bar) {
+  const int K = a.K, R = a.rank;
+  const int lane = tid & 31, wid = tid >> 5, nw = nthreads >> 5;
+  for (int t = 0; t < a.T; ++t) {
+    const int ad = a.tok_adapter != nullptr ? a.tok_adapter[t] : 0;
+    if (ad < 0 || ad >= a.pro_a_adapters) continue;  // no LoRA for this token: its down is not read
+    const bf16* A = a.pro_a + (int64_t)ad * R * K;
+    const uint8_t* xr = xs + t * xrow;
+    for (int r0 = 0; r0 < R; r0 += 16) {
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+      for (int k = tid * 8; k < K; k += nthreads * 8) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(xr + k * 2);
+        const uint32_t* xu = reinterpret_cast<const uint32_t*>(&xv);
+        float xf[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(xu[q]);
+          xf[2 * q] = f.x;
+          xf[2 * q + 1] = f.y;
+        }
+        uint4 av[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          av[i] = r0 + i < R ? __ldg(reinterpret_cast<const uint4*>(A + (int64_t)(r0 + i) * K + k))
+                             : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t* au = reinterpret_cast<const uint32_t*>(&av[i]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = unpack_bf16x2(au[q]);
+            acc[i] = fmaf(xf[2 * q], f.x, acc[i]);
+            acc[i] = fmaf(xf[2 * q + 1], f.y, acc[i]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float v = warp_sum(acc[i]);
+        if (lane == 0 && r0 + i < R) scratch[(wid * a.T + t) * R + r0 + i] = v;
+      }
+    }
+  }
+  named_barrier(bar, nthreads);
+  for (int i = tid; i < a.T * R; i += nthreads) {
+    float v = 0.f;
+    for (int w = 0; w < nw; ++w) v += scratch[w * a.T * R + i];  // fixed order
+    down[i] = v;
+  }
+  named_barrier(bar, nthreads);
 }
 
 // Stage the activations of all tokens as bf16 rows (stride xrow bytes) in
@@ -168,7 +230,7 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int S = a.stages, KC = a.kc;
-  const GemvSmem L = gemv_smem_layout(a.T, a.K, S, KC);
+  const GemvSmem L = gemv_smem_layout(a.T, a.K, S, KC, a.pro_a != nullptr ? a.T * a.rank : 0);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty_bar = full_bar + S;
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + L.misc_off);
@@ -250,6 +312,15 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
   if (ctid == 0) PL_TRACE_POINT(4);
 
   stage_activations(a, xs, XROW, ctid, NC, reinterpret_cast<float*>(smem + L.misc_off + 16), 1);
+  // LoRA down: computed here from the staged x (a.pro_a), else read from a.lora_down
+  const float* down = a.lora_down;
+  int64_t dstride = a.down_stride;
+  if (a.pro_a != nullptr) {
+    float* dsm = reinterpret_cast<float*>(smem + L.down_off);
+    down_from_staged(a, xs, XROW, dsm, tacc, ctid, NC, 1);
+    down = dsm;
+    dstride = a.rank;
+  }
   if (ctid == 0) PL_TRACE_POINT(5);
 
   const int g = lane >> 2, tq = lane & 3;
@@ -327,7 +398,7 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < NCW; ++w) v += *reinterpret_cast<volatile float*>(&slots[w * kTileRows * T + e]);
-        if (o < r1) gemv_epilogue(a, o, tok, v);
+        if (o < r1) gemv_epilogue(a, o, tok, v, down, dstride);
       }
       __syncwarp();
       if (lane == 0) {
@@ -633,16 +704,22 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
                                                void* y, int64_t y_stride, const void* shrink_a, int32_t n_shrink,
                                                float* shrink_out, int64_t shrink_stride, int32_t flags,
                                                int32_t* status_dev, void* stream) {
-  if (num_tokens == 0 || (n_out == 0 && n_shrink == 0)) return PL_OK;
+  const bool down_from_x = (flags & PL_FLAG_DOWN_FROM_X) != 0;
+  if (down_from_x) {  // shrink_a is the LoRA A stack [n_shrink adapters][lora_rank][k_in]
+    if (lora_b == nullptr || shrink_a == nullptr || n_shrink < 1 || lora_rank <= 0 || num_slices > 1)
+      return PL_ERR_INVALID_ARGUMENT;
+    if (lora_rank > 64) return PL_ERR_UNSUPPORTED;
+  }
+  if (num_tokens == 0 || (n_out == 0 && (n_shrink == 0 || down_from_x))) return PL_OK;
   if (x == nullptr || w == nullptr || num_tokens < 0 || num_tokens > pl::kMaxTok || k_in <= 0 || n_out < 0 ||
       n_shrink < 0)
     return PL_ERR_INVALID_ARGUMENT;
   if (k_in % 16 != 0) return PL_ERR_UNSUPPORTED;
   if (n_out > 0 && y == nullptr) return PL_ERR_INVALID_ARGUMENT;
-  if (n_shrink > 0 && (shrink_a == nullptr || shrink_out == nullptr)) return PL_ERR_INVALID_ARGUMENT;
+  if (!down_from_x && n_shrink > 0 && (shrink_a == nullptr || shrink_out == nullptr)) return PL_ERR_INVALID_ARGUMENT;
   if (prologue == PL_PROLOGUE_RMSNORM && norm_w == nullptr) return PL_ERR_INVALID_ARGUMENT;
   if (prologue < 0 || prologue > 2) return PL_ERR_INVALID_ARGUMENT;
-  if (lora_b != nullptr && (lora_down == nullptr || lora_rank <= 0 || num_slices < 1 || num_slices > 4 ||
+  if (lora_b != nullptr && ((lora_down == nullptr && !down_from_x) || lora_rank <= 0 || num_slices < 1 || num_slices > 4 ||
                             (num_slices > 1 && slice_end == nullptr)))
     return PL_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) || (x_stride % 8) ||
@@ -674,10 +751,16 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   a.res_stride = res_stride;
   a.y = static_cast<pl::bf16*>(y);
   a.y_stride = y_stride;
-  a.shrink_a = static_cast<const pl::bf16*>(shrink_a);
+  if (down_from_x) {
+    a.pro_a = static_cast<const pl::bf16*>(shrink_a);
+    a.pro_a_adapters = n_shrink;
+    n_shrink = 0;  // no shrink rows: the down values stay in the kernel
+  } else {
+    a.shrink_a = static_cast<const pl::bf16*>(shrink_a);
+    a.shrink_out = shrink_out;
+    a.shrink_stride = shrink_stride;
+  }
   a.n_shrink = n_shrink;
-  a.shrink_out = shrink_out;
-  a.shrink_stride = shrink_stride;
   a.early_weights = (flags & 1) ? 1 : 0;
   a.status = status_dev;
 
@@ -685,7 +768,7 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   if (sms <= 0) sms = 148;
   const int64_t rows = (int64_t)n_out + n_shrink;
   const int64_t tiles = (rows + pl::kTileRows - 1) / pl::kTileRows;
-  const bool ldg = k_in % 32 == 0 &&
+  const bool ldg = !down_from_x && k_in % 32 == 0 &&
                    (g_gemv_mode == 2 || (g_gemv_mode == 0 && rows * k_in * 2 <= g_auto_ldg_max_bytes));
   if (ldg) {
     // register-direct variant: several CTAs per SM, tiles strided over the grid
@@ -710,7 +793,8 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   const int grid = (int)(tiles < max_ctas ? tiles : max_ctas);
   // Largest ring that fits: the tuned shape, then shallower / narrower stages.
   int stages = g_gemv_stages, kc = g_gemv_kc;
-  pl::GemvSmem L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc);
+  const int down_floats = a.pro_a != nullptr ? num_tokens * lora_rank : 0;
+  pl::GemvSmem L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc, down_floats);
   while (L.total > 227 * 1024 && (stages > 2 || kc > 256)) {
     if (stages > 2) {
       --stages;
@@ -718,7 +802,7 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
       kc /= 2;
       stages = g_gemv_stages;
     }
-    L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc);
+    L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc, down_floats);
   }
   if (L.total > 227 * 1024) return PL_ERR_UNSUPPORTED;
   a.stages = stages;

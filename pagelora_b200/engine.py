@@ -3,16 +3,16 @@
 ``DecodeEngine`` runs the decode layer of the reference
 (model/flashinfer/layer_runner.py:283-337, cuda_graph.py:245-263) with the
 no-merge LoRA delta (packed_ops.py:105-165, multilora/linear.py:200-231) on
-this package's kernels, six launches per layer:
+this package's kernels, five launches per layer:
 
   1. linear_lora_fused   RMSNorm -> [W_q;W_k;W_v] and the packed LoRA A rows
   2. paged_decode_qkv    + B.down (packed expand), q/k head norm, RoPE, KV append,
                          then split-KV paged attention with the split merge
                          (thread-block cluster or arrival ticket) in the kernel
-  3. lora_shrink_seg     attn . A_o^T
-  4. linear_lora_fused   W_o with the LoRA expand and the residual in the epilogue
-  5. linear_lora_fused   RMSNorm -> [W_gate;W_up]
-  6. linear_lora_fused   SiLU-and-mul -> W_down with the residual in the epilogue
+  3. linear_lora_fused   attn . A_o^T in the prologue (every CTA), then W_o with
+                         the LoRA expand and the residual in the epilogue
+  4. linear_lora_fused   RMSNorm -> [W_gate;W_up]
+  5. linear_lora_fused   SiLU-and-mul -> W_down with the residual in the epilogue
 
 plus page-table advance + embedding in front and the final norm + lm_head +
 argmax behind.  The page table lives on the device and is advanced inside
@@ -88,6 +88,9 @@ class DecodeEngine:
         self.lora_rank = lora_spec.rank if (lora and lora_spec) else 0
         self.lora_scale = lora_spec.scale if (lora and lora_spec) else 1.0
         self.qkv_lora_scale = 1.0
+        # o projection: the LoRA shrink runs inside the o GEMV's prologue
+        # (PL_FLAG_DOWN_FROM_X); False keeps the separate pl_lora_shrink_seg launch
+        self.fold_o_shrink = True
         dev, bf = self.device, torch.bfloat16
         H, D = spec.hidden, spec.head_dim
 
@@ -306,10 +309,16 @@ class DecodeEngine:
                                lora_down=self.down_qkv if L.b_qkv is not None else None, lora_b=L.b_qkv,
                                lora_scale=self.qkv_lora_scale, q_norm_weight=L.q_norm, k_norm_weight=L.k_norm,
                                norm_eps=s.rms_eps, out=self.attn, status=st)
-            if L.a_o is not None:
-                K.lora_shrink_seg(attn2d, L.a_o, self.seg_indptr, self.seg_adapter, out=self.down_o)
-            K.linear_lora_fused(attn2d, L.w_o, lora_down=self.down_o if L.b_o is not None else None, lora_b=L.b_o,
-                                lora_scale=self.lora_scale, residual=self.x, out=self.x, weights_static=True, status=st)
+            if self.fold_o_shrink and L.a_o is not None:
+                # the o GEMV computes attn . A_o^T in its prologue: no shrink launch
+                K.linear_lora_fused(attn2d, L.w_o, lora_a=L.a_o, lora_b=L.b_o, lora_scale=self.lora_scale,
+                                    residual=self.x, out=self.x, weights_static=True, status=st)
+            else:
+                if L.a_o is not None:
+                    K.lora_shrink_seg(attn2d, L.a_o, self.seg_indptr, self.seg_adapter, out=self.down_o)
+                K.linear_lora_fused(attn2d, L.w_o, lora_down=self.down_o if L.b_o is not None else None,
+                                    lora_b=L.b_o, lora_scale=self.lora_scale, residual=self.x, out=self.x,
+                                    weights_static=True, status=st)
             K.linear_lora_fused(self.x, L.w_gate_up, prologue=PL_PROLOGUE_RMSNORM, norm_weight=L.post_norm,
                                 norm_eps=s.rms_eps, out=self.gate_up, weights_static=True, status=st)
             K.linear_lora_fused(self.gate_up, L.w_down, prologue=PL_PROLOGUE_SILU_MUL, residual=self.x,
@@ -319,7 +328,7 @@ class DecodeEngine:
         K.argmax(self.logits, self.token_buf, self.argmax_ws)
 
     def launches_per_step(self) -> int:
-        per_layer = 5 + sum(1 for L in self.layers[:1] if L.a_o is not None)
+        per_layer = 5 + sum(1 for L in self.layers[:1] if L.a_o is not None and not self.fold_o_shrink)
         return 2 + per_layer * len(self.layers) + 2
 
     def capture(self) -> None:

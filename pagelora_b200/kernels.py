@@ -349,6 +349,7 @@ def linear_lora_fused(
     out: torch.Tensor | None = None,
     shrink_a: torch.Tensor | None = None,
     shrink_out: torch.Tensor | None = None,
+    lora_a: torch.Tensor | None = None,
     weights_static: bool = False,
     status: torch.Tensor | None = None,
 ) -> torch.Tensor:
@@ -357,7 +358,9 @@ def linear_lora_fused(
     ``x`` is [T, K] (or [T, 2K] for the SiLU-and-mul prologue), ``weight``
     [N, K], ``lora_b`` [n_adapters, N, rank] with scale folded in,
     ``lora_down`` [T, >= num_slices*rank] fp32, ``shrink_a`` [n_shrink, K]
-    whose fp32 products go to ``shrink_out`` [T, n_shrink].
+    whose fp32 products go to ``shrink_out`` [T, n_shrink].  With ``lora_a``
+    [n_adapters, rank, K] instead of ``lora_down`` the kernel computes the
+    down values x . A^T itself (PL_FLAG_DOWN_FROM_X; one LoRA slice).
     """
 
     _need_cuda(x, weight)
@@ -379,10 +382,18 @@ def linear_lora_fused(
         num_slices = len(slice_ends) + 1 if slice_ends else 1
         if slice_ends:
             slice_ptr, slice_keepalive = ctypes_int32_array(slice_ends)
-    n_shrink = 0 if shrink_a is None else shrink_a.shape[0]
-    if shrink_a is not None and shrink_out is None:
-        shrink_out = torch.empty(t, n_shrink, dtype=torch.float32, device=x.device)
     flags = _capi.PL_FLAG_WEIGHTS_STATIC if weights_static else 0
+    if lora_a is not None:
+        if shrink_a is not None or lora_down is not None or lora_b is None or slice_ends:
+            raise ValueError("lora_a replaces lora_down / shrink_a and needs lora_b with one slice")
+        if lora_a.dim() == 2:
+            lora_a = lora_a.unsqueeze(0)
+        if not lora_a.is_contiguous() or lora_a.shape[1] != rank or lora_a.shape[2] != k:
+            raise ValueError("lora_a must be a contiguous [n_adapters, rank, in] stack")
+        shrink_a, flags = lora_a, flags | _capi.PL_FLAG_DOWN_FROM_X
+    n_shrink = 0 if shrink_a is None else shrink_a.shape[0]
+    if shrink_a is not None and shrink_out is None and lora_a is None:
+        shrink_out = torch.empty(t, n_shrink, dtype=torch.float32, device=x.device)
     call("pl_linear_lora_expand_fused", ptr(x), _row_stride(x, "x"), int(t), int(k), int(prologue),
          ptr(norm_weight), float(norm_eps), ptr(weight), int(n), ptr(bias), ptr(lora_down),
          0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),

@@ -541,6 +541,36 @@ def test_linear_lora_fused_prologues_and_epilogues_vs_oracle(K, t, gemv_tuning):
     _ulps_close(_np(y2), bf16(gu[:, :k_in].astype(np.float64) @ w.T.astype(np.float64)), ulps=3)
 
 
+@pytest.mark.parametrize("t,r", [(1, 16), (5, 16), (8, 32), (3, 64)])
+def test_linear_lora_fused_down_from_x_vs_oracle(K, t, r):
+    """PL_FLAG_DOWN_FROM_X: the LoRA down x . A^T computed in the GEMV's
+    prologue (per-token adapters, one with no LoRA) gives the reference's
+    LoRALinear output (multilora/linear.py:226-231 rounding points)."""
+
+    rng = np.random.default_rng(7 * t + r)
+    k_in, n, n_ad = 4096, 1000, 3
+    x = bf16(rng.normal(size=(t, k_in)))
+    res = bf16(rng.normal(size=(t, n)))
+    w = bf16(rng.normal(size=(n, k_in)) * 0.02)
+    a_st = bf16(rng.normal(size=(n_ad, r, k_in)) * 0.02)
+    bmat = bf16(rng.normal(size=(n_ad, n, r)) * 0.05)
+    tok_ad = rng.integers(-1, n_ad, size=t)
+    tok_ad[0] = 1
+    y = K.linear_lora_fused(_t(x), _t(w), lora_a=_t(a_st), lora_b=_t(bmat), lora_scale=0.5,
+                            tok_adapter=_i32(tok_ad), residual=_t(res), weights_static=True)
+    torch.cuda.synchronize()
+    base = bf16(x.astype(np.float64) @ w.T.astype(np.float64))
+    want = np.zeros((t, n), np.float32)
+    for i in range(t):
+        yi = base[i]
+        if tok_ad[i] >= 0:
+            down = bf16(x[i].astype(np.float64) @ a_st[tok_ad[i]].T.astype(np.float64))
+            yi = bf16(yi + bf16(bf16(bmat[tok_ad[i]] @ down) * 0.5))
+        want[i] = bf16(res[i] + yi)
+    # the fp32 down sum order may move bf16(down) by one ulp
+    _ulps_close(_np(y), want, ulps=3, magnitude=np.abs(base))
+
+
 def test_linear_lora_fused_large_shapes(K, gemv_tuning):
     """Decode shapes of Qwen3-8B (qkv, o, gate_up, down) at one token."""
 
