@@ -93,6 +93,7 @@ struct DecodeCfg {
   static constexpr int kScratchRow = D + 4;                             // padded: conflict-free writes
   static_assert(kConsumerWarps * 16 * kScratchRow * 4 <= kStages * kStageBytes, "merge scratch must fit the stage ring");
   static_assert(kStages >= kPagesPerBatch, "one producer batch must map to distinct stages");
+  static_assert(kStages >= kConsumerWarps, "every consumer warp owns at least one stage");
 };
 
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128B-swizzled box.
@@ -164,11 +165,21 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
       int32_t last_len = args.last_page_len[b];
       last_len = last_len < 0 ? 0 : (last_len > PS ? PS : last_len);
       const int box = lane % C::kBoxesPerPage;
+      const bool lane_used = lane < C::kBoxesPerPage * C::kPagesPerBatch;
+      // Page ids are read one batch ahead, so the index load's latency hides
+      // behind the wait for free stages instead of delaying the copies.
+      int32_t pid_next = (lane_used && lane / C::kBoxesPerPage < n)
+                             ? args.indices[row_begin + p0 + lane / C::kBoxesPerPage]
+                             : 0;
       int issued = 0;
       for (int i0 = 0; i0 < n; i0 += C::kPagesPerBatch) {
         const int i = i0 + lane / C::kBoxesPerPage;
-        const bool active = lane < C::kBoxesPerPage * C::kPagesPerBatch && i < n;
+        const bool active = lane_used && i < n;
         const int s = i % C::kStages;
+        const int32_t pid_here = pid_next;
+        pid_next = (lane_used && i + C::kPagesPerBatch < n)
+                       ? args.indices[row_begin + p0 + i + C::kPagesPerBatch]
+                       : 0;
         bool ok = true;
         if (active && i >= C::kStages) ok = mbar_wait(&empty_bar[s], ((i / C::kStages) - 1) & 1);
         if (!__all_sync(0xffffffffu, ok)) {
@@ -177,7 +188,7 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
           break;
         }
         const int32_t page_idx = p0 + i;
-        const int32_t pid = active ? args.indices[row_begin + page_idx] : 0;
+        const int32_t pid = active ? pid_here : 0;
         const int32_t ntok = (page_idx == n_pages - 1) ? last_len : PS;
         const bool valid = active && pid >= 0 && static_cast<int64_t>(pid) < args.num_pages && ntok > 0;
         if (active && box == 0) {
@@ -289,7 +300,17 @@ __global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __gr
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     const float sl2 = args.scale_log2;
 
-    for (int i = cw; i < n; i += kConsumerWarps) {
+    // Stage s is always consumed by warp s % kConsumerWarps, in page order, so
+    // each full barrier has one waiter that never runs a phase ahead.  (Dealt
+    // round-robin across the ring's laps, a warp could reach page i while the
+    // copy of page i - kStages into the same stage is still in flight: a
+    // parity wait cannot tell that phase's successor from its predecessor and
+    // would return at once on the old contents.)
+    auto next_page = [&](int i) {
+      return (i % C::kStages) + kConsumerWarps < C::kStages ? i + kConsumerWarps
+                                                            : (i / C::kStages + 1) * C::kStages + cw;
+    };
+    for (int i = cw; i < n; i = next_page(i)) {
       const int s = i % C::kStages;
       if (!mbar_wait(&full_bar[s], (i / C::kStages) & 1)) {
         set_status(args.status, PL_ERR_TIMEOUT);

@@ -105,4 +105,126 @@ __device__ __forceinline__ void epilogue_rows4(const GemvArgs& a, int64_t o0, in
   }
 }
 
+// Rank-16 LoRA dot product with the B row held in registers (16 bf16) and
+// the down row already rounded to bf16: the fma order of lora_dot.
+__device__ __forceinline__ float lora_dot16(const uint4 (&b)[2], const float* d) {
+  float acc = 0.f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float4 d0 = *reinterpret_cast<const float4*>(d + 8 * h);
+    const float4 d1 = *reinterpret_cast<const float4*>(d + 8 * h + 4);
+    const float2 b0 = unpack_bf16x2(b[h].x), b1 = unpack_bf16x2(b[h].y), b2 = unpack_bf16x2(b[h].z),
+                 b3 = unpack_bf16x2(b[h].w);
+    acc = fmaf(b0.x, d0.x, acc);
+    acc = fmaf(b0.y, d0.y, acc);
+    acc = fmaf(b1.x, d0.z, acc);
+    acc = fmaf(b1.y, d0.w, acc);
+    acc = fmaf(b2.x, d1.x, acc);
+    acc = fmaf(b2.y, d1.y, acc);
+    acc = fmaf(b3.x, d1.z, acc);
+    acc = fmaf(b3.y, d1.w, acc);
+  }
+  return acc;
+}
+
+// Epilogue of rows o0..o0+3 (o0 % 4 == 0) for the tokens tok[0..nt) (nt <= 4),
+// with the values of epilogue_value.  Every input of the tokens (adapter ids,
+// residuals, rank-16 LoRA rows) is loaded before the first result is formed
+// and the results are stored last, so the tokens' memory latencies overlap
+// instead of adding up.  Other shapes fall back to one token at a time.
+// sdown / sad (optional, rank 16): the down rows [T][sR] rounded to bf16 and
+// the adapter ids [T], staged in shared memory; each adapter's B rows are then
+// loaded once for consecutive tokens that share it.
+__device__ __forceinline__ void epilogue_rows4_x4(const GemvArgs& a, int64_t o0, const int (&tok)[4], int nt,
+                                                  const float (&v)[4][4], const float* sdown = nullptr,
+                                                  int sR = 0, const int32_t* sad = nullptr) {
+  if (o0 >= a.n_out) return;
+  const bool vec = o0 + 4 <= a.n_out && (a.lora_b == nullptr || a.rank == 16) &&
+                   ((a.y_stride | a.res_stride) & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(a.y) | reinterpret_cast<uintptr_t>(a.residual)) & 7) == 0;
+  if (!vec) {
+    for (int k = 0; k < nt; ++k) epilogue_rows4(a, o0, tok[k], v[k]);
+    return;
+  }
+  float bias[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bias[i] = bf2f(a.bias[o0 + i]);
+  }
+  int ad[4] = {0, 0, 0, 0};
+  if (a.lora_b != nullptr && sad != nullptr) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ad[k] = k < nt ? sad[tok[k]] : -1;
+  } else if (a.lora_b != nullptr && a.tok_adapter != nullptr) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ad[k] = k < nt ? a.tok_adapter[tok[k]] : -1;
+  }
+  uint2 res[4] = {};
+  if (a.residual != nullptr) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (k < nt) res[k] = *reinterpret_cast<const uint2*>(a.residual + tok[k] * a.res_stride + o0);
+  }
+  float dl[4][4] = {};
+  if (a.lora_b != nullptr) {
+    int sl[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sl[i] = 0;
+      while (sl[i] < a.num_slices - 1 && o0 + i >= a.slice_end[sl[i]]) ++sl[i];
+    }
+    if (sdown != nullptr) {
+      int cur = -1;  // adapter whose B rows are in b
+      uint4 b[4][2] = {};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (k < nt && ad[k] >= 0) {
+          if (ad[k] != cur) {
+            cur = ad[k];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4* br = reinterpret_cast<const uint4*>(a.lora_b + ((int64_t)cur * a.n_out + o0 + i) * 16);
+              b[i][0] = br[0];
+              b[i][1] = br[1];
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dl[k][i] = lora_dot16(b[i], sdown + tok[k] * sR + sl[i] * 16);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (k < nt && ad[k] >= 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dl[k][i] = lora_dot(a.lora_b + ((int64_t)ad[k] * a.n_out + o0 + i) * 16,
+                                a.lora_down + tok[k] * a.down_stride + sl[i] * 16, 16);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (k >= nt) continue;
+    const float2 r01 = unpack_bf16x2(res[k].x), r23 = unpack_bf16x2(res[k].y);
+    const float rv[4] = {r01.x, r01.y, r23.x, r23.y};
+    float out[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float x = v[k][i];
+      if (a.bias != nullptr) x += bias[i];
+      if (a.lora_b != nullptr) {
+        float vb = bfr(x);
+        if (ad[k] >= 0) vb = bfr(vb + bfr(bfr(dl[k][i]) * a.lora_scale));
+        x = vb;
+      }
+      if (a.residual != nullptr) x = rv[i] + bfr(x);
+      out[i] = x;
+    }
+    *reinterpret_cast<uint2*>(a.y + tok[k] * a.y_stride + o0) =
+        make_uint2(pack_bf16x2(out[0], out[1]), pack_bf16x2(out[2], out[3]));
+  }
+}
+
 }  // namespace pl

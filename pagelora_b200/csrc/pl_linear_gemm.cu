@@ -42,6 +42,7 @@ struct GemmArgs {
   int32_t max_slots;   // partial slots per tile
   float* partial;      // [m_tiles][max_slots][N][128] fp32
   int32_t* counters;   // [m_tiles] arrival tickets, zero between calls
+  int32_t lora_stage;  // bytes of shared memory holding the rank-16 LoRA down rows and adapter ids (0: none)
 };
 
 // N: tokens padded (UMMA N).  KCS: 64-column chunks per K block; with KCS > 1
@@ -60,8 +61,8 @@ struct GemmCfg {
   static_assert(kBTile % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
 };
 
-__host__ __device__ inline int gemm_smem_bytes(int stage_bytes, int stages) {
-  return 1024 + stages * stage_bytes + 16 * kGemmM * 4 + (2 * stages + 4) * 8 + 32;
+__host__ __device__ inline int gemm_smem_bytes(int stage_bytes, int stages, int lora_stage) {
+  return 1024 + stages * stage_bytes + 16 * kGemmM * 4 + lora_stage + (2 * stages + 4) * 8 + 32;
 }
 
 __host__ __device__ inline int unit_begin(int c, int units, int ctas) {
@@ -93,7 +94,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = g.stages;
   float* stile = reinterpret_cast<float*>(smem + S * C::kStageBytes);  // [16 tokens][128 rows]
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes + C::kStageTile);
+  // Rank-16 LoRA epilogue inputs, staged once: down rows rounded to bf16
+  // [T][num_slices * 16], then the tokens' adapter ids [T].
+  float* lds = reinterpret_cast<float*>(smem + S * C::kStageBytes + C::kStageTile);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes + C::kStageTile + g.lora_stage);
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;  // [2] accumulator ready
   uint64_t* acce = accf + 2;   // [2] accumulator drained
@@ -230,6 +234,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     const int T = g.e.T;
     constexpr int kEpiThreads = 128;
+    const int R = g.e.num_slices * 16;
+    const float* sdown = nullptr;
+    const int32_t* sad = nullptr;
+    if (g.lora_stage) {
+      int32_t* lad = reinterpret_cast<int32_t*>(lds + T * R);
+      for (int idx = ew * 32 + lane; idx < T * R; idx += kEpiThreads)
+        lds[idx] = bfr(g.e.lora_down[(int64_t)(idx / R) * g.e.down_stride + idx % R]);
+      for (int t2 = ew * 32 + lane; t2 < T; t2 += kEpiThreads)
+        lad[t2] = g.e.tok_adapter != nullptr ? g.e.tok_adapter[t2] : 0;
+      named_barrier(1, kEpiThreads);
+      sdown = lds;
+      sad = lad;
+    }
     int seg = 0;
     for (int i = 0; i < n;) {
       const int u = u0 + i, t = u / KB, ka = u % KB;
@@ -255,11 +272,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int j = 0; j < 16; ++j) stile[j * kGemmM + row] = v[j];
           named_barrier(1, kEpiThreads);
           if (!flags[0]) {
-            for (int j = ew; j < 16 && 16 * c + j < T; j += 4) {
+            // tokens 4ew .. 4ew+3 of this chunk (adjacent tokens usually
+            // share an adapter), finished together
+            int toks[4];
+            float vals[4][4];
+            int nt = 0;
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const int j = 4 * ew + h;
+              toks[h] = 16 * c + j;
               const float4 r4 = *reinterpret_cast<const float4*>(stile + j * kGemmM + 4 * lane);
-              const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
-              epilogue_rows4(g.e, o4, 16 * c + j, rv);
+              vals[h][0] = r4.x;
+              vals[h][1] = r4.y;
+              vals[h][2] = r4.z;
+              vals[h][3] = r4.w;
+              if (16 * c + j < T) nt = h + 1;
             }
+            epilogue_rows4_x4(g.e, o4, toks, nt, vals, sdown, R, sad);
           }
           named_barrier(1, kEpiThreads);
         }
@@ -295,25 +324,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __threadfence();
           const int nslots = c_last - c_first + 1;
           const float* base = g.partial + (int64_t)t * g.max_slots * N * kGemmM + 4 * lane;
-          // Two tokens x four slots of loads in flight per lane; slots are
+          // Four tokens x four slots of loads in flight per lane; slots are
           // added in order, so the sum does not depend on timing.
 #pragma unroll 1
-          for (int tok = ew; tok < T; tok += 8) {
-            float a4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            const bool two = tok + 4 < T;
+          for (int tok = 4 * ew; tok < T; tok += 16) {
+            float a4[4][4] = {};
+            int toks[4];
+            int nt = 0;
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              toks[h] = tok + h;
+              if (tok + h < T) nt = h + 1;
+            }
 #pragma unroll 1
             for (int sl = 0; sl < nslots; sl += 4) {
-              float4 p[2][4];
+              float4 p[4][4];
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
+              for (int h = 0; h < 4; ++h)
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                  p[h][k] = (sl + k < nslots && (h == 0 || two))
+                  p[h][k] = (sl + k < nslots && h < nt)
                                 ? __ldcg(reinterpret_cast<const float4*>(
-                                      base + ((int64_t)(sl + k) * N + tok + 4 * h) * kGemmM))
+                                      base + ((int64_t)(sl + k) * N + tok + h) * kGemmM))
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
+              for (int h = 0; h < 4; ++h)
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                   a4[h][0] += p[h][k].x;
@@ -322,10 +357,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                   a4[h][3] += p[h][k].w;
                 }
             }
-            if (!flags[0]) {
-              epilogue_rows4(g.e, o4, tok, a4[0]);
-              if (two) epilogue_rows4(g.e, o4, tok + 4, a4[1]);
-            }
+            if (!flags[0]) epilogue_rows4_x4(g.e, o4, toks, nt, a4, sdown, R, sad);
           }
           if (ew == 0 && lane == 0) g.counters[t] = 0;
         }
@@ -502,7 +534,8 @@ int gemm_n(int tokens) { return tokens <= 16 ? 16 : tokens <= 32 ? 32 : tokens <
 
 int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
-constexpr int kGemmSmemBudget = 212 * 1024;
+constexpr int kGemmSmemBudget = 200 * 1024;
+constexpr int kLoraStageMax = 16 * 1024;
 
 struct GemmShape {
   int n, kcs, stages, m_tiles, kblocks, units, ctas, max_slots, stage_bytes;
@@ -543,7 +576,7 @@ template <int N, int KCS>
 int32_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int ctas, int stages,
                     void* stream) {
   auto kern = pl::linear_tc_kernel<N, KCS>;
-  const int smem = pl::gemm_smem_bytes(pl::GemmCfg<N, KCS>::kStageBytes, stages);
+  const int smem = pl::gemm_smem_bytes(pl::GemmCfg<N, KCS>::kStageBytes, stages, g.lora_stage);
   int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (st != PL_OK) return st;
   return pl_host::launch_pdl(kern, dim3(ctas), dim3(pl::kGemmThreads), smem, stream, wm, xm, g);
@@ -647,6 +680,12 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   g.counters = reinterpret_cast<int32_t*>(ws);
   g.partial = sh.max_slots > 1 ? reinterpret_cast<float*>(ws + align256((int64_t)sh.m_tiles * 4)) : nullptr;
+  // Rank-16 LoRA: stage the (small) down rows and adapter ids in shared
+  // memory so the epilogue reads them once per CTA instead of per element.
+  if (lora_b != nullptr && lora_rank == 16 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0) {
+    const int64_t bytes = (int64_t)num_tokens * a.num_slices * 16 * 4 + (((int64_t)num_tokens * 4 + 15) & ~int64_t(15));
+    if (bytes <= kLoraStageMax) g.lora_stage = static_cast<int32_t>(bytes);
+  }
 
   switch (sh.n) {
     case 16: return launch_gemm_n<16>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);

@@ -351,6 +351,41 @@ def test_paged_decode_empty_row_and_long_context(K):
     np.testing.assert_allclose(lse[1:], ref_lse[1:], rtol=1e-3, atol=1e-3)
 
 
+@pytest.mark.parametrize("hq,hkv,splits", [(32, 8, 2), (32, 32, 1)])
+def test_paged_decode_many_ring_laps_is_deterministic(K, hq, hkv, splits):
+    """Splits of hundreds of pages cycle the stage ring many times (the
+    config-3 / config-5 regime).  Every launch must finish with status 0, give
+    bit-identical outputs, and agree with a torch fp32 reference."""
+
+    rows, ctx, d, ps = 4, 8192 - 5, 128, 16
+    g = torch.Generator(device="cuda").manual_seed(7)
+    pages = -(-ctx // ps)
+    pool = rows * pages + 8
+    cache = torch.randn(pool, 2, ps, hkv, d, device="cuda", dtype=torch.bfloat16, generator=g)
+    perm = torch.randperm(pool, device="cuda", generator=g)[: rows * pages].to(torch.int32)
+    indptr = _i32(np.arange(rows + 1) * pages)
+    last = _i32([ctx - (pages - 1) * ps] * rows)
+    q = torch.randn(rows, hq, d, device="cuda", dtype=torch.bfloat16, generator=g)
+    ws = torch.zeros(rows * hq * splits * (d + 1) * 4 + (1 << 20), dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    outs = []
+    for _ in range(12):
+        outs.append(K.paged_decode(q, cache, indptr, perm, last, num_splits=splits, workspace=ws, status=status))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    # torch fp32 reference over the gathered pages
+    kv = cache[perm.long()].view(rows, pages, 2, ps, hkv, d).float()
+    k = kv[:, :, 0].reshape(rows, pages * ps, hkv, d)[:, :ctx]
+    v = kv[:, :, 1].reshape(rows, pages * ps, hkv, d)[:, :ctx]
+    grp = hq // hkv
+    qf = q.float().view(rows, hkv, grp, d)
+    s = torch.einsum("bhgd,bthd->bhgt", qf, k) / math.sqrt(d)
+    ref = torch.einsum("bhgt,bthd->bhgd", torch.softmax(s, dim=-1), v).reshape(rows, hq, d)
+    assert float((outs[0].float() - ref).abs().max()) <= ATOL
+
+
 def test_paged_decode_reports_out_of_range_page(K):
     cache = torch.zeros(4, 2, 16, 2, 64, dtype=torch.bfloat16, device="cuda")
     q = torch.ones(1, 4, 64, dtype=torch.bfloat16, device="cuda")
