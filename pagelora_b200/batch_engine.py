@@ -386,9 +386,15 @@ class BatchDecodeEngine:
         """Branch batch (the reference's generation.py:872-1132 shape): every
         row continues the same `prefix` with its own suffix.  The prefix K/V
         are stored once in shared pages; each row's page table holds only its
-        suffix (and the tokens it decodes), and decode attends to the prefix
-        through the shared-prefix pass.  All rows must use the same adapter
-        (the prefix K/V depend on it).  Returns each row's first token."""
+        own tokens, and decode attends to the shared pages through the
+        shared-prefix pass.  As in the reference's KV manager
+        (pagelora_b200.prefix_plan.plan_prefix), only whole pages of the
+        prefix are shared: a partial last page is recomputed into each row's
+        own pages.  All rows must use the same adapter (the prefix K/V depend
+        on it).  Returns each row's first token."""
+
+        from pagelora_b200.page_table import KVBlockSpan
+        from pagelora_b200.prefix_plan import plan_prefix
 
         if len(suffixes) != self.rows:
             raise ValueError("one suffix per row")
@@ -397,23 +403,33 @@ class BatchDecodeEngine:
         ps = self.page_size
         n_pre = len(prefix)
         prefix_pages = [self._alloc_page() for _ in range(-(-n_pre // ps))]
+        # what each branch would reuse after the prefix was cached: its radix
+        # match is the prefix, its spans the prefix pages
+        spans = [KVBlockSpan(p, 0, min(ps, n_pre - i * ps)) for i, p in enumerate(prefix_pages)]
+        n_shared = min(plan_prefix(n_pre + len(suf), n_pre, spans, ps).prefill_from for suf in suffixes)
+        shared_pages = prefix_pages[: n_shared // ps]
+        for p in prefix_pages[n_shared // ps:]:
+            self.free_pages.append(p)
         firsts = []
         self.prefill_logits = []
         for r, suf in enumerate(suffixes):
             n = n_pre + len(suf)
-            pages = [self._alloc_page() for _ in range(-(-len(suf) // ps))]
-            self.host_pages[r], self.host_last[r] = list(pages), len(suf) - (len(pages) - 1) * ps
+            pages = [self._alloc_page() for _ in range(-(-(n - n_shared) // ps))]
+            self.host_pages[r], self.host_last[r] = list(pages), (n - n_shared) - (len(pages) - 1) * ps
             pos = torch.arange(n)
-            page_of = torch.tensor([prefix_pages[p // ps] if p < n_pre else pages[(p - n_pre) // ps]
+            page_of = torch.tensor([shared_pages[p // ps] if p < n_shared else pages[(p - n_shared) // ps]
                                     for p in pos.tolist()], dtype=torch.int32, device=self.device)
-            off_of = torch.tensor([p % ps if p < n_pre else (p - n_pre) % ps for p in pos.tolist()],
+            off_of = torch.tensor([p % ps if p < n_shared else (p - n_shared) % ps for p in pos.tolist()],
                                   dtype=torch.int32, device=self.device)
-            keep = torch.arange(0 if r == 0 else n_pre, n, device=self.device)  # the prefix K/V once
+            keep = torch.arange(0 if r == 0 else n_shared, n, device=self.device)  # the shared K/V once
             logits = self._forward_prompt(prefix + suf, self.row_adapter[r], page_of, off_of, keep)
             self.prefill_logits.append(logits)
             firsts.append(int(torch.argmax(logits).item()))
         self.context_len = [n_pre + len(suf) for suf in suffixes]
-        self._set_shared_prefix(prefix_pages, n_pre)
+        if n_shared > 0:
+            self._set_shared_prefix(shared_pages, n_shared)
+        else:
+            self.cascade, self.prefix_pages, self.prefix_len = None, [], 0
         self._sync_rows()
         self.token_buf.copy_(torch.tensor(firsts, dtype=torch.int64))
         self.plan()

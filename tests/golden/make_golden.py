@@ -15,6 +15,11 @@ Fixtures written next to this script:
                           packed LoRA delta, merge_serve_lora and
                           effective_weights.effective_linear /
                           effective_packed_linear outputs
+  prefix_plans.json       model/kvcache/paged_kvcache_manager.py prefix reuse
+                          (radix lookup result -> match_len, prefill_from,
+                          prefix_spans), the batch page table of branch
+                          batches (the config-4 shape) and the admission
+                          estimates
   tiny_llama_greedy.npz   BASELINE config 1: the reference's HF eager
                           generate path (model/generation.py:312-375) on a
                           random-init tiny Llama with LoRA (q, v) wrapped by
@@ -256,6 +261,72 @@ def make_tiny_greedy(out: Path) -> None:
     print(f"tiny_llama_greedy.npz: tokens {new[:8]}... checksum {checksum:.6f}")
 
 
+def make_prefix_plans(out: Path) -> None:
+    """model/kvcache/paged_kvcache_manager.py on CPU: commit cached prompts,
+    then begin requests (single and branch batches, the config-4 shape at
+    page 16) and record each radix lookup result (key_match_len, key_spans)
+    with the request's match_len / prefill_from / prefix_spans, the batch page
+    table and the admission answers."""
+
+    from model.kvcache.flashinfer_page_table import build_flashinfer_batch_page_table
+    from model.kvcache.paged_kvcache_manager import FlashInferPagedKVCacheManager
+    from model.kvcache.radix_types import FULL_KEY
+
+    def spans_of(spans):
+        return [[int(s.block_id), int(s.start), int(s.length)] for s in spans]
+
+    rng = random.Random(4)
+    cases = []
+    scenarios = [
+        # (page_size, committed prompt lengths, new prompts as (base index, shared len, extra len))
+        (16, [2048], [(0, 2048, 64)] * 16),               # config 4: shared prefix + 64-token suffixes
+        (16, [2050], [(0, 2050, 64), (0, 2050, 0), (0, 2049, 5), (0, 17, 3)]),
+        (16, [100, 40], [(0, 100, 0), (1, 33, 10), (0, 96, 1), (1, 0, 7)]),
+        (4, [9, 13], [(0, 9, 2), (1, 13, 0), (1, 8, 8), (0, 4, 0)]),
+    ]
+    for ps, committed, news in scenarios:
+        mgr = FlashInferPagedKVCacheManager(num_layers=1, page_size=ps, max_pages=4096)
+        bases = []
+        for n in committed:
+            toks = [rng.randrange(1, 32000) for _ in range(n)]
+            req = mgr.begin_request(toks, "a")
+            mgr.reserve_chunk(req, n - req.prefill_from)
+            mgr.commit_request(req, toks)
+            bases.append(toks)
+        prompts = []
+        for bi, shared, extra in news:
+            prompts.append(bases[bi][:shared] + [rng.randrange(1, 32000) for _ in range(extra)])
+        lookups = []
+        for p in prompts:
+            m = mgr._prefix_cache.lookup(p, keys=(FULL_KEY("a"),))
+            lookups.append({"key_match_len": int(m.key_match_len.get(FULL_KEY("a"), 0)),
+                            "key_spans": spans_of(m.key_spans.get(FULL_KEY("a"), []))})
+        available = int(mgr.available_pages)
+        reqs = mgr.begin_batch_requests(prompts, "a")
+        rows = []
+        for p, r, lk in zip(prompts, reqs, lookups):
+            new = len(p) - r.prefill_from
+            rows.append({"prompt_len": len(p), **lk, "match_len": int(r.match_len), "prefill_from": int(r.prefill_from),
+                         "prefix_spans": spans_of(r.prefix_spans),
+                         "new_pages": int(mgr.estimate_request_new_pages(r, prefill_tokens=new, max_decode_tokens=128)),
+                         "fits": bool(mgr.can_fit_request(r, prefill_tokens=new, max_decode_tokens=128,
+                                                          reserve_pages=len(prompts))),
+                         "max_decode": int(mgr.max_decode_tokens_that_fit(r, prefill_tokens=new,
+                                                                          requested_decode_tokens=100000,
+                                                                          reserve_pages=len(prompts)))})
+        for r in reqs:
+            mgr.reserve_chunk(r, len(r.token_ids) - r.prefill_from)
+        table = build_flashinfer_batch_page_table([r.prefix_spans + r.new_spans for r in reqs], page_size=ps,
+                                                  device=torch.device("cpu"))
+        cases.append({"page_size": ps, "available_pages": available, "rows": rows,
+                      "row_spans": [spans_of(r.prefix_spans + r.new_spans) for r in reqs],
+                      "indptr": table.paged_kv_indptr.tolist(), "indices": table.paged_kv_indices.tolist(),
+                      "last_page_len": table.paged_kv_last_page_len.tolist()})
+        mgr.abort_batch_requests(reqs)
+    out.write_text(json.dumps({"source": "model/kvcache/paged_kvcache_manager.py", "cases": cases}))
+    print(f"prefix_plans.json: {len(cases)} scenarios, {sum(len(c['rows']) for c in cases)} requests")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("PAGELORA_REFERENCE", "/root/reference"))
@@ -263,13 +334,15 @@ def main() -> None:
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    todo = args.only.split(",") if args.only else ["page_tables", "lora", "tiny"]
+    todo = args.only.split(",") if args.only else ["page_tables", "lora", "tiny", "prefix"]
     if "page_tables" in todo:
         make_page_tables(HERE / "page_tables.json")
     if "lora" in todo:
         make_lora_cases(HERE / "lora_cases.npz")
     if "tiny" in todo:
         make_tiny_greedy(HERE / "tiny_llama_greedy.npz")
+    if "prefix" in todo:
+        make_prefix_plans(HERE / "prefix_plans.json")
 
 
 if __name__ == "__main__":

@@ -101,11 +101,14 @@ def test_batch_decode_crosses_page_boundaries_and_random_pages(cuda_device):
 SMALL_QWEN = ModelSpec("small-qwen3", 2, 512, 8, 2, 128, 1024, 4096, 1.0e6, 1e-6, qk_norm=True)
 
 
-@pytest.mark.parametrize("rows", [6, 10], ids=["6rows-gemv", "10rows-gemm"])
-def test_shared_prefix_branches_match_oracle(cuda_device, rows):
-    """Branch batch: rows continue one shared prefix (stored once) with their
-    own suffixes; decode runs the shared-prefix pass + suffix pass + merge.
-    Every row's logits equal an oracle decoder that ran prefix + suffix alone."""
+@pytest.mark.parametrize("rows,prefix_len", [(6, 48), (10, 48), (6, 53)],
+                         ids=["6rows-gemv", "10rows-gemm", "6rows-prefix-mid-page"])
+def test_shared_prefix_branches_match_oracle(cuda_device, rows, prefix_len):
+    """Branch batch: rows continue one shared prefix (its whole pages stored
+    once, a partial last page recomputed per row as the reference's KV manager
+    does) with their own suffixes; decode runs the shared-prefix pass + suffix
+    pass + merge.  Every row's logits equal an oracle decoder that ran
+    prefix + suffix alone."""
 
     from pagelora_b200.batch_engine import BatchDecodeEngine
 
@@ -116,10 +119,11 @@ def test_shared_prefix_branches_match_oracle(cuda_device, rows):
     eng = BatchDecodeEngine(spec, dict(w), adapters=[lo], lora_spec=lspec, row_adapter=[0] * rows, page_size=16,
                             max_context=160, device=cuda_device)
     eng.shuffle_free_pages(seed=9)
-    prefix = random_prompt(spec.vocab, 48, seed=1)          # ends on a page boundary
+    prefix = random_prompt(spec.vocab, prefix_len, seed=1)
     rng = np.random.default_rng(rows)
     suffixes = [random_prompt(spec.vocab, int(n), seed=20 + i) for i, n in enumerate(rng.integers(1, 30, size=rows))]
     eng.prefill_shared(prefix, suffixes)
+    assert eng.prefix_len == prefix_len // 16 * 16  # whole pages only
     oracles, nxt = [], []
     for suf in suffixes:
         o = OracleDecoder(spec, {k: v.float() for k, v in w.items()},
