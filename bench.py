@@ -29,6 +29,11 @@ workloads (``--no-extra`` skips them), reported under "workloads":
   config5  Llama-3-8B arch, 8 x 32768-token contexts, split-KV over the N
            ranks with an NCCL all-gather of the partial (O, LSE) per layer.
 Their contexts hold random K/V (their prefill is not part of a decode step).
+Kernel-level workloads follow: the paged prefill kernel (prefill_config2 /
+prefill_config5, TFLOP/s against the bf16 peak) and the paged decode
+attention kernel alone at the config-3 / config-5 layer shapes
+(decode_attention_config3 / _config5, GB/s against the measured HBM peak).
+``--prefill-only`` / ``--attention-only`` run just those (profiling runs).
 """
 
 from __future__ import annotations
@@ -575,6 +580,83 @@ def run_prefill(device, steps: int, warmup: int) -> dict:
     return out
 
 
+def run_decode_attention(device, steps: int, warmup: int) -> dict:
+    """Paged decode attention (pl_paged_decode) alone at the layer shapes of
+    config 3 (64 rows, contexts U[512, 4096] seed 0, Llama-2-7B heads 32/32)
+    and config 5 (8 rows x 32768, Llama-3-8B heads 32/8): page size 16,
+    shuffled pages, random q / K / V, the plan's split count.  Eight launches
+    over the same pool (1.1 / 2.4 GB, larger than L2) are replayed as one CUDA
+    graph; bytes are the K/V read plus q and O."""
+
+    import numpy as np
+    import torch
+
+    from pagelora_b200 import kernels as K
+    from pagelora_b200.synthetic import WORKLOADS
+
+    peak, kind = _peaks()
+    cases = (("config3", np.random.default_rng(0).integers(512, 4097, size=64).tolist()),
+             ("config5", [32768] * 8))
+    out = {}
+    for name, lens in cases:
+        spec = WORKLOADS[name].model
+        hq, hkv, d, ps = spec.num_qo_heads, spec.num_kv_heads, spec.head_dim, 16
+        pages = [-(-n // ps) for n in lens]
+        total = sum(pages)
+        g = torch.Generator(device=device).manual_seed(len(lens))
+        cache = torch.randn(total + 16, 2, ps, hkv, d, generator=g, device=device).to(torch.bfloat16)
+        i32 = dict(dtype=torch.int32, device=device)
+        indices = torch.randperm(total + 16, generator=g, device=device)[:total].to(torch.int32)
+        indptr = torch.tensor(np.cumsum([0] + pages).tolist(), **i32)
+        last = torch.tensor([n - (p - 1) * ps for n, p in zip(lens, pages)], **i32)
+        q = torch.randn(len(lens), hq, d, generator=g, device=device).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        plan = K.decode_plan(len(lens), hq, hkv, d, ps, total)
+        ws_buf = torch.zeros(max(int(plan.workspace_bytes), 256), dtype=torch.uint8, device=device)
+        status = torch.zeros(1, **i32)
+
+        def launch():
+            K.paged_decode(q, cache, indptr, indices, last, num_splits=int(plan.num_splits), workspace=ws_buf,
+                           status=status, out=o)
+
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                launch()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(8):
+                launch()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        if int(status.item()) != 0:
+            raise RuntimeError(f"decode attention status {int(status.item())}")
+        us = e0.elapsed_time(e1) * 1e3 / (8 * steps)
+        nbytes = sum(lens) * hkv * d * 2 * 2 + 2 * len(lens) * hq * d * 2
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"metric": f"paged decode attention, one layer of {len(lens)} rows ({spec.name} heads {hq}/{hkv}, "
+                               f"head_dim {d}, page 16)", "value": gbs, "unit": "GB/s", "us_per_launch": us,
+                     "bytes_per_launch": nbytes, "num_splits": int(plan.num_splits), "ctas": int(plan.ctas),
+                     "steps": steps, "warmup": warmup,
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                                  "peak_kind": kind},
+                     "l2": "pool larger than L2 (no flush)", "gpu_launches_per_step": 8,
+                     "timing": "8 launches replayed as one CUDA graph, CUDA events around the replays",
+                     "data": "synthetic: random q/K/V, shuffled pages"}
+        del cache, graph
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -594,6 +676,13 @@ def run_ours(args) -> None:
     if plbuild.is_stale():
         plbuild.build()
     load_library()
+    if args.attention_only:  # profiling runs of the decode attention kernel alone
+        at = run_decode_attention(device, max(1, args.steps), max(3, args.warmup))
+        if rank == 0:
+            print(json.dumps({"profile": "decode_attention", **{k: v["value"] for k, v in at.items()}}), flush=True)
+        if ws > 1:
+            dist.destroy_process_group()
+        return
     if args.prefill_only:  # profiling runs of the prefill kernel alone
         pf = run_prefill(device, max(1, args.steps), max(3, args.warmup))
         if rank == 0:
@@ -737,6 +826,20 @@ def run_ours(args) -> None:
             r["roofline"]["frac"] = r["value"] / r["roofline"]["peak"]
             r["scaling"] = f"replicas x{ws}" if ws > 1 else "1 GPU"
             extra[f"prefill_{k}"] = r
+        # decode attention alone at the config-3 / config-5 layer shapes
+        at = run_decode_attention(device, xs, xw)
+        atv = torch.tensor([at[k]["us_per_launch"] for k in ("config3", "config5")], device=device,
+                           dtype=torch.float64)
+        if ws > 1:
+            dist.all_reduce(atv, op=dist.ReduceOp.MAX)
+        for i, k in enumerate(("config3", "config5")):
+            r = at[k]
+            r["us_per_launch"] = float(atv[i])
+            r["value"] = r["bytes_per_launch"] / (r["us_per_launch"] * 1e-6) / 1e9
+            r["roofline"]["achieved"] = r["value"]
+            r["roofline"]["frac"] = r["value"] / r["roofline"]["peak"]
+            r["scaling"] = f"replicas x{ws}" if ws > 1 else "1 GPU"
+            extra[f"decode_attention_{k}"] = r
     if rank == 0:
         value = ws * steps / (ms * 1e-3)
         e2e = ws * steps / (ms_e2e * 1e-3)
@@ -790,6 +893,8 @@ def main() -> None:
                     help="profiling run: prefill, capture and the timed graph replays only")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the secondary workloads (configs 3, 4 and 5) after the headline measurement")
+    ap.add_argument("--attention-only", action="store_true",
+                    help="profiling run: the decode attention workloads (configs 3 and 5 layer shapes) only")
     ap.add_argument("--prefill-only", action="store_true",
                     help="profiling run: the paged prefill attention workloads only")
     ap.add_argument("--layers", type=int, default=0,
