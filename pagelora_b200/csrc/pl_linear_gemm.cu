@@ -178,6 +178,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     if (lane == 0) flags[2] = i0 < n ? (i0 > pre ? i0 : pre) : n;
+    if (lane == 0) PL_TRACE_POINT(9);
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -197,6 +198,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
+        if (i == 0) PL_TRACE_POINT(2);
         const uint32_t a0 = smem_u32(smem + s * C::kStageBytes);
         const uint32_t b0 = a0 + C::kABytes;
         const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols);
@@ -214,6 +216,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       flags[3] = i;
+      PL_TRACE_POINT(3);
       if (!ok) {
         // Release the epilogue for the segments that will not be computed.
         for (int i2 = i; i2 < n; ++i2) {
@@ -258,6 +261,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         flags[0] = 1;
       }
       tc_fence_after();
+      if (threadIdx.x == 64) {
+        if (seg == 0) PL_TRACE_POINT(4);
+        PL_TRACE_MAX(5);
+      }
       const uint32_t acc = lane_base + (uint32_t)(b * C::kAccCols);
       const int64_t o4 = (int64_t)t * kGemmM + 4 * lane;
       const bool whole = (ka == 0 && len == KB);
@@ -320,6 +327,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           flags[1] = ticket == c_last - c_first ? 1 : 0;
         }
         named_barrier(1, kEpiThreads);
+        if (threadIdx.x == 64) PL_TRACE_MAX(6);
         if (flags[1]) {
           __threadfence();
           const int nslots = c_last - c_first + 1;
