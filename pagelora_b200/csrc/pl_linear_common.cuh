@@ -105,6 +105,8 @@ __device__ __forceinline__ void epilogue_rows4(const GemvArgs& a, int64_t o0, in
   }
 }
 
+constexpr int kGemmTileRows = 128;  // weight rows of one tcgen05 GEMM tile
+
 // Rank-16 LoRA dot product with the B row held in registers (16 bf16) and
 // the down row already rounded to bf16: the fma order of lora_dot.
 __device__ __forceinline__ float lora_dot16(const uint4 (&b)[2], const float* d) {
@@ -135,9 +137,13 @@ __device__ __forceinline__ float lora_dot16(const uint4 (&b)[2], const float* d)
 // sdown / sad (optional, rank 16): the down rows [T][sR] rounded to bf16 and
 // the adapter ids [T], staged in shared memory; each adapter's B rows are then
 // loaded once for consecutive tokens that share it.
+// sdelta (optional, with sad): the finished LoRA terms bf16(bf16(d) * scale)
+// of this tile, [T][128] bf16 with row o0 at column o0 - sdelta_row0,
+// computed ahead by the caller; they replace the expand here.
 __device__ __forceinline__ void epilogue_rows4_x4(const GemvArgs& a, int64_t o0, const int (&tok)[4], int nt,
                                                   const float (&v)[4][4], const float* sdown = nullptr,
-                                                  int sR = 0, const int32_t* sad = nullptr) {
+                                                  int sR = 0, const int32_t* sad = nullptr,
+                                                  const bf16* sdelta = nullptr, int64_t sdelta_row0 = 0) {
   if (o0 >= a.n_out) return;
   const bool vec = o0 + 4 <= a.n_out && (a.lora_b == nullptr || a.rank == 16) &&
                    ((a.y_stride | a.res_stride) & 3) == 0 &&
@@ -166,7 +172,19 @@ __device__ __forceinline__ void epilogue_rows4_x4(const GemvArgs& a, int64_t o0,
       if (k < nt) res[k] = *reinterpret_cast<const uint2*>(a.residual + tok[k] * a.res_stride + o0);
   }
   float dl[4][4] = {};
-  if (a.lora_b != nullptr) {
+  if (a.lora_b != nullptr && sdelta != nullptr) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k < nt) {
+        const uint2 d2 = *reinterpret_cast<const uint2*>(sdelta + tok[k] * kGemmTileRows + (o0 - sdelta_row0));
+        const float2 d01 = unpack_bf16x2(d2.x), d23 = unpack_bf16x2(d2.y);
+        dl[k][0] = d01.x;
+        dl[k][1] = d01.y;
+        dl[k][2] = d23.x;
+        dl[k][3] = d23.y;
+      }
+    }
+  } else if (a.lora_b != nullptr) {
     int sl[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -216,7 +234,7 @@ __device__ __forceinline__ void epilogue_rows4_x4(const GemvArgs& a, int64_t o0,
       if (a.bias != nullptr) x += bias[i];
       if (a.lora_b != nullptr) {
         float vb = bfr(x);
-        if (ad[k] >= 0) vb = bfr(vb + bfr(bfr(dl[k][i]) * a.lora_scale));
+        if (ad[k] >= 0) vb = bfr(vb + (sdelta != nullptr ? dl[k][i] : bfr(bfr(dl[k][i]) * a.lora_scale)));
         x = vb;
       }
       if (a.residual != nullptr) x = rv[i] + bfr(x);

@@ -43,6 +43,7 @@ struct GemmArgs {
   float* partial;      // [m_tiles][max_slots][N][128] fp32
   int32_t* counters;   // [m_tiles] arrival tickets, zero between calls
   int32_t lora_stage;  // bytes of shared memory holding the rank-16 LoRA down rows and adapter ids (0: none)
+  int32_t lora_delta;  // bytes holding the precomputed LoRA terms of the CTA's last tile (0: none)
 };
 
 // N: tokens padded (UMMA N).  KCS: 64-column chunks per K block; with KCS > 1
@@ -63,6 +64,9 @@ struct GemmCfg {
 
 __host__ __device__ inline int gemm_smem_bytes(int stage_bytes, int stages, int lora_stage) {
   return 1024 + stages * stage_bytes + 16 * kGemmM * 4 + lora_stage + (2 * stages + 4) * 8 + 32;
+}
+__host__ __device__ inline int gemm_smem_bytes(int stage_bytes, int stages, int lora_stage, int lora_delta) {
+  return gemm_smem_bytes(stage_bytes, stages, lora_stage) + lora_delta;
 }
 
 __host__ __device__ inline int unit_begin(int c, int units, int ctas) {
@@ -97,7 +101,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Rank-16 LoRA epilogue inputs, staged once: down rows rounded to bf16
   // [T][num_slices * 16], then the tokens' adapter ids [T].
   float* lds = reinterpret_cast<float*>(smem + S * C::kStageBytes + C::kStageTile);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes + C::kStageTile + g.lora_stage);
+  // The precomputed LoRA terms of the CTA's last tile, [T][128] bf16.
+  bf16* sdl = reinterpret_cast<bf16*>(smem + S * C::kStageBytes + C::kStageTile + g.lora_stage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes + C::kStageTile + g.lora_stage +
+                                               g.lora_delta);
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;  // [2] accumulator ready
   uint64_t* acce = accf + 2;   // [2] accumulator drained
@@ -250,6 +257,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       sdown = lds;
       sad = lad;
     }
+    // The LoRA terms of the tile that this CTA's last segment covers: its
+    // epilogue (a whole tile, or the merge of the shared tile's partials, at
+    // the very end of the CTA) then only adds them.  Computed here, while the
+    // first accumulator is still being filled.
+    // Only a CTA with at least half a tile of units of its own: with fewer,
+    // a tile has many contributors that finish together, the precomputed terms
+    // are mostly unused, and computing them delays the partials.
+    const int t_pre = (g.lora_delta && 2 * n >= KB) ? (u1 - 1) / KB : -1;
+    if (t_pre >= 0) {
+      const int64_t row0 = (int64_t)t_pre * kGemmM;
+      // lane: rows 4*lane .. 4*lane+3 of the tile; warp ew: a contiguous quarter
+      // of the tokens, so a B row set is loaded once per adapter run
+      const int64_t o0 = row0 + 4 * lane;
+      int sl[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sl[i] = 0;
+        while (sl[i] < g.e.num_slices - 1 && o0 + i >= g.e.slice_end[sl[i]]) ++sl[i];
+      }
+      const bool rows_ok = o0 + 4 <= g.e.n_out;
+      int cur = -1;
+      uint4 b[4][2] = {};
+      const int tq = (T + 3) / 4;
+      for (int tok = ew * tq; tok < T && tok < (ew + 1) * tq; ++tok) {
+        const int ad = sad[tok];
+        float dv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ad >= 0 && rows_ok) {
+          if (ad != cur) {
+            cur = ad;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4* br = reinterpret_cast<const uint4*>(g.e.lora_b + ((int64_t)ad * g.e.n_out + o0 + i) * 16);
+              b[i][0] = br[0];
+              b[i][1] = br[1];
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dv[i] = bfr(bfr(lora_dot16(b[i], sdown + tok * R + sl[i] * 16)) * g.e.lora_scale);
+        }
+        *reinterpret_cast<uint2*>(sdl + tok * kGemmM + 4 * lane) =
+            make_uint2(pack_bf16x2(dv[0], dv[1]), pack_bf16x2(dv[2], dv[3]));
+      }
+      named_barrier(1, kEpiThreads);
+    }
     int seg = 0;
     for (int i = 0; i < n;) {
       const int u = u0 + i, t = u / KB, ka = u % KB;
@@ -295,7 +347,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               vals[h][3] = r4.w;
               if (16 * c + j < T) nt = h + 1;
             }
-            epilogue_rows4_x4(g.e, o4, toks, nt, vals, sdown, R, sad);
+            epilogue_rows4_x4(g.e, o4, toks, nt, vals, sdown, R, sad, t == t_pre ? sdl : nullptr,
+                              (int64_t)t * kGemmM);
           }
           named_barrier(1, kEpiThreads);
         }
@@ -365,7 +418,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                   a4[h][3] += p[h][k].w;
                 }
             }
-            if (!flags[0]) epilogue_rows4_x4(g.e, o4, toks, nt, a4, sdown, R, sad);
+            if (!flags[0])
+              epilogue_rows4_x4(g.e, o4, toks, nt, a4, sdown, R, sad, t == t_pre ? sdl : nullptr,
+                                (int64_t)t * kGemmM);
           }
           if (ew == 0 && lane == 0) g.counters[t] = 0;
         }
@@ -544,6 +599,7 @@ int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
 constexpr int kGemmSmemBudget = 200 * 1024;
 constexpr int kLoraStageMax = 16 * 1024;
+constexpr int kGemmSmemMax = 227 * 1024;  // dynamic shared memory per CTA on sm_100
 
 struct GemmShape {
   int n, kcs, stages, m_tiles, kblocks, units, ctas, max_slots, stage_bytes;
@@ -584,7 +640,7 @@ template <int N, int KCS>
 int32_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int ctas, int stages,
                     void* stream) {
   auto kern = pl::linear_tc_kernel<N, KCS>;
-  const int smem = pl::gemm_smem_bytes(pl::GemmCfg<N, KCS>::kStageBytes, stages, g.lora_stage);
+  const int smem = pl::gemm_smem_bytes(pl::GemmCfg<N, KCS>::kStageBytes, stages, g.lora_stage, g.lora_delta);
   int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (st != PL_OK) return st;
   return pl_host::launch_pdl(kern, dim3(ctas), dim3(pl::kGemmThreads), smem, stream, wm, xm, g);
@@ -693,6 +749,10 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   if (lora_b != nullptr && lora_rank == 16 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0) {
     const int64_t bytes = (int64_t)num_tokens * a.num_slices * 16 * 4 + (((int64_t)num_tokens * 4 + 15) & ~int64_t(15));
     if (bytes <= kLoraStageMax) g.lora_stage = static_cast<int32_t>(bytes);
+    // and the last tile's finished LoRA terms, when they fit beside the ring
+    const int32_t delta = num_tokens * pl::kGemmM * 2;
+    if (g.lora_stage && pl::gemm_smem_bytes(sh.stage_bytes, sh.stages, g.lora_stage, delta) <= kGemmSmemMax)
+      g.lora_delta = delta;
   }
 
   switch (sh.n) {
