@@ -137,59 +137,24 @@ def _dist():
     return ws, rank, local
 
 
-# -------------------------------------------------------------- CPU oracle
-def cpu_decode_sample(context: int, steps: int, warmup: int) -> dict:
-    """Time the oracle port's decode step on a bounded sample: 2 full-size
-    Qwen3-8B layers + lm_head at the given context, scaled to 36 layers."""
+# ------------------------------------------------------ CPU reference path
+def host_threads() -> int:
+    """Host threads this process may run on (torchrun's OMP_NUM_THREADS=1 is overridden explicitly)."""
 
-    import numpy as np
-    import torch
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
-    from oracle.decoder import OracleDecoder
-    from pagelora_b200.synthetic import WORKLOADS, ModelSpec, make_lora_weights, make_model_weights
 
-    wl = WORKLOADS[WORKLOAD]
-    full = wl.model
-    sample_layers = 2
-    # Tied embeddings: the head matvec has the full [vocab, hidden] cost without a second table.
-    spec = ModelSpec(full.name + "-sample", sample_layers, full.hidden, full.num_qo_heads, full.num_kv_heads,
-                     full.head_dim, full.intermediate, full.vocab, full.rope_theta, full.rms_eps, full.qk_norm,
-                     tie_embeddings=True)
-    torch.set_num_threads(os.cpu_count() or 1)
-    weights = make_model_weights(spec, seed=0, dtype=torch.float32)
-    loras = make_lora_weights(spec, wl.lora, dtype=torch.float32)
-    pages = -(-(context + steps + warmup + 2) // wl.page_size)
-    dec = OracleDecoder(spec, weights, loras, wl.lora.scale, page_size=wl.page_size, num_pages=pages + 2,
-                        bf16=False)
-    del weights
-    rng = np.random.default_rng(0)
-    # Fill the context with random K/V instead of a CPU prefill (decode cost
-    # does not depend on where the cached K/V came from).
-    n_ctx_pages = -(-context // wl.page_size)
-    for _ in range(n_ctx_pages):
-        dec.pages.append(dec.free.pop())
-    dec.cache[:, dec.pages] = rng.normal(size=dec.cache[:, dec.pages].shape).astype(np.float32)
-    dec.last = context - (n_ctx_pages - 1) * wl.page_size
-    dec.pos = context
-    # Split the step's time into layers and head by timing the head separately.
-    head = dec.w.get("lm_head.weight", dec.w["model.embed_tokens.weight"])
-    tok = 1
-    for _ in range(warmup):
-        tok, _ = dec.step(tok)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        tok, _ = dec.step(tok)
-    t_step = (time.perf_counter() - t0) / steps
-    x = np.ones((1, spec.hidden), np.float32)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        x @ head.T
-    t_head = (time.perf_counter() - t0) / steps
-    per_token = (t_step - t_head) / sample_layers * full.num_layers + t_head
-    return {"value": 1.0 / per_token, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": (f"oracle numpy decode step, {sample_layers} of {full.num_layers} full-size layers + lm_head at "
-                       f"context {context}, {steps} steps, scaled to {full.num_layers} layers"),
-            "s_per_token": per_token}
+def cpu_decode_sample(steps: int, warmup: int) -> dict:
+    """The reference's HF eager CPU path at the config-2 workload (all 36
+    full-size layers + lm_head, context 2048), timed over ``steps`` decode
+    tokens on all host threads (oracle.hf_eager)."""
+
+    from oracle.hf_eager import time_decode
+
+    return time_decode(WORKLOAD, steps=steps, warmup=warmup, threads=host_threads())
 
 
 def run_reference(args) -> None:
@@ -197,13 +162,19 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     steps = max(1, args.steps)
-    cb = cpu_decode_sample(2048, steps, max(0, args.warmup))
+    warmup = max(0, args.warmup)
+    t0 = time.perf_counter()
+    cb = cpu_decode_sample(steps, warmup)
     line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": steps, "warmup": args.warmup, "ms_per_step": 1000.0 * cb["s_per_token"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "steps": steps, "warmup": warmup, "ms_per_step": 1000.0 * cb["s_per_token"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
             "config": {"workload": WORKLOAD, "model": "Qwen3-8B-arch random init", "global_batch": 1,
-                       "context": 2048, "page_size": 16, "lora": "r16 q/k/v/o no-merge"},
+                       "prompt_len": 2048, "page_size": 16, "lora": "r16 alpha32 q/k/v/o no-merge",
+                       "path": "HF transformers eager forward + LoRALinear (model/generation.py:312-375)",
+                       "device": "cpu", "cpu": cb["cpu"], "threads": cb["cores"]},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "build_s": cb["build_s"], "run_s": time.perf_counter() - t0,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -847,7 +818,7 @@ def run_ours(args) -> None:
         stream_gbs = dom["bytes_per_launch"] / (gstream["us_per_launch"] * 1e-6) / 1e9
         if args.layers:
             raise SystemExit("--layers is for profiling runs only (use it with --profile)")
-        cpu = cpu_decode_sample(wl.prompt_len, 3, 1) if ws == 1 else None
+        cpu = cpu_decode_sample(3, 1) if ws == 1 else None
         # attention + LoRA bytes of one step over its measured kernel time
         att = kern.get("paged_decode_qkv", kern.get("paged_decode", {}))
         line = {
@@ -874,10 +845,17 @@ def run_ours(args) -> None:
             "attention_gbs": att.get("achieved_gbs"),
             "clocks": clk.summary(),
         }
-        if extra:
-            line["workloads"] = extra
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if extra:
+            line["workloads"] = extra
+            # Last key, short: the per-workload figures stay readable in a truncated tail of the line.
+            line["workloads_summary"] = {
+                "n_gpus": ws, "config2_tok_s": round(value, 1),
+                **{f"{k}_tok_s": round(extra[k]["value"], 1) for k in ("config3", "config4", "config5")},
+                **{f"{k}_ms_per_step": round(extra[k]["ms_per_step"], 3) for k in ("config3", "config4", "config5")},
+                **{f"{k}_frac": round(extra[k]["frac_of_peak_per_gpu"], 3) for k in ("config3", "config4", "config5")},
+            }
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.destroy_process_group()

@@ -273,9 +273,15 @@ int32_t pl_paged_decode_f32(const void *q, int64_t q_stride_b, int64_t q_stride_
  *     remaining ~4 MiB.
  *   - The first call on each device (that device current) looks up the
  *     array's address and clears it on `stream`; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The array of a freshly loaded library is
+ *     zero already, so the clear is a defensive reset.  The address is
+ *     looked up again (and the array cleared) when the device's current
+ *     context changes, e.g. after cudaDeviceReset.
  *   - One array per device: calls that overlap on a device (two streams,
  *     two host threads) race on it.  Serialise them.
+ *   - Every completed call leaves the counters at zero.  A call whose
+ *     kernel gave up a bounded wait (status word PL_ERR_TIMEOUT) may leave
+ *     a partial count; call pl_fixed_scratch_clear before the next call.
  */
 #define PL_FIXED_SCRATCH_BYTES (4 * 1024 * 1024)
 int32_t pl_paged_decode_fixed_scratch(const void *q, int64_t q_stride_b,
@@ -290,6 +296,15 @@ int32_t pl_paged_decode_fixed_scratch(const void *q, int64_t q_stride_b,
                                       int64_t o_stride_b, int64_t o_stride_h,
                                       float *out_lse, int32_t *status_dev,
                                       void *stream);
+
+/*
+ * Re-zero the arrival counters of this device's fixed scratch array on
+ * `stream` (no reference counterpart; it belongs to
+ * pl_paged_decode_fixed_scratch).  Needed only after a call whose status
+ * word reported PL_ERR_TIMEOUT; allocates nothing.  Same first-call rule as
+ * pl_paged_decode_fixed_scratch.
+ */
+int32_t pl_fixed_scratch_clear(void *stream);
 
 /*
  * Merge S partial attention states per (row, head) by log-sum-exp.
@@ -512,6 +527,17 @@ int32_t pl_linear_lora_gemm(const void *x, int64_t x_stride, int32_t num_tokens,
 int32_t pl_rmsnorm(const void *x, int64_t x_stride, int32_t num_tokens,
                    int32_t k_in, const void *w, float eps, void *y,
                    int64_t y_stride, void *stream);
+
+/*
+ * Hugging Face RMSNorm over rows (two bf16 roundings, as LlamaRMSNorm /
+ * Qwen3RMSNorm compute it): y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))).
+ * With one row per (token, head) and K = head_dim it is the Qwen3 q/k head
+ * norm of model/flashinfer/projection.py:248-262 (_apply_optional_head_norm,
+ * the module call when the FlashInfer norm is off).  K % 8 == 0.
+ */
+int32_t pl_rmsnorm_hf(const void *x, int64_t x_stride, int32_t num_rows,
+                      int32_t k_in, const void *w, float eps, void *y,
+                      int64_t y_stride, void *stream);
 
 /*
  * SwiGLU activation over packed [gate | up] rows: y[t, k] =

@@ -75,6 +75,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I32,
         [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _P, _P],
     ),
+    "pl_fixed_scratch_clear": (_I32, [_P]),
     "pl_paged_decode_f32": (
         _I32,
         [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _P,
@@ -114,6 +115,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _I64, _I32, _P, _P],
     ),
     "pl_rmsnorm": (_I32, [_P, _I64, _I32, _I32, _P, _F, _P, _I64, _P]),
+    "pl_rmsnorm_hf": (_I32, [_P, _I64, _I32, _I32, _P, _F, _P, _I64, _P]),
     "pl_silu_mul": (_I32, [_P, _I64, _I32, _I32, _P, _I64, _P]),
     "pl_lora_merge_weight": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _F, _I32, _I32, _P]),
     "pl_kv_append": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),

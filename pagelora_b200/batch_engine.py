@@ -34,8 +34,7 @@ from pagelora_b200.engine import _rmsnorm_fused, _rmsnorm_hf, _rope
 from pagelora_b200.split_kv import shard_row
 from pagelora_b200.synthetic import LoRASpec, ModelSpec
 
-GEMV_MAX_ROWS = 8
-GEMV_MAX_STAGED_BYTES = 96 * 1024  # activations the decode GEMV keeps in shared memory
+GEMV_MAX_ROWS = K.GEMV_MAX_ROWS
 
 
 def uses_gemv(rows: int, k_in: int) -> bool:
@@ -43,7 +42,7 @@ def uses_gemv(rows: int, k_in: int) -> bool:
     decode GEMV (all rows' activations staged in shared memory) rather than
     the tcgen05 GEMM."""
 
-    return rows <= GEMV_MAX_ROWS and rows * (2 * k_in + 16) <= GEMV_MAX_STAGED_BYTES
+    return K.gemv_fits(rows, k_in)
 
 
 class BatchDecodeEngine:

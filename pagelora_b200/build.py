@@ -13,6 +13,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
@@ -21,6 +22,7 @@ CSRC_DIR = PKG_DIR / "csrc"
 INCLUDE_DIR = REPO_DIR / "include"
 LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libpagelora_b200.so"
+OBJ_DIR = LIB_DIR / "obj"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -62,20 +64,56 @@ def is_stale() -> bool:
     return any(p.stat().st_mtime > built for p in _inputs())
 
 
-def build(verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
-    """Compile all CUDA sources into the shared library and return its path."""
-
-    LIB_DIR.mkdir(parents=True, exist_ok=True)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *(extra_flags or []), f"-I{INCLUDE_DIR}", "-o", str(tmp)]
-    cmd += [str(p) for p in sources()]
+def _run(cmd: list[str], verbose: bool) -> str:
     if verbose:
         print(" ".join(cmd), flush=True)
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stdout}\n{proc.stderr}")
-    if verbose and (proc.stdout or proc.stderr):
-        print(proc.stdout, proc.stderr, sep="\n", flush=True)
+    return proc.stdout + proc.stderr
+
+
+def _obj_stale(src: Path, obj: Path, flags_file: Path, flags: str) -> bool:
+    """An object is rebuilt when missing, older than its source or any shared
+    header, or built with other flags."""
+
+    if not obj.exists() or not flags_file.exists() or flags_file.read_text() != flags:
+        return True
+    built = obj.stat().st_mtime
+    headers = sorted(CSRC_DIR.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h"))
+    return any(p.stat().st_mtime > built for p in [src, *headers])
+
+
+def build(verbose: bool = False, extra_flags: list[str] | None = None, *, force: bool = False) -> Path:
+    """Compile all CUDA sources into the shared library and return its path.
+
+    Each source is compiled to its own object file (in parallel: the files
+    share no device symbols; objects newer than their inputs are kept unless
+    ``force``), then nvcc links them into one shared object."""
+
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    OBJ_DIR.mkdir(parents=True, exist_ok=True)
+    tmp = LIB_PATH.with_suffix(".so.tmp")
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+    objs, jobs = [], []
+    for src in sources():
+        obj = OBJ_DIR / (src.stem + ".o")
+        cmd = [_nvcc(), *ARCH_FLAGS, *compile_flags, *(extra_flags or []), f"-I{INCLUDE_DIR}", "-c", "-o", str(obj),
+               str(src)]
+        flags_file = obj.with_suffix(".flags")
+        objs.append(obj)
+        if force or _obj_stale(src, obj, flags_file, " ".join(cmd)):
+            jobs.append((cmd, flags_file))
+    workers = max(1, min(len(jobs), os.cpu_count() or 1))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        logs = list(pool.map(lambda job: _run(job[0], verbose), jobs))
+    for cmd, flags_file in jobs:
+        flags_file.write_text(" ".join(cmd))
+    if verbose:
+        for log in logs:
+            if log.strip():
+                print(log, flush=True)
+    _run([_nvcc(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *(str(obj) for obj in objs)], verbose)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 
@@ -88,4 +126,4 @@ def ensure_built() -> Path:
 
 if __name__ == "__main__":
     flags = ["-Xptxas", "-v"] if "--ptxas-info" in sys.argv else None
-    print(build(verbose=True, extra_flags=flags))
+    print(build(verbose=True, extra_flags=flags, force="--force" in sys.argv))

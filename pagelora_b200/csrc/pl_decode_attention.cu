@@ -1081,12 +1081,15 @@ extern "C" int32_t pl_merge_states(const float* v_partial, const float* lse_part
 // pl_paged_decode_fixed_scratch: the same kernel, with its split partials
 // and arrival counters in a file-scope device array instead of a caller
 // workspace, for callers that cannot allocate device memory.  One array per
-// device (a __device__ variable exists once in every context); its address
-// is looked up, and the whole array cleared on the caller's stream, by the
-// first call on each device.  Its first kFixedCounterBytes hold the arrival
-// counters whatever the shape, so that calls of different shapes may follow
-// one another (a shape-sized counter region would let one call's partials
-// land on another's counters).
+// context (a __device__ variable exists once in every context that loads
+// the library's module); its address is looked up, and the whole array
+// cleared on the caller's stream, by the first call on each device and again
+// whenever that device's current context is a different one (after a
+// device reset the module is loaded anew and the array may move).  A fresh
+// module's array is zero already; the clear is a defensive reset.  Its first
+// kFixedCounterBytes hold the arrival counters whatever the shape, so that
+// calls of different shapes may follow one another (a shape-sized counter
+// region would let one call's partials land on another's counters).
 
 static __device__ __align__(256) uint8_t g_decode_fixed_scratch[PL_FIXED_SCRATCH_BYTES];
 constexpr int64_t kFixedCounterBytes = 64 * 1024;  // (row, kv head) pairs up to 16384
@@ -1095,27 +1098,64 @@ namespace {
 constexpr int kScratchDevices = 64;
 std::mutex g_fixed_scratch_mu;
 void* g_fixed_scratch_ptr[kScratchDevices] = {};
+void* g_fixed_scratch_ctx[kScratchDevices] = {};
+
+using CtxGetCurrentFn = int (*)(void**);  // cuCtxGetCurrent (CUresult, CUcontext*)
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
 
 int32_t fixed_scratch(void* stream, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return pl_host::record_cuda_error(e);
   if (dev < 0 || dev >= kScratchDevices) return PL_ERR_UNSUPPORTED;
+  const CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  if (get_ctx == nullptr) return PL_ERR_CUDA;
+  void* ctx = nullptr;
+  if (get_ctx(&ctx) != 0) return PL_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_fixed_scratch_mu);
-  if (g_fixed_scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_fixed_scratch);
-    if (e != cudaSuccess) return pl_host::record_cuda_error(e);
-    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255)) return PL_ERR_CUDA;
-    // The counters at the front must start at zero; every call leaves them so.
+  if (ctx != nullptr && ctx == g_fixed_scratch_ctx[dev] && g_fixed_scratch_ptr[dev] != nullptr) {
+    *out = g_fixed_scratch_ptr[dev];
+    return PL_OK;
+  }
+  // First call on this device, a host thread with no context bound yet, or
+  // a new context: look the array up (this binds the device's primary
+  // context when none is current) and clear it only if its context is new.
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_decode_fixed_scratch);
+  if (e != cudaSuccess) return pl_host::record_cuda_error(e);
+  if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255)) return PL_ERR_CUDA;
+  if (get_ctx(&ctx) != 0 || ctx == nullptr) return PL_ERR_CUDA;
+  if (ctx != g_fixed_scratch_ctx[dev] || p != g_fixed_scratch_ptr[dev]) {
+    // The counters at the front must start at zero; every completed call leaves them so.
     e = cudaMemsetAsync(p, 0, PL_FIXED_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return pl_host::record_cuda_error(e);
     g_fixed_scratch_ptr[dev] = p;
+    g_fixed_scratch_ctx[dev] = ctx;
   }
-  *out = g_fixed_scratch_ptr[dev];
+  *out = p;
   return PL_OK;
 }
 }  // namespace
+
+extern "C" int32_t pl_fixed_scratch_clear(void* stream) {
+  void* scratch = nullptr;
+  int32_t st = fixed_scratch(stream, &scratch);
+  if (st != PL_OK) return st;
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, kFixedCounterBytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PL_OK : pl_host::record_cuda_error(e);
+}
 
 extern "C" int32_t pl_paged_decode_fixed_scratch(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                                                  const void* kv_cache, int64_t num_pages, const int32_t* indptr,

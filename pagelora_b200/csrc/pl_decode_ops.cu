@@ -476,6 +476,48 @@ __global__ void __launch_bounds__(256) argmax_kernel(const bf16* __restrict__ lo
   }
 }
 
+// Hugging Face RMSNorm rounding (Qwen3 q/k head norm, LlamaRMSNorm):
+// y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))), one warp per row of K
+// elements (K % 8 == 0), 8 rows per CTA.
+__global__ void __launch_bounds__(256) rmsnorm_hf_kernel(const bf16* __restrict__ x, int64_t x_stride, int rows,
+                                                         int K, const bf16* __restrict__ w, float eps,
+                                                         bf16* __restrict__ y, int64_t y_stride) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bf16* xr = x + (int64_t)row * x_stride;
+  float ss = 0.f;
+  for (int k = lane * 8; k < K; k += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(u[q]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)K + eps);
+  for (int k = lane * 8; k < K; k += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + k);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+    const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 out;
+    uint32_t* uo = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(u[q]);
+      const float2 gw = unpack_bf16x2(uw[q]);
+      const float2 n = unpack_bf16x2(pack_bf16x2(f.x * r, f.y * r));
+      uo[q] = pack_bf16x2(gw.x * n.x, gw.y * n.y);
+    }
+    *reinterpret_cast<uint4*>(y + (int64_t)row * y_stride + k) = out;
+  }
+}
+
 }  // namespace pl
 
 // =================================================================== host
@@ -611,4 +653,16 @@ extern "C" int32_t pl_argmax(const void* logits, int64_t stride, int32_t vocab, 
   return pl_host::launch_pdl(pl::argmax_kernel, dim3(chunks, num_tokens), dim3(256), 0, stream,
                              static_cast<const pl::bf16*>(logits), stride, (int)vocab, chunk, out_ids, cand_v, cand_i,
                              tickets);
+}
+
+extern "C" int32_t pl_rmsnorm_hf(const void* x, int64_t x_stride, int32_t num_rows, int32_t k_in, const void* w,
+                                 float eps, void* y, int64_t y_stride, void* stream) {
+  if (num_rows == 0) return PL_OK;
+  if (x == nullptr || w == nullptr || y == nullptr || num_rows < 0 || k_in <= 0) return PL_ERR_INVALID_ARGUMENT;
+  if (k_in % 8 || x_stride % 8 || y_stride % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+    return PL_ERR_UNSUPPORTED;
+  return pl_host::launch_pdl(pl::rmsnorm_hf_kernel, dim3((num_rows + 7) / 8), dim3(256), 0, stream,
+                             static_cast<const pl::bf16*>(x), x_stride, (int)num_rows, (int)k_in,
+                             static_cast<const pl::bf16*>(w), eps, static_cast<pl::bf16*>(y), y_stride);
 }

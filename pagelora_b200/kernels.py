@@ -406,6 +406,18 @@ def linear_lora_fused(
     return out
 
 
+GEMV_MAX_ROWS = 8
+GEMV_MAX_STAGED_BYTES = 96 * 1024  # activations the decode GEMV keeps in shared memory
+GEMM_MAX_ROWS = 128
+
+
+def gemv_fits(rows: int, k_in: int) -> bool:
+    """Whether :func:`linear_lora_fused` takes ``rows`` tokens of ``k_in``
+    inputs: every row's activations are staged in shared memory."""
+
+    return rows <= GEMV_MAX_ROWS and rows * (2 * k_in + 16) <= GEMV_MAX_STAGED_BYTES
+
+
 def gemm_plan(num_tokens: int, k_in: int, n_out: int, num_ctas: int = 0) -> _capi.GemmPlan:
     """Work split of :func:`linear_lora_gemm` (``num_ctas`` 0: one CTA per SM)."""
 
@@ -479,6 +491,19 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor
     if out is None:
         out = torch.empty_like(x)
     call("pl_rmsnorm", ptr(x), _row_stride(x, "x"), int(x.shape[0]), int(x.shape[1]), ptr(weight), float(eps),
+         ptr(out), _row_stride(out, "out"), stream_handle())
+    return out
+
+
+def rmsnorm_hf(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Hugging Face RMSNorm (two bf16 roundings) over rows of ``x`` [R, K]."""
+
+    _need_cuda(x, weight)
+    _need(x, torch.bfloat16, "x")
+    _need(weight, torch.bfloat16, "weight")
+    if out is None:
+        out = torch.empty_like(x)
+    call("pl_rmsnorm_hf", ptr(x), _row_stride(x, "x"), int(x.shape[0]), int(x.shape[1]), ptr(weight), float(eps),
          ptr(out), _row_stride(out, "out"), stream_handle())
     return out
 

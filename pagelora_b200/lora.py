@@ -2,24 +2,35 @@
 
 Mirrors the reference's LoRA-linear interface:
   * LoRAModuleWeights, LoRALinear               multilora/linear.py:30-231
-  * project_qkv_packed, project_linear          model/flashinfer/packed_ops.py:105-165, 251-265
+  * project_qkv_packed, project_gate_up_packed,
+    get_base_gate_up_packed_linear,
+    apply_gate_up_activation, project_down,
+    project_linear                              model/flashinfer/packed_ops.py:105-265
+  * project_qkv_with_optional_norm, ProjectedQKV
+                                                model/flashinfer/projection.py:15-110, 248-262
   * effective_linear, effective_packed_linear,
     clear_flashinfer_effective_weight_cache     model/flashinfer/effective_weights.py:53-137
 with the same names, arguments, roles (base / serve / train), environment
 switches (MINI_OPENCLAW_FLASHINFER_*) and return values.
 
-On CUDA bf16 inputs of at most 8 tokens (decode) the forward is two launches:
-the segment shrink x.A^T and the base projection with the LoRA expand fused
-into its epilogue; LoRALinear scales the rounded B product (linear.py:230-231)
-while the packed q/k/v path folds the scale into B (packed_ops.py:371-373),
-and the kernel reproduces both roundings.  Merged ("effective") weights are built by the
-on-device merge kernel.  Longer inputs (prefill) and the train role use
-torch ops on the GPU; those are outside the decode hot path.  CPU inputs
-raise: there is no CPU path.
+A projection of T bf16 tokens runs on one kernel with the LoRA expand fused
+into its epilogue, after the segment shrink x.A^T:
+  * T <= 8 whose activations fit in shared memory: the decode GEMV
+    (pl_linear_lora_expand_fused);
+  * otherwise T <= 128 (batched decode, branch batches, prefill chunks): the
+    tcgen05 GEMM (pl_linear_lora_gemm), with one zeroed workspace per device
+    that every call leaves zeroed again.
+LoRALinear scales the rounded B product (linear.py:230-231) while the packed
+paths fold the scale into B (packed_ops.py:371-373); the kernels reproduce
+both roundings.  Merged ("effective") weights are built by the on-device
+merge kernel.  More than 128 tokens in one call (a whole prompt) and the
+train role use torch ops on the GPU, as the reference does; neither is on
+the decode path.  CPU inputs raise: there is no CPU path.
 """
 
 from __future__ import annotations
 
+import itertools
 import math
 import os
 from dataclasses import dataclass
@@ -31,7 +42,7 @@ import torch.nn.functional as F
 
 from pagelora_b200 import kernels as K
 
-MAX_KERNEL_TOKENS = 8
+MAX_KERNEL_TOKENS = K.GEMM_MAX_ROWS  # tokens one kernel call projects (GEMV up to 8, tcgen05 GEMM above)
 
 
 def _env_enabled(name: str, *, default: bool) -> bool:
@@ -61,6 +72,42 @@ def _single_segment(device: torch.device, tokens: int) -> tuple[torch.Tensor, to
 
 def _tensor_key(t: torch.Tensor) -> tuple:
     return (t.data_ptr(), tuple(t.shape), t.dtype, t.device, int(getattr(t, "_version", 0)))
+
+
+_gemm_ws: dict[torch.device, torch.Tensor] = {}
+
+
+def _gemm_workspace(device: torch.device, tokens: int, k_in: int, n_out: int) -> torch.Tensor:
+    """The device's shared GEMM workspace (zeroed once; each completed call leaves it zeroed)."""
+
+    need = int(K.gemm_plan(tokens, k_in, n_out).workspace_bytes)
+    ws = _gemm_ws.get(device)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 16), dtype=torch.uint8, device=device)
+        _gemm_ws[device] = ws
+    return ws
+
+
+def _kernel_kind(x2: torch.Tensor, k_in: int) -> str | None:
+    """Which kernel projects the rows of ``x2`` [T, K]: "gemv", "gemm" or None (torch)."""
+
+    if x2.dtype != torch.bfloat16 or torch.is_grad_enabled() or k_in % 16:
+        return None
+    t = x2.shape[0]
+    if K.gemv_fits(t, k_in):
+        return "gemv"
+    if t <= K.GEMM_MAX_ROWS:
+        return "gemm"
+    return None
+
+
+def _project(kind: str, x2: torch.Tensor, w: torch.Tensor, **epilogue) -> torch.Tensor:
+    """x2 . W^T with the fused epilogue (bias, LoRA expand) on the chosen kernel."""
+
+    if kind == "gemv":
+        return K.linear_lora_fused(x2, w, **epilogue)
+    ws = _gemm_workspace(x2.device, x2.shape[0], w.shape[1], w.shape[0])
+    return K.linear_lora_gemm(x2, w, workspace=ws, **epilogue)
 
 
 @dataclass
@@ -193,21 +240,18 @@ class LoRALinear(nn.Module):
         self.active_role = "train"
 
     # ---------------------------------------------------------- forward
-    def _kernel_ok(self, x: torch.Tensor) -> bool:
-        tokens = x.numel() // max(1, self.in_features)
-        return (x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16 and tokens <= MAX_KERNEL_TOKENS
-                and self.in_features % 16 == 0 and not torch.is_grad_enabled())
-
     def forward(self, x: torch.Tensor, *, return_lora_down: bool = False):
         _need_cuda(x)
         lora_on = self.active_role != "base" and not self.is_lora_merged()
-        if self.active_role == "train" and lora_on or not self._kernel_ok(x):
-            return self._forward_torch(x, return_lora_down=return_lora_down)
         shape = x.shape
-        x2 = x.reshape(-1, self.in_features).contiguous()
+        x2 = x.reshape(-1, self.in_features)
+        kind = None if self.weight.dtype != torch.bfloat16 else _kernel_kind(x2, self.in_features)
+        if kind is None or lora_on and (self.active_role == "train" or not self._dropout_mergeable()):
+            return self._forward_torch(x, return_lora_down=return_lora_down)
+        x2 = x2.contiguous()
         w = self.weight.contiguous()
         if not lora_on:
-            y = K.linear_lora_fused(x2, w, bias=self.bias).view(*shape[:-1], self.out_features)
+            y = _project(kind, x2, w, bias=self.bias).view(*shape[:-1], self.out_features)
             return (y, None) if return_lora_down else y
         if self.serve_a is None or self.serve_b is None:
             raise RuntimeError("serve mode active without bound serve parameters")
@@ -215,11 +259,10 @@ class LoRALinear(nn.Module):
         seg_indptr, seg_adapter = _single_segment(x.device, x2.shape[0])
         down = K.lora_shrink_seg(x2, a.unsqueeze(0), seg_indptr, seg_adapter)
         if return_lora_down:
-            base = K.linear_lora_fused(x2, w, bias=self.bias).view(*shape[:-1], self.out_features)
+            base = _project(kind, x2, w, bias=self.bias).view(*shape[:-1], self.out_features)
             return base, down.to(x.dtype).view(*shape[:-1], -1)
         b = self.serve_b.detach().to(w.dtype).contiguous()
-        y = K.linear_lora_fused(x2, w, bias=self.bias, lora_down=down, lora_b=b.unsqueeze(0),
-                                lora_scale=float(self.scale))
+        y = _project(kind, x2, w, bias=self.bias, lora_down=down, lora_b=b.unsqueeze(0), lora_scale=float(self.scale))
         return y.view(*shape[:-1], self.out_features)
 
     def _forward_torch(self, x: torch.Tensor, *, return_lora_down: bool):
@@ -381,23 +424,88 @@ def clear_flashinfer_effective_weight_cache(*roots: object) -> None:
         visit(root)
 
 
-def _packed_cache(owner: object, modules: tuple) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
-    """Packed base W, packed A (equal ranks) and packed B*scale for q/k/v."""
+@dataclass(frozen=True)
+class PackedGroup:
+    """Packed base weights of a module group and, when every module serves a
+    LoRA of one rank, the packed A rows and B * scale (packed_ops.py:314-384)."""
 
-    key = tuple((_tensor_key(m.weight), *(_tensor_key(t) for t in (m.serve_a, m.serve_b) if t is not None),
-                 getattr(m, "active_role", "base")) for m in modules)
-    cached = getattr(owner, "_b200_packed_qkv", None)
+    weight: torch.Tensor
+    bias: torch.Tensor | None
+    out_features: tuple[int, ...]
+    a_cat: torch.Tensor | None
+    b_cat: torch.Tensor | None
+
+
+def _lora_pack_info(module) -> tuple[torch.Tensor, torch.Tensor, float] | None:
+    """A serve LoRA that may be packed: not merged, identity dropout (packed_ops.py:475-502)."""
+
+    checker = getattr(module, "is_lora_merged", None)
+    if callable(checker) and checker():
+        return None
+    if getattr(module, "active_role", "base") != "serve":
+        return None
+    dropout = getattr(module, "dropout", None)
+    if dropout is not None and not isinstance(dropout, nn.Identity) and not (
+            isinstance(dropout, nn.Dropout) and float(dropout.p) == 0.0):
+        return None
+    a, b = getattr(module, "serve_a", None), getattr(module, "serve_b", None)
+    if not isinstance(a, torch.Tensor) or not isinstance(b, torch.Tensor) or a.ndim != 2 or b.ndim != 2:
+        return None
+    return a, b, float(getattr(module, "scale", 1.0))
+
+
+def _packed_group(owner: object, attr: str, modules: tuple) -> PackedGroup:
+    key = tuple((_tensor_key(m.weight), *(_tensor_key(t) for t in (getattr(m, "serve_a", None),
+                                                                   getattr(m, "serve_b", None)) if t is not None),
+                 getattr(m, "active_role", "base"), float(getattr(m, "scale", 1.0))) for m in modules)
+    cached = getattr(owner, attr, None)
     if cached is not None and cached[0] == key:
         return cached[1]
     w = torch.cat([m.weight.detach() for m in modules], 0).contiguous()
-    los = [_serve_lora(m) for m in modules]
+    outs = tuple(m.weight.size(0) for m in modules)
+    biases = [getattr(m, "bias", None) for m in modules]
+    bias = None
+    if any(bb is not None for bb in biases):
+        bias = torch.cat([torch.zeros(od, device=w.device, dtype=w.dtype) if bb is None else bb.detach().to(w.dtype)
+                          for bb, od in zip(biases, outs)]).contiguous()
+    infos = [_lora_pack_info(m) for m in modules]
     a_cat = b_cat = None
-    if all(l is not None for l in los) and len({l[0].shape[0] for l in los}) == 1:
-        a_cat = torch.cat([l[0].detach().to(w.dtype) for l in los], 0).contiguous()
-        b_cat = torch.cat([(l[1].detach().to(w.dtype) * l[2]).to(w.dtype) for l in los], 0).unsqueeze(0).contiguous()
-    val = (w, a_cat, b_cat)
-    setattr(owner, "_b200_packed_qkv", (key, val))
+    if all(i is not None for i in infos) and len({i[0].shape[0] for i in infos}) == 1:
+        a_cat = torch.cat([i[0].detach().to(w.dtype) for i in infos], 0).contiguous()
+        b_cat = torch.cat([(i[1].detach().to(w.dtype) * i[2]).to(w.dtype) for i in infos], 0).unsqueeze(0).contiguous()
+    val = PackedGroup(weight=w, bias=bias, out_features=outs, a_cat=a_cat, b_cat=b_cat)
+    setattr(owner, attr, (key, val))
     return val
+
+
+def _project_group(group: PackedGroup, modules: tuple, hidden: torch.Tensor) -> tuple[torch.Tensor, ...] | None:
+    """One packed projection of a module group plus its LoRA deltas, split per
+    module (packed_ops.py:140-165, 184-203); None when no kernel takes the input."""
+
+    shape = hidden.shape
+    x2 = hidden.reshape(-1, shape[-1])
+    kind = _kernel_kind(x2, shape[-1])
+    if kind is None:
+        return None
+    x2 = x2.contiguous()
+    dims = list(group.out_features)
+    ends = tuple(itertools.accumulate(dims[:-1]))
+    packed_delta = _env_enabled("MINI_OPENCLAW_FLASHINFER_PACKED_LORA_DELTA", default=True)
+    if group.a_cat is not None and packed_delta and len(dims) <= 4:
+        seg_indptr, seg_adapter = _single_segment(x2.device, x2.shape[0])
+        down = K.lora_shrink_seg(x2, group.a_cat.unsqueeze(0), seg_indptr, seg_adapter)
+        out = _project(kind, x2, group.weight, bias=group.bias, lora_down=down, lora_b=group.b_cat,
+                       slice_ends=ends)
+        return tuple(torch.split(out.view(*shape[:-1], -1), dims, dim=-1))
+    if not any(getattr(m, "active_role", "base") != "base" and not getattr(m, "is_lora_merged", lambda: False)()
+               for m in modules):
+        out = _project(kind, x2, group.weight, bias=group.bias)
+        return tuple(torch.split(out.view(*shape[:-1], -1), dims, dim=-1))
+    # Per-module deltas (packed delta off, or ranks differ): each module's own
+    # projection carries its delta, bf16(base) + bf16(bf16(down.B^T) * scale).
+    return tuple(m(hidden) if getattr(m, "active_role", "base") != "base" else
+                 _project(kind, x2, m.weight.contiguous(), bias=getattr(m, "bias", None)).view(*shape[:-1], -1)
+                 for m in modules)
 
 
 def project_qkv_packed(layer, plan, hidden: torch.Tensor):
@@ -413,36 +521,78 @@ def project_qkv_packed(layer, plan, hidden: torch.Tensor):
         if eff is not None:
             qkv = project_dense(hidden, eff.weight, eff.bias)
             return torch.split(qkv, list(eff.out_features), dim=-1)
-    if any(getattr(m, "bias", None) is not None for m in mods):
-        outs = [project_linear(m, hidden) for m in mods]
-        return tuple(outs)
-    w, a_cat, b_cat = _packed_cache(plan, mods)
-    dims = [m.weight.size(0) for m in mods]
-    shape = hidden.shape
-    x2 = hidden.reshape(-1, shape[-1]).contiguous()
-    kernel_ok = (x2.dtype == torch.bfloat16 and x2.shape[0] <= MAX_KERNEL_TOKENS and shape[-1] % 16 == 0
-                 and not torch.is_grad_enabled())
-    if not kernel_ok:
-        outs = [m(hidden) for m in mods]
-        return tuple(outs)
-    packed_delta = _env_enabled("MINI_OPENCLAW_FLASHINFER_PACKED_LORA_DELTA", default=True)
-    if a_cat is not None and packed_delta:
-        seg_indptr, seg_adapter = _single_segment(x2.device, x2.shape[0])
-        down = K.lora_shrink_seg(x2, a_cat.unsqueeze(0), seg_indptr, seg_adapter)
-        qkv = K.linear_lora_fused(x2, w, lora_down=down, lora_b=b_cat, slice_ends=(dims[0], dims[0] + dims[1]))
-        return torch.split(qkv.view(*shape[:-1], -1), dims, dim=-1)
-    return tuple(project_linear(m, hidden) for m in mods)
+    group = _packed_group(plan, "_b200_packed_qkv", mods)
+    out = _project_group(group, mods, hidden)
+    if out is not None:
+        return out
+    return tuple(m(hidden) for m in mods)
+
+
+def get_base_gate_up_packed_linear(mlp):
+    """Packed gate/up parameters (packed_ops.py:206-228): effective weights when
+    enabled, else the packed base weights; None when packing is off."""
+
+    if not _env_enabled("MINI_OPENCLAW_FLASHINFER_PACKED_MLP", default=True):
+        return None
+    gate, up = getattr(mlp, "gate_proj", None), getattr(mlp, "up_proj", None)
+    if gate is None or up is None:
+        return None
+    if not any(getattr(m, "is_lora_merged", lambda: False)() for m in (gate, up)):
+        eff = effective_packed_linear(owner=mlp, attr="_flashinfer_effective_gate_up", modules=(gate, up))
+        if eff is not None:
+            return eff
+    return _packed_group(mlp, "_b200_packed_gate_up", (gate, up))
+
+
+def project_gate_up_packed(mlp, hidden: torch.Tensor):
+    """MLP gate/up from one packed projection plus LoRA deltas (packed_ops.py:168-203)."""
+
+    packed = get_base_gate_up_packed_linear(mlp)
+    if packed is None:
+        return None
+    _need_cuda(hidden)
+    if isinstance(packed, EffectivePackedLinear):
+        return project_dense(hidden, packed.weight, packed.bias)
+    mods = (mlp.gate_proj, mlp.up_proj)
+    out = _project_group(packed, mods, hidden)
+    if out is None:
+        return torch.cat([m(hidden) for m in mods], dim=-1)
+    return torch.cat(out, dim=-1) if len(out) > 1 else out[0]
+
+
+def apply_gate_up_activation(gate_up: torch.Tensor, act_fn) -> torch.Tensor:
+    """SwiGLU over packed [gate | up] (packed_ops.py:231-240) on the SiLU-and-mul kernel."""
+
+    name = act_fn.__class__.__name__.lower()
+    silu = (name in {"silu", "siluactivation", "swishactivation"}
+            or getattr(act_fn, "__name__", "").lower() in {"silu", "swish"})
+    fused = _env_enabled("MINI_OPENCLAW_FLASHINFER_FUSED_ACT", default=True)
+    if (fused and silu and gate_up.dtype == torch.bfloat16 and gate_up.device.type == "cuda"
+            and gate_up.size(-1) % 16 == 0):
+        shape = gate_up.shape
+        return K.silu_mul(gate_up.reshape(-1, shape[-1]).contiguous()).view(*shape[:-1], shape[-1] // 2)
+    gate, up = gate_up.chunk(2, dim=-1)
+    return act_fn(gate) * up
+
+
+def project_down(mlp, hidden: torch.Tensor) -> torch.Tensor:
+    """The MLP down projection with its optional LoRA wrapper (packed_ops.py:243-248)."""
+
+    down = getattr(mlp, "down_proj", None)
+    if down is None:
+        raise RuntimeError("MLP module does not expose down_proj")
+    return project_linear(down, hidden)
 
 
 def project_dense(hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
-    """F.linear on the fused kernel for decode-sized bf16 inputs."""
+    """F.linear on the GEMV / tcgen05 GEMM for up to 128 bf16 tokens."""
 
     _need_cuda(hidden)
     shape = hidden.shape
     x2 = hidden.reshape(-1, shape[-1])
-    if (x2.dtype == torch.bfloat16 and x2.shape[0] <= MAX_KERNEL_TOKENS and shape[-1] % 16 == 0
-            and not torch.is_grad_enabled()):
-        return K.linear_lora_fused(x2.contiguous(), weight.contiguous(), bias=bias).view(*shape[:-1], -1)
+    kind = _kernel_kind(x2, shape[-1]) if weight.dtype == torch.bfloat16 else None
+    if kind is not None:
+        return _project(kind, x2.contiguous(), weight.contiguous(), bias=bias).view(*shape[:-1], -1)
     return F.linear(hidden, weight, bias)
 
 
@@ -461,3 +611,59 @@ def project_linear(module, hidden: torch.Tensor) -> torch.Tensor:
     if isinstance(weight, torch.Tensor) and weight.ndim == 2:
         return project_dense(hidden, weight, getattr(module, "bias", None))
     return module(hidden)
+
+
+# ------------------------------------------------------- q/k/v + head norm
+@dataclass(frozen=True)
+class ProjectedQKV:
+    """Q/K/V after projection and optional per-head Q/K normalisation (projection.py:15-22)."""
+
+    q_bshd: torch.Tensor
+    k_bshd: torch.Tensor
+    v_bshd: torch.Tensor
+    v_bhsd: torch.Tensor | None
+
+
+def _head_norm(states: torch.Tensor, norm, *, use_flashinfer_norm: bool) -> torch.Tensor:
+    """Per-head RMSNorm of [B, S, H, D] states (projection.py:248-262): the
+    FlashInfer rounding (once) when enabled, else the Hugging Face module's
+    (normalise, round, scale, round)."""
+
+    weight = getattr(norm, "weight", None)
+    eps = float(getattr(norm, "variance_epsilon", getattr(norm, "eps", 1e-6)))
+    if (not isinstance(weight, torch.Tensor) or states.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16
+            or states.device.type != "cuda" or states.size(-1) % 8):
+        return norm(states)
+    flat = states.reshape(-1, states.size(-1)).contiguous()
+    fn = K.rmsnorm if use_flashinfer_norm else K.rmsnorm_hf
+    return fn(flat, weight.contiguous(), eps).view_as(states)
+
+
+def project_qkv_with_optional_norm(layer, plan, normed_hidden: torch.Tensor, *,
+                                   use_flashinfer_norm: bool | None = None) -> ProjectedQKV:
+    """Project Q/K/V (packed, with LoRA) and apply the model's optional q/k
+    head norms (projection.py:34-110)."""
+
+    attn = layer.self_attn
+    if use_flashinfer_norm is None:
+        use_flashinfer_norm = _env_enabled("MINI_OPENCLAW_FLASHINFER_QK_NORM", default=False)
+    config = attn.config
+    num_qo_heads = int(config.num_attention_heads)
+    num_kv_heads = int(getattr(config, "num_key_value_heads", num_qo_heads))
+    head_dim = int(attn.head_dim)
+    bsz, seqlen, _ = normed_hidden.shape
+    packed = project_qkv_packed(layer, plan, normed_hidden)
+    if packed is None:
+        mods = tuple(plan.modules.get(f"self_attn.{n}_proj") or getattr(attn, f"{n}_proj") for n in "qkv")
+        packed = tuple(project_linear(m, normed_hidden) for m in mods)
+    q_flat, k_flat, v_flat = packed
+    q_bshd = q_flat.reshape(bsz, seqlen, num_qo_heads, head_dim)
+    k_bshd = k_flat.reshape(bsz, seqlen, num_kv_heads, head_dim)
+    q_norm, k_norm = getattr(attn, "q_norm", None), getattr(attn, "k_norm", None)
+    if q_norm is not None:
+        q_bshd = _head_norm(q_bshd, q_norm, use_flashinfer_norm=use_flashinfer_norm)
+    if k_norm is not None:
+        k_bshd = _head_norm(k_bshd, k_norm, use_flashinfer_norm=use_flashinfer_norm)
+    v_bshd = v_flat.reshape(bsz, seqlen, num_kv_heads, head_dim)
+    return ProjectedQKV(q_bshd=q_bshd, k_bshd=k_bshd, v_bshd=v_bshd,
+                        v_bhsd=None if bsz == 1 else v_bshd.transpose(1, 2).contiguous())

@@ -15,6 +15,11 @@ Fixtures written next to this script:
                           packed LoRA delta, merge_serve_lora and
                           effective_weights.effective_linear /
                           effective_packed_linear outputs
+  lora_batched_cases.npz  the same LoRA surfaces at batched-decode token
+                          counts (16, 64, 128 rows), plus
+                          packed_ops.project_gate_up_packed and
+                          projection.project_qkv_with_optional_norm (Qwen3
+                          q/k head norms), bf16
   prefix_plans.json       model/kvcache/paged_kvcache_manager.py prefix reuse
                           (radix lookup result -> match_len, prefill_from,
                           prefix_spans), the batch page table of branch
@@ -215,6 +220,126 @@ def make_lora_cases(out: Path) -> None:
     print(f"lora_cases.npz: {len(arrays)} arrays")
 
 
+def make_lora_batched_cases(out: Path) -> None:
+    """Batched-token LoRA surfaces: LoRALinear.forward, project_qkv_packed,
+    project_gate_up_packed and project_qkv_with_optional_norm (bf16)."""
+
+    os.environ["MINI_OPENCLAW_FLASHINFER_PACKED_QKV"] = "1"
+    os.environ["MINI_OPENCLAW_FLASHINFER_PACKED_MLP"] = "1"
+    os.environ["MINI_OPENCLAW_FLASHINFER_PACKED_LORA_DELTA"] = "1"
+    os.environ["MINI_OPENCLAW_FLASHINFER_EFFECTIVE_WEIGHTS"] = "0"
+    os.environ["MINI_OPENCLAW_FLASHINFER_QK_NORM"] = "0"
+    from types import SimpleNamespace
+
+    import torch.nn as nn
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+
+    from model.flashinfer.packed_ops import project_gate_up_packed, project_qkv_packed
+    from model.flashinfer.projection import project_qkv_with_optional_norm
+    from multilora.linear import LoRALinear
+
+    g = torch.Generator().manual_seed(11)
+    bf = torch.bfloat16
+    arrays: dict[str, np.ndarray] = {}
+
+    def rnd(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g) * std).to(bf)
+
+    def module(w, lora=None, bias=None):
+        lin = nn.Linear(w.shape[1], w.shape[0], bias=bias is not None, dtype=bf)
+        with torch.no_grad():
+            lin.weight.copy_(w)
+            if bias is not None:
+                lin.bias.copy_(bias)
+        if lora is None:
+            return lin
+        a, b, r, alpha = lora
+        m = LoRALinear(lin, rank=r, alpha=alpha, dropout=0.0)
+        m.bind_serve(nn.Parameter(a.clone(), requires_grad=False), nn.Parameter(b.clone(), requires_grad=False))
+        m.set_active_serve()
+        return m
+
+    def put(prefix, **tensors):  # bf16 bit patterns as uint16 (half the fixture size)
+        for k, v in tensors.items():
+            arrays[prefix + k] = (np.zeros(0, np.uint16) if v is None
+                                  else v.detach().contiguous().view(torch.int16).numpy().view(np.uint16))
+
+    # 1. LoRALinear.forward at batched token counts ([T, K] and [1, T, K] inputs).
+    for case, (t, k, n, r, alpha, with_bias, lead) in enumerate(
+            [(16, 128, 192, 16, 32.0, False, False), (64, 128, 320, 8, 16.0, True, True),
+             (128, 256, 128, 16, 32.0, False, False), (9, 384, 64, 16, 32.0, False, True)]):
+        x = rnd(t, k, std=1.0)
+        w, a, b = rnd(n, k), rnd(r, k), rnd(n, r)
+        bias = rnd(n, std=0.1) if with_bias else None
+        m = module(w, (a, b, r, alpha), bias)
+        with torch.no_grad():
+            y = m(x[None] if lead else x)
+        put(f"linear_{case}_", x=x, w=w, a=a, b=b, bias=bias, y=y.reshape(t, n))
+        arrays[f"linear_{case}_meta"] = np.array([r, alpha, int(lead)], np.float32)
+
+    # 2. project_qkv_packed: packed delta (LoRA on q/k/v) and per-module deltas (LoRA on q/v).
+    for case, (t, hidden, hq, hkv, d, r, alpha, targets) in enumerate(
+            [(64, 128, 4, 2, 64, 16, 32.0, "qkv"), (16, 128, 4, 2, 64, 8, 16.0, "qv"),
+             (128, 128, 2, 2, 64, 16, 32.0, "qkv")]):
+        x = rnd(1, t, hidden, std=1.0)
+        mods = []
+        for name, od in (("q", hq * d), ("k", hkv * d), ("v", hkv * d)):
+            w = rnd(od, hidden)
+            lora = (rnd(r, hidden), rnd(od, r), r, alpha) if name in targets else None
+            mods.append(module(w, lora))
+            put(f"qkv_{case}_{name}_", w=w, a=None if lora is None else lora[0], b=None if lora is None else lora[1])
+        attn = SimpleNamespace(q_proj=mods[0], k_proj=mods[1], v_proj=mods[2])
+        plan = SimpleNamespace(modules={f"self_attn.{n}_proj": m for n, m in zip("qkv", mods)})
+        with torch.no_grad():
+            q, k, v = project_qkv_packed(SimpleNamespace(self_attn=attn), plan, x)
+        put(f"qkv_{case}_", x=x[0], q=q[0], k=k[0], v=v[0])
+        arrays[f"qkv_{case}_meta"] = np.array([r, alpha], np.float32)
+
+    # 3. project_gate_up_packed: packed delta, per-module delta (LoRA on up only), no LoRA.
+    for case, (t, hidden, inter, r, alpha, targets) in enumerate(
+            [(64, 128, 256, 8, 16.0, "gu"), (16, 128, 192, 16, 32.0, "u"), (1, 256, 128, 16, 32.0, "")]):
+        x = rnd(1, t, hidden, std=1.0)
+        mods = {}
+        for name in "gu":
+            w = rnd(inter, hidden)
+            lora = (rnd(r, hidden), rnd(inter, r), r, alpha) if name in targets else None
+            mods[name] = module(w, lora)
+            put(f"gu_{case}_{name}_", w=w, a=None if lora is None else lora[0], b=None if lora is None else lora[1])
+        mlp = SimpleNamespace(gate_proj=mods["g"], up_proj=mods["u"])
+        with torch.no_grad():
+            y = project_gate_up_packed(mlp, x)
+        put(f"gu_{case}_", x=x[0], y=y[0])
+        arrays[f"gu_{case}_meta"] = np.array([r, alpha], np.float32)
+
+    # 4. project_qkv_with_optional_norm on a Qwen3-style attention (q/k head norms).
+    for case, (bsz, seqlen, hidden, hq, hkv, d, r, alpha) in enumerate(
+            [(1, 1, 128, 4, 2, 64, 16, 32.0), (1, 64, 128, 4, 2, 64, 16, 32.0), (2, 32, 128, 4, 2, 128, 8, 16.0)]):
+        x = rnd(bsz, seqlen, hidden, std=1.0)
+        mods = []
+        for name, od in (("q", hq * d), ("k", hkv * d), ("v", hkv * d)):
+            w, a, b = rnd(od, hidden), rnd(r, hidden), rnd(od, r)
+            mods.append(module(w, (a, b, r, alpha)))
+            put(f"norm_{case}_{name}_", w=w, a=a, b=b)
+        norms = []
+        for name in "qk":
+            nm = Qwen3RMSNorm(d, eps=1e-6).to(bf)
+            with torch.no_grad():
+                nm.weight.copy_((1.0 + torch.randn(d, generator=g) * 0.1).to(bf))
+            norms.append(nm)
+            put(f"norm_{case}_{name}norm_", w=nm.weight.detach())
+        cfg = SimpleNamespace(num_attention_heads=hq, num_key_value_heads=hkv)
+        attn = SimpleNamespace(config=cfg, head_dim=d, q_proj=mods[0], k_proj=mods[1], v_proj=mods[2],
+                               q_norm=norms[0], k_norm=norms[1])
+        plan = SimpleNamespace(modules={f"self_attn.{n}_proj": m for n, m in zip("qkv", mods)})
+        with torch.no_grad():
+            res = project_qkv_with_optional_norm(SimpleNamespace(self_attn=attn), plan, x)
+        put(f"norm_{case}_", x=x, q=res.q_bshd, k=res.k_bshd, v=res.v_bshd)
+        arrays[f"norm_{case}_meta"] = np.array([bsz, seqlen, hq, hkv, d, r, alpha], np.float32)
+    np.savez_compressed(out, **arrays)
+    print(f"lora_batched_cases.npz: {len(arrays)} arrays")
+
+
+
 def make_tiny_greedy(out: Path) -> None:
     import torch.nn as nn
     from transformers import LlamaConfig, LlamaForCausalLM
@@ -329,16 +454,21 @@ def make_prefix_plans(out: Path) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("PAGELORA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("PAGELORA_REFERENCE"),
+                    help="checkout of the PageLoRA reference (or set PAGELORA_REFERENCE)")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or PAGELORA_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    todo = args.only.split(",") if args.only else ["page_tables", "lora", "tiny", "prefix"]
+    todo = args.only.split(",") if args.only else ["page_tables", "lora", "lora_batched", "tiny", "prefix"]
     if "page_tables" in todo:
         make_page_tables(HERE / "page_tables.json")
     if "lora" in todo:
         make_lora_cases(HERE / "lora_cases.npz")
+    if "lora_batched" in todo:
+        make_lora_batched_cases(HERE / "lora_batched_cases.npz")
     if "tiny" in todo:
         make_tiny_greedy(HERE / "tiny_llama_greedy.npz")
     if "prefix" in todo:

@@ -29,7 +29,11 @@ def _ulps_close(actual, expected, magnitude, ulps=2):
     actual, expected = np.asarray(actual, np.float32), np.asarray(expected, np.float32)
     mag = np.maximum(np.abs(expected), np.abs(magnitude))
     tol = ulps * np.maximum(mag, 1e-3) * 2.0 ** -8 + 1e-6
-    assert not (np.abs(actual - expected) > tol).any()
+    over = np.abs(actual - expected) - tol
+    if (over > 0).any():
+        i = np.unravel_index(int(np.argmax(over)), over.shape)
+        raise AssertionError(f"{int((over > 0).sum())} elements beyond {ulps} ulps; worst at {i}: "
+                             f"got {actual[i]!r}, expected {expected[i]!r}, magnitude {np.abs(magnitude)[i]!r}")
 
 
 def _paged_inputs(seed=0, batch=3, hq=32, hkv=8, d=128, ps=16, lens=(1, 40, 300)):
@@ -270,3 +274,134 @@ def test_decode_matches_flashinfer_reference_path(cuda_device):
     err = (mine.float() - ref.float()).abs().max().item()
     print(f"max |B200 - FlashInfer {flashinfer.__version__}| = {err:.3e}")
     assert err <= 2e-2
+
+
+# ---------------------------------------------------------------- batched
+def _bf(z, key):
+    """A bf16 fixture array (stored as uint16 bit patterns) on the GPU, or None."""
+
+    a = z[key]
+    if a.size == 0:
+        return None
+    return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16).cuda()
+
+
+def _same_bits_or_ulps(got, ref, base, ulps=2):
+    _ulps_close(*(t.detach().float().cpu().numpy() for t in (got, ref, base)), ulps)
+
+
+def _lora_mod(w, a, b, rank, alpha, bias=None):
+    from pagelora_b200.lora import LoRALinear
+
+    lin = nn.Linear(w.shape[1], w.shape[0], bias=bias is not None, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+        if bias is not None:
+            lin.bias.copy_(bias)
+    m = LoRALinear(lin, rank=rank, alpha=alpha, dropout=0.0)
+    if a is not None:
+        m.bind_serve(nn.Parameter(a, requires_grad=False), nn.Parameter(b, requires_grad=False))
+        m.set_active_serve()
+    return m
+
+
+def test_batched_lora_linear_matches_reference(cuda_device, golden_dir, monkeypatch):
+    """LoRALinear.forward at 9-128 tokens (the tcgen05 GEMM path) vs the
+    reference module's bf16 outputs (multilora/linear.py:200-231)."""
+
+    from pagelora_b200 import lora as L
+
+    monkeypatch.setenv("MINI_OPENCLAW_FLASHINFER_EFFECTIVE_WEIGHTS", "0")
+    z = np.load(golden_dir / "lora_batched_cases.npz")
+    for case in range(4):
+        p = f"linear_{case}_"
+        r, alpha, lead = z[p + "meta"]
+        x, w = _bf(z, p + "x"), _bf(z, p + "w")
+        m = _lora_mod(w, _bf(z, p + "a"), _bf(z, p + "b"), int(r), float(alpha), _bf(z, p + "bias"))
+        with torch.no_grad():
+            assert L._kernel_kind(x, x.shape[1]) == "gemm", case
+            y = m(x[None] if lead else x).reshape(x.shape[0], -1)
+        _same_bits_or_ulps(y, _bf(z, p + "y"), torch.nn.functional.linear(x, w).float())
+
+
+def test_batched_project_qkv_packed_matches_reference(cuda_device, golden_dir, monkeypatch):
+    """project_qkv_packed at 16-128 tokens: the packed LoRA delta (q/k/v) and
+    the per-module deltas (q/v only), packed_ops.py:105-165."""
+
+    from types import SimpleNamespace
+
+    from pagelora_b200.lora import project_qkv_packed
+
+    monkeypatch.setenv("MINI_OPENCLAW_FLASHINFER_EFFECTIVE_WEIGHTS", "0")
+    z = np.load(golden_dir / "lora_batched_cases.npz")
+    for case in range(3):
+        p = f"qkv_{case}_"
+        r, alpha = z[p + "meta"]
+        mods = [_lora_mod(_bf(z, f"{p}{n}_w"), _bf(z, f"{p}{n}_a"), _bf(z, f"{p}{n}_b"), int(r), float(alpha))
+                for n in "qkv"]
+        attn = SimpleNamespace(q_proj=mods[0], k_proj=mods[1], v_proj=mods[2])
+        plan = SimpleNamespace(modules={f"self_attn.{n}_proj": m for n, m in zip("qkv", mods)})
+        x = _bf(z, p + "x")
+        with torch.no_grad():
+            q, k, v = project_qkv_packed(SimpleNamespace(self_attn=attn), plan, x[None])
+        base = torch.cat([torch.nn.functional.linear(x, m.weight.detach()) for m in mods], -1)
+        got = torch.cat([q[0], k[0], v[0]], -1)
+        ref = torch.cat([_bf(z, p + "q"), _bf(z, p + "k"), _bf(z, p + "v")], -1)
+        try:
+            _same_bits_or_ulps(got, ref, base)
+        except AssertionError as exc:
+            raise AssertionError(f"case {case}: {exc}") from None
+
+
+def test_batched_project_gate_up_packed_matches_reference(cuda_device, golden_dir, monkeypatch):
+    """project_gate_up_packed (packed_ops.py:168-203): packed delta, a delta on
+    one module only, and no LoRA."""
+
+    from types import SimpleNamespace
+
+    from pagelora_b200.lora import project_gate_up_packed
+
+    monkeypatch.setenv("MINI_OPENCLAW_FLASHINFER_EFFECTIVE_WEIGHTS", "0")
+    z = np.load(golden_dir / "lora_batched_cases.npz")
+    for case in range(3):
+        p = f"gu_{case}_"
+        r, alpha = z[p + "meta"]
+        mods = {n: _lora_mod(_bf(z, f"{p}{n}_w"), _bf(z, f"{p}{n}_a"), _bf(z, f"{p}{n}_b"), int(r), float(alpha))
+                for n in "gu"}
+        mlp = SimpleNamespace(gate_proj=mods["g"], up_proj=mods["u"])
+        x = _bf(z, p + "x")
+        with torch.no_grad():
+            y = project_gate_up_packed(mlp, x[None])[0]
+        base = torch.cat([torch.nn.functional.linear(x, mods[n].weight.detach()) for n in "gu"], -1)
+        _same_bits_or_ulps(y, _bf(z, p + "y"), base)
+
+
+def test_project_qkv_with_optional_norm_matches_reference(cuda_device, golden_dir, monkeypatch):
+    """project_qkv_with_optional_norm (projection.py:34-110) with Qwen3 q/k head
+    norms in the Hugging Face rounding, at 1, 64 and 2 x 32 tokens."""
+
+    from types import SimpleNamespace
+
+    from pagelora_b200.lora import project_qkv_with_optional_norm
+
+    monkeypatch.setenv("MINI_OPENCLAW_FLASHINFER_EFFECTIVE_WEIGHTS", "0")
+    monkeypatch.setenv("MINI_OPENCLAW_FLASHINFER_QK_NORM", "0")
+    z = np.load(golden_dir / "lora_batched_cases.npz")
+    for case in range(3):
+        p = f"norm_{case}_"
+        bsz, seqlen, hq, hkv, d, r, alpha = (float(v) for v in z[p + "meta"])
+        bsz, seqlen, hq, hkv, d, r = (int(v) for v in (bsz, seqlen, hq, hkv, d, r))
+        mods = [_lora_mod(_bf(z, f"{p}{n}_w"), _bf(z, f"{p}{n}_a"), _bf(z, f"{p}{n}_b"), r, alpha) for n in "qkv"]
+        norms = [SimpleNamespace(weight=_bf(z, f"{p}{n}norm_w"), variance_epsilon=1e-6) for n in "qk"]
+        attn = SimpleNamespace(config=SimpleNamespace(num_attention_heads=hq, num_key_value_heads=hkv), head_dim=d,
+                               q_proj=mods[0], k_proj=mods[1], v_proj=mods[2], q_norm=norms[0], k_norm=norms[1])
+        plan = SimpleNamespace(modules={f"self_attn.{n}_proj": m for n, m in zip("qkv", mods)})
+        x = _bf(z, p + "x")
+        with torch.no_grad():
+            res = project_qkv_with_optional_norm(SimpleNamespace(self_attn=attn), plan, x)
+        for name, got in (("q", res.q_bshd), ("k", res.k_bshd), ("v", res.v_bshd)):
+            ref = _bf(z, p + name)
+            # head norms renormalise, so the magnitude scale is the output's own
+            _same_bits_or_ulps(got.reshape(ref.shape), ref, ref)
+        if bsz > 1:
+            assert torch.equal(res.v_bhsd, res.v_bshd.transpose(1, 2))

@@ -1,62 +1,106 @@
 """End-to-end decode on the B200 kernels vs the CPU oracle decoder.
 
-The engine's decode step (7 kernel launches per layer, CUDA graph) is run on
-a small Qwen3-style model (q/k norm, GQA 4, LoRA on q/k/v/o) and on the
-config-1 tiny Llama (LoRA on q/v); the oracle decoder runs the same weights
-with the reference's bf16 rounding points.
+The engine's decode step (five kernel launches per layer, CUDA graph) runs
+  * a small Qwen3-style model (q/k norm, GQA 4, LoRA on q/k/v/o),
+  * the config-1 tiny Llama (LoRA r8 on q/v),
+  * a Qwen3-8B model cut to 4 layers: every per-layer shape of config 2
+    (hidden 4096, 32/8 heads, head_dim 128, q/k norm, SwiGLU 12288,
+    vocab 151936, LoRA r16 on q/k/v/o),
+and the oracle decoder runs the same weights with the reference's bf16
+rounding points (the reference's FlashInfer path: model/flashinfer/
+layer_runner.py:283-337, packed_ops.py:105-165, linear.py:200-231).
+
+The acceptance gate follows scripts/check_inference_correctness.py:226-258:
+greedy tokens plus first-step logits within atol 0.1 / rtol 0.01.  With
+random-init weights the top-2 logit margin is often below the bf16 noise of
+any implementation (at the Qwen3-8B shapes the bf16 and fp32 oracles differ
+by ~0.1 in the logits, and about one step in five has a margin under 0.1),
+so a free-running greedy stream of two bf16 implementations that sum in
+different orders parts at the first such near-tie.  The gate is therefore
+applied teacher-forced (both sides fed the oracle's tokens, 32 decode
+steps): the engine's token equals the oracle's at every step whose oracle
+top-2 margin exceeds twice the step's logits error, and at every other step
+it is within that error of the oracle's best; over the steps the engine's
+logits stay as close to the bf16 oracle as the bf16 oracle is to the fp32
+one, or within two bf16 ulps of the largest logit (two bf16 paths may each
+round the output once).  Free running, the small Qwen3 model keeps all 32 tokens identical.
 """
 
 from __future__ import annotations
+
+from dataclasses import replace
 
 import numpy as np
 import pytest
 import torch
 
 from oracle.decoder import OracleDecoder
-from pagelora_b200.synthetic import WORKLOADS, LoRASpec, ModelSpec, make_lora_weights, make_model_weights, random_prompt
+from pagelora_b200.synthetic import (QWEN3_8B, WORKLOADS, LoRASpec, ModelSpec, make_lora_weights, make_model_weights,
+                                     random_prompt)
 
 pytestmark = pytest.mark.gpu
 
 SMALL_QWEN = ModelSpec("small-qwen3", 3, 512, 8, 2, 128, 1024, 4096, 1.0e6, 1e-6, qk_norm=True)
 SMALL_LORA = LoRASpec(16, 32.0, ("q", "k", "v", "o"))
+QWEN3_8B_4L = replace(QWEN3_8B, num_layers=4, name="qwen3-8b-4layers")
+CONFIG2_LORA = WORKLOADS["config2"].lora
+
+# max |logits - oracle| of a decode step after a prompt prefill, small
+# models: one bf16 ulp of logits in [2, 4) is 1.56e-2, the measured maximum.
+LOGITS_TOL = 2e-2
+# The reference's own first-step logits gate (check_inference_correctness.py).
+GATE_ATOL, GATE_RTOL = 0.1, 0.01
 
 
-def _engine(spec, lspec, device, max_len=512):
+def _engine(spec, lspec, device, max_len=512, *, weights_on_device=False, with_fp32_oracle=False):
     from pagelora_b200.engine import DecodeEngine
 
-    w = make_model_weights(spec, seed=0, dtype=torch.float32, norm_jitter=0.1)
-    w = {k: v.bfloat16() for k, v in w.items()}
-    lo = make_lora_weights(spec, lspec, dtype=torch.bfloat16)
-    oracle = OracleDecoder(spec, {k: v.float() for k, v in w.items()},
-                           {k: (a.float(), b.float()) for k, (a, b) in lo.items()}, lspec.scale,
-                           page_size=16, num_pages=64, bf16=True)
+    if weights_on_device:  # large models: draw on the GPU, the oracle gets a host copy
+        w = make_model_weights(spec, seed=0, device=device, dtype=torch.bfloat16, norm_jitter=0.1)
+        lo = make_lora_weights(spec, lspec, device=device, dtype=torch.bfloat16)
+    else:
+        w = make_model_weights(spec, seed=0, dtype=torch.float32, norm_jitter=0.1)
+        w = {k: v.bfloat16() for k, v in w.items()}
+        lo = make_lora_weights(spec, lspec, dtype=torch.bfloat16)
+    oracle = OracleDecoder(spec, {k: v.float().cpu() for k, v in w.items()},
+                           {k: (a.float().cpu(), b.float().cpu()) for k, (a, b) in lo.items()}, lspec.scale,
+                           page_size=16, num_pages=max_len // 16 + 4, bf16=True)
     eng = DecodeEngine(spec, dict(w), lora=lo, lora_spec=lspec, page_size=16, max_seq_len=max_len, device=device)
+    if with_fp32_oracle:
+        oracle32 = OracleDecoder(spec, oracle.w, oracle.loras, lspec.scale, page_size=16,
+                                 num_pages=max_len // 16 + 4, bf16=False)
+        return eng, oracle, oracle32
     return eng, oracle
+
+
+def _spec(which):
+    return {"small-qwen3": (SMALL_QWEN, SMALL_LORA), "config1": (WORKLOADS["config1"].model, WORKLOADS["config1"].lora),
+            "qwen3-8b-4layers": (QWEN3_8B_4L, CONFIG2_LORA)}[which]
 
 
 @pytest.mark.parametrize("which", ["small-qwen3", "config1"])
 def test_decode_step_logits_match_oracle(cuda_device, which):
-    if which == "config1":
-        spec, lspec = WORKLOADS["config1"].model, WORKLOADS["config1"].lora
-    else:
-        spec, lspec = SMALL_QWEN, SMALL_LORA
+    """Prompt prefill (torch GEMMs + the paged prefill kernel), then 32 decode
+    steps fed the oracle's tokens so both sides see the same inputs."""
+
+    spec, lspec = _spec(which)
     eng, oracle = _engine(spec, lspec, cuda_device)
     prompt = random_prompt(spec.vocab, 40, seed=3)
     eng.prefill(prompt)
-    # Oracle: token-by-token over the same prompt (bf16 rounding points).
     o_next, o_logits = 0, None
     for t in prompt:
         o_next, o_logits = oracle.step(t)
     pre_err = float(np.max(np.abs(eng.prefill_logits.float().cpu().numpy() - o_logits)))
-    assert pre_err < 0.1, pre_err
-    # Decode steps through the kernels (eager), fed the oracle's tokens so both see the same inputs.
-    for _ in range(3):
+    eng.capture()
+    errs = []
+    for _ in range(32):
         eng.step_host(o_next)
         o_next, o_logits = oracle.step(o_next)
-        got = eng.logits[0].float().cpu().numpy()
-        err = float(np.max(np.abs(got - o_logits)))
-        print(f"{which}: decode-step logits max|err| vs oracle {err:.3e} (prefill {pre_err:.3e})")
-        assert err < 0.1, err
+        errs.append(float(np.max(np.abs(eng.logits[0].float().cpu().numpy() - o_logits))))
+    print(f"{which}: decode-step logits max|err| vs oracle over 32 steps {max(errs):.3e} "
+          f"(mean {np.mean(errs):.3e}; prefill {pre_err:.3e})")
+    assert pre_err <= LOGITS_TOL, pre_err
+    assert max(errs) <= LOGITS_TOL, errs
     assert int(eng.status.item()) == 0
 
 
@@ -70,27 +114,76 @@ def test_graph_replay_equals_eager(cuda_device):
     assert torch.equal(eng.logits, eager_logits)
 
 
-def test_greedy_stream_vs_oracle(cuda_device):
-    """Greedy tokens of the kernel path vs the bf16 oracle decoder (both
-    prefill token by token through the same decode math)."""
+def _free_running(eng, oracle, prompt, n=32):
+    """Free-running greedy streams of the engine (decode kernels for every
+    prompt token after the first, CUDA graph) and the oracle."""
 
-    eng, oracle = _engine(SMALL_QWEN, SMALL_LORA, cuda_device)
-    prompt = random_prompt(SMALL_QWEN.vocab, 20, seed=2)
-    # Engine: prefill only the first token with torch, then feed the rest of the
-    # prompt through the decode kernels so both sides share the decode math.
     eng.prefill(prompt[:1])
     eng.capture()
-    nxt = None
-    for t in prompt[1:]:
-        nxt = eng.step_host(t)
-    toks = [nxt]
-    for _ in range(31):
+    nxt = o_next = None
+    for i, t in enumerate(prompt):
+        o_next, _ = oracle.step(t)
+        if i:
+            nxt = eng.step_host(t)
+    toks, o_toks = [nxt], [o_next]
+    while len(toks) < n:
         toks.append(eng.step_host(toks[-1]))
-    o_toks, _ = oracle.generate(prompt, 32)
-    agree = 0
-    for a, b in zip(toks, o_toks):
-        if a != b:
-            break
-        agree += 1
-    print(f"greedy agreement with the oracle: {agree}/32 tokens")
-    assert agree >= 8
+        o_toks.append(oracle.step(o_toks[-1])[0])
+    return toks, o_toks
+
+
+def test_greedy_stream_free_running_32_identical(cuda_device):
+    eng, oracle = _engine(SMALL_QWEN, SMALL_LORA, cuda_device)
+    prompt = random_prompt(SMALL_QWEN.vocab, 20, seed=2)
+    toks, o_toks = _free_running(eng, oracle, prompt)
+    agree = next((i for i, (a, b) in enumerate(zip(toks, o_toks)) if a != b), len(toks))
+    print(f"small-qwen3: free-running greedy agreement with the oracle {agree}/32 tokens")
+    assert toks == o_toks
+    assert int(eng.status.item()) == 0
+
+
+@pytest.mark.parametrize("which", ["small-qwen3", "config1", "qwen3-8b-4layers"])
+def test_greedy_tokens_teacher_forced_32_steps(cuda_device, which):
+    spec, lspec = _spec(which)
+    eng, oracle, oracle32 = _engine(spec, lspec, cuda_device, weights_on_device=which == "qwen3-8b-4layers",
+                                    with_fp32_oracle=True)
+    prompt = random_prompt(spec.vocab, 20, seed=2)
+    eng.prefill(prompt[:1])
+    eng.capture()
+    o_next = e_next = None
+    for i, t in enumerate(prompt):
+        o_next, o_logits = oracle.step(t)
+        _, o32_logits = oracle32.step(t)
+        if i:
+            e_next = eng.step_host(t)
+    decisive = agree = 0
+    err_engine, err_bf16, ulp2 = [], [], []
+    for step in range(32):
+        got = eng.logits[0].float().cpu().numpy()
+        diff = np.abs(got - o_logits)
+        if step == 0:  # the reference's first-step logits gate
+            assert bool(np.all(diff <= GATE_ATOL + GATE_RTOL * np.abs(o_logits))), float(diff.max())
+        err_engine.append(float(diff.max()))
+        err_bf16.append(float(np.abs(o_logits - o32_logits).max()))
+        ulp2.append(2.0 ** (np.floor(np.log2(np.abs(o_logits).max())) - 6))  # two bf16 ulps
+        mine = e_next  # the engine's own greedy token (its argmax kernel)
+        assert got[mine] == got.max(), step
+        top2 = np.sort(o_logits)[-2:]
+        # With every logit within err of the oracle's, the greedy token can
+        # only differ where the oracle's top-2 margin is below 2 * err.
+        err = err_engine[-1]
+        if top2[1] - top2[0] > 2 * err:
+            decisive += 1
+            assert mine == o_next, (step, mine, o_next, float(top2[1] - top2[0]), err)
+        else:
+            assert o_logits[mine] >= top2[1] - 2 * err, (step, mine, o_next)
+        agree += mine == o_next
+        feed = o_next  # every side takes the bf16 oracle's token
+        e_next = eng.step_host(feed)
+        o_next, o_logits = oracle.step(feed)
+        _, o32_logits = oracle32.step(feed)
+    print(f"{which}: teacher-forced 32 steps: {agree}/32 tokens equal, {decisive} decisive steps all equal; "
+          f"logits max|err| vs bf16 oracle {max(err_engine):.3e} (bf16 vs fp32 oracle {max(err_bf16):.3e}, "
+          f"two ulps {max(ulp2):.3e})")
+    assert max(err_engine) <= max(max(err_bf16), max(ulp2)), (max(err_engine), max(err_bf16), max(ulp2))
+    assert int(eng.status.item()) == 0

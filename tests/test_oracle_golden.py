@@ -186,3 +186,29 @@ def test_page_table_advance_matches_reserve_semantics():
     assert (slot_p, slot_o, pos) == ([3, 4], [0, 0], [0, 16])
     slot_p, slot_o, pos = opt.advance(rows, last, [9, 9], 16)
     assert (slot_p, slot_o, pos) == ([3, 4], [1, 1], [1, 17])
+
+
+def test_hf_eager_baseline_reproduces_reference_greedy(golden_dir):
+    """The CPU baseline's restatement of the reference's HF eager path
+    (oracle.hf_eager: transformers forward + the LoRALinear serve math), run
+    in fp32 on BASELINE config 1, gives the reference's own 32 greedy tokens
+    and first-step logits (fixture made by the reference's generate path)."""
+
+    import torch
+
+    from oracle.hf_eager import HFEagerDecoder
+    from pagelora_b200.synthetic import WORKLOADS, make_lora_weights, make_model_weights
+
+    z = np.load(golden_dir / "tiny_llama_greedy.npz")
+    wl = WORKLOADS["config1"]
+    weights = make_model_weights(wl.model, seed=0, dtype=torch.float32)
+    assert math.isclose(sum(float(v.double().sum()) for v in weights.values()), float(z["weight_checksum"][0]),
+                        rel_tol=1e-9)
+    loras = make_lora_weights(wl.model, wl.lora, dtype=torch.float32)
+    dec = HFEagerDecoder(wl.model, weights, loras, wl.lora.scale, dtype=torch.float32)
+    first = dec.prefill(z["prompt"].tolist())
+    assert float((dec.logits[0] - torch.from_numpy(z["first_logits"])).abs().max()) <= 1e-4
+    toks = [first]
+    while len(toks) < 32:
+        toks.append(dec.step(toks[-1]))
+    assert toks == z["tokens"].tolist()

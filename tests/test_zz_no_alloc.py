@@ -107,3 +107,41 @@ def test_fixed_scratch_rejects_shapes_beyond_its_size(cuda_device):
     with pytest.raises(PageLoRAError) as err:
         _run("pl_paged_decode_fixed_scratch", *args, splits)
     assert err.value.status == PL_ERR_WORKSPACE_TOO_SMALL
+
+
+def test_fixed_scratch_rejects_too_many_row_head_pairs(cuda_device):
+    """The counter region holds 16384 (row, kv head) pairs: 2100 rows x 8 kv
+    heads is rejected before any launch, even with one split (no partials)."""
+
+    from pagelora_b200._capi import PL_ERR_WORKSPACE_TOO_SMALL, PageLoRAError, call, ptr, stream_handle
+
+    batch, hq, hkv, d, ps = 2100, 32, 8, 128, 16
+    assert batch * hkv > 16384
+    q = torch.zeros((batch, hq, d), dtype=torch.bfloat16, device="cuda")
+    cache = torch.zeros((1, 2, ps, hkv, d), dtype=torch.bfloat16, device="cuda")
+    indptr = torch.zeros(batch + 1, dtype=torch.int32, device="cuda")
+    indices = torch.zeros(1, dtype=torch.int32, device="cuda")
+    last = torch.zeros(batch, dtype=torch.int32, device="cuda")
+    out = torch.zeros_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(PageLoRAError) as err:
+        call("pl_paged_decode_fixed_scratch", ptr(q), q.stride(0), q.stride(1), ptr(cache), 1, ptr(indptr),
+             ptr(indices), ptr(last), batch, hq, hkv, d, ps, d ** -0.5, 1, ptr(out), out.stride(0), out.stride(1),
+             None, ptr(status), stream_handle())
+    assert err.value.status == PL_ERR_WORKSPACE_TOO_SMALL
+
+
+def test_fixed_scratch_clear_then_calls_match(cuda_device):
+    """pl_fixed_scratch_clear (the reset after a PL_ERR_TIMEOUT status) leaves
+    the array ready: the following calls match the workspace entry point."""
+
+    from pagelora_b200._capi import call, stream_handle
+
+    args = _case(41, batch_lens=[300, 17, 1000], hq=32, hkv=8, d=128, ps=16)
+    ws = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+    ref_o, ref_lse = _run("pl_paged_decode", *args, 9, workspace=ws)
+    for _ in range(2):
+        call("pl_fixed_scratch_clear", stream_handle())
+        o, lse = _run("pl_paged_decode_fixed_scratch", *args, 9)
+        assert np.max(np.abs(o - ref_o)) <= ATOL
+        np.testing.assert_allclose(lse, ref_lse, rtol=1e-3, atol=1e-3)
