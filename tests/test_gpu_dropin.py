@@ -286,7 +286,11 @@ def _bf(z, key):
     return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16).cuda()
 
 
-def _same_bits_or_ulps(got, ref, base, ulps=2):
+def _same_bits_or_ulps(got, ref, base, ulps=3):
+    """Within ``ulps`` units of 2^-8 |value| (two bf16 ulps in the worst binade
+    position): the base projection, the LoRA down values and the delta may
+    each round the other way when fp32 sums are ordered differently."""
+
     _ulps_close(*(t.detach().float().cpu().numpy() for t in (got, ref, base)), ulps)
 
 
