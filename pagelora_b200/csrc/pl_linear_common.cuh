@@ -92,16 +92,19 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int64_t o, int 
 
 // Epilogue of rows o0..o0+3 (o0 % 4 == 0) of one token, stored as one 8-byte
 // vector when the four rows exist and the destination is 8-byte aligned.
-__device__ __forceinline__ void epilogue_rows4(const GemvArgs& a, int64_t o0, int tok, const float* v) {
-  if (o0 >= a.n_out) return;
+// Rows at or past row_end (default: n_out) are left alone.
+__device__ __forceinline__ void epilogue_rows4(const GemvArgs& a, int64_t o0, int tok, const float* v,
+                                               int64_t row_end = -1) {
+  if (row_end < 0 || row_end > a.n_out) row_end = a.n_out;
+  if (o0 >= row_end) return;
   bf16* dst = a.y + tok * a.y_stride + o0;
-  if (o0 + 4 <= a.n_out && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+  if (o0 + 4 <= row_end && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
     float r[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) r[i] = epilogue_value(a, o0 + i, tok, v[i]);
     *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
   } else {
-    for (int i = 0; i < 4 && o0 + i < a.n_out; ++i) dst[i] = f2bf(epilogue_value(a, o0 + i, tok, v[i]));
+    for (int i = 0; i < 4 && o0 + i < row_end; ++i) dst[i] = f2bf(epilogue_value(a, o0 + i, tok, v[i]));
   }
 }
 
@@ -140,16 +143,19 @@ __device__ __forceinline__ float lora_dot16(const uint4 (&b)[2], const float* d)
 // sdelta (optional, with sad): the finished LoRA terms bf16(bf16(d) * scale)
 // of this tile, [T][128] bf16 with row o0 at column o0 - sdelta_row0,
 // computed ahead by the caller; they replace the expand here.
+// Rows at or past row_end (default: n_out) are left alone.
 __device__ __forceinline__ void epilogue_rows4_x4(const GemvArgs& a, int64_t o0, const int (&tok)[4], int nt,
                                                   const float (&v)[4][4], const float* sdown = nullptr,
                                                   int sR = 0, const int32_t* sad = nullptr,
-                                                  const bf16* sdelta = nullptr, int64_t sdelta_row0 = 0) {
-  if (o0 >= a.n_out) return;
-  const bool vec = o0 + 4 <= a.n_out && (a.lora_b == nullptr || a.rank == 16) &&
+                                                  const bf16* sdelta = nullptr, int64_t sdelta_row0 = 0,
+                                                  int64_t row_end = -1) {
+  if (row_end < 0 || row_end > a.n_out) row_end = a.n_out;
+  if (o0 >= row_end) return;
+  const bool vec = o0 + 4 <= row_end && (a.lora_b == nullptr || a.rank == 16) &&
                    ((a.y_stride | a.res_stride) & 3) == 0 &&
                    ((reinterpret_cast<uintptr_t>(a.y) | reinterpret_cast<uintptr_t>(a.residual)) & 7) == 0;
   if (!vec) {
-    for (int k = 0; k < nt; ++k) epilogue_rows4(a, o0, tok[k], v[k]);
+    for (int k = 0; k < nt; ++k) epilogue_rows4(a, o0, tok[k], v[k], row_end);
     return;
   }
   float bias[4] = {0.f, 0.f, 0.f, 0.f};

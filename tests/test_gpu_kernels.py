@@ -645,9 +645,9 @@ def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
 @pytest.mark.parametrize("t", [1, 9, 16, 33, 64, 100, 128])
 def test_linear_lora_gemm_vs_oracle(K, t, k_in):
     """tcgen05 multi-token linear: multi-adapter LoRA epilogue, partial row
-    tile, K tails (600: 2-D tiles with a partial 64-column chunk; 640: 3-D
-    tiles, last K block half empty), grids of 1 CTA (whole tiles), one per
-    SM and 7 CTAs (tiles shared between CTAs, partials merged in order)."""
+    bands, K tails (600: a partial 64-column chunk; 640: the last K block
+    half empty), grids of 1 CTA (one band of six 120-row segments), one per
+    SM (8-row bands) and 7 CTAs (100-row bands)."""
 
     rng = np.random.default_rng(300 + t + k_in)
     n, r, n_ad = 700, 16, 3
@@ -684,8 +684,39 @@ def test_linear_lora_gemm_llama2_shapes(K):
         ref = x.double() @ w.double().T
         tol = torch.abs(ref) * 2.0 ** -8 + 1e-3
         assert bool(torch.all(torch.abs(y.double() - ref) <= tol)), (n, k)
-        y2 = K.linear_lora_gemm(x, w, weights_static=True)  # counters were left at zero
+        y2 = K.linear_lora_gemm(x, w, weights_static=True)  # deterministic
         assert torch.equal(y, y2)
+
+
+@pytest.mark.parametrize("t", [16, 64])
+def test_linear_lora_gemm_qwen3_shapes_and_bands(K, t):
+    """Qwen3-8B projections (q/k/v 6144, gate_up 24576, lm_head 151936 rows:
+    bands of one, two and nine segments per CTA) with rank-16 LoRA on 4
+    adapters and a residual, against an fp64 reference on the GPU."""
+
+    g = torch.Generator(device="cuda").manual_seed(2)
+    for n, k, lora in ((6144, 4096, True), (24576, 4096, False), (151936, 4096, True)):
+        w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+        x = torch.randn(t, k, generator=g, device="cuda").bfloat16()
+        kw = {}
+        ref = x.double() @ w.double().T
+        mag = ref.abs()
+        if lora:
+            down = torch.randn(t, 16, generator=g, device="cuda")
+            bmat = (torch.randn(4, n, 16, generator=g, device="cuda") * 0.05).bfloat16()
+            tok_ad = torch.arange(t, device="cuda", dtype=torch.int32) % 5 - 1  # -1: no adapter
+            res = torch.randn(t, n, generator=g, device="cuda").bfloat16()
+            kw = dict(lora_down=down, lora_b=bmat, lora_scale=2.0, tok_adapter=tok_ad, residual=res)
+            delta = torch.einsum("tnr,tr->tn", bmat[tok_ad.clamp(min=0).long()].double(),
+                                 down.bfloat16().double()) * 2.0
+            delta[tok_ad < 0] = 0
+            ref = res.double() + ref + delta
+            mag = torch.maximum(mag, torch.maximum(res.double().abs(), ref.abs()))
+        y = K.linear_lora_gemm(x, w, weights_static=True, **kw)
+        # a few bf16 roundings of fp32 results (base, delta, sum, residual)
+        tol = mag * 2.0 ** -6 + 1e-3
+        assert bool(torch.all(torch.abs(y.double() - ref) <= tol)), (n, k)
+        del w
 
 
 def test_rmsnorm_and_silu_mul_vs_oracle(K):
