@@ -472,25 +472,23 @@ int32_t pl_linear_set_l2_prefetch(int64_t max_bytes);
 /* ------------------------------------------- multi-token linear (tcgen05) */
 
 typedef struct pl_gemm_plan_t {
-  int32_t ctas;              /* grid size: row bands (at most num_ctas)         */
-  int32_t max_slots;         /* CTAs sharing an output row: always 1            */
-  int64_t workspace_bytes;   /* bytes of workspace pl_linear_lora_gemm needs: 0 */
+  int32_t ctas;              /* grid size (one CTA per SM unless capped)        */
+  int32_t max_slots;         /* most CTAs sharing one 128-row weight tile       */
+  int64_t workspace_bytes;   /* bytes of workspace pl_linear_lora_gemm needs   */
 } pl_gemm_plan_t;
 
 /*
  * Work split of pl_linear_lora_gemm for T tokens (1..128), K inputs and
- * n_out rows over at most num_ctas CTAs (0: one per SM of the current
- * device): each CTA owns a band of about n_out / num_ctas weight rows (a
- * multiple of 4) over the whole of K.
+ * n_out rows over num_ctas CTAs (0: one per SM of the current device).
  */
 int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t n_out,
                             int32_t num_ctas, pl_gemm_plan_t *plan);
 
 /*
  * Multi-token LoRA linear on the tcgen05 tensor cores (TMA-fed, accumulator
- * in tensor memory, one CTA per band of weight rows, so no output is shared
- * between CTAs and nothing is merged): the batched-decode / prefill-chunk
- * counterpart of pl_linear_lora_expand_fused for 1..128 tokens.  Replaces
+ * in tensor memory, persistent grid sharing 128-row x 256-column units
+ * evenly over the SMs): the batched-decode / prefill-chunk counterpart of
+ * pl_linear_lora_expand_fused for 1..128 tokens.  Replaces
  * multilora/linear.py:200-231 (LoRALinear.forward: F.linear + the LoRA
  * delta) and model/flashinfer/packed_ops.py:105-165, 251-265
  * (project_qkv_packed / project_linear) for a multi-sequence batch.
@@ -501,9 +499,12 @@ int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t n_out,
  *               pl_linear_lora_expand_fused; tok_adapter[t] selects token
  *               t's adapter (-1: none), so a batch mixes adapters
  *               (segment-grouped shrink: pl_lora_shrink_seg)
- *   num_ctas    most CTAs (0: one per SM); the result does not depend on
- *               it and is deterministic
- *   workspace   unused (kept for callers of earlier versions; may be NULL)
+ *   num_ctas    grid size (0: one per SM); the result does not depend on it
+ *               beyond fp32 summation order, and is deterministic for a
+ *               given value
+ *   workspace   256-byte aligned, pl_linear_gemm_plan's workspace_bytes for
+ *               the same num_ctas; its first 4 * ceil(n_out / 128) bytes
+ *               are arrival counters: zero before the first call, left zero.
  */
 int32_t pl_linear_lora_gemm(const void *x, int64_t x_stride, int32_t num_tokens,
                             int32_t k_in, const void *w, int32_t n_out,

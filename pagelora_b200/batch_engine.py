@@ -166,6 +166,12 @@ class BatchDecodeEngine:
         self.act = torch.zeros(B, spec.intermediate, device=dev, dtype=bf)
         self.logits = torch.zeros(B, spec.vocab, device=dev, dtype=bf)
         self.argmax_ws = torch.zeros(K.argmax_workspace_bytes(B), device=dev, dtype=torch.uint8)
+        ws = 256
+        for n, k in ((spec.qkv_dim, H), (H, spec.q_dim), (2 * spec.intermediate, H), (H, spec.intermediate),
+                     (spec.vocab, H)):
+            if not uses_gemv(B, k):
+                ws = max(ws, int(K.gemm_plan(B, k, n).workspace_bytes))
+        self.gemm_ws = torch.zeros(ws, device=dev, dtype=torch.uint8)
         self.num_splits = 1
         self.workspace = torch.zeros(1 << 20, device=dev, dtype=torch.uint8)
         if self.world > 1:
@@ -465,7 +471,7 @@ class BatchDecodeEngine:
             x = K.rmsnorm(x, norm_weight, s.rms_eps, out=self.xn)
         elif prologue == PL_PROLOGUE_SILU_MUL:
             x = K.silu_mul(x, out=self.act)
-        return K.linear_lora_gemm(x, w, weights_static=True, status=self.status, **kw)
+        return K.linear_lora_gemm(x, w, workspace=self.gemm_ws, weights_static=True, status=self.status, **kw)
 
     def _decode_body(self) -> None:
         s = self.spec

@@ -3,95 +3,118 @@
 // feed it.
 //
 // pl_linear_lora_gemm computes y[t, n] = epilogue(sum_k x[t, k] * w[n, k]).
-// CTA c of the grid owns the weight-row band [c*R, c*R + R) over the whole
-// of K, so no output is shared between CTAs: nothing is merged, and the
-// only tail after the last MMA is the band's own epilogue.  R is about
-// n_out / SMs (a multiple of 4), cut into segments of at most 128 rows
-// (one UMMA M tile, rows past the segment read as garbage and are never
-// stored); every SM streams the same number of weight bytes.  Per CTA:
-//   warp 0     streams each unit (one segment x one K block of kcs x 64
-//              columns) as kcs 2-D TMA copies of the segment's rows plus
-//              kcs copies of the activation chunk into a shared-memory
-//              ring, several units per issuing instruction;
+// Work is cut into units of one 128-row weight tile x one K block (4 chunks
+// of 64 columns, 2 when N = 128); the persistent grid has one CTA per SM and
+// CTA c takes the contiguous unit range [c*U/P, (c+1)*U/P) -- every SM
+// streams the same number of bytes whatever the tile count (per-SM copy
+// throughput, not HBM, is the limit when SMs idle).  Per CTA:
+//   warp 0     streams each unit's weight tile (128 rows x 256 columns, one
+//              3-D TMA copy reading 512 contiguous bytes per row) and the
+//              activation tile into a shared-memory ring, several units per
+//              issuing instruction;
 //   warp 1     (one lane) issues tcgen05.mma (M = 128, N = tokens padded to
 //              16/32/64/128, K = 16) into one of two tensor-memory
-//              accumulators, one per segment;
+//              accumulators, one per tile segment;
 //   warps 2-5  read a finished accumulator with tcgen05.ld (warp w owns
 //              lanes 32(w%4)..) while the next segment accumulates, and run
 //              the decode GEMV's epilogue (bias, per-token LoRA expand with
 //              the token's adapter, residual; the reference's bf16 rounding
 //              points), staged through shared memory into 8-byte stores.
-//              With rank-16 LoRA they first compute the LoRA terms of the
-//              CTA's last segment while the weights stream.
+// A tile split between CTAs is finished by the last contributor (arrival
+// ticket per tile), which adds the contributors' fp32 partials in CTA order
+// -- deterministic -- and runs the epilogue.  No wait depends on another CTA.
 #include "pl_linear_common.cuh"
 
 #include <mutex>
 
 namespace pl {
 
-constexpr int kGemmM = 128;      // UMMA M: rows one accumulator holds
+constexpr int kGemmM = 128;      // weight rows per tile (UMMA M)
 constexpr int kGemmKC = 64;      // K per chunk: one 128-byte swizzled row of bf16
 constexpr int kGemmThreads = 192;
 constexpr int kGemmIssue = 4;    // units per producer TMA instruction
-constexpr int kGemmGuard = kGemmM * 128;  // MMA reads 128 rows from a slot: slack after the ring
 
 struct GemmArgs {
   GemvArgs e;          // epilogue fields: n_out, bias, LoRA, residual, y, status; T, K
-  int32_t kblocks;     // K blocks per segment
-  int32_t band_rows;   // rows per CTA
-  int32_t seg_rows;    // rows per segment (<= 128, a multiple of 4)
-  int32_t nseg;        // segments per band
-  int32_t a_slot;      // bytes of one weight chunk slot (seg_rows rounded up to 8, x 128 B)
-  int32_t stage_bytes;
+  int32_t kblocks;     // K blocks per tile
+  int32_t units;       // m_tiles * kblocks
   int32_t stages;
+  int32_t max_slots;   // partial slots per tile
+  float* partial;      // [m_tiles][max_slots][N][128] fp32
+  int32_t* counters;   // [m_tiles] arrival tickets, zero between calls
   int32_t lora_stage;  // bytes of shared memory holding the rank-16 LoRA down rows and adapter ids (0: none)
-  int32_t lora_delta;  // bytes holding the precomputed LoRA terms of the CTA's last segment (0: none)
+  int32_t lora_delta;  // bytes holding the precomputed LoRA terms of the CTA's last tile (0: none)
 };
 
-template <int N>
+// N: tokens padded (UMMA N).  KCS: 64-column chunks per K block; with KCS > 1
+// the tiles come from 3-D tensor maps (64, rows, K / 64) so that one copy
+// reads KCS x 128 contiguous bytes of every weight row.
+template <int N, int KCS>
 struct GemmCfg {
-  static constexpr int kBSlot = N * 128;        // activation chunk slot
+  static constexpr int kATile = kGemmM * 128;   // 16 KB weight tile per chunk
+  static constexpr int kBTile = N * 128;        // activation tile per chunk
+  static constexpr int kABytes = KCS * kATile;
+  static constexpr int kBBytes = KCS * kBTile;
+  static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kAccCols = N < 16 ? 16 : N;
   static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;  // two accumulators
   static constexpr int kStageTile = 16 * kGemmM * 4;                          // epilogue staging
-  static_assert(kBSlot % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
+  static_assert(kBTile % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
 };
 
-__host__ __device__ inline int gemm_smem_bytes(int ring_bytes, int lora_stage, int lora_delta, int stages) {
-  return 1024 + ring_bytes + kGemmGuard + 16 * kGemmM * 4 + lora_stage + lora_delta + (2 * stages + 4) * 8 + 32;
+__host__ __device__ inline int gemm_smem_bytes(int stage_bytes, int stages, int lora_stage) {
+  return 1024 + stages * stage_bytes + 16 * kGemmM * 4 + lora_stage + (2 * stages + 4) * 8 + 32;
+}
+__host__ __device__ inline int gemm_smem_bytes(int stage_bytes, int stages, int lora_stage, int lora_delta) {
+  return gemm_smem_bytes(stage_bytes, stages, lora_stage) + lora_delta;
+}
+
+__host__ __device__ inline int unit_begin(int c, int units, int ctas) {
+  return (int)(((int64_t)c * units) / ctas);
+}
+// The CTA whose unit range holds unit u.
+__host__ __device__ inline int cta_of_unit(int u, int units, int ctas) {
+  int c = (int)(((int64_t)u * ctas) / units);
+  while (c + 1 < ctas && unit_begin(c + 1, units, ctas) <= u) ++c;
+  while (c > 0 && unit_begin(c, units, ctas) > u) --c;
+  return c;
+}
+
+template <int KCS>
+__device__ __forceinline__ void gemm_tile_load(void* dst, const CUtensorMap* map, int kb, int row0, uint64_t* bar,
+                                               uint64_t pol) {
+  if constexpr (KCS == 1)
+    tma_load_2d(dst, map, kb * kGemmKC, row0, bar, pol);
+  else
+    tma_load_3d(dst, map, 0, row0, kb * KCS, bar, pol);
 }
 
 template <int N, int KCS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                      const GemmArgs g) {
-  using C = GemmCfg<N>;
+  using C = GemmCfg<N, KCS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = g.stages;
-  const int SB = g.stage_bytes;
-  const int AS = g.a_slot;
-  uint8_t* tail = smem + S * SB + kGemmGuard;
-  float* stile = reinterpret_cast<float*>(tail);  // [16 tokens][128 rows]
+  float* stile = reinterpret_cast<float*>(smem + S * C::kStageBytes);  // [16 tokens][128 rows]
   // Rank-16 LoRA epilogue inputs, staged once: down rows rounded to bf16
   // [T][num_slices * 16], then the tokens' adapter ids [T].
-  float* lds = reinterpret_cast<float*>(tail + C::kStageTile);
-  // The precomputed LoRA terms of the CTA's last segment, [T][128] bf16.
-  bf16* sdl = reinterpret_cast<bf16*>(tail + C::kStageTile + g.lora_stage);
-  uint64_t* full = reinterpret_cast<uint64_t*>(tail + C::kStageTile + g.lora_stage + g.lora_delta);
+  float* lds = reinterpret_cast<float*>(smem + S * C::kStageBytes + C::kStageTile);
+  // The precomputed LoRA terms of the CTA's last tile, [T][128] bf16.
+  bf16* sdl = reinterpret_cast<bf16*>(smem + S * C::kStageBytes + C::kStageTile + g.lora_stage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes + C::kStageTile + g.lora_stage +
+                                               g.lora_delta);
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;  // [2] accumulator ready
   uint64_t* acce = accf + 2;   // [2] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
-  volatile int32_t* flags = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);  // abort, -, issued, consumed
+  volatile int32_t* flags = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);  // abort, last, issued, consumed
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int KB = g.kblocks;
-  const int64_t band0 = (int64_t)blockIdx.x * g.band_rows;
-  // Segments of this band that hold rows (the last band may be short).
-  int nseg = g.nseg;
-  while (nseg > 0 && band0 + (int64_t)(nseg - 1) * g.seg_rows >= g.e.n_out) --nseg;
-  const int n = nseg * KB;  // units
+  const int P = gridDim.x, U = g.units, KB = g.kblocks;
+  const int u0 = unit_begin(blockIdx.x, U, P), u1 = unit_begin(blockIdx.x + 1, U, P);
+  const int n = u1 - u0;  // >= 1: the grid never exceeds the unit count
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -123,53 +146,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // A TMA instruction costs a fixed issue time however many lanes issue
-    // it, so the warp issues up to kGemmIssue units per instruction: lanes
-    // 2*KCS*j .. 2*KCS*j + KCS - 1 load unit j's weight chunks (the first
-    // one arms the unit's barrier), the next KCS lanes its activation chunks.
+    // it, so the warp issues up to kGemmIssue units per instruction: lane 2j
+    // loads unit j's weight tile (and arms its barrier), lane 2j+1 its
+    // activation tile.
     const uint64_t pol = l2_evict_first_policy();
-    const int tx = KCS * (g.seg_rows * 128 + C::kBSlot);
     const int pre = g.e.early_weights ? (n < S ? n : S) : 0;
-    // Weights are not produced upstream: start the first stages now.
-    for (int idx = lane; idx < pre * KCS; idx += 32) {
-      const int i = idx / KCS, j = idx % KCS;
-      const int seg = i / KB, kb = i % KB;
-      if (j == 0) mbar_arrive_expect_tx(&full[i], tx);
-      __syncwarp(__activemask());
-      tma_load_2d(smem + i * SB + j * AS, &wmap, (kb * KCS + j) * kGemmKC,
-                  (int32_t)(band0 + (int64_t)seg * g.seg_rows), &full[i], pol);
+    for (int i = lane; i < pre; i += 32) {  // weights are not produced upstream: start them now
+      const int u = u0 + i;
+      mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+      gemm_tile_load<KCS>(smem + i * C::kStageBytes, &wmap, u % KB, (u / KB) * kGemmM, &full[i], pol);
     }
     pdl_wait();
     if (lane == 0) PL_TRACE_POINT(1);
-    constexpr int kLanesPerUnit = 2 * KCS;
-    constexpr int kBatch = 32 / kLanesPerUnit < kGemmIssue ? 32 / kLanesPerUnit : kGemmIssue;
-    const int batch = S < kBatch ? S : kBatch;  // a batch never reuses its own stages
-    const int jb = lane / kLanesPerUnit, part = lane % kLanesPerUnit;
-    const bool is_w = part < KCS;
-    const int j = is_w ? part : part - KCS;
+    const int jb = lane >> 1, kind = lane & 1;
+    // A batch of units is issued only once all of their stages are free, so
+    // it stays smaller than the ring: a batch as deep as the ring would drain
+    // it before every refill and leave the CTA idle for a whole memory
+    // latency per ring's worth of data.
+    int batch = S - 1 < kGemmIssue ? S - 1 : kGemmIssue;
+    if (batch < 1) batch = 1;
     int i0 = 0;
     for (; i0 < n; i0 += batch) {
       const int i = i0 + jb;
-      const bool active = jb < batch && i < n;
+      const bool active = lane < 2 * batch && i < n;
       const int s = i % S;
       bool ok = true;
-      if (active && part == 0 && i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1);
+      if (active && i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) set_status(g.e.status, PL_ERR_TIMEOUT);
         flags[0] = 1;
         break;
       }
-      __syncwarp();  // every lane of a unit sees its stage free before any copy into it
-      const int seg = i / KB, kb = i % KB;
-      uint8_t* st = smem + s * SB;
-      if (active && part == 0 && i >= pre) mbar_arrive_expect_tx(&full[s], tx);
+      const int u = u0 + i;
+      uint8_t* st = smem + s * C::kStageBytes;
+      if (active && kind == 0 && i >= pre) mbar_arrive_expect_tx(&full[s], C::kStageBytes);
       __syncwarp();
       if (active) {
-        if (is_w) {
-          if (i >= pre)
-            tma_load_2d(st + j * AS, &wmap, (kb * KCS + j) * kGemmKC, (int32_t)(band0 + (int64_t)seg * g.seg_rows),
-                        &full[s], pol);
+        if (kind == 0) {
+          if (i >= pre) gemm_tile_load<KCS>(st, &wmap, u % KB, (u / KB) * kGemmM, &full[s], pol);
         } else {
-          tma_load_2d(st + KCS * AS + j * C::kBSlot, &xmap, (kb * KCS + j) * kGemmKC, 0, &full[s], 0ull);
+          gemm_tile_load<KCS>(st + C::kABytes, &xmap, u % KB, 0, &full[s], 0ull);
         }
       }
     }
@@ -179,12 +195,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(kGemmM, N);
-      int i = 0;
+      int i = 0, seg = 0;
       bool ok = true;
       for (; i < n; ++i) {
-        const int seg = i / KB, kb = i % KB;
+        const int u = u0 + i, kb = u % KB;
+        const bool first = (i == 0 || kb == 0), last = (i == n - 1 || kb == KB - 1);
         const int b = seg & 1;
-        if (kb == 0 && seg >= 2) ok = mbar_wait(&acce[b], ((seg >> 1) - 1) & 1);
+        if (first && seg >= 2) ok = mbar_wait(&acce[b], ((seg >> 1) - 1) & 1);
         const int s = i % S;
         if (ok) ok = mbar_wait(&full[s], (i / S) & 1);
         if (!ok) {
@@ -194,24 +211,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         if (i == 0) PL_TRACE_POINT(2);
-        const uint32_t a0 = smem_u32(smem + s * SB);
-        const uint32_t b0 = a0 + KCS * AS;
+        const uint32_t a0 = smem_u32(smem + s * C::kStageBytes);
+        const uint32_t b0 = a0 + C::kABytes;
         const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols);
 #pragma unroll
-        for (int jj = 0; jj < KCS; ++jj) {
+        for (int j = 0; j < KCS; ++j) {
 #pragma unroll
           for (int k = 0; k < kGemmKC / 16; ++k)
-            umma_bf16(acc, umma_desc_k_sw128(a0 + jj * AS + 32 * k), umma_desc_k_sw128(b0 + jj * C::kBSlot + 32 * k),
-                      idesc, (kb > 0 || jj > 0 || k > 0) ? 1u : 0u);
+            umma_bf16(acc, umma_desc_k_sw128(a0 + j * C::kATile + 32 * k),
+                      umma_desc_k_sw128(b0 + j * C::kBTile + 32 * k), idesc, (!first || j > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
-        if (kb == KB - 1) umma_commit(&accf[b]);
+        if (last) {
+          umma_commit(&accf[b]);
+          ++seg;
+        }
       }
       flags[3] = i;
       PL_TRACE_POINT(3);
       if (!ok) {
         // Release the epilogue for the segments that will not be computed.
-        for (int seg = i / KB; seg < nseg; ++seg) umma_commit(&accf[seg & 1]);
+        for (int i2 = i; i2 < n; ++i2) {
+          const int kb = (u0 + i2) % KB;
+          if (i2 == n - 1 || kb == KB - 1) {
+            umma_commit(&accf[seg & 1]);
+            ++seg;
+          }
+        }
       }
     }
   } else {
@@ -236,15 +262,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       sdown = lds;
       sad = lad;
     }
-    // The LoRA terms of the CTA's last segment, computed while the weights
-    // stream: its epilogue, at the very end of the CTA, then only adds them.
-    const int seg_pre = (g.lora_delta && nseg > 0) ? nseg - 1 : -1;
-    if (seg_pre >= 0) {
-      const int64_t row0 = band0 + (int64_t)seg_pre * g.seg_rows;
-      int64_t row_end = row0 + g.seg_rows;
-      if (row_end > g.e.n_out) row_end = g.e.n_out;
-      // lane: rows 4*lane .. 4*lane+3 of the segment; warp ew: a contiguous
-      // quarter of the tokens, so a B row set is loaded once per adapter run
+    // The LoRA terms of the tile that this CTA's last segment covers: its
+    // epilogue (a whole tile, or the merge of the shared tile's partials, at
+    // the very end of the CTA) then only adds them.  Computed here, while the
+    // first accumulator is still being filled.
+    // Only a CTA with at least half a tile of units of its own: with fewer,
+    // a tile has many contributors that finish together, the precomputed terms
+    // are mostly unused, and computing them delays the partials.
+    const int t_pre = (g.lora_delta && 2 * n >= KB) ? (u1 - 1) / KB : -1;
+    if (t_pre >= 0) {
+      const int64_t row0 = (int64_t)t_pre * kGemmM;
+      // lane: rows 4*lane .. 4*lane+3 of the tile; warp ew: a contiguous quarter
+      // of the tokens, so a B row set is loaded once per adapter run
       const int64_t o0 = row0 + 4 * lane;
       int sl[4];
 #pragma unroll
@@ -252,7 +281,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         sl[i] = 0;
         while (sl[i] < g.e.num_slices - 1 && o0 + i >= g.e.slice_end[sl[i]]) ++sl[i];
       }
-      const bool rows_ok = o0 + 4 <= row_end;
+      const bool rows_ok = o0 + 4 <= g.e.n_out;
       int cur = -1;
       uint4 b[4][2] = {};
       const int tq = (T + 3) / 4;
@@ -273,14 +302,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int i = 0; i < 4; ++i)
             dv[i] = bfr(bfr(lora_dot16(b[i], sdown + tok * R + sl[i] * 16)) * g.e.lora_scale);
         }
-        if (rows_ok)
-          *reinterpret_cast<uint2*>(sdl + tok * kGemmM + 4 * lane) =
-              make_uint2(pack_bf16x2(dv[0], dv[1]), pack_bf16x2(dv[2], dv[3]));
+        *reinterpret_cast<uint2*>(sdl + tok * kGemmM + 4 * lane) =
+            make_uint2(pack_bf16x2(dv[0], dv[1]), pack_bf16x2(dv[2], dv[3]));
       }
       named_barrier(1, kEpiThreads);
-      if (threadIdx.x == 64) PL_TRACE_POINT(10);
     }
-    for (int seg = 0; seg < nseg; ++seg) {
+    int seg = 0;
+    for (int i = 0; i < n;) {
+      const int u = u0 + i, t = u / KB, ka = u % KB;
+      int len = KB - ka;
+      if (len > n - i) len = n - i;
       const int b = seg & 1;
       if (!mbar_wait(&accf[b], (seg >> 1) & 1)) {
         set_status(g.e.status, PL_ERR_TIMEOUT);
@@ -291,44 +322,117 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (seg == 0) PL_TRACE_POINT(4);
         PL_TRACE_MAX(5);
       }
-      const int64_t row0 = band0 + (int64_t)seg * g.seg_rows;
-      int64_t row_end = row0 + g.seg_rows;
-      if (row_end > g.e.n_out) row_end = g.e.n_out;
       const uint32_t acc = lane_base + (uint32_t)(b * C::kAccCols);
-      const int64_t o4 = row0 + 4 * lane;
-      // Stage [16 tokens][128 rows] through shared memory, then warp ew
-      // finishes tokens 4ew .. 4ew+3 of the chunk (4 rows a lane; adjacent
-      // tokens usually share an adapter).
+      const int64_t o4 = (int64_t)t * kGemmM + 4 * lane;
+      const bool whole = (ka == 0 && len == KB);
+      if (whole) {
+        // The whole tile is here: stage [16 tokens][128 rows] through shared
+        // memory, then warp ew finishes tokens ew, ew+4, ... (4 rows a lane).
 #pragma unroll 1
-      for (int c = 0; c < N / 16 && 16 * c < T; ++c) {
-        float v[16];
-        tmem_ld16(acc + 16 * c, v);
+        for (int c = 0; c < N / 16 && 16 * c < T; ++c) {
+          float v[16];
+          tmem_ld16(acc + 16 * c, v);
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) stile[jj * kGemmM + row] = v[jj];
-        named_barrier(1, kEpiThreads);
-        if (!flags[0] && o4 < row_end) {
-          int toks[4];
-          float vals[4][4];
-          int nt = 0;
+          for (int j = 0; j < 16; ++j) stile[j * kGemmM + row] = v[j];
+          named_barrier(1, kEpiThreads);
+          if (!flags[0]) {
+            // tokens 4ew .. 4ew+3 of this chunk (adjacent tokens usually
+            // share an adapter), finished together
+            int toks[4];
+            float vals[4][4];
+            int nt = 0;
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const int jj = 4 * ew + h;
-            toks[h] = 16 * c + jj;
-            const float4 r4 = *reinterpret_cast<const float4*>(stile + jj * kGemmM + 4 * lane);
-            vals[h][0] = r4.x;
-            vals[h][1] = r4.y;
-            vals[h][2] = r4.z;
-            vals[h][3] = r4.w;
-            if (16 * c + jj < T) nt = h + 1;
+            for (int h = 0; h < 4; ++h) {
+              const int j = 4 * ew + h;
+              toks[h] = 16 * c + j;
+              const float4 r4 = *reinterpret_cast<const float4*>(stile + j * kGemmM + 4 * lane);
+              vals[h][0] = r4.x;
+              vals[h][1] = r4.y;
+              vals[h][2] = r4.z;
+              vals[h][3] = r4.w;
+              if (16 * c + j < T) nt = h + 1;
+            }
+            epilogue_rows4_x4(g.e, o4, toks, nt, vals, sdown, R, sad, t == t_pre ? sdl : nullptr,
+                              (int64_t)t * kGemmM);
           }
-          epilogue_rows4_x4(g.e, o4, toks, nt, vals, sdown, R, sad, seg == seg_pre ? sdl : nullptr, row0,
-                            row_end);
+          named_barrier(1, kEpiThreads);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[b]);
+      } else {
+        // Part of a tile: leave the fp32 partial in this CTA's slot; the last
+        // contributor adds the slots in order and runs the epilogue.
+        const int c_first = cta_of_unit(t * KB, U, P);
+        const int c_last = cta_of_unit(t * KB + KB - 1, U, P);
+        const int slot = blockIdx.x - c_first;
+        float* mine = g.partial + ((int64_t)t * g.max_slots + slot) * N * kGemmM;
+#pragma unroll 1
+        for (int c = 0; c < N / 16 && 16 * c < T; ++c) {
+          float v[16];
+          tmem_ld16(acc + 16 * c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (16 * c + j < T) __stcg(mine + (16 * c + j) * kGemmM + row, v[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[b]);
+        __threadfence();
+        named_barrier(1, kEpiThreads);
+        if (ew == 0 && lane == 0) {
+          const int32_t ticket = atomicAdd(&g.counters[t], 1);
+          flags[1] = ticket == c_last - c_first ? 1 : 0;
         }
         named_barrier(1, kEpiThreads);
+        if (threadIdx.x == 64) PL_TRACE_MAX(6);
+        if (flags[1]) {
+          __threadfence();
+          const int nslots = c_last - c_first + 1;
+          const float* base = g.partial + (int64_t)t * g.max_slots * N * kGemmM + 4 * lane;
+          // Four tokens x four slots of loads in flight per lane; slots are
+          // added in order, so the sum does not depend on timing.
+#pragma unroll 1
+          for (int tok = 4 * ew; tok < T; tok += 16) {
+            float a4[4][4] = {};
+            int toks[4];
+            int nt = 0;
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              toks[h] = tok + h;
+              if (tok + h < T) nt = h + 1;
+            }
+#pragma unroll 1
+            for (int sl = 0; sl < nslots; sl += 4) {
+              float4 p[4][4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  p[h][k] = (sl + k < nslots && h < nt)
+                                ? __ldcg(reinterpret_cast<const float4*>(
+                                      base + ((int64_t)(sl + k) * N + tok + h) * kGemmM))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  a4[h][0] += p[h][k].x;
+                  a4[h][1] += p[h][k].y;
+                  a4[h][2] += p[h][k].z;
+                  a4[h][3] += p[h][k].w;
+                }
+            }
+            if (!flags[0])
+              epilogue_rows4_x4(g.e, o4, toks, nt, a4, sdown, R, sad, t == t_pre ? sdl : nullptr,
+                                (int64_t)t * kGemmM);
+          }
+          if (ew == 0 && lane == 0) g.counters[t] = 0;
+        }
+        named_barrier(1, kEpiThreads);  // flags[1] is reused by the next segment
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[b]);
+      i += len;
+      ++seg;
     }
     if (threadIdx.x == 64) PL_TRACE_POINT(7);
   }
@@ -496,56 +600,52 @@ int32_t matrix_map(const void* ptr, int64_t inner, int64_t rows, int64_t stride,
 
 int gemm_n(int tokens) { return tokens <= 16 ? 16 : tokens <= 32 ? 32 : tokens <= 64 ? 64 : 128; }
 
-constexpr int kGemmRingBudget = 176 * 1024;
-constexpr int kLoraStageMax = 16 * 1024;
+int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
-int gemm_smem_optin() {
-  static int limit[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 227 * 1024;
-  if (limit[dev] == 0) {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
-      v = 227 * 1024;
-    limit[dev] = v;
-  }
-  return limit[dev];
-}
+constexpr int kGemmSmemBudget = 200 * 1024;
+constexpr int kLoraStageMax = 16 * 1024;
+constexpr int kGemmSmemMax = 227 * 1024;  // dynamic shared memory per CTA on sm_100
 
 struct GemmShape {
-  int n, kcs, seg_rows, nseg, band_rows, kblocks, ctas, a_slot, stage_bytes, stages;
+  int n, kcs, stages, m_tiles, kblocks, units, ctas, max_slots, stage_bytes;
 };
 
-// Row bands: the fewest rows per CTA (a multiple of 4) that cover n_out
-// with at most max_ctas CTAs, cut into nseg equal segments of <= 128 rows.
-// K blocks of kcs x 64 columns (kcs 4 up to 32 tokens, 2 at 64, 1 at 128:
-// a stage stays small enough for several of them); as many ring stages as
-// fit.
-GemmShape gemm_shape(int tokens, int k_in, int n_out, int max_ctas) {
+// Tile geometry: K blocks of kcs x 64 columns (kcs 4, or 2 at N = 128, when
+// K % 64 == 0; else 1), as many ring stages as fit; `ctas` CTAs (one per SM
+// by default) share the m_tiles x kblocks units evenly.
+GemmShape gemm_shape(int tokens, int k_in, int n_out, int ctas, bool allow_3d) {
   GemmShape s;
   s.n = gemm_n(tokens);
-  s.kcs = s.n <= 32 ? 4 : (s.n == 64 ? 2 : 1);
-  const int per = (int)(((int64_t)n_out + max_ctas - 1) / max_ctas);
-  s.nseg = (per + pl::kGemmM - 1) / pl::kGemmM;
-  const int seg = (int)(((int64_t)n_out + (int64_t)max_ctas * s.nseg - 1) / ((int64_t)max_ctas * s.nseg));
-  s.seg_rows = (seg + 3) & ~3;
-  if (s.seg_rows > pl::kGemmM) s.seg_rows = pl::kGemmM;
-  s.band_rows = s.seg_rows * s.nseg;
-  s.ctas = (int)(((int64_t)n_out + s.band_rows - 1) / s.band_rows);
+  s.kcs = (allow_3d && k_in % pl::kGemmKC == 0) ? (s.n == 128 ? 2 : 4) : 1;
+  s.stage_bytes = s.kcs * (pl::kGemmM * 128 + s.n * 128);
+  s.m_tiles = (n_out + pl::kGemmM - 1) / pl::kGemmM;
   const int block_cols = pl::kGemmKC * s.kcs;
   s.kblocks = (k_in + block_cols - 1) / block_cols;
-  s.a_slot = ((s.seg_rows + 7) & ~7) * 128;
-  s.stage_bytes = s.kcs * (s.a_slot + s.n * 128);
-  int stages = kGemmRingBudget / s.stage_bytes;
+  s.units = s.m_tiles * s.kblocks;
+  s.ctas = ctas < s.units ? ctas : s.units;
+  int stages = kGemmSmemBudget / s.stage_bytes;
   if (stages > 8) stages = 8;
   s.stages = stages < 2 ? 2 : stages;
+  s.max_slots = 1;
+  for (int t = 0; t < s.m_tiles; ++t) {
+    const int c0 = pl::cta_of_unit(t * s.kblocks, s.units, s.ctas);
+    const int c1 = pl::cta_of_unit(t * s.kblocks + s.kblocks - 1, s.units, s.ctas);
+    if (c1 - c0 + 1 > s.max_slots) s.max_slots = c1 - c0 + 1;
+  }
   return s;
 }
 
+int64_t gemm_workspace_bytes(const GemmShape& s) {
+  int64_t b = align256((int64_t)s.m_tiles * 4);
+  if (s.max_slots > 1) b += (int64_t)s.m_tiles * s.max_slots * s.n * pl::kGemmM * 4;
+  return b;
+}
+
 template <int N, int KCS>
-int32_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int ctas, void* stream) {
+int32_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int ctas, int stages,
+                    void* stream) {
   auto kern = pl::linear_tc_kernel<N, KCS>;
-  const int smem = pl::gemm_smem_bytes(g.stages * g.stage_bytes, g.lora_stage, g.lora_delta, g.stages);
+  const int smem = pl::gemm_smem_bytes(pl::GemmCfg<N, KCS>::kStageBytes, stages, g.lora_stage, g.lora_delta);
   int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (st != PL_OK) return st;
   return pl_host::launch_pdl(kern, dim3(ctas), dim3(pl::kGemmThreads), smem, stream, wm, xm, g);
@@ -553,16 +653,24 @@ int32_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const pl::Gemm
 
 template <int N>
 int32_t launch_gemm_n(int kcs, const CUtensorMap& wm, const CUtensorMap& xm, const pl::GemmArgs& g, int ctas,
-                      void* stream) {
-  (void)kcs;  // fixed by N, as in gemm_shape
-  if constexpr (N == 128) return launch_gemm<N, 1>(wm, xm, g, ctas, stream);
-  else if constexpr (N == 64) return launch_gemm<N, 2>(wm, xm, g, ctas, stream);
-  else return launch_gemm<N, 4>(wm, xm, g, ctas, stream);
+                      int stages, void* stream) {
+  if (kcs == 1) return launch_gemm<N, 1>(wm, xm, g, ctas, stages, stream);
+  if constexpr (N == 128) return launch_gemm<N, 2>(wm, xm, g, ctas, stages, stream);
+  else return launch_gemm<N, 4>(wm, xm, g, ctas, stages, stream);
 }
 
 int sm_count_or_default() {
   const int sms = pl_host::sm_count();
   return sms > 0 ? sms : 148;
+}
+
+// One CTA per SM when the row tiles alone cover the device; otherwise 7/8 of
+// the SMs, which measured faster (fewer contributors per shared tile, less
+// partial traffic) on the 4096-row projections.
+int default_ctas(int n_out) {
+  const int sms = sm_count_or_default();
+  const int m_tiles = (n_out + pl::kGemmM - 1) / pl::kGemmM;
+  return m_tiles >= sms ? sms : (sms * 7) / 8;
 }
 
 }  // namespace
@@ -571,10 +679,11 @@ extern "C" int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t
                                        pl_gemm_plan_t* plan) {
   if (plan == nullptr || num_tokens < 1 || num_tokens > 128 || k_in <= 0 || n_out <= 0 || num_ctas < 0)
     return PL_ERR_INVALID_ARGUMENT;
-  const GemmShape s = gemm_shape(num_tokens, k_in, n_out, num_ctas > 0 ? num_ctas : sm_count_or_default());
+  const GemmShape s = gemm_shape(num_tokens, k_in, n_out, num_ctas > 0 ? num_ctas : default_ctas(n_out),
+                                 k_in % pl::kGemmKC == 0);
   plan->ctas = s.ctas;
-  plan->max_slots = 1;
-  plan->workspace_bytes = 0;
+  plan->max_slots = s.max_slots;
+  plan->workspace_bytes = gemm_workspace_bytes(s);
   return PL_OK;
 }
 
@@ -585,11 +694,9 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
                                        const void* residual, int64_t res_stride, void* y, int64_t y_stride,
                                        int32_t num_ctas, void* workspace, int64_t workspace_bytes, int32_t flags,
                                        int32_t* status_dev, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (num_tokens == 0 || n_out == 0) return PL_OK;
   if (x == nullptr || w == nullptr || y == nullptr || num_tokens < 0 || num_tokens > 128 || k_in <= 0 ||
-      n_out < 0 || num_ctas < 0)
+      n_out < 0 || workspace == nullptr || num_ctas < 0)
     return PL_ERR_INVALID_ARGUMENT;
   if (k_in % 8 != 0 || x_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
       (reinterpret_cast<uintptr_t>(w) & 15))
@@ -597,11 +704,19 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   if (lora_b != nullptr && (lora_down == nullptr || lora_rank <= 0 || num_slices < 1 || num_slices > 4 ||
                             (num_slices > 1 && slice_end == nullptr)))
     return PL_ERR_INVALID_ARGUMENT;
-  const GemmShape sh = gemm_shape(num_tokens, k_in, n_out, num_ctas > 0 ? num_ctas : sm_count_or_default());
+  const int ctas = num_ctas > 0 ? num_ctas : default_ctas(n_out);
+  GemmShape sh = gemm_shape(num_tokens, k_in, n_out, ctas, true);
   CUtensorMap wm, xm;
-  int32_t st = matrix_map(w, k_in, n_out, k_in, sh.seg_rows, 1, &wm);
-  if (st == PL_OK) st = matrix_map(x, k_in, num_tokens, x_stride, sh.n, 1, &xm);
+  int32_t st = matrix_map(w, k_in, n_out, k_in, pl::kGemmM, sh.kcs, &wm);
+  if (st == PL_OK) st = matrix_map(x, k_in, num_tokens, x_stride, sh.n, sh.kcs, &xm);
+  if (st == PL_ERR_UNSUPPORTED && sh.kcs > 1) {  // no 3-D map: one chunk per K block
+    sh = gemm_shape(num_tokens, k_in, n_out, ctas, false);
+    st = matrix_map(w, k_in, n_out, k_in, pl::kGemmM, 1, &wm);
+    if (st == PL_OK) st = matrix_map(x, k_in, num_tokens, x_stride, sh.n, 1, &xm);
+  }
   if (st != PL_OK) return st;
+  if (workspace_bytes < gemm_workspace_bytes(sh) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return PL_ERR_WORKSPACE_TOO_SMALL;
 
   pl::GemmArgs g = {};
   pl::GemvArgs& a = g.e;
@@ -628,29 +743,28 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   a.early_weights = (flags & PL_FLAG_WEIGHTS_STATIC) ? 1 : 0;
   a.status = status_dev;
   g.kblocks = sh.kblocks;
-  g.band_rows = sh.band_rows;
-  g.seg_rows = sh.seg_rows;
-  g.nseg = sh.nseg;
-  g.a_slot = sh.a_slot;
-  g.stage_bytes = sh.stage_bytes;
+  g.units = sh.units;
   g.stages = sh.stages;
+  g.max_slots = sh.max_slots;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  g.counters = reinterpret_cast<int32_t*>(ws);
+  g.partial = sh.max_slots > 1 ? reinterpret_cast<float*>(ws + align256((int64_t)sh.m_tiles * 4)) : nullptr;
   // Rank-16 LoRA: stage the (small) down rows and adapter ids in shared
-  // memory so the epilogue reads them once per CTA instead of per element,
-  // and compute the last segment's LoRA terms ahead when they fit.
+  // memory so the epilogue reads them once per CTA instead of per element.
   if (lora_b != nullptr && lora_rank == 16 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0) {
     const int64_t bytes = (int64_t)num_tokens * a.num_slices * 16 * 4 + (((int64_t)num_tokens * 4 + 15) & ~int64_t(15));
     if (bytes <= kLoraStageMax) g.lora_stage = static_cast<int32_t>(bytes);
+    // and the last tile's finished LoRA terms, when they fit beside the ring
     const int32_t delta = num_tokens * pl::kGemmM * 2;
-    if (g.lora_stage &&
-        pl::gemm_smem_bytes(sh.stages * sh.stage_bytes, g.lora_stage, delta, sh.stages) <= gemm_smem_optin())
+    if (g.lora_stage && pl::gemm_smem_bytes(sh.stage_bytes, sh.stages, g.lora_stage, delta) <= kGemmSmemMax)
       g.lora_delta = delta;
   }
 
   switch (sh.n) {
-    case 16: return launch_gemm_n<16>(sh.kcs, wm, xm, g, sh.ctas, stream);
-    case 32: return launch_gemm_n<32>(sh.kcs, wm, xm, g, sh.ctas, stream);
-    case 64: return launch_gemm_n<64>(sh.kcs, wm, xm, g, sh.ctas, stream);
-    default: return launch_gemm_n<128>(sh.kcs, wm, xm, g, sh.ctas, stream);
+    case 16: return launch_gemm_n<16>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
+    case 32: return launch_gemm_n<32>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
+    case 64: return launch_gemm_n<64>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
+    default: return launch_gemm_n<128>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);
   }
 }
 

@@ -419,8 +419,7 @@ def gemv_fits(rows: int, k_in: int) -> bool:
 
 
 def gemm_plan(num_tokens: int, k_in: int, n_out: int, num_ctas: int = 0) -> _capi.GemmPlan:
-    """Work split of :func:`linear_lora_gemm`: its grid of row bands (``num_ctas``
-    0: at most one CTA per SM); ``workspace_bytes`` is 0."""
+    """Work split of :func:`linear_lora_gemm` (``num_ctas`` 0: one CTA per SM)."""
 
     plan = _capi.GemmPlan()
     call("pl_linear_gemm_plan", int(num_tokens), int(k_in), int(n_out), int(num_ctas), _capi.ctypes.byref(plan))
@@ -447,8 +446,9 @@ def linear_lora_gemm(
     """y = x . W^T (+bias) (+ per-token LoRA expand) (+ residual) for 1..128
     tokens on the tcgen05 tensor cores.  ``x`` [T, K] is used as given (apply
     :func:`rmsnorm` / :func:`silu_mul` first); the epilogue arguments are those
-    of :func:`linear_lora_fused`.  ``workspace`` is accepted for older callers
-    and unused (each CTA owns a band of output rows: nothing is merged)."""
+    of :func:`linear_lora_fused`.  ``workspace`` (uint8, zeroed once) is sized
+    by :func:`gemm_plan` for the same ``num_ctas``; one is allocated when
+    omitted."""
 
     _need_cuda(x, weight)
     _need(x, torch.bfloat16, "x")
@@ -459,6 +459,9 @@ def linear_lora_gemm(
     n, k = weight.shape
     if out is None:
         out = torch.empty(t, n, dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        need = int(gemm_plan(t, k, n, num_ctas).workspace_bytes)
+        workspace = torch.zeros(need, dtype=torch.uint8, device=x.device)
     rank = 0
     num_slices = 1
     slice_ptr, slice_keepalive = None, None
@@ -474,8 +477,7 @@ def linear_lora_gemm(
          ptr(lora_down), 0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
          float(lora_scale), slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
          0 if residual is None else _row_stride(residual, "residual"), ptr(out), _row_stride(out, "out"),
-         int(num_ctas), ptr(workspace), 0 if workspace is None else int(workspace.numel()), int(flags), ptr(status),
-         stream_handle())
+         int(num_ctas), ptr(workspace), int(workspace.numel()), int(flags), ptr(status), stream_handle())
     del slice_keepalive
     return out
 

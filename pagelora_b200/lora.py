@@ -18,7 +18,8 @@ into its epilogue, after the segment shrink x.A^T:
   * T <= 8 whose activations fit in shared memory: the decode GEMV
     (pl_linear_lora_expand_fused);
   * otherwise T <= 128 (batched decode, branch batches, prefill chunks): the
-    tcgen05 GEMM (pl_linear_lora_gemm).
+    tcgen05 GEMM (pl_linear_lora_gemm), with one zeroed workspace per device
+    that every call leaves zeroed again.
 LoRALinear scales the rounded B product (linear.py:230-231) while the packed
 paths fold the scale into B (packed_ops.py:371-373); the kernels reproduce
 both roundings.  Merged ("effective") weights are built by the on-device
@@ -73,6 +74,20 @@ def _tensor_key(t: torch.Tensor) -> tuple:
     return (t.data_ptr(), tuple(t.shape), t.dtype, t.device, int(getattr(t, "_version", 0)))
 
 
+_gemm_ws: dict[torch.device, torch.Tensor] = {}
+
+
+def _gemm_workspace(device: torch.device, tokens: int, k_in: int, n_out: int) -> torch.Tensor:
+    """The device's shared GEMM workspace (zeroed once; each completed call leaves it zeroed)."""
+
+    need = int(K.gemm_plan(tokens, k_in, n_out).workspace_bytes)
+    ws = _gemm_ws.get(device)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 16), dtype=torch.uint8, device=device)
+        _gemm_ws[device] = ws
+    return ws
+
+
 def _kernel_kind(x2: torch.Tensor, k_in: int) -> str | None:
     """Which kernel projects the rows of ``x2`` [T, K]: "gemv", "gemm" or None (torch)."""
 
@@ -91,7 +106,8 @@ def _project(kind: str, x2: torch.Tensor, w: torch.Tensor, **epilogue) -> torch.
 
     if kind == "gemv":
         return K.linear_lora_fused(x2, w, **epilogue)
-    return K.linear_lora_gemm(x2, w, **epilogue)
+    ws = _gemm_workspace(x2.device, x2.shape[0], w.shape[1], w.shape[0])
+    return K.linear_lora_gemm(x2, w, workspace=ws, **epilogue)
 
 
 @dataclass

@@ -645,9 +645,9 @@ def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
 @pytest.mark.parametrize("t", [1, 9, 16, 33, 64, 100, 128])
 def test_linear_lora_gemm_vs_oracle(K, t, k_in):
     """tcgen05 multi-token linear: multi-adapter LoRA epilogue, partial row
-    bands, K tails (600: a partial 64-column chunk; 640: the last K block
-    half empty), grids of 1 CTA (one band of six 120-row segments), one per
-    SM (8-row bands) and 7 CTAs (100-row bands)."""
+    tile, K tails (600: 2-D tiles with a partial 64-column chunk; 640: 3-D
+    tiles, last K block half empty), grids of 1 CTA (whole tiles), one per
+    SM and 7 CTAs (tiles shared between CTAs, partials merged in order)."""
 
     rng = np.random.default_rng(300 + t + k_in)
     n, r, n_ad = 700, 16, 3
@@ -684,15 +684,16 @@ def test_linear_lora_gemm_llama2_shapes(K):
         ref = x.double() @ w.double().T
         tol = torch.abs(ref) * 2.0 ** -8 + 1e-3
         assert bool(torch.all(torch.abs(y.double() - ref) <= tol)), (n, k)
-        y2 = K.linear_lora_gemm(x, w, weights_static=True)  # deterministic
+        y2 = K.linear_lora_gemm(x, w, weights_static=True)  # counters were left at zero
         assert torch.equal(y, y2)
 
 
 @pytest.mark.parametrize("t", [16, 64])
 def test_linear_lora_gemm_qwen3_shapes_and_bands(K, t):
-    """Qwen3-8B projections (q/k/v 6144, gate_up 24576, lm_head 151936 rows:
-    bands of one, two and nine segments per CTA) with rank-16 LoRA on 4
-    adapters and a residual, against an fp64 reference on the GPU."""
+    """Qwen3-8B projections (q/k/v 6144, gate_up 24576 and lm_head 151936
+    rows: tiles shared by several CTAs, and CTAs with many whole tiles) with
+    rank-16 LoRA on 4 adapters and a residual, against an fp64 reference on
+    the GPU."""
 
     g = torch.Generator(device="cuda").manual_seed(2)
     for n, k, lora in ((6144, 4096, True), (24576, 4096, False), (151936, 4096, True)):
