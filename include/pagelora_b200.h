@@ -164,6 +164,19 @@ int32_t pl_paged_decode(const void *q, int64_t q_stride_b, int64_t q_stride_h,
                         int32_t *status_dev, void *stream);
 
 /*
+ * RoPE table of one decode step: cos_sin[r][i] = (cos, sin) of
+ * positions[r] * theta^(-2i / head_dim), i < head_dim / 2, fp32 (the
+ * non-interleaved rotation of model/flashinfer/projection.py:155-190, as
+ * FlashInfer's apply_rope_pos_ids computes it).  The positions are those of
+ * every layer of the step, so one launch serves them all
+ * (pl_paged_decode_qkv's rope_cos_sin).  head_dim % 32 == 0; cos_sin
+ * 16-byte aligned.
+ */
+int32_t pl_rope_cos_sin(const int32_t *positions, int32_t rows,
+                        int32_t head_dim, float rope_theta, float *cos_sin,
+                        void *stream);
+
+/*
  * One decoder layer's attention from the packed q/k/v projection row:
  * per-head LoRA-B expand, Qwen3 q/k RMSNorm (HF rounding), RoPE, the paged
  * append of the new token's K/V and the paged decode, in one launch.
@@ -171,6 +184,10 @@ int32_t pl_paged_decode(const void *q, int64_t q_stride_b, int64_t q_stride_h,
  * norms, RoPE via model/flashinfer/projection.py:34-190), :399-412
  * (_append_decode_kv_static) and attention_backend.py:120-131 (run_decode).
  *   qkv .. rope_theta  as pl_qkv_rope_append (rows = batch rows)
+ *   rope_cos_sin       nullable: the step's RoPE table from pl_rope_cos_sin
+ *                      ([batch][head_dim / 2] (cos, sin) fp32, 16-byte
+ *                      aligned); without it every launch evaluates the
+ *                      angles itself (the same values)
  *   slot_page/offset   where row b's new token goes; it must be the last
  *                      slot of the row's last page in the page table
  *                      (pl_page_table_advance writes both); a row whose slot
@@ -187,7 +204,8 @@ int32_t pl_paged_decode_qkv(const void *qkv, int64_t qkv_stride,
                             float lora_scale, const int32_t *tok_adapter,
                             const void *q_norm_w, const void *k_norm_w,
                             float norm_eps, const int32_t *positions,
-                            float rope_theta, const int32_t *slot_page,
+                            float rope_theta, const float *rope_cos_sin,
+                            const int32_t *slot_page,
                             const int32_t *slot_offset, void *q_out,
                             void *kv_cache, int64_t num_pages,
                             const int32_t *indptr, const int32_t *indices,

@@ -83,9 +83,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "pl_paged_decode_qkv": (
         _I32,
-        [_P, _I64, _P, _I64, _P, _I32, _F, _P, _P, _P, _F, _P, _F, _P, _P, _P, _P, _I64, _P, _P, _P, _I32, _I32,
-         _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _I32, _P, _I64, _P, _P],
+        [_P, _I64, _P, _I64, _P, _I32, _F, _P, _P, _P, _F, _P, _F, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _I32,
+         _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _I32, _P, _I64, _P, _P],
     ),
+    "pl_rope_cos_sin": (_I32, [_P, _I32, _I32, _F, _P, _P]),
     "pl_paged_decode_shared": (
         _I32,
         [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P,

@@ -172,6 +172,7 @@ class BatchDecodeEngine:
             if not uses_gemv(B, k):
                 ws = max(ws, int(K.gemm_plan(B, k, n).workspace_bytes))
         self.gemm_ws = torch.zeros(ws, device=dev, dtype=torch.uint8)
+        self.rope_cs = torch.zeros(B, spec.head_dim // 2, 2, device=dev, dtype=torch.float32)
         self.num_splits = 1
         self.workspace = torch.zeros(1 << 20, device=dev, dtype=torch.uint8)
         if self.world > 1:
@@ -488,6 +489,8 @@ class BatchDecodeEngine:
                 K.page_table_advance(self.row_num_pages, self.last_page_len, self.row_pages, self.new_page_ids,
                                      self.page_size, self.indptr, self.indices, self.slot_page, self.slot_off,
                                      None, st)
+        # the step's RoPE angles, read by every layer's attention launch
+        K.rope_cos_sin(self.positions, s.head_dim, s.rope_theta, out=self.rope_cs)
         K.embed(self.token_buf, self.embed, self.x, st)
         attn2d = self.attn.view(self.rows, s.q_dim)
         lora = self.lora_rank > 0
@@ -509,7 +512,8 @@ class BatchDecodeEngine:
                             num_splits=self.num_splits, workspace=self.workspace,
                             lora_down=self.down_qkv if lora else None, lora_b=L["b_qkv"] if lora else None,
                             lora_scale=self.qkv_lora_scale, tok_adapter=self.tok_adapter if lora else None,
-                            q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps, status=st)
+                            q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps, status=st,
+                            rope_cos_sin=self.rope_cs)
             if self.cascade is not None:
                 # shared prefix: append + rotate, then prefix pass + suffix pass + merge
                 K.qkv_rope_append(self.qkv, num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads,
@@ -518,7 +522,7 @@ class BatchDecodeEngine:
                                   q_out=self.q, lora_down=qkv_args["lora_down"], lora_b=qkv_args["lora_b"],
                                   lora_scale=self.qkv_lora_scale, tok_adapter=qkv_args["tok_adapter"],
                                   q_norm_weight=L["q_norm"], k_norm_weight=L["k_norm"], norm_eps=s.rms_eps,
-                                  status=st)
+                                  status=st)  # (no table argument: evaluates its angles)
                 self.cascade.run(self.q, self.kv[li], self.indptr, self.indices, self.last_page_len, self.attn, st)
             elif self.world == 1:
                 K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len,
@@ -574,7 +578,7 @@ class BatchDecodeEngine:
         per_layer += 1 if uses_gemv(B, s.intermediate) else 2  # (SiLU-mul +) down
         head = 1 if uses_gemv(B, s.hidden) else 2  # (norm +) lm_head
         advance = 1 if (self.world == 1 or self.owner) else 0
-        return advance + 1 + per_layer * s.num_layers + head + 1
+        return advance + 2 + per_layer * s.num_layers + head + 1  # + RoPE table, embed; argmax
 
     def capture(self) -> None:
         """Capture one decode step into a CUDA graph (after an eager warm-up

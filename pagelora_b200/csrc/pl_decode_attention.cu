@@ -2,16 +2,24 @@
 //
 // One CTA per (row, kv head, kv split).  All `group` query heads that share
 // the kv head sit in one CTA, so each KV page is read from HBM exactly once.
-// Warp 0 is the producer: one lane walks the page table and issues TMA tile
-// loads (one 64-dim x page_size box per half head, 128B-swizzled) into a
-// ring of shared-memory stages, each guarded by a full/empty mbarrier pair.
-// Warps 1..4 are consumers: each takes whole pages round-robin and runs
+// Warp 0 is the producer: one lane per (page, K/V, 64-dim half) box issues
+// TMA tile loads (128B-swizzled) for 8 pages per instruction into a ring of
+// shared-memory stages, each guarded by a full/empty mbarrier pair, with the
+// page ids read one batch ahead.  Warps 1..kConsumerWarps are consumers:
+// stage s always belongs to consumer warp s % kConsumerWarps, which takes its
+// pages in order (one waiter per full barrier, never a phase ahead), and runs
 // Q.K^T and P.V on the tensor cores (mma.sync m16n8k16, fp32 accumulate;
 // query heads are the M rows, only `group` of 16 used) with an online
-// softmax in the log2 domain.  The four per-warp states are merged through
-// shared memory; with several splits the partial states go to the
-// workspace and the last CTA of each (row, kv head) to arrive merges them,
-// so split-KV needs no second launch.
+// softmax in the log2 domain.  The consumer warps' states are combined
+// through shared memory.  With several splits, the splits of a (row, kv
+// head) form one thread-block cluster when the plan says so: every CTA
+// pushes its (O, LSE) chunks into the reducing CTA's shared memory over
+// DSMEM and each CTA reduces its own chunks after one cluster barrier;
+// otherwise the partial states go to the workspace and the last CTA to
+// arrive (atomic ticket, no spin) merges them.  Either way split-KV needs no
+// second launch.  The fused form (pl_paged_decode_qkv) computes the rotated
+// q heads from the packed projection row, and appends the new token's K/V,
+// inside the same launch (pl_qkv_head.cuh).
 //
 // Semantics follow model/flashinfer/attention_backend.py:97,120-131:
 // O = softmax((q/16) . K^T * 16/sqrt(D)) . V = softmax(q.K^T * sm_scale) . V
@@ -24,8 +32,12 @@
 
 namespace pl {
 
-constexpr int kConsumerWarps = 6;
-constexpr int kDecodeThreads = 32 * (1 + kConsumerWarps);
+// Consumer warps: 7 when a split's pages fit the ring in one lap (several
+// splits of a short context: two pages at most per warp), 6 for long splits
+// (where the 16-stage ring's ownership is as even at 6 and the extra warp
+// measured slower).
+template <int NCW>
+constexpr int decode_threads() { return 32 * (1 + NCW); }
 
 struct DecodeArgs {
   const bf16* q;
@@ -62,8 +74,9 @@ struct DecodeArgs {
   int32_t* status;
 };
 
-template <int D, int PS>
+template <int D, int PS, int NCW>
 struct DecodeCfg {
+  static constexpr int kConsumerWarps = NCW;
   static constexpr int kHalves = D / 64;              // 64-dim (128 B) boxes per tile
   static constexpr int kHalfBytes = PS * 128;         // one box: PS rows x 128 B
   static constexpr int kTileBytes = kHalves * kHalfBytes;  // K (or V) of one page/head
@@ -99,10 +112,12 @@ struct DecodeCfg {
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128B-swizzled box.
 __device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-template <int D, int PS>
-__global__ void __launch_bounds__(kDecodeThreads) paged_decode_kernel(const __grid_constant__ CUtensorMap kv_map,
-                                                                       const DecodeArgs args) {
-  using C = DecodeCfg<D, PS>;
+template <int D, int PS, int NCW>
+__global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                                              const DecodeArgs args) {
+  using C = DecodeCfg<D, PS, NCW>;
+  constexpr int kConsumerWarps = NCW;
+  constexpr int kDecodeThreads = decode_threads<NCW>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
@@ -765,16 +780,27 @@ int64_t decode_workspace_bytes(int batch, int hq, int hkv, int d, int splits) {
          align256((int64_t)batch * hq * splits * 4);
 }
 
-template <int D, int PS>
-int32_t launch_decode(const CUtensorMap& map, const pl::DecodeArgs& a, int batch, int hkv, int splits, void* stream) {
-  using C = pl::DecodeCfg<D, PS>;
-  auto kern = pl::paged_decode_kernel<D, PS>;
+// Consumer warps of a launch with `splits` splits (see decode_threads).
+constexpr int consumer_warps_for(int splits) { return splits >= 3 ? 7 : 6; }
+
+template <int D, int PS, int NCW>
+int32_t launch_decode_ncw(const CUtensorMap& map, const pl::DecodeArgs& a, int batch, int hkv, int splits,
+                          void* stream) {
+  using C = pl::DecodeCfg<D, PS, NCW>;
+  auto kern = pl::paged_decode_kernel<D, PS, NCW>;
+  constexpr int threads = pl::decode_threads<NCW>();
   int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (st != PL_OK) return st;
   if (a.cluster)
-    return pl_host::launch_pdl_cluster(kern, dim3(splits, hkv, batch), dim3(pl::kDecodeThreads), C::kSmemBytes,
-                                       stream, splits, map, a);
-  return pl_host::launch_pdl(kern, dim3(splits, hkv, batch), dim3(pl::kDecodeThreads), C::kSmemBytes, stream, map, a);
+    return pl_host::launch_pdl_cluster(kern, dim3(splits, hkv, batch), dim3(threads), C::kSmemBytes, stream, splits,
+                                       map, a);
+  return pl_host::launch_pdl(kern, dim3(splits, hkv, batch), dim3(threads), C::kSmemBytes, stream, map, a);
+}
+
+template <int D, int PS>
+int32_t launch_decode(const CUtensorMap& map, const pl::DecodeArgs& a, int batch, int hkv, int splits, void* stream) {
+  if (consumer_warps_for(splits) == 7) return launch_decode_ncw<D, PS, 7>(map, a, batch, hkv, splits, stream);
+  return launch_decode_ncw<D, PS, 6>(map, a, batch, hkv, splits, stream);
 }
 
 // Split merge through a thread-block cluster (the splits of one (row, kv
@@ -790,10 +816,10 @@ struct ClusterFit {
 std::mutex g_fit_mu;
 std::vector<ClusterFit> g_fits;
 
-template <int D, int PS>
-int cluster_capacity(int splits) {
-  using C = pl::DecodeCfg<D, PS>;
-  auto kern = pl::paged_decode_kernel<D, PS>;
+template <int D, int PS, int NCW>
+int cluster_capacity_ncw(int splits) {
+  using C = pl::DecodeCfg<D, PS, NCW>;
+  auto kern = pl::paged_decode_kernel<D, PS, NCW>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   {
@@ -807,7 +833,7 @@ int cluster_capacity(int splits) {
        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(splits, 1, 1);
-    cfg.blockDim = dim3(pl::kDecodeThreads);
+    cfg.blockDim = dim3(pl::decode_threads<NCW>());
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -822,6 +848,12 @@ int cluster_capacity(int splits) {
   std::lock_guard<std::mutex> lock(g_fit_mu);
   g_fits.push_back({reinterpret_cast<const void*>(kern), dev, splits, active});
   return active;
+}
+
+template <int D, int PS>
+int cluster_capacity(int splits) {
+  if (consumer_warps_for(splits) == 7) return cluster_capacity_ncw<D, PS, 7>(splits);
+  return cluster_capacity_ncw<D, PS, 6>(splits);
 }
 
 int cluster_capacity_for(int head_dim, int page_size, int splits) {
@@ -1011,7 +1043,8 @@ extern "C" int32_t pl_paged_decode_qkv(const void* qkv, int64_t qkv_stride, cons
                                        int64_t down_stride, const void* lora_b, int32_t lora_rank, float lora_scale,
                                        const int32_t* tok_adapter, const void* q_norm_w, const void* k_norm_w,
                                        float norm_eps, const int32_t* positions, float rope_theta,
-                                       const int32_t* slot_page, const int32_t* slot_offset, void* q_out,
+                                       const float* rope_cos_sin, const int32_t* slot_page,
+                                       const int32_t* slot_offset, void* q_out,
                                        void* kv_cache, int64_t num_pages, const int32_t* indptr,
                                        const int32_t* indices, const int32_t* last_page_len, int32_t batch,
                                        int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
@@ -1032,6 +1065,9 @@ extern "C" int32_t pl_paged_decode_qkv(const void* qkv, int64_t qkv_stride, cons
   h.eps = norm_eps;
   h.positions = positions;
   h.theta = rope_theta;
+  h.rope_cs = rope_cos_sin;
+  if (rope_cos_sin != nullptr && ((reinterpret_cast<uintptr_t>(rope_cos_sin) & 15) || head_dim % 32))
+    return PL_ERR_UNSUPPORTED;
   h.Hq = num_qo_heads;
   h.Hkv = num_kv_heads;
   return paged_decode_impl(nullptr, 0, 0, kv_cache, num_pages, indptr, indices, last_page_len, batch, num_qo_heads,

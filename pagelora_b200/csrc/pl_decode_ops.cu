@@ -518,6 +518,23 @@ __global__ void __launch_bounds__(256) rmsnorm_hf_kernel(const bf16* __restrict_
   }
 }
 
+// (cos, sin) of every RoPE angle of every row's position: [rows][D/2][2]
+// fp32.  Positions are the same for all layers of a decode step, so the
+// step's launches read this table instead of evaluating powf / sincosf per
+// layer (the same rope_angle_cs, hence the same values).
+__global__ void rope_cos_sin_kernel(const int32_t* __restrict__ positions, int half, int D, float theta,
+                                    float* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int row = blockIdx.x;
+  const float pos = (float)positions[row];
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float cs, sn;
+    rope_angle_cs(pos, i, D, theta, cs, sn);
+    *reinterpret_cast<float2*>(out + ((int64_t)row * half + i) * 2) = make_float2(cs, sn);
+  }
+}
+
 }  // namespace pl
 
 // =================================================================== host
@@ -605,6 +622,7 @@ extern "C" int32_t pl_qkv_rope_append(const void* qkv, int64_t qkv_stride, const
   a.eps = norm_eps;
   a.positions = positions;
   a.theta = rope_theta;
+  a.rope_cs = nullptr;
   a.Hq = num_qo_heads;
   a.Hkv = num_kv_heads;
   const int warps = num_tokens * (num_qo_heads + 2 * num_kv_heads);
@@ -665,4 +683,15 @@ extern "C" int32_t pl_rmsnorm_hf(const void* x, int64_t x_stride, int32_t num_ro
   return pl_host::launch_pdl(pl::rmsnorm_hf_kernel, dim3((num_rows + 7) / 8), dim3(256), 0, stream,
                              static_cast<const pl::bf16*>(x), x_stride, (int)num_rows, (int)k_in,
                              static_cast<const pl::bf16*>(w), eps, static_cast<pl::bf16*>(y), y_stride);
+}
+
+extern "C" int32_t pl_rope_cos_sin(const int32_t* positions, int32_t rows, int32_t head_dim, float rope_theta,
+                                   float* cos_sin, void* stream) {
+  if (rows == 0) return PL_OK;
+  if (positions == nullptr || cos_sin == nullptr || rows < 0 || head_dim <= 0 || head_dim % 32 != 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(cos_sin) & 15) return PL_ERR_UNSUPPORTED;
+  const int half = head_dim / 2;
+  return pl_host::launch_pdl(pl::rope_cos_sin_kernel, dim3(rows), dim3(half < 1024 ? half : 1024), 0, stream,
+                             positions, half, (int)head_dim, rope_theta, cos_sin);
 }

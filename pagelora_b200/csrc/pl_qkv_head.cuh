@@ -25,8 +25,18 @@ struct QkvHeadArgs {
   float eps;
   const int32_t* positions; // [T]
   float theta;
+  const float* rope_cs;     // nullable: [T][D/2] (cos, sin) pairs of pl_rope_cos_sin; else computed here
   int32_t Hq, Hkv;
 };
+
+// cos and sin of RoPE angle i (0 <= i < D/2) at position pos, in fp32
+// (non-interleaved rotation of projection.py:155-190).  The one definition
+// used both by the per-step table kernel and by the inline path, so the two
+// give identical values.
+__device__ __forceinline__ void rope_angle_cs(float pos, int i, int D, float theta, float& cs, float& sn) {
+  const float inv_freq = 1.0f / powf(theta, (float)(2 * i) / (float)D);
+  sincosf(pos * inv_freq, &sn, &cs);
+}
 
 __device__ __forceinline__ void prefetch_l2_line(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
@@ -70,7 +80,7 @@ __device__ __forceinline__ void qkv_head_transform(const QkvHeadArgs& a, int t, 
 #pragma unroll
     for (int e = 0; e < E; ++e) v[e] = bf2f(src[e]);
   }
-  const float pos = kind < 2 ? (float)a.positions[t] : 0.f;
+  const float pos = (kind < 2 && a.rope_cs == nullptr) ? (float)a.positions[t] : 0.f;
   const int ad = (lora && a.tok_adapter != nullptr) ? a.tok_adapter[t] : 0;
   float wn[E];
 #pragma unroll
@@ -141,13 +151,19 @@ __device__ __forceinline__ void qkv_head_transform(const QkvHeadArgs& a, int t, 
       PL_TRACE_POINT(15);
     }
     float out[E];
+    float csn[2 * E];  // (cos, sin) of the E rotation angles of this lane
+    if (a.rope_cs != nullptr) {
+      const float* src = a.rope_cs + ((int64_t)t * (D / 2) + d0 % (D / 2)) * 2;
+#pragma unroll
+      for (int e = 0; e < 2 * E; e += 4) *reinterpret_cast<float4*>(csn + e) = *reinterpret_cast<const float4*>(src + e);
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) rope_angle_cs(pos, (d0 + e) % (D / 2), D, a.theta, csn[2 * e], csn[2 * e + 1]);
+    }
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
-      const int i = (d0 + e) % (D / 2);
-      const float inv_freq = 1.0f / powf(a.theta, (float)(2 * i) / (float)D);
-      float sn, cs;
-      sincosf(pos * inv_freq, &sn, &cs);
+      const float cs = csn[2 * e], sn = csn[2 * e + 1];
       out[e] = lane < 16 ? v[e] * cs - partner * sn : v[e] * cs + partner * sn;
     }
 #pragma unroll

@@ -171,6 +171,7 @@ class DecodeEngine:
         self.gate_up = torch.zeros(1, 2 * spec.intermediate, device=dev, dtype=bf)
         self.logits = torch.zeros(1, spec.vocab, device=dev, dtype=bf)
         self.argmax_ws = torch.zeros(K.argmax_workspace_bytes(1), device=dev, dtype=torch.uint8)
+        self.rope_cs = torch.zeros(1, D // 2, 2, device=dev, dtype=torch.float32)
         self.num_splits = 1
         self.workspace = torch.zeros(1 << 20, device=dev, dtype=torch.uint8)
         # Host mirror of the row state (decides when a new page is needed).
@@ -294,6 +295,8 @@ class DecodeEngine:
         K.page_table_advance(self.row_num_pages, self.last_page_len, self.row_pages, self.new_page_ids,
                              self.page_size, self.indptr, self.indices, self.slot_page, self.slot_off,
                              self.positions, st)
+        # the step's RoPE angles, read by every layer's attention launch
+        K.rope_cos_sin(self.positions, s.head_dim, s.rope_theta, out=self.rope_cs)
         K.embed(self.token_buf, self.embed, self.x, st)
         attn2d = self.attn.view(1, s.q_dim)
         for li, L in enumerate(self.layers):
@@ -308,7 +311,7 @@ class DecodeEngine:
                                num_splits=self.num_splits, workspace=self.workspace,
                                lora_down=self.down_qkv if L.b_qkv is not None else None, lora_b=L.b_qkv,
                                lora_scale=self.qkv_lora_scale, q_norm_weight=L.q_norm, k_norm_weight=L.k_norm,
-                               norm_eps=s.rms_eps, out=self.attn, status=st)
+                               norm_eps=s.rms_eps, out=self.attn, status=st, rope_cos_sin=self.rope_cs)
             if self.fold_o_shrink and L.a_o is not None:
                 # the o GEMV computes attn . A_o^T in its prologue: no shrink launch
                 K.linear_lora_fused(attn2d, L.w_o, lora_a=L.a_o, lora_b=L.b_o, lora_scale=self.lora_scale,
@@ -329,7 +332,7 @@ class DecodeEngine:
 
     def launches_per_step(self) -> int:
         per_layer = 5 + sum(1 for L in self.layers[:1] if L.a_o is not None and not self.fold_o_shrink)
-        return 2 + per_layer * len(self.layers) + 2
+        return 3 + per_layer * len(self.layers) + 2
 
     def capture(self) -> None:
         """Capture one decode step into a CUDA graph (after an eager warm-up

@@ -200,10 +200,13 @@ def paged_decode_qkv(
     q_out: torch.Tensor | None = None,
     status: torch.Tensor | None = None,
     sm_scale: float | None = None,
+    rope_cos_sin: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """q/k head norm + RoPE + paged append + paged decode in one launch, from
     the packed projection rows ``qkv`` [B, (Hq + 2 Hkv) * D] bf16; ``out`` is
-    [B, Hq, D] bf16, or fp32 for a split-KV partial."""
+    [B, Hq, D] bf16, or fp32 for a split-KV partial.  ``rope_cos_sin``: the
+    step's table from :func:`rope_cos_sin` (else the angles are evaluated in
+    the launch)."""
 
     _need_cuda(qkv, kv_cache, indptr, indices, last_page_len, positions, slot_page, slot_offset)
     _need(qkv, torch.bfloat16, "qkv")
@@ -227,10 +230,24 @@ def paged_decode_qkv(
     call("pl_paged_decode_qkv", ptr(qkv), _row_stride(qkv, "qkv"), ptr(lora_down),
          0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank), float(lora_scale),
          ptr(tok_adapter), ptr(q_norm_weight), ptr(k_norm_weight), float(norm_eps), ptr(positions),
-         float(rope_theta), ptr(slot_page), ptr(slot_offset), ptr(q_out), ptr(kv_cache), int(num_pages), ptr(indptr),
+         float(rope_theta), ptr(rope_cos_sin), ptr(slot_page), ptr(slot_offset), ptr(q_out), ptr(kv_cache),
+         int(num_pages), ptr(indptr),
          ptr(indices), ptr(last_page_len), int(batch), int(num_qo_heads), int(num_kv_heads), int(d),
          int(page_size), scale, int(num_splits), ptr(out), out.stride(0), out.stride(1), ptr(out_lse), int(flags),
          ptr(workspace), int(ws_bytes), ptr(status), stream_handle())
+    return out
+
+
+def rope_cos_sin(positions: torch.Tensor, head_dim: int, rope_theta: float,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """(cos, sin) of every RoPE angle of each row's position: [rows, D/2, 2] fp32."""
+
+    _need_cuda(positions)
+    _need(positions, torch.int32, "positions")
+    rows = positions.numel()
+    if out is None:
+        out = torch.empty(rows, head_dim // 2, 2, dtype=torch.float32, device=positions.device)
+    call("pl_rope_cos_sin", ptr(positions), int(rows), int(head_dim), float(rope_theta), ptr(out), stream_handle())
     return out
 
 

@@ -274,8 +274,18 @@ def test_paged_decode_qkv_matches_rope_then_decode(K, d, hq, hkv, qk_norm):
         o_f = K.paged_decode_qkv(qkv, c_f, dev_ip, dev_idx, dev_last, num_qo_heads=hq, num_kv_heads=hkv,
                                  positions=pos, rope_theta=1e6, slot_page=sp, slot_offset=so, num_splits=splits,
                                  workspace=ws, out_lse=lse_f, q_out=q_f, status=status, **common)
+        # the same launch reading the step's RoPE table instead of evaluating the angles
+        c_t = cache.clone()
+        q_t = torch.zeros_like(q_f)
+        lse_t = torch.empty_like(lse_f)
+        o_t = K.paged_decode_qkv(qkv, c_t, dev_ip, dev_idx, dev_last, num_qo_heads=hq, num_kv_heads=hkv,
+                                 positions=pos, rope_theta=1e6, slot_page=sp, slot_offset=so, num_splits=splits,
+                                 workspace=ws, out_lse=lse_t, q_out=q_t, status=status,
+                                 rope_cos_sin=K.rope_cos_sin(pos, d, 1e6), **common)
         torch.cuda.synchronize()
         assert int(status.item()) == 0
+        assert torch.equal(q_t, q_f) and torch.equal(o_t, o_f) and torch.equal(c_t, c_f)
+        assert torch.equal(lse_t, lse_f)
         assert torch.equal(q_f, q_ref)
         # appended K/V: identical where the row owns its slot; row 2's slot page untouched by the fused call
         for i in (0, 1, 3):
