@@ -224,7 +224,7 @@ def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
     ctx_tokens = (len(engine.host_pages) - 1) * engine.page_size + engine.host_last + 1
     attn_bytes = ctx_tokens * s.num_kv_heads * s.head_dim * 2 * bf + 2 * s.q_dim * bf
     names = ("linear_lora_fused", "paged_decode", "paged_decode_qkv", "lora_shrink_seg", "qkv_rope_append",
-             "page_table_advance", "embed", "argmax")
+             "page_table_advance", "rope_cos_sin", "embed", "argmax")
     orig = {n: getattr(K, n) for n in names}
 
     def gemv_bytes(x, weight, kw):
@@ -259,6 +259,8 @@ def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
             "qkv_rope_append", qkv.numel() * bf + s.q_dim * bf + 2 * s.kv_dim * bf
             + (kw["lora_b"].numel() * bf if kw.get("lora_b") is not None else 0), orig["qkv_rope_append"], qkv, **kw),
         "page_table_advance": lambda *a, **kw: timed("page_table_advance", 64, orig["page_table_advance"], *a, **kw),
+        "rope_cos_sin": lambda pos, d, *a, **kw: timed("rope_cos_sin", pos.numel() * (4 + d * 4),
+                                                       orig["rope_cos_sin"], pos, d, *a, **kw),
         "embed": lambda *a, **kw: timed("embed", 2 * s.hidden * bf, orig["embed"], *a, **kw),
         "argmax": lambda *a, **kw: timed("argmax", s.vocab * bf, orig["argmax"], *a, **kw),
     }

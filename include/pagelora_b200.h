@@ -503,6 +503,18 @@ int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t n_out,
                             int32_t num_ctas, pl_gemm_plan_t *plan);
 
 /*
+ * Whether pl_linear_lora_gemm with these sizes and a rank-16 LoRA (16-byte
+ * aligned B) computes the LoRA terms of a CTA's last tile ahead, while the
+ * weights stream (1), or expands them in the final merge (0); negative on
+ * invalid sizes.  CTAs owning fewer than half a tile of units expand in the
+ * merge either way.  No reference counterpart (a query of this library's
+ * plan, for tests and tuning).
+ */
+int32_t pl_linear_gemm_lora_precompute(int32_t num_tokens, int32_t k_in,
+                                       int32_t n_out, int32_t num_ctas,
+                                       int32_t lora_rank, int32_t num_slices);
+
+/*
  * Multi-token LoRA linear on the tcgen05 tensor cores (TMA-fed, accumulator
  * in tensor memory, persistent grid sharing 128-row x 256-column units
  * evenly over the SMs): the batched-decode / prefill-chunk counterpart of

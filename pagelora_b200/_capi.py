@@ -110,6 +110,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pl_linear_set_tuning": (_I32, [_I32, _I32, _I32, _I32, _I32]),
     "pl_linear_set_l2_prefetch": (_I32, [_I64]),
     "pl_linear_gemm_plan": (_I32, [_I32, _I32, _I32, _I32, POINTER(GemmPlan)]),
+    "pl_linear_gemm_lora_precompute": (_I32, [_I32, _I32, _I32, _I32, _I32, _I32]),
     "pl_linear_lora_gemm": (
         _I32,
         [_P, _I64, _I32, _I32, _P, _I32, _P, _P, _I64, _P, _I32, _F, _P, _I32, _P, _P, _I64, _P, _I64, _I32, _P,

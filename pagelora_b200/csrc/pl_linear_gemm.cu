@@ -604,7 +604,21 @@ int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
 constexpr int kGemmSmemBudget = 200 * 1024;
 constexpr int kLoraStageMax = 16 * 1024;
-constexpr int kGemmSmemMax = 227 * 1024;  // dynamic shared memory per CTA on sm_100
+// Dynamic shared memory a CTA may opt into on the current device (227 KB on
+// B200), read once per device.
+int gemm_smem_optin() {
+  static int limit[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 227 * 1024;
+  if (limit[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
+      v = 227 * 1024;
+    limit[dev] = v;
+  }
+  return limit[dev];
+}
+
 
 struct GemmShape {
   int n, kcs, stages, m_tiles, kblocks, units, ctas, max_slots, stage_bytes;
@@ -639,6 +653,19 @@ int64_t gemm_workspace_bytes(const GemmShape& s) {
   int64_t b = align256((int64_t)s.m_tiles * 4);
   if (s.max_slots > 1) b += (int64_t)s.m_tiles * s.max_slots * s.n * pl::kGemmM * 4;
   return b;
+}
+
+// Shared-memory bytes of the rank-16 LoRA staging (down rows + adapter ids)
+// and of the precomputed last-tile LoRA terms, 0 when a part is not used.
+void gemm_lora_smem(int tokens, int num_slices, int lora_rank, bool b_aligned, const GemmShape& sh, int32_t* stage,
+                    int32_t* delta) {
+  *stage = *delta = 0;
+  if (lora_rank != 16 || !b_aligned) return;
+  const int64_t bytes = (int64_t)tokens * num_slices * 16 * 4 + (((int64_t)tokens * 4 + 15) & ~int64_t(15));
+  if (bytes > kLoraStageMax) return;
+  *stage = static_cast<int32_t>(bytes);
+  const int32_t d = tokens * pl::kGemmM * 2;  // when it fits beside the ring
+  if (pl::gemm_smem_bytes(sh.stage_bytes, sh.stages, *stage, d) <= gemm_smem_optin()) *delta = d;
 }
 
 template <int N, int KCS>
@@ -685,6 +712,18 @@ extern "C" int32_t pl_linear_gemm_plan(int32_t num_tokens, int32_t k_in, int32_t
   plan->max_slots = s.max_slots;
   plan->workspace_bytes = gemm_workspace_bytes(s);
   return PL_OK;
+}
+
+extern "C" int32_t pl_linear_gemm_lora_precompute(int32_t num_tokens, int32_t k_in, int32_t n_out, int32_t num_ctas,
+                                                  int32_t lora_rank, int32_t num_slices) {
+  if (num_tokens < 1 || num_tokens > 128 || k_in <= 0 || n_out <= 0 || num_ctas < 0 || num_slices < 1 ||
+      num_slices > 4)
+    return PL_ERR_INVALID_ARGUMENT;
+  const GemmShape s = gemm_shape(num_tokens, k_in, n_out, num_ctas > 0 ? num_ctas : default_ctas(n_out),
+                                 k_in % pl::kGemmKC == 0);
+  int32_t stage = 0, delta = 0;
+  gemm_lora_smem(num_tokens, num_slices, lora_rank, true, s, &stage, &delta);
+  return delta > 0 ? 1 : 0;
 }
 
 extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
@@ -751,14 +790,9 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   g.partial = sh.max_slots > 1 ? reinterpret_cast<float*>(ws + align256((int64_t)sh.m_tiles * 4)) : nullptr;
   // Rank-16 LoRA: stage the (small) down rows and adapter ids in shared
   // memory so the epilogue reads them once per CTA instead of per element.
-  if (lora_b != nullptr && lora_rank == 16 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0) {
-    const int64_t bytes = (int64_t)num_tokens * a.num_slices * 16 * 4 + (((int64_t)num_tokens * 4 + 15) & ~int64_t(15));
-    if (bytes <= kLoraStageMax) g.lora_stage = static_cast<int32_t>(bytes);
-    // and the last tile's finished LoRA terms, when they fit beside the ring
-    const int32_t delta = num_tokens * pl::kGemmM * 2;
-    if (g.lora_stage && pl::gemm_smem_bytes(sh.stage_bytes, sh.stages, g.lora_stage, delta) <= kGemmSmemMax)
-      g.lora_delta = delta;
-  }
+  if (lora_b != nullptr)
+    gemm_lora_smem(num_tokens, a.num_slices, lora_rank, (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0, sh,
+                   &g.lora_stage, &g.lora_delta);
 
   switch (sh.n) {
     case 16: return launch_gemm_n<16>(sh.kcs, wm, xm, g, sh.ctas, sh.stages, stream);

@@ -669,6 +669,11 @@ def test_linear_lora_gemm_vs_oracle(K, t, k_in):
     bmat = bf16(rng.normal(size=(n_ad, n, r)) * 0.05)
     tok_ad = rng.integers(-1, n_ad, size=t)
     mag, want = _gemm_oracle(x, w, bias, down, bmat, tok_ad, 300, res, scale=2.0)
+    if t == 16:  # these shapes compute the last tile's LoRA terms ahead (that path is covered here)
+        from pagelora_b200._capi import load_library
+
+        lib = load_library()
+        assert all(lib.pl_linear_gemm_lora_precompute(t, k_in, n, c, r, 2) == 1 for c in (1, 7))
     outs = []
     for ctas in (1, 0, 7):
         y = K.linear_lora_gemm(_t(x), _t(w), bias=_t(bias), lora_down=_t(down, torch.float32), lora_b=_t(bmat),
