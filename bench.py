@@ -66,68 +66,135 @@ def _peaks() -> tuple[float, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region.
+
+    NVML (read-only queries: current SM clock, max SM clock, active clock-event
+    reasons) is polled every ``period_s`` from a thread, so that a timed region
+    of a few tens of milliseconds still holds many samples; nvidia-smi at its
+    100 ms minimum is the fallback when NVML is not importable. The GPU is found
+    by the CUDA device's UUID, so CUDA_VISIBLE_DEVICES remapping is honoured.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int) -> None:
-        self.gpu = gpu_index
+    def __init__(self, device, period_s: float = 0.005) -> None:
+        self.device = device
+        self.period = period_s
         self.proc = None
         self.lines: list[str] = []
+        self.samples: list[tuple[float, float, set]] = []   # (sm MHz, max MHz, reasons)
+        self.source = None
         self._thread = None
+        self._stop = threading.Event()
+        self._nvml = None
+        self._handle = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.device).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+            self._handle = self._nvml_handle()
+            self.source = f"nvml every {self.period * 1e3:.0f} ms"
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
+            return self
+        except Exception:
+            self._handle = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device.index or 0}",
+                                          f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi every 100 ms"
             self._thread = threading.Thread(target=self._read, daemon=True)
             self._thread.start()
         except Exception:
             self.proc = None
         return self
 
+    def _reasons_from_mask(self, mask: int) -> set:
+        n = self._nvml
+        bits = {"hw_slowdown": getattr(n, "nvmlClocksEventReasonHwSlowdown", 0x8),
+                "hw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+                "sw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+                "sw_power_cap": getattr(n, "nvmlClocksEventReasonSwPowerCap", 0x4)}
+        return {name for name, bit in bits.items() if mask & bit}
+
+    def _poll(self) -> None:
+        n, h = self._nvml, self._handle
+        try:
+            mx = float(n.nvmlDeviceGetMaxClockInfo(h, n.NVML_CLOCK_SM))
+        except Exception:
+            mx = 0.0
+        while not self._stop.is_set():
+            try:
+                sm = float(n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM))
+                mask = int(n.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((sm, mx, self._reasons_from_mask(mask)))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
     def wait_first(self, timeout: float = 3.0) -> None:
-        """Block until nvidia-smi has printed its first sample, so that the
-        samples fall inside the timed region that follows."""
+        """Block until the first sample is in, so that the samples fall inside
+        the timed region that follows."""
 
         t0 = time.monotonic()
-        while self.proc is not None and not self.lines and time.monotonic() - t0 < timeout:
-            time.sleep(0.01)
+        while (self._thread is not None and not self.samples and not self.lines
+               and time.monotonic() - t0 < timeout):
+            time.sleep(0.001)
 
     def _read(self) -> None:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self._stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-            if self._thread is not None:
-                self._thread.join(timeout=2)
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        if self._nvml is not None:
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], 0.0, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        samples = list(self.samples)
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
+                sm, mx = float(parts[1]), float(parts[2])
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
+            reasons = {name for name, val in zip(self.REASON_NAMES, parts[5:9])
+                       if val.lower() == "active"}
+            samples.append((sm, mx, reasons))
+        sm = [s[0] for s in samples]
+        mx = max((s[1] for s in samples), default=0.0)
+        reasons = set().union(*(s[2] for s in samples)) if samples else set()
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": self.source}
 
 
 def _dist():
@@ -691,7 +758,7 @@ def run_ours(args) -> None:
         engine.step_device()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index or 0) as clk:
+    with ClockSampler(device) as clk:
         clk.wait_first()
         e0.record(stream)
         for _ in range(steps):
