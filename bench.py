@@ -290,8 +290,8 @@ def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
 
     ctx_tokens = (len(engine.host_pages) - 1) * engine.page_size + engine.host_last + 1
     attn_bytes = ctx_tokens * s.num_kv_heads * s.head_dim * 2 * bf + 2 * s.q_dim * bf
-    names = ("linear_lora_fused", "paged_decode", "paged_decode_qkv", "lora_shrink_seg", "qkv_rope_append",
-             "page_table_advance", "rope_cos_sin", "embed", "argmax")
+    names = ("linear_lora_fused", "linear_lora_chain", "paged_decode", "paged_decode_qkv", "lora_shrink_seg",
+             "qkv_rope_append", "page_table_advance", "rope_cos_sin", "embed", "argmax")
     orig = {n: getattr(K, n) for n in names}
 
     def gemv_bytes(x, weight, kw):
@@ -313,6 +313,9 @@ def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
     wrap = {
         "linear_lora_fused": lambda x, w, **kw: timed("linear_lora_fused", gemv_bytes(x, w, kw),
                                                       orig["linear_lora_fused"], x, w, **kw),
+        "linear_lora_chain": lambda phases, **kw: timed("linear_lora_chain",
+                                                        sum(gemv_bytes(x, w, k) for x, w, k in phases),
+                                                        orig["linear_lora_chain"], phases, **kw),
         "paged_decode": lambda *a, **kw: timed("paged_decode", attn_bytes, orig["paged_decode"], *a, **kw),
         # fused: reads the packed qkv rows instead of q, writes the new K/V rows
         "paged_decode_qkv": lambda qkv, *a, **kw: timed(
@@ -366,30 +369,30 @@ def kernel_roofline(engine, peak_gbs: float, replays: int = 5) -> dict:
     return out
 
 
-def gemv_stream_roofline(engine, replays: int = 20) -> dict:
-    """The step's GEMV launches (linear_lora_fused) timed as they run in the
-    step: one decode step is captured with every other kernel left out, so
-    the graph holds only the GEMV launches with their programmatic overlap;
-    CUDA events around ``replays`` replays on the launching stream give the
-    average launch duration (weights 16 GB >> L2, so no flush is needed)."""
+def projection_stream_roofline(engine, kernel: str, replays: int = 20) -> dict:
+    """The step's projection launches of one kind (``kernel``: the chained
+    launches, linear_lora_chain, or the single ones, linear_lora_fused)
+    timed as they run in the step: one decode step is captured with every
+    other kernel left out, so the graph holds only those launches with their
+    programmatic overlap; CUDA events around ``replays`` replays on the
+    launching stream give the average launch duration (weights 16 GB >> L2,
+    so no flush is needed)."""
 
     import torch
 
     from pagelora_b200 import kernels as K
 
-    names = ("paged_decode", "paged_decode_qkv", "lora_shrink_seg", "qkv_rope_append", "page_table_advance",
-             "embed", "argmax")
+    names = ("linear_lora_fused", "linear_lora_chain", "paged_decode", "paged_decode_qkv", "lora_shrink_seg",
+             "qkv_rope_append", "page_table_advance", "rope_cos_sin", "embed", "argmax")
     orig = {n: getattr(K, n) for n in names}
     count = [0]
-    orig_lin = K.linear_lora_fused
 
-    def lin(*a, **kw):
+    def kept(*a, **kw):
         count[0] += 1
-        return orig_lin(*a, **kw)
+        return orig[kernel](*a, **kw)
 
     for n in names:
-        setattr(K, n, lambda *a, **kw: None)
-    K.linear_lora_fused = lin
+        setattr(K, n, kept if n == kernel else (lambda *a, **kw: None))
     try:
         stream = torch.cuda.Stream()
         stream.wait_stream(torch.cuda.current_stream())
@@ -399,7 +402,6 @@ def gemv_stream_roofline(engine, replays: int = 20) -> dict:
     finally:
         for n in names:
             setattr(K, n, orig[n])
-        K.linear_lora_fused = orig_lin
     launches = count[0]
     for _ in range(3):
         g.replay()
@@ -793,7 +795,8 @@ def run_ours(args) -> None:
     # ---- per-kernel roofline (eager pass with CUDA events around each launch)
     peak, peak_kind = _peaks()
     kern = kernel_roofline(engine, peak)
-    gstream = gemv_stream_roofline(engine)
+    dom_name = "linear_lora_chain" if "linear_lora_chain" in kern else "linear_lora_fused"
+    gstream = projection_stream_roofline(engine, dom_name)
 
     t = torch.tensor([ms, ms_e2e], device=device, dtype=torch.float64)
     if ws > 1:
@@ -883,7 +886,7 @@ def run_ours(args) -> None:
     if rank == 0:
         value = ws * steps / (ms * 1e-3)
         e2e = ws * steps / (ms_e2e * 1e-3)
-        dom = kern["linear_lora_fused"]
+        dom = kern[dom_name]
         stream_gbs = dom["bytes_per_launch"] / (gstream["us_per_launch"] * 1e-6) / 1e9
         if args.layers:
             raise SystemExit("--layers is for profiling runs only (use it with --profile)")
@@ -900,13 +903,13 @@ def run_ours(args) -> None:
                        "cuda_graph": True, "l2": "weights 16 GB > L2 126 MB; no flush"},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 8},
             "gpu_launches": launches * steps,
-            "roofline": {"bound": "hbm", "kernel": "linear_lora_fused", "achieved": stream_gbs,
+            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": stream_gbs,
                          "peak": peak, "unit": "GB/s", "frac": stream_gbs / peak, "peak_kind": peak_kind,
-                         "traffic": _ncu_traffic("linear_lora_fused"),
+                         "traffic": _ncu_traffic(dom_name),
                          "algorithmic_bytes_per_launch": dom["bytes_per_launch"],
                          "us_per_launch": gstream["us_per_launch"],
-                         "timing": (f"the step's {gstream['launches_per_replay']} GEMV launches replayed back to back "
-                                    f"(graph of those launches only, programmatic overlap on), "
+                         "timing": (f"the step's {gstream['launches_per_replay']} {dom_name} launches replayed back "
+                                    f"to back (graph of those launches only, programmatic overlap on), "
                                     f"{gstream['replays']} replays"),
                          "achieved_isolated": dom["achieved_gbs"],
                          "isolated_timing": "each launch alone between event nodes (no overlap)"},

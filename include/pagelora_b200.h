@@ -462,6 +462,66 @@ int32_t pl_linear_lora_expand_fused(
     int32_t *status_dev, void *stream);
 
 /*
+ * One projection of pl_linear_lora_chain: the arguments of
+ * pl_linear_lora_expand_fused, with the slice bounds held in the struct.
+ */
+typedef struct PlGemvPhase {
+  const void *x;
+  int64_t x_stride;
+  int32_t num_tokens, k_in, prologue;
+  const void *norm_w;
+  float norm_eps;
+  const void *w;
+  int32_t n_out;
+  const void *bias;
+  const float *lora_down;
+  int64_t down_stride;
+  const void *lora_b;
+  int32_t lora_rank;
+  float lora_scale;
+  int32_t slice_end[3];
+  int32_t num_slices;
+  const int32_t *tok_adapter;
+  const void *residual;
+  int64_t res_stride;
+  void *y;
+  int64_t y_stride;
+  const void *shrink_a;
+  int32_t n_shrink;
+  float *shrink_out;
+  int64_t shrink_stride;
+  int32_t flags;
+} PlGemvPhase;
+
+/*
+ * Consecutive projections of one decoder layer in ONE launch, each with the
+ * semantics and rounding of pl_linear_lora_expand_fused, e.g. o (LoRA
+ * expand + residual) -> gate_up (RMSNorm) -> down (SiLU-and-mul + residual)
+ * -> the next layer's packed q/k/v (RMSNorm + LoRA shrink rows): the
+ * o_proj / mlp / next qkv_proj sequence of
+ * model/flashinfer/layer_runner.py:338-396 for num_tokens <= 8.
+ * Phase p reads what phase p-1 wrote: the launch is persistent (one CTA
+ * per SM, all resident), the weights of every phase stream through one
+ * shared-memory ring without waiting for the activations, and the CTAs meet
+ * at a grid barrier between phases.
+ *   phases       host array of num_phases (1..6) projections, all with the
+ *                same num_tokens; read during the call
+ *   grid_barrier device int32, zero before the first call; every call leaves
+ *                it zero again.  After a call whose status word reports
+ *                PL_ERR_TIMEOUT it may be left non-zero: zero it before the
+ *                next call.  Only needed when num_phases > 1.
+ * A phase's lora_down must not be the shrink output of an earlier phase of
+ * the same call (PL_ERR_UNSUPPORTED): it is read through L1.  x / residual
+ * of a later phase may be any earlier phase's y (read from L2).  Weights are
+ * streamed before the preceding kernel on the stream has finished, as with
+ * PL_FLAG_WEIGHTS_STATIC: no upstream kernel may write them.  Bounded waits
+ * report PL_ERR_TIMEOUT through *status_dev.
+ */
+int32_t pl_linear_lora_chain(const PlGemvPhase *phases, int32_t num_phases,
+                             int32_t *grid_barrier, int32_t *status_dev,
+                             void *stream);
+
+/*
  * Kernel variant and pipeline shape of pl_linear_lora_expand_fused for this
  * process.  No reference counterpart (a tuning knob).
  *   mode -1: restore the built-in defaults (tuning and L2 prefetch).

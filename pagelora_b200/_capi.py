@@ -52,6 +52,19 @@ class GemmPlan(Structure):
     _fields_ = [("ctas", c_int32), ("max_slots", c_int32), ("workspace_bytes", c_int64)]
 
 
+class GemvPhase(Structure):
+    """PlGemvPhase: one projection of pl_linear_lora_chain."""
+
+    _fields_ = [("x", c_void_p), ("x_stride", c_int64), ("num_tokens", c_int32), ("k_in", c_int32),
+                ("prologue", c_int32), ("norm_w", c_void_p), ("norm_eps", c_float), ("w", c_void_p),
+                ("n_out", c_int32), ("bias", c_void_p), ("lora_down", c_void_p), ("down_stride", c_int64),
+                ("lora_b", c_void_p), ("lora_rank", c_int32), ("lora_scale", c_float),
+                ("slice_end", c_int32 * 3), ("num_slices", c_int32), ("tok_adapter", c_void_p),
+                ("residual", c_void_p), ("res_stride", c_int64), ("y", c_void_p), ("y_stride", c_int64),
+                ("shrink_a", c_void_p), ("n_shrink", c_int32), ("shrink_out", c_void_p),
+                ("shrink_stride", c_int64), ("flags", c_int32)]
+
+
 _P = c_void_p
 _I32 = c_int32
 _I64 = c_int64
@@ -107,6 +120,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _I64, _P, _I32, _F, _P, _I32, _P, _P, _I64, _P,
          _I64, _P, _I32, _P, _I64, _I32, _P, _P],
     ),
+    "pl_linear_lora_chain": (_I32, [POINTER(GemvPhase), _I32, _P, _P, _P]),
     "pl_linear_set_tuning": (_I32, [_I32, _I32, _I32, _I32, _I32]),
     "pl_linear_set_l2_prefetch": (_I32, [_I64]),
     "pl_linear_gemm_plan": (_I32, [_I32, _I32, _I32, _I32, POINTER(GemmPlan)]),

@@ -43,7 +43,25 @@ struct GemvArgs {
   int32_t kc;             // columns per stage (multiple of 16)
   int32_t prefetch_tiles; // tiles per CTA whose weights are pulled into L2 before the dependency resolves
   int32_t* status;
+  int32_t coherent;       // activations / residual may have been written by other CTAs of this launch: read them
+                          // from L2 (ld.global.cg), never from a possibly stale L1 line
 };
+
+// 16 activation bytes; from L2 when kCg (data written by other CTAs of the same launch).
+template <bool kCg>
+__device__ __forceinline__ uint4 ld_act16(const void* p) {
+  if constexpr (kCg) {
+    return __ldcg(reinterpret_cast<const uint4*>(p));
+  } else {
+    return *reinterpret_cast<const uint4*>(p);
+  }
+}
+
+__device__ __forceinline__ bf16 ld_bf16_cg(const bf16* p) {
+  unsigned short u;
+  asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(u) : "l"(p));
+  return __ushort_as_bfloat16(u);
+}
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
@@ -68,7 +86,10 @@ __device__ __forceinline__ float epilogue_value(const GemvArgs& a, int64_t o, in
     }
     v = vb;
   }
-  if (a.residual != nullptr) v = bf2f(a.residual[tok * a.res_stride + o]) + bfr(v);
+  if (a.residual != nullptr) {
+    const bf16* rp = a.residual + tok * a.res_stride + o;
+    v = bf2f(a.coherent ? ld_bf16_cg(rp) : *rp) + bfr(v);
+  }
   return v;
 }
 

@@ -111,7 +111,10 @@ __device__ __forceinline__ void down_from_staged(const GemvArgs& a, const uint8_
 // Stage the activations of all tokens as bf16 rows (stride xrow bytes) in
 // shared memory, applying the input prologue.  Loads are issued four chunks
 // at a time per thread so each pass costs one or two memory round trips.
+// kCg: the activations were written by other CTAs of the same launch (read
+// them from L2).
 // `part` holds one float per warp; `bar` is a named barrier over `nthreads`.
+template <bool kCg = false>
 __device__ __forceinline__ void stage_activations(const GemvArgs& a, uint8_t* xs, int xrow, int tid, int nthreads,
                                                   float* part, int bar) {
   const int K = a.K;
@@ -120,14 +123,58 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& a, uint8_t* xs
   for (int t = 0; t < a.T; ++t) {
     const bf16* xr = a.x + (int64_t)t * a.x_stride;
     uint8_t* dst = xs + t * xrow;
-    if (a.prologue == PL_PROLOGUE_RMSNORM) {
+    if (a.prologue == PL_PROLOGUE_RMSNORM && K <= 4 * step) {
+      // one pass: x and the norm weights stay in registers across the
+      // reduction (same sum order as the two-pass form below)
+      uint4 v[4], wv[4];
+      const int k0 = tid * 8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = k0 + i * step;
+        v[i] = k < K ? ld_act16<kCg>(xr + k) : make_uint4(0, 0, 0, 0);
+        wv[i] = k < K ? *reinterpret_cast<const uint4*>(a.norm_w + k) : make_uint4(0, 0, 0, 0);
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(u[q]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) part[wid] = ss;
+      named_barrier(bar, nthreads);
+      float tot = 0.f;
+      for (int w = 0; w < nthreads / 32; ++w) tot += part[w];
+      const float rstd = rsqrtf(tot / (float)K + a.eps);
+      named_barrier(bar, nthreads);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = k0 + i * step;
+        if (k >= K) break;
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+        const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv[i]);
+        uint4 o;
+        uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(u[q]);
+          const float2 g = unpack_bf16x2(uw[q]);
+          uo[q] = pack_bf16x2(f.x * rstd * g.x, f.y * rstd * g.y);
+        }
+        *reinterpret_cast<uint4*>(dst + k * 2) = o;
+      }
+    } else if (a.prologue == PL_PROLOGUE_RMSNORM) {
       float ss = 0.f;
       for (int k0 = tid * 8; k0 < K; k0 += 4 * step) {
         uint4 v[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int k = k0 + i * step;
-          v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+          v[i] = k < K ? ld_act16<kCg>(xr + k) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -151,7 +198,7 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& a, uint8_t* xs
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int k = k0 + i * step;
-          v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+          v[i] = k < K ? ld_act16<kCg>(xr + k) : make_uint4(0, 0, 0, 0);
           wv[i] = k < K ? *reinterpret_cast<const uint4*>(a.norm_w + k) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
@@ -177,8 +224,8 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& a, uint8_t* xs
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int k = k0 + i * step;
-          gv[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
-          uv[i] = k < K ? *reinterpret_cast<const uint4*>(xr + K + k) : make_uint4(0, 0, 0, 0);
+          gv[i] = k < K ? ld_act16<kCg>(xr + k) : make_uint4(0, 0, 0, 0);
+          uv[i] = k < K ? ld_act16<kCg>(xr + K + k) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -203,7 +250,7 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& a, uint8_t* xs
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int k = k0 + i * step;
-          v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+          v[i] = k < K ? ld_act16<kCg>(xr + k) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -216,144 +263,147 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& a, uint8_t* xs
   named_barrier(bar, nthreads);
 }
 
-// One CTA per SM streams the weight rows [r0, r1) of its balanced share as
-// 16-row x kc-column tiles.  The producer warp loads a stage with one
-// instruction: lane r issues the bulk copy of row r's kc columns (4 KB at
-// kc = 2048), because a TMA instruction costs ~0.3 us of issue time however
-// many lanes take part.  Consumer warps split the k-steps of each stage and
-// run mma.sync m16n8k16 (weight rows = M, tokens = N); at the end of a tile
-// each warp adds its partial tile into a shared accumulator with shared-
-// memory atomics and the last warp to arrive applies the epilogue, so no
-// CTA-wide barrier ever stalls the stream.
-template <int NCW>
-__global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const GemvArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const int S = a.stages, KC = a.kc;
-  const GemvSmem L = gemv_smem_layout(a.T, a.K, S, KC, a.pro_a != nullptr ? a.T * a.rank : 0);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-  uint64_t* empty_bar = full_bar + S;
-  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + L.misc_off);
-  float* tacc = reinterpret_cast<float*>(smem + L.acc_off);      // [nbuf][NCW][16][T]
-  int32_t* tcnt = reinterpret_cast<int32_t*>(smem + L.cnt_off);  // [nbuf]
-  uint8_t* xs = smem + L.x_off;
-  const int XROW = a.K * 2 + 16;
-  const int RB = L.row_bytes;
+// Shared-memory pieces of one GEMV CTA (linear_lora_kernel, linear_chain_kernel).
+struct GemvRing {
+  uint8_t* smem;
+  GemvSmem L;
+  uint64_t* full_bar;
+  uint64_t* empty_bar;
+  volatile int32_t* abort_flag;
+  float* tacc;    // [nbuf][NCW][16][T] partial tiles
+  int32_t* tcnt;  // [nbuf] warps done with a tile
+  uint8_t* xs;    // staged activations
+  int S, KC;
+};
 
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int K = a.K;
-  const int64_t rows_total = (int64_t)a.n_out + a.n_shrink;
-  const int64_t r0 = rows_total * blockIdx.x / gridDim.x;
-  const int64_t r1 = rows_total * (blockIdx.x + 1) / gridDim.x;
+__device__ __forceinline__ GemvRing gemv_ring(uint8_t* smem_raw, const GemvSmem& L, int S, int KC) {
+  GemvRing R;
+  R.smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  R.L = L;
+  R.full_bar = reinterpret_cast<uint64_t*>(R.smem + L.bar_off);
+  R.empty_bar = R.full_bar + S;
+  R.abort_flag = reinterpret_cast<volatile int32_t*>(R.smem + L.misc_off);
+  R.tacc = reinterpret_cast<float*>(R.smem + L.acc_off);
+  R.tcnt = reinterpret_cast<int32_t*>(R.smem + L.cnt_off);
+  R.xs = R.smem + L.x_off;
+  R.S = S;
+  R.KC = KC;
+  return R;
+}
+
+// Barriers, tile counters and the zero slot; ends with a CTA barrier.
+template <int NCW>
+__device__ __forceinline__ void gemv_ring_init(const GemvRing& R) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < R.S; ++s) {
+      mbar_init(&R.full_bar[s], 1);
+      mbar_init(&R.empty_bar[s], NCW);
+    }
+    *R.abort_flag = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < R.L.nbuf; i += blockDim.x) R.tcnt[i] = 0;
+  if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(R.smem + R.L.zero_off)[threadIdx.x] = 0u;
+  __syncthreads();
+}
+
+// Producer warp: stream the 16-row x kc-column tiles of weight rows [r0, r1)
+// into the ring as ring units u_base, u_base + 1, ...  Lane r issues the
+// bulk copy of row r's kc columns, because a TMA instruction costs ~0.3 us
+// of issue time however many lanes take part.  Returns the units issued
+// (fewer after an abort).
+__device__ __forceinline__ int gemv_produce(const GemvArgs& a, const GemvRing& R, int64_t r0, int64_t r1, int u_base,
+                                            uint64_t pol, int lane) {
+  const int S = R.S, KC = R.KC, K = a.K;
   const int n_tiles = (int)((r1 - r0 + kTileRows - 1) / kTileRows);
   const int n_kc = (K + KC - 1) / KC;
   const int n_units = n_tiles * n_kc;
-
-  if (threadIdx.x == 0) {
-    PL_TRACE_POINT(0);
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], NCW);
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  for (int i = threadIdx.x; i < L.nbuf; i += blockDim.x) tcnt[i] = 0;
-  if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(smem + L.zero_off)[threadIdx.x] = 0u;
-  __syncthreads();
-  pdl_launch_dependents();
-
-  if (warp == 0) {
-    // --------------------------------------------------------- producer warp
-    if (!a.early_weights) pdl_wait();
-    const uint64_t pol = l2_evict_first_policy();
-    int issued = 0;
-    for (int u = 0; u < n_units; ++u) {
-      const int s = u % S;
-      if (u >= S) {
-        if (!mbar_wait(&empty_bar[s], ((u / S) - 1) & 1)) {
-          if (lane == 0) {
-            set_status(a.status, PL_ERR_TIMEOUT);
-            *abort_flag = 1;
-          }
+  const int RB = R.L.row_bytes;
+  int issued = 0;
+  for (int lu = 0; lu < n_units; ++lu) {
+    const int u = u_base + lu;
+    const int s = u % S;
+    if (u >= S) {
+      if (!mbar_wait(&R.empty_bar[s], ((u / S) - 1) & 1)) {
+        if (lane == 0) {
+          set_status(a.status, PL_ERR_TIMEOUT);
+          *R.abort_flag = 1;
         }
       }
-      __syncwarp();
-      if (*abort_flag) break;
-      const int tile = u / n_kc, kc = u % n_kc;
-      const int64_t row0 = r0 + (int64_t)tile * kTileRows;
-      const int rows = (int)((r1 - row0) < kTileRows ? (r1 - row0) : kTileRows);
-      const int k0 = kc * KC;
-      const int kw = min(KC, K - k0);
-      if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(rows * kw * 2));
-      __syncwarp();
-      if (lane < rows) {
-        const int64_t row = row0 + lane;
-        const bf16* src = row < a.n_out ? a.w + row * K : a.shrink_a + (row - a.n_out) * K;
-        bulk_g2s(smem + s * L.stage_bytes + lane * RB, src + k0, (uint32_t)(kw * 2), &full_bar[s], pol);
-      }
-      if (lane == 0 && u == 0) PL_TRACE_POINT(1);
-      if (lane == 0 && u == S) PL_TRACE_POINT(2);
-      ++issued;
     }
-    if (lane == 0) PL_TRACE_POINT(3);
-    if (lane == 0 && *abort_flag) {
-      for (int u = issued - S < 0 ? 0 : issued - S; u < issued; ++u)
-        (void)mbar_wait(&full_bar[u % S], (u / S) & 1);
+    __syncwarp();
+    if (*R.abort_flag) break;
+    const int tile = lu / n_kc, kc = lu % n_kc;
+    const int64_t row0 = r0 + (int64_t)tile * kTileRows;
+    const int rows = (int)((r1 - row0) < kTileRows ? (r1 - row0) : kTileRows);
+    const int k0 = kc * KC;
+    const int kw = min(KC, K - k0);
+    if (lane == 0) mbar_arrive_expect_tx(&R.full_bar[s], (uint32_t)(rows * kw * 2));
+    __syncwarp();
+    if (lane < rows) {
+      const int64_t row = row0 + lane;
+      const bf16* src = row < a.n_out ? a.w + row * K : a.shrink_a + (row - a.n_out) * K;
+      bulk_g2s(R.smem + s * R.L.stage_bytes + lane * RB, src + k0, (uint32_t)(kw * 2), &R.full_bar[s], pol);
     }
-    return;
+    if (lane == 0 && u == 0) PL_TRACE_POINT(1);
+    if (lane == 0 && u == S) PL_TRACE_POINT(2);
+    ++issued;
   }
+  return issued;
+}
 
-  // ------------------------------------------------------------- consumers
-  const int cw = warp - 1;
-  const int ctid = threadIdx.x - 32;
-  constexpr int NC = 32 * NCW;
-  pdl_wait();
-  if (ctid == 0) PL_TRACE_POINT(4);
+// After an abort: wait (bounded) for the copies still in flight, the last
+// min(issued, S) units, so that no TMA write lands after the CTA exits.
+__device__ __forceinline__ void gemv_drain(const GemvRing& R, int issued) {
+  for (int u = issued - R.S < 0 ? 0 : issued - R.S; u < issued; ++u)
+    (void)mbar_wait(&R.full_bar[u % R.S], (u / R.S) & 1);
+}
 
-  stage_activations(a, xs, XROW, ctid, NC, reinterpret_cast<float*>(smem + L.misc_off + 16), 1);
-  // LoRA down: computed here from the staged x (a.pro_a), else read from a.lora_down
-  const float* down = a.lora_down;
-  int64_t dstride = a.down_stride;
-  if (a.pro_a != nullptr) {
-    float* dsm = reinterpret_cast<float*>(smem + L.down_off);
-    down_from_staged(a, xs, XROW, dsm, tacc, ctid, NC, 1);
-    down = dsm;
-    dstride = a.rank;
-  }
-  if (ctid == 0) PL_TRACE_POINT(5);
-
+// Consumer warps: multiply the ring units u_base, ... (weight rows [r0, r1)
+// of one projection) against the staged activations with mma.sync
+// m16n8k16 (weight rows = M, tokens = N); the warps split the k-steps of
+// each stage, and at the end of a tile each warp stores its partial tile
+// in its own slot and the last warp to arrive sums the slots in warp order
+// (deterministic) and runs the epilogue, so no CTA-wide barrier ever stalls
+// the stream.  Returns false after an abort.
+template <int NCW>
+__device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const GemvRing& R, int64_t r0, int64_t r1, int u_base,
+                                             const float* down, int64_t dstride, int cw, int ctid, int lane,
+                                             bool trace = true) {
+  const int S = R.S, KC = R.KC, K = a.K;
+  const int n_tiles = (int)((r1 - r0 + kTileRows - 1) / kTileRows);
+  const int n_kc = (K + KC - 1) / KC;
+  const int n_units = n_tiles * n_kc;
+  const int RB = R.L.row_bytes;
+  const int XROW = K * 2 + 16;
   const int g = lane >> 2, tq = lane & 3;
-  const uint32_t zero_addr = smem_u32(smem + L.zero_off);
+  const uint32_t zero_addr = smem_u32(R.smem + R.L.zero_off);
   // Per-lane ldmatrix row addresses.
   const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
   const int a_col = 8 * (lane >> 4);
   const int b_tok = lane & 7;
   const int b_col = 8 * ((lane >> 3) & 1);
   const bool b_valid = b_tok < a.T;
-  const uint32_t xs_base = smem_u32(xs + b_tok * XROW + b_col * 2);
+  const uint32_t xs_base = smem_u32(R.xs + b_tok * XROW + b_col * 2);
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     // two independent accumulators so consecutive mma's do not serialise
     float acc0[4] = {0.f, 0.f, 0.f, 0.f};
     float acc1[4] = {0.f, 0.f, 0.f, 0.f};
-    bool ok = true;
     for (int kc = 0; kc < n_kc; ++kc) {
-      const int u = tile * n_kc + kc;
+      const int lu = tile * n_kc + kc;
+      const int u = u_base + lu;
       const int s = u % S;
-      if (!mbar_wait(&full_bar[s], (u / S) & 1)) {
+      if (!mbar_wait(&R.full_bar[s], (u / S) & 1)) {
         if (lane == 0) set_status(a.status, PL_ERR_TIMEOUT);
-        *abort_flag = 1;
+        *R.abort_flag = 1;
       }
-      if (*abort_flag) {
-        ok = false;
-        break;
-      }
-      if (ctid == 0 && u == 0) PL_TRACE_POINT(6);
-      if (ctid == 0 && u == n_units - 1) PL_TRACE_POINT(7);
+      if (*R.abort_flag) return false;
+      if (trace && ctid == 0 && u == 0) PL_TRACE_POINT(6);
+      if (trace && ctid == 0 && lu == n_units - 1) PL_TRACE_POINT(7);
       const int k0 = kc * KC;
       const int ksteps = min(KC, K - k0) / 16;
-      const uint32_t stage = smem_u32(smem + s * L.stage_bytes) + a_row * RB + a_col * 2;
+      const uint32_t stage = smem_u32(R.smem + s * R.L.stage_bytes) + a_row * RB + a_col * 2;
       const uint32_t xcol = xs_base + k0 * 2;
       for (int ks = cw; ks < ksteps; ks += 2 * NCW) {
         const bool two = ks + NCW < ksteps;
@@ -368,14 +418,11 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
         if (two) mma_bf16_16816(acc1, a1, b1);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[s]);
+      if (lane == 0) mbar_arrive(&R.empty_bar[s]);
     }
-    if (!ok) break;
-    // Store this warp's 16 x T partial in its slot; the last warp to arrive
-    // sums the slots in warp order (deterministic) and runs the epilogue.
     const int T = a.T;
-    const int buf = tile % L.nbuf;
-    float* slots = tacc + buf * (NCW * kTileRows * T);
+    const int buf = tile % R.L.nbuf;
+    float* slots = R.tacc + buf * (NCW * kTileRows * T);
     float* mine = slots + cw * (kTileRows * T);
     if (2 * tq < T) {
       mine[g * T + 2 * tq] = acc0[0] + acc1[0];
@@ -388,7 +435,7 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
     __threadfence_block();
     __syncwarp();
     int last = 0;
-    if (lane == 0) last = (atomicAdd(&tcnt[buf], 1) == NCW - 1);
+    if (lane == 0) last = (atomicAdd(&R.tcnt[buf], 1) == NCW - 1);
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
       __threadfence_block();
@@ -403,11 +450,196 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
-        tcnt[buf] = 0;
+        R.tcnt[buf] = 0;
       }
     }
   }
+  return true;
+}
+
+// Stage the activations (and the in-kernel LoRA down) of one projection;
+// returns the down rows the epilogue reads.
+template <bool kCg>
+__device__ __forceinline__ const float* gemv_stage(const GemvArgs& a, const GemvRing& R, int ctid, int nc,
+                                                   int64_t& dstride) {
+  const int XROW = a.K * 2 + 16;
+  stage_activations<kCg>(a, R.xs, XROW, ctid, nc, reinterpret_cast<float*>(R.smem + R.L.misc_off + 16), 1);
+  dstride = a.down_stride;
+  if (a.pro_a == nullptr) return a.lora_down;
+  float* dsm = reinterpret_cast<float*>(R.smem + R.L.down_off);
+  down_from_staged(a, R.xs, XROW, dsm, R.tacc, ctid, nc, 1);
+  dstride = a.rank;
+  return dsm;
+}
+
+// One CTA per SM streams the weight rows [r0, r1) of its balanced share as
+// 16-row x kc-column tiles through an S-deep shared-memory ring (one
+// producer warp, NCW consumer warps).
+template <int NCW>
+__global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const GemvArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const GemvSmem L = gemv_smem_layout(a.T, a.K, a.stages, a.kc, a.pro_a != nullptr ? a.T * a.rank : 0);
+  const GemvRing R = gemv_ring(smem_raw, L, a.stages, a.kc);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t rows_total = (int64_t)a.n_out + a.n_shrink;
+  const int64_t r0 = rows_total * blockIdx.x / gridDim.x;
+  const int64_t r1 = rows_total * (blockIdx.x + 1) / gridDim.x;
+
+  if (threadIdx.x == 0) PL_TRACE_POINT(0);
+  gemv_ring_init<NCW>(R);
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // --------------------------------------------------------- producer warp
+    if (!a.early_weights) pdl_wait();
+    const int issued = gemv_produce(a, R, r0, r1, 0, l2_evict_first_policy(), lane);
+    if (lane == 0) PL_TRACE_POINT(3);
+    if (lane == 0 && *R.abort_flag) gemv_drain(R, issued);
+    return;
+  }
+
+  // ------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int ctid = threadIdx.x - 32;
+  pdl_wait();
+  if (ctid == 0) PL_TRACE_POINT(4);
+  int64_t dstride;
+  const float* down = gemv_stage<false>(a, R, ctid, 32 * NCW, dstride);
+  if (ctid == 0) PL_TRACE_POINT(5);
+  gemv_consume<NCW>(a, R, r0, r1, 0, down, dstride, cw, ctid, lane);
   if (lane == 0) PL_TRACE_MAX(8);
+}
+
+// ------------------------------------------------------- projection chain
+// Up to kMaxChainPhases projections in one persistent launch (one CTA per
+// SM, all resident), e.g. o -> gate_up -> down -> the next layer's q/k/v.
+// The producer warp streams the weights of every phase back to back through
+// one ring: the weights depend on nothing upstream, so the ring keeps
+// filling while the consumers of phase p wait for the outputs of phase p-1.
+// Between phases the consumer warps of all CTAs meet at a grid barrier (a
+// global arrival counter; bounded wait); the activations and residuals
+// written inside the launch are then read from L2.  The counter resets
+// itself: each CTA adds one more arrival after passing the last barrier and
+// the CTA that brings the count to num_phases x grid puts it back to zero.
+// Trace points (-DPL_TRACE builds): 0 start, 1 / 2 producer issued unit 0 /
+// unit S, 3 producer done, 4 consumers past the upstream wait, 5 phase-0
+// activations staged, 6 + p phase p's tiles done (p < 4), 10 + p grid
+// barrier before phase p passed (p = 1..3), 14 phase-1 activations staged,
+// 15 last consumer warp done.
+constexpr int kMaxChainPhases = 6;
+
+struct GemvChainArgs {
+  GemvArgs ph[kMaxChainPhases];
+  int32_t num_phases;
+  int32_t stages, kc, k_max, down_max;
+  int32_t* barrier;
+  int32_t* status;
+};
+
+__device__ __forceinline__ void red_release_gpu_add(int32_t* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier of the consumer warps: all CTAs have finished the phases
+// before `target / gridDim.x`.  Every consumer thread calls it (a warp that
+// gave up in the previous phase too), and all of them get the same answer:
+// thread 0 decides and broadcasts it through shared memory, so either every
+// consumer warp goes on to the next phase's named barriers or none does.
+// False on timeout or after an abort anywhere in the CTA (status set).
+__device__ __forceinline__ bool chain_grid_barrier(const GemvChainArgs& c, const GemvRing& R, int target, int ctid,
+                                                   int nc) {
+  volatile int32_t* go = reinterpret_cast<volatile int32_t*>(R.smem + R.L.misc_off + 4);
+  named_barrier(1, nc);  // every epilogue store of this CTA's phase is issued
+  if (ctid == 0) {
+    bool ok = *R.abort_flag == 0;
+    if (ok) {
+      // release: this CTA's stores (ordered before by the named barrier) are
+      // visible to whoever acquires the count; acquire: the other CTAs' are
+      // visible here, and through the named barrier below to every warp
+      red_release_gpu_add(c.barrier, 1);
+      const long long c0 = clock64();
+      for (uint32_t i = 1;; ++i) {
+        if (ld_acquire_gpu(c.barrier) >= target) break;
+        if ((i & 255u) == 0 && clock64() - c0 > kWaitTimeoutCycles) {
+          set_status(c.status, PL_ERR_TIMEOUT);
+          *R.abort_flag = 1;
+          ok = false;
+          break;
+        }
+      }
+    }
+    *go = ok ? 1 : 0;
+  }
+  named_barrier(1, nc);
+  return *go != 0;
+}
+
+template <int NCW>
+__global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_chain_kernel(const __grid_constant__ GemvChainArgs c) {
+  extern __shared__ uint8_t smem_raw[];
+  const GemvSmem L = gemv_smem_layout(c.ph[0].T, c.k_max, c.stages, c.kc, c.down_max);
+  const GemvRing R = gemv_ring(smem_raw, L, c.stages, c.kc);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int G = gridDim.x;
+
+  if (threadIdx.x == 0) PL_TRACE_POINT(0);
+  gemv_ring_init<NCW>(R);
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // Producer: every phase's weights, back to back (static: no upstream wait).
+    const uint64_t pol = l2_evict_first_policy();
+    int u_base = 0;
+    for (int p = 0; p < c.num_phases; ++p) {
+      const GemvArgs& a = c.ph[p];
+      const int64_t rows_total = (int64_t)a.n_out + a.n_shrink;
+      const int64_t r0 = rows_total * blockIdx.x / G, r1 = rows_total * (blockIdx.x + 1) / G;
+      const int n_units = (int)((r1 - r0 + kTileRows - 1) / kTileRows) * ((a.K + R.KC - 1) / R.KC);
+      const int issued = gemv_produce(a, R, r0, r1, u_base, pol, lane);
+      if (issued < n_units) {
+        if (lane == 0) gemv_drain(R, u_base + issued);
+        return;
+      }
+      u_base += n_units;
+    }
+    if (lane == 0) PL_TRACE_POINT(3);
+    // no copy may land after the CTA exits (the consumers can stop early)
+    if (lane == 0) gemv_drain(R, u_base);
+    return;
+  }
+
+  const int cw = warp - 1;
+  const int ctid = threadIdx.x - 32;
+  constexpr int NC = 32 * NCW;
+  pdl_wait();  // phase 0's activations come from the upstream kernel
+  if (ctid == 0) PL_TRACE_POINT(4);
+  int u_base = 0;
+  for (int p = 0; p < c.num_phases; ++p) {
+    const GemvArgs& a = c.ph[p];
+    if (p > 0 && !chain_grid_barrier(c, R, p * G, ctid, NC)) break;
+    if (ctid == 0 && p > 0 && p < 4) PL_TRACE_POINT(10 + p);
+    if (c.num_phases > 1 && p == c.num_phases - 1 && ctid == 0) {
+      // past the last barrier: the extra arrival that lets the counter reset
+      if (atomicAdd(c.barrier, 1) == c.num_phases * G - 1) atomicExch(c.barrier, 0);
+    }
+    const int64_t rows_total = (int64_t)a.n_out + a.n_shrink;
+    const int64_t r0 = rows_total * blockIdx.x / G, r1 = rows_total * (blockIdx.x + 1) / G;
+    int64_t dstride;
+    const float* down = gemv_stage<true>(a, R, ctid, NC, dstride);
+    if (ctid == 0 && p < 2) PL_TRACE_POINT(p == 0 ? 5 : 14);
+    // a warp that gives up (bounded wait) still meets the others at the next
+    // grid barrier, which then stops every warp of the CTA together
+    (void)gemv_consume<NCW>(a, R, r0, r1, u_base, down, dstride, cw, ctid, lane, false);
+    if (ctid == 0 && p < 4) PL_TRACE_POINT(6 + p);
+    u_base += (int)((r1 - r0 + kTileRows - 1) / kTileRows) * ((a.K + R.KC - 1) / R.KC);
+  }
+  if (lane == 0) PL_TRACE_MAX(15);
 }
 
 // ------------------------------------------------- register-direct variant
@@ -694,6 +926,102 @@ int64_t g_auto_ldg_max_bytes = int64_t(64) << 20;  // mode 0: register-direct up
 int64_t g_l2_prefetch_bytes = 0;  // register-direct variant: L2 prefetch budget per launch
 }  // namespace
 
+namespace {
+// Checks the arguments of one fused GEMV projection and fills its argument
+// block; *skip = true when there is nothing to compute.
+int32_t gemv_args_from(const PlGemvPhase& q, pl::GemvArgs& a, bool* skip) {
+  *skip = false;
+  const void* x = q.x;
+  const int64_t x_stride = q.x_stride;
+  const int32_t num_tokens = q.num_tokens, k_in = q.k_in, prologue = q.prologue, n_out = q.n_out;
+  const int32_t lora_rank = q.lora_rank, num_slices = q.num_slices, flags = q.flags;
+  int32_t n_shrink = q.n_shrink;
+  const bool down_from_x = (flags & PL_FLAG_DOWN_FROM_X) != 0;
+  if (down_from_x) {  // shrink_a is the LoRA A stack [n_shrink adapters][lora_rank][k_in]
+    if (q.lora_b == nullptr || q.shrink_a == nullptr || n_shrink < 1 || lora_rank <= 0 || num_slices > 1)
+      return PL_ERR_INVALID_ARGUMENT;
+    if (lora_rank > 64) return PL_ERR_UNSUPPORTED;
+  }
+  if (num_tokens == 0 || (n_out == 0 && (n_shrink == 0 || down_from_x))) {
+    *skip = true;
+    return PL_OK;
+  }
+  if (x == nullptr || q.w == nullptr || num_tokens < 0 || num_tokens > pl::kMaxTok || k_in <= 0 || n_out < 0 ||
+      n_shrink < 0)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (k_in % 16 != 0) return PL_ERR_UNSUPPORTED;
+  if (n_out > 0 && q.y == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  if (!down_from_x && n_shrink > 0 && (q.shrink_a == nullptr || q.shrink_out == nullptr))
+    return PL_ERR_INVALID_ARGUMENT;
+  if (prologue == PL_PROLOGUE_RMSNORM && q.norm_w == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  if (prologue < 0 || prologue > 2) return PL_ERR_INVALID_ARGUMENT;
+  if (q.lora_b != nullptr && ((q.lora_down == nullptr && !down_from_x) || lora_rank <= 0 || num_slices < 1 ||
+                              num_slices > 4))
+    return PL_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q.w) & 15) || (x_stride % 8) ||
+      (q.shrink_a != nullptr && (reinterpret_cast<uintptr_t>(q.shrink_a) & 15)) ||
+      (q.norm_w != nullptr && (reinterpret_cast<uintptr_t>(q.norm_w) & 15)))
+    return PL_ERR_INVALID_ARGUMENT;
+
+  a = {};
+  a.x = static_cast<const pl::bf16*>(x);
+  a.x_stride = x_stride;
+  a.T = num_tokens;
+  a.K = k_in;
+  a.prologue = prologue;
+  a.norm_w = static_cast<const pl::bf16*>(q.norm_w);
+  a.eps = q.norm_eps;
+  a.w = static_cast<const pl::bf16*>(q.w);
+  a.n_out = n_out;
+  a.bias = static_cast<const pl::bf16*>(q.bias);
+  a.lora_down = q.lora_down;
+  a.down_stride = q.down_stride;
+  a.lora_b = static_cast<const pl::bf16*>(q.lora_b);
+  a.rank = lora_rank;
+  a.lora_scale = q.lora_scale;
+  a.num_slices = num_slices < 1 ? 1 : num_slices;
+  for (int i = 0; i < 4; ++i) a.slice_end[i] = n_out;
+  for (int i = 0; i < num_slices - 1 && i < 3; ++i) a.slice_end[i] = q.slice_end[i];
+  a.tok_adapter = q.tok_adapter;
+  a.residual = static_cast<const pl::bf16*>(q.residual);
+  a.res_stride = q.res_stride;
+  a.y = static_cast<pl::bf16*>(q.y);
+  a.y_stride = q.y_stride;
+  if (down_from_x) {
+    a.pro_a = static_cast<const pl::bf16*>(q.shrink_a);
+    a.pro_a_adapters = n_shrink;
+    n_shrink = 0;  // no shrink rows: the down values stay in the kernel
+  } else {
+    a.shrink_a = static_cast<const pl::bf16*>(q.shrink_a);
+    a.shrink_out = q.shrink_out;
+    a.shrink_stride = q.shrink_stride;
+  }
+  a.n_shrink = n_shrink;
+  a.early_weights = (flags & PL_FLAG_WEIGHTS_STATIC) ? 1 : 0;
+  return PL_OK;
+}
+
+// Largest ring that fits: the tuned shape, then shallower / narrower stages.
+bool gemv_ring_shape(int T, int k_max, int down_floats, int* stages_out, int* kc_out, int* smem_out) {
+  int stages = g_gemv_stages, kc = g_gemv_kc;
+  pl::GemvSmem L = pl::gemv_smem_layout(T, k_max, stages, kc, down_floats);
+  while (L.total > 227 * 1024 && (stages > 2 || kc > 256)) {
+    if (stages > 2) {
+      --stages;
+    } else {
+      kc /= 2;
+      stages = g_gemv_stages;
+    }
+    L = pl::gemv_smem_layout(T, k_max, stages, kc, down_floats);
+  }
+  if (L.total > 227 * 1024) return false;
+  *stages_out = stages;
+  *kc_out = kc;
+  *smem_out = L.total;
+  return true;
+}
+}  // namespace
+
 extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
                                                int32_t prologue, const void* norm_w, float norm_eps, const void* w,
                                                int32_t n_out, const void* bias, const float* lora_down,
@@ -704,65 +1032,43 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
                                                void* y, int64_t y_stride, const void* shrink_a, int32_t n_shrink,
                                                float* shrink_out, int64_t shrink_stride, int32_t flags,
                                                int32_t* status_dev, void* stream) {
-  const bool down_from_x = (flags & PL_FLAG_DOWN_FROM_X) != 0;
-  if (down_from_x) {  // shrink_a is the LoRA A stack [n_shrink adapters][lora_rank][k_in]
-    if (lora_b == nullptr || shrink_a == nullptr || n_shrink < 1 || lora_rank <= 0 || num_slices > 1)
-      return PL_ERR_INVALID_ARGUMENT;
-    if (lora_rank > 64) return PL_ERR_UNSUPPORTED;
-  }
-  if (num_tokens == 0 || (n_out == 0 && (n_shrink == 0 || down_from_x))) return PL_OK;
-  if (x == nullptr || w == nullptr || num_tokens < 0 || num_tokens > pl::kMaxTok || k_in <= 0 || n_out < 0 ||
-      n_shrink < 0)
-    return PL_ERR_INVALID_ARGUMENT;
-  if (k_in % 16 != 0) return PL_ERR_UNSUPPORTED;
-  if (n_out > 0 && y == nullptr) return PL_ERR_INVALID_ARGUMENT;
-  if (!down_from_x && n_shrink > 0 && (shrink_a == nullptr || shrink_out == nullptr)) return PL_ERR_INVALID_ARGUMENT;
-  if (prologue == PL_PROLOGUE_RMSNORM && norm_w == nullptr) return PL_ERR_INVALID_ARGUMENT;
-  if (prologue < 0 || prologue > 2) return PL_ERR_INVALID_ARGUMENT;
-  if (lora_b != nullptr && ((lora_down == nullptr && !down_from_x) || lora_rank <= 0 || num_slices < 1 || num_slices > 4 ||
-                            (num_slices > 1 && slice_end == nullptr)))
-    return PL_ERR_INVALID_ARGUMENT;
-  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) || (x_stride % 8) ||
-      (shrink_a != nullptr && (reinterpret_cast<uintptr_t>(shrink_a) & 15)) ||
-      (norm_w != nullptr && (reinterpret_cast<uintptr_t>(norm_w) & 15)))
-    return PL_ERR_INVALID_ARGUMENT;
-
-  pl::GemvArgs a = {};
-  a.x = static_cast<const pl::bf16*>(x);
-  a.x_stride = x_stride;
-  a.T = num_tokens;
-  a.K = k_in;
-  a.prologue = prologue;
-  a.norm_w = static_cast<const pl::bf16*>(norm_w);
-  a.eps = norm_eps;
-  a.w = static_cast<const pl::bf16*>(w);
-  a.n_out = n_out;
-  a.bias = static_cast<const pl::bf16*>(bias);
-  a.lora_down = lora_down;
-  a.down_stride = down_stride;
-  a.lora_b = static_cast<const pl::bf16*>(lora_b);
-  a.rank = lora_rank;
-  a.lora_scale = lora_scale;
-  a.num_slices = num_slices < 1 ? 1 : num_slices;
-  for (int i = 0; i < 4; ++i) a.slice_end[i] = n_out;
-  for (int i = 0; i < num_slices - 1 && slice_end != nullptr; ++i) a.slice_end[i] = slice_end[i];
-  a.tok_adapter = tok_adapter;
-  a.residual = static_cast<const pl::bf16*>(residual);
-  a.res_stride = res_stride;
-  a.y = static_cast<pl::bf16*>(y);
-  a.y_stride = y_stride;
-  if (down_from_x) {
-    a.pro_a = static_cast<const pl::bf16*>(shrink_a);
-    a.pro_a_adapters = n_shrink;
-    n_shrink = 0;  // no shrink rows: the down values stay in the kernel
-  } else {
-    a.shrink_a = static_cast<const pl::bf16*>(shrink_a);
-    a.shrink_out = shrink_out;
-    a.shrink_stride = shrink_stride;
-  }
-  a.n_shrink = n_shrink;
-  a.early_weights = (flags & 1) ? 1 : 0;
+  PlGemvPhase q = {};
+  q.x = x;
+  q.x_stride = x_stride;
+  q.num_tokens = num_tokens;
+  q.k_in = k_in;
+  q.prologue = prologue;
+  q.norm_w = norm_w;
+  q.norm_eps = norm_eps;
+  q.w = w;
+  q.n_out = n_out;
+  q.bias = bias;
+  q.lora_down = lora_down;
+  q.down_stride = down_stride;
+  q.lora_b = lora_b;
+  q.lora_rank = lora_rank;
+  q.lora_scale = lora_scale;
+  q.num_slices = num_slices;
+  if (num_slices > 4) return PL_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < num_slices - 1 && slice_end != nullptr; ++i) q.slice_end[i] = slice_end[i];
+  q.tok_adapter = tok_adapter;
+  q.residual = residual;
+  q.res_stride = res_stride;
+  q.y = y;
+  q.y_stride = y_stride;
+  q.shrink_a = shrink_a;
+  q.n_shrink = n_shrink;
+  q.shrink_out = shrink_out;
+  q.shrink_stride = shrink_stride;
+  q.flags = flags;
+  pl::GemvArgs a;
+  bool skip = false;
+  if (num_slices > 1 && slice_end == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  int32_t st0 = gemv_args_from(q, a, &skip);
+  if (st0 != PL_OK || skip) return st0;
   a.status = status_dev;
+  const bool down_from_x = a.pro_a != nullptr;
+  n_shrink = a.n_shrink;
 
   int sms = pl_host::sm_count();
   if (sms <= 0) sms = 148;
@@ -791,30 +1097,79 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   }
   const int64_t max_ctas = (int64_t)sms * g_gemv_ctas_per_sm;
   const int grid = (int)(tiles < max_ctas ? tiles : max_ctas);
-  // Largest ring that fits: the tuned shape, then shallower / narrower stages.
-  int stages = g_gemv_stages, kc = g_gemv_kc;
+  int stages, kc, smem;
   const int down_floats = a.pro_a != nullptr ? num_tokens * lora_rank : 0;
-  pl::GemvSmem L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc, down_floats);
-  while (L.total > 227 * 1024 && (stages > 2 || kc > 256)) {
-    if (stages > 2) {
-      --stages;
-    } else {
-      kc /= 2;
-      stages = g_gemv_stages;
-    }
-    L = pl::gemv_smem_layout(num_tokens, k_in, stages, kc, down_floats);
-  }
-  if (L.total > 227 * 1024) return PL_ERR_UNSUPPORTED;
+  if (!gemv_ring_shape(num_tokens, k_in, down_floats, &stages, &kc, &smem)) return PL_ERR_UNSUPPORTED;
   a.stages = stages;
   a.kc = kc;
   if (g_gemv_consumers == 8) {
-    int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<8>), L.total);
+    int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<8>), smem);
     if (st != PL_OK) return st;
-    return pl_host::launch_pdl(pl::linear_lora_kernel<8>, dim3(grid), dim3(32 * 9), L.total, stream, a);
+    return pl_host::launch_pdl(pl::linear_lora_kernel<8>, dim3(grid), dim3(32 * 9), smem, stream, a);
   }
-  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<4>), L.total);
+  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<4>), smem);
   if (st != PL_OK) return st;
-  return pl_host::launch_pdl(pl::linear_lora_kernel<4>, dim3(grid), dim3(32 * 5), L.total, stream, a);
+  return pl_host::launch_pdl(pl::linear_lora_kernel<4>, dim3(grid), dim3(32 * 5), smem, stream, a);
+}
+
+extern "C" int32_t pl_linear_lora_chain(const PlGemvPhase* phases, int32_t num_phases, int32_t* grid_barrier,
+                                        int32_t* status_dev, void* stream) {
+  if (num_phases == 0) return PL_OK;
+  if (phases == nullptr || num_phases < 0) return PL_ERR_INVALID_ARGUMENT;
+  if (num_phases > pl::kMaxChainPhases) return PL_ERR_UNSUPPORTED;
+  if (num_phases > 1 && (grid_barrier == nullptr || (reinterpret_cast<uintptr_t>(grid_barrier) & 3)))
+    return PL_ERR_INVALID_ARGUMENT;
+  pl::GemvChainArgs c = {};
+  int n = 0, k_max = 0, down_max = 0, T = -1;
+  for (int p = 0; p < num_phases; ++p) {
+    const PlGemvPhase& q = phases[p];
+    if (q.num_slices > 1 && q.num_slices <= 4) {
+      for (int i = 0; i < q.num_slices - 1; ++i)
+        if (q.slice_end[i] <= 0) return PL_ERR_INVALID_ARGUMENT;
+    }
+    bool skip = false;
+    pl::GemvArgs a;
+    const int32_t st = gemv_args_from(q, a, &skip);
+    if (st != PL_OK) return st;
+    if (skip) continue;
+    if (T < 0) T = a.T;
+    if (a.T != T) return PL_ERR_INVALID_ARGUMENT;  // one token count for the whole chain
+    // lora_down is read through L1: it must not be the shrink output of an earlier phase
+    for (int e = 0; e < n && a.lora_down != nullptr; ++e) {
+      const pl::GemvArgs& b = c.ph[e];
+      if (b.shrink_out != nullptr && a.lora_down >= b.shrink_out &&
+          a.lora_down < b.shrink_out + (int64_t)(b.T - 1) * b.shrink_stride + b.n_shrink)
+        return PL_ERR_UNSUPPORTED;
+    }
+    a.status = status_dev;
+    a.coherent = 1;
+    a.early_weights = 1;  // the producer streams every phase's weights without an upstream wait
+    if (a.K > k_max) k_max = a.K;
+    const int df = a.pro_a != nullptr ? a.T * a.rank : 0;
+    if (df > down_max) down_max = df;
+    c.ph[n++] = a;
+  }
+  if (n == 0) return PL_OK;
+  int stages, kc, smem;
+  if (!gemv_ring_shape(T, k_max, down_max, &stages, &kc, &smem)) return PL_ERR_UNSUPPORTED;
+  for (int p = 0; p < n; ++p) {
+    c.ph[p].stages = stages;
+    c.ph[p].kc = kc;
+  }
+  c.num_phases = n;
+  c.stages = stages;
+  c.kc = kc;
+  c.k_max = k_max;
+  c.down_max = down_max;
+  c.barrier = grid_barrier;
+  c.status = status_dev;
+  if (n > 1 && grid_barrier == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  // One CTA per SM: every CTA is resident at once (the grid barrier relies on it).
+  int sms = pl_host::sm_count();
+  if (sms <= 0) return PL_ERR_NO_DEVICE;
+  int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_chain_kernel<8>), smem);
+  if (st != PL_OK) return st;
+  return pl_host::launch_pdl(pl::linear_chain_kernel<8>, dim3(sms), dim3(32 * 9), smem, stream, c);
 }
 
 extern "C" int32_t pl_linear_set_tuning(int32_t mode, int32_t stages, int32_t cols_per_stage,

@@ -15,7 +15,9 @@ this package's kernels, five launches per layer:
   5. linear_lora_fused   SiLU-and-mul -> W_down with the residual in the epilogue
 
 plus page-table advance + embedding in front and the final norm + lm_head +
-argmax behind.  The page table lives on the device and is advanced inside
+argmax behind.  With ``chain_projections`` launches 3-5 and the next
+layer's launch 1 (or lm_head) run as one persistent launch
+(pl_linear_lora_chain: grid barriers between the projections).  The page table lives on the device and is advanced inside
 the step, so one captured CUDA graph serves every context length (the
 reference recaptures whenever the page count changes, cuda_graph.py:90).
 Consecutive kernels use programmatic dependent launch, so each weight
@@ -91,6 +93,13 @@ class DecodeEngine:
         # o projection: the LoRA shrink runs inside the o GEMV's prologue
         # (PL_FLAG_DOWN_FROM_X); False keeps the separate pl_lora_shrink_seg launch
         self.fold_o_shrink = True
+        # True: o -> gate_up -> down -> next q/k/v (or lm_head) as one
+        # persistent launch (pl_linear_lora_chain, 2 launches per layer
+        # instead of 5).  Off by default: inside the CUDA graph the chain's
+        # grid barriers cost more than the programmatic launch boundaries
+        # they replace (config 2: 3.57 vs 3.37 ms per step); it pays where
+        # launches are issued one by one from the host.
+        self.chain_projections = False
         dev, bf = self.device, torch.bfloat16
         H, D = spec.hidden, spec.head_dim
 
@@ -159,6 +168,7 @@ class DecodeEngine:
         self.slot_off = torch.zeros(1, **i32)
         self.positions = torch.zeros(1, **i32)
         self.status = torch.zeros(1, **i32)
+        self.chain_barrier = torch.zeros(1, **i32)  # grid barrier of the chained projections
         self.seg_indptr = torch.tensor([0, 1], **i32)
         self.seg_adapter = torch.zeros(1, **i32)
         self.token_buf = torch.zeros(1, device=dev, dtype=torch.int64)
@@ -299,11 +309,33 @@ class DecodeEngine:
         K.rope_cos_sin(self.positions, s.head_dim, s.rope_theta, out=self.rope_cs)
         K.embed(self.token_buf, self.embed, self.x, st)
         attn2d = self.attn.view(1, s.q_dim)
+
+        def qkv_phase(L: LayerWeights) -> tuple:
+            return (self.x, L.w_qkv, dict(prologue=PL_PROLOGUE_RMSNORM, norm_weight=L.input_norm,
+                                          norm_eps=s.rms_eps, out=self.qkv, shrink_a=L.a_qkv,
+                                          shrink_out=self.down_qkv if L.a_qkv is not None else None,
+                                          weights_static=True))
+
+        def o_phase(L: LayerWeights) -> tuple:
+            if self.fold_o_shrink and L.a_o is not None:
+                # the o GEMV computes attn . A_o^T in its prologue: no shrink launch
+                return (attn2d, L.w_o, dict(lora_a=L.a_o, lora_b=L.b_o, lora_scale=self.lora_scale,
+                                            residual=self.x, out=self.x, weights_static=True))
+            return (attn2d, L.w_o, dict(lora_down=self.down_o if L.b_o is not None else None, lora_b=L.b_o,
+                                        lora_scale=self.lora_scale, residual=self.x, out=self.x,
+                                        weights_static=True))
+
+        def mlp_phases(L: LayerWeights) -> list:
+            return [(self.x, L.w_gate_up, dict(prologue=PL_PROLOGUE_RMSNORM, norm_weight=L.post_norm,
+                                               norm_eps=s.rms_eps, out=self.gate_up, weights_static=True)),
+                    (self.gate_up, L.w_down, dict(prologue=PL_PROLOGUE_SILU_MUL, residual=self.x, out=self.x,
+                                                  weights_static=True))]
+
+        head = (self.x, self.lm_head, dict(prologue=PL_PROLOGUE_RMSNORM, norm_weight=self.final_norm,
+                                           norm_eps=s.rms_eps, out=self.logits, weights_static=True))
+        x0, w0, kw0 = qkv_phase(self.layers[0])
+        K.linear_lora_fused(x0, w0, status=st, **kw0)
         for li, L in enumerate(self.layers):
-            K.linear_lora_fused(self.x, L.w_qkv, prologue=PL_PROLOGUE_RMSNORM, norm_weight=L.input_norm,
-                                norm_eps=s.rms_eps, out=self.qkv, shrink_a=L.a_qkv,
-                                shrink_out=self.down_qkv if L.a_qkv is not None else None, weights_static=True,
-                                status=st)
             # q/k head norm + RoPE + KV append + paged decode: one launch
             K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len,
                                num_qo_heads=s.num_qo_heads, num_kv_heads=s.num_kv_heads, positions=self.positions,
@@ -312,27 +344,21 @@ class DecodeEngine:
                                lora_down=self.down_qkv if L.b_qkv is not None else None, lora_b=L.b_qkv,
                                lora_scale=self.qkv_lora_scale, q_norm_weight=L.q_norm, k_norm_weight=L.k_norm,
                                norm_eps=s.rms_eps, out=self.attn, status=st, rope_cos_sin=self.rope_cs)
-            if self.fold_o_shrink and L.a_o is not None:
-                # the o GEMV computes attn . A_o^T in its prologue: no shrink launch
-                K.linear_lora_fused(attn2d, L.w_o, lora_a=L.a_o, lora_b=L.b_o, lora_scale=self.lora_scale,
-                                    residual=self.x, out=self.x, weights_static=True, status=st)
+            if not (self.fold_o_shrink and L.a_o is not None) and L.a_o is not None:
+                K.lora_shrink_seg(attn2d, L.a_o, self.seg_indptr, self.seg_adapter, out=self.down_o)
+            nxt = qkv_phase(self.layers[li + 1]) if li + 1 < len(self.layers) else head
+            phases = [o_phase(L)] + mlp_phases(L) + [nxt]
+            if self.chain_projections:
+                K.linear_lora_chain(phases, grid_barrier=self.chain_barrier, status=st)
             else:
-                if L.a_o is not None:
-                    K.lora_shrink_seg(attn2d, L.a_o, self.seg_indptr, self.seg_adapter, out=self.down_o)
-                K.linear_lora_fused(attn2d, L.w_o, lora_down=self.down_o if L.b_o is not None else None,
-                                    lora_b=L.b_o, lora_scale=self.lora_scale, residual=self.x, out=self.x,
-                                    weights_static=True, status=st)
-            K.linear_lora_fused(self.x, L.w_gate_up, prologue=PL_PROLOGUE_RMSNORM, norm_weight=L.post_norm,
-                                norm_eps=s.rms_eps, out=self.gate_up, weights_static=True, status=st)
-            K.linear_lora_fused(self.gate_up, L.w_down, prologue=PL_PROLOGUE_SILU_MUL, residual=self.x,
-                                out=self.x, weights_static=True, status=st)
-        K.linear_lora_fused(self.x, self.lm_head, prologue=PL_PROLOGUE_RMSNORM, norm_weight=self.final_norm,
-                            norm_eps=s.rms_eps, out=self.logits, weights_static=True, status=st)
+                for x_, w_, kw_ in phases:
+                    K.linear_lora_fused(x_, w_, status=st, **kw_)
         K.argmax(self.logits, self.token_buf, self.argmax_ws)
 
     def launches_per_step(self) -> int:
-        per_layer = 5 + sum(1 for L in self.layers[:1] if L.a_o is not None and not self.fold_o_shrink)
-        return 3 + per_layer * len(self.layers) + 2
+        shrink = sum(1 for L in self.layers[:1] if L.a_o is not None and not self.fold_o_shrink)
+        per_layer = 1 + shrink + (1 if self.chain_projections else 4)
+        return 3 + 1 + per_layer * len(self.layers) + 1
 
     def capture(self) -> None:
         """Capture one decode step into a CUDA graph (after an eager warm-up

@@ -349,7 +349,7 @@ def lora_shrink_seg(x: torch.Tensor, a_stack: torch.Tensor, seg_indptr: torch.Te
     return out
 
 
-def linear_lora_fused(
+def _gemv_phase(
     x: torch.Tensor,
     weight: torch.Tensor,
     *,
@@ -368,17 +368,10 @@ def linear_lora_fused(
     shrink_out: torch.Tensor | None = None,
     lora_a: torch.Tensor | None = None,
     weights_static: bool = False,
-    status: torch.Tensor | None = None,
-) -> torch.Tensor:
-    """y = x . W^T (+bias) (+ LoRA expand) (+ residual) for <= 8 tokens.
-
-    ``x`` is [T, K] (or [T, 2K] for the SiLU-and-mul prologue), ``weight``
-    [N, K], ``lora_b`` [n_adapters, N, rank] with scale folded in,
-    ``lora_down`` [T, >= num_slices*rank] fp32, ``shrink_a`` [n_shrink, K]
-    whose fp32 products go to ``shrink_out`` [T, n_shrink].  With ``lora_a``
-    [n_adapters, rank, K] instead of ``lora_down`` the kernel computes the
-    down values x . A^T itself (PL_FLAG_DOWN_FROM_X; one LoRA slice).
-    """
+) -> tuple[_capi.GemvPhase, torch.Tensor | None, list]:
+    """Checks one fused projection and packs it as a PlGemvPhase; returns the
+    phase, the output tensor and the tensors it created (kept alive by the
+    caller until the launch is enqueued)."""
 
     _need_cuda(x, weight)
     _need(x, torch.bfloat16, "x")
@@ -387,18 +380,18 @@ def linear_lora_fused(
         raise ValueError("weight must be contiguous [out, in]")
     t = x.shape[0]
     n, k = weight.shape
+    keep = []
     if out is None and n > 0:
         out = torch.empty(t, n, dtype=torch.bfloat16, device=x.device)
     rank = 0
     num_slices = 1
-    slice_ptr, slice_keepalive = None, None
     if lora_b is not None:
         if lora_b.dim() == 2:
             lora_b = lora_b.unsqueeze(0)
         rank = lora_b.shape[-1]
         num_slices = len(slice_ends) + 1 if slice_ends else 1
-        if slice_ends:
-            slice_ptr, slice_keepalive = ctypes_int32_array(slice_ends)
+        if num_slices > 4:
+            raise ValueError("at most 4 LoRA slices")
     flags = _capi.PL_FLAG_WEIGHTS_STATIC if weights_static else 0
     if lora_a is not None:
         if shrink_a is not None or lora_down is not None or lora_b is None or slice_ends:
@@ -411,16 +404,86 @@ def linear_lora_fused(
     n_shrink = 0 if shrink_a is None else shrink_a.shape[0]
     if shrink_a is not None and shrink_out is None and lora_a is None:
         shrink_out = torch.empty(t, n_shrink, dtype=torch.float32, device=x.device)
-    call("pl_linear_lora_expand_fused", ptr(x), _row_stride(x, "x"), int(t), int(k), int(prologue),
-         ptr(norm_weight), float(norm_eps), ptr(weight), int(n), ptr(bias), ptr(lora_down),
-         0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
-         float(lora_scale), slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
-         0 if residual is None else _row_stride(residual, "residual"), ptr(out),
-         0 if out is None else _row_stride(out, "out"), ptr(shrink_a), int(n_shrink), ptr(shrink_out),
-         0 if shrink_out is None else _row_stride(shrink_out, "shrink_out"), int(flags), ptr(status),
-         stream_handle())
-    del slice_keepalive
+    keep += [out, shrink_out, lora_b, lora_a]
+    ph = _capi.GemvPhase()
+    ph.x, ph.x_stride, ph.num_tokens, ph.k_in, ph.prologue = ptr(x), _row_stride(x, "x"), int(t), int(k), int(prologue)
+    ph.norm_w, ph.norm_eps, ph.w, ph.n_out, ph.bias = ptr(norm_weight), float(norm_eps), ptr(weight), int(n), ptr(bias)
+    ph.lora_down = ptr(lora_down)
+    ph.down_stride = 0 if lora_down is None else _row_stride(lora_down, "lora_down")
+    ph.lora_b, ph.lora_rank, ph.lora_scale = ptr(lora_b), int(rank), float(lora_scale)
+    for i, e in enumerate(slice_ends if lora_b is not None else ()):
+        ph.slice_end[i] = int(e)
+    ph.num_slices = int(num_slices)
+    ph.tok_adapter, ph.residual = ptr(tok_adapter), ptr(residual)
+    ph.res_stride = 0 if residual is None else _row_stride(residual, "residual")
+    ph.y, ph.y_stride = ptr(out), 0 if out is None else _row_stride(out, "out")
+    ph.shrink_a, ph.n_shrink, ph.shrink_out = ptr(shrink_a), int(n_shrink), ptr(shrink_out)
+    ph.shrink_stride = 0 if shrink_out is None else _row_stride(shrink_out, "shrink_out")
+    ph.flags = int(flags)
+    return ph, out, keep
+
+
+def linear_lora_fused(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    *,
+    status: torch.Tensor | None = None,
+    **kw,
+) -> torch.Tensor:
+    """y = x . W^T (+bias) (+ LoRA expand) (+ residual) for <= 8 tokens.
+
+    ``x`` is [T, K] (or [T, 2K] for the SiLU-and-mul prologue), ``weight``
+    [N, K], ``lora_b`` [n_adapters, N, rank] with scale folded in,
+    ``lora_down`` [T, >= num_slices*rank] fp32, ``shrink_a`` [n_shrink, K]
+    whose fp32 products go to ``shrink_out`` [T, n_shrink].  With ``lora_a``
+    [n_adapters, rank, K] instead of ``lora_down`` the kernel computes the
+    down values x . A^T itself (PL_FLAG_DOWN_FROM_X; one LoRA slice).
+    Keywords: bias, prologue, norm_weight, norm_eps, lora_down, lora_b,
+    lora_scale, slice_ends, tok_adapter, residual, out, shrink_a, shrink_out,
+    lora_a, weights_static.
+    """
+
+    ph, out, keep = _gemv_phase(x, weight, **kw)
+    slice_ptr, slice_keepalive = None, None
+    if ph.num_slices > 1:
+        slice_ptr, slice_keepalive = ctypes_int32_array(list(ph.slice_end)[: ph.num_slices - 1])
+    call("pl_linear_lora_expand_fused", ph.x, ph.x_stride, ph.num_tokens, ph.k_in, ph.prologue, ph.norm_w,
+         ph.norm_eps, ph.w, ph.n_out, ph.bias, ph.lora_down, ph.down_stride, ph.lora_b, ph.lora_rank,
+         ph.lora_scale, slice_ptr, ph.num_slices, ph.tok_adapter, ph.residual, ph.res_stride, ph.y, ph.y_stride,
+         ph.shrink_a, ph.n_shrink, ph.shrink_out, ph.shrink_stride, ph.flags, ptr(status), stream_handle())
+    del slice_keepalive, keep
     return out
+
+
+CHAIN_MAX_PHASES = 6
+
+
+def linear_lora_chain(phases: list[tuple[torch.Tensor, torch.Tensor, dict]], *, grid_barrier: torch.Tensor | None,
+                      status: torch.Tensor | None = None) -> list[torch.Tensor | None]:
+    """Consecutive fused projections in one persistent launch
+    (pl_linear_lora_chain).  ``phases`` holds (x, weight, keywords of
+    linear_lora_fused) per projection; a later phase may read an earlier
+    phase's output as its x or residual.  ``grid_barrier``: device int32,
+    zero before the first call (left zero by every call that completes).
+    Returns each phase's output."""
+
+    if not 1 <= len(phases) <= CHAIN_MAX_PHASES:
+        raise ValueError(f"1 to {CHAIN_MAX_PHASES} phases")
+    if grid_barrier is not None:
+        _need_cuda(grid_barrier)
+        _need(grid_barrier, torch.int32, "grid_barrier")
+    elif len(phases) > 1:
+        raise ValueError("grid_barrier is required for more than one phase")
+    arr = (_capi.GemvPhase * len(phases))()
+    outs, keep = [], []
+    for i, (x, w, kw) in enumerate(phases):
+        ph, out, kp = _gemv_phase(x, w, **kw)
+        arr[i] = ph
+        outs.append(out)
+        keep += kp
+    call("pl_linear_lora_chain", arr, len(phases), ptr(grid_barrier), ptr(status), stream_handle())
+    del keep
+    return outs
 
 
 GEMV_MAX_ROWS = 8

@@ -187,3 +187,33 @@ def test_greedy_tokens_teacher_forced_32_steps(cuda_device, which):
           f"two ulps {max(ulp2):.3e})")
     assert max(err_engine) <= max(max(err_bf16), max(ulp2)), (max(err_engine), max(err_bf16), max(ulp2))
     assert int(eng.status.item()) == 0
+
+
+@pytest.mark.parametrize("which", ["small-qwen3", "config1", "qwen3-8b-4layers"])
+def test_chained_projections_equal_single_launches(cuda_device, which):
+    """The engine's persistent projection chain (o -> gate_up -> down -> next
+    q/k/v or lm_head in one launch, pl_linear_lora_chain) gives bit-identical
+    logits to the same projections launched one by one, eager and replayed
+    from the CUDA graph, and leaves its grid barrier at zero."""
+
+    spec, lspec = _spec(which)
+    eng, _ = _engine(spec, lspec, cuda_device, weights_on_device=which == "qwen3-8b-4layers")
+    eng.chain_projections = True
+    prompt = random_prompt(spec.vocab, 37, seed=5)
+    n_chain = eng.launches_per_step()
+    toks_chain = eng.generate(prompt, 12, use_graph=True)
+    logits_chain = eng.logits.clone()
+    assert int(eng.chain_barrier.item()) == 0
+    eng.chain_projections = False
+    eng.graph = None
+    assert eng.launches_per_step() == n_chain + 3 * spec.num_layers
+    toks_single = eng.generate(prompt, 12, use_graph=True)
+    assert toks_chain == toks_single
+    assert torch.equal(eng.logits, logits_chain)
+    eng.chain_projections = True
+    eng.graph = None
+    toks_eager = eng.generate(prompt, 12, use_graph=False)
+    assert toks_eager == toks_chain
+    assert torch.equal(eng.logits, logits_chain)
+    assert int(eng.chain_barrier.item()) == 0
+    assert int(eng.status.item()) == 0

@@ -630,6 +630,69 @@ def test_linear_lora_fused_large_shapes(K, gemv_tuning):
         assert bool(torch.all(torch.abs(y.double() - ref) <= tol))
 
 
+@pytest.mark.parametrize("t", [1, 3, 8])
+def test_linear_lora_chain_equals_single_launches(K, t):
+    """pl_linear_lora_chain: five dependent projections (LoRA down from x +
+    residual in place, RMSNorm, SiLU-and-mul + residual, RMSNorm + bias +
+    sliced LoRA + shrink rows, plain) in one persistent launch give the same
+    bits as the same projections launched one by one (each of which is held
+    to the oracle above), and the grid barrier is back at zero."""
+
+    g = torch.Generator(device="cuda").manual_seed(40 + t)
+
+    def rnd(*shape, s=1.0):
+        return (torch.randn(*shape, generator=g, device="cuda") * s).bfloat16()
+
+    H, Q, I, N4, r = 768, 512, 1024, 640, 16
+    attn, x0 = rnd(t, Q), rnd(t, H)
+    w_o, a_o, b_o = rnd(H, Q, s=0.03), rnd(2, r, Q, s=0.03), rnd(2, H, r, s=0.05)
+    w_gu, n1 = rnd(2 * I, H, s=0.03), (1 + 0.1 * torch.randn(H, generator=g, device="cuda")).bfloat16()
+    w_dn = rnd(H, I, s=0.03)
+    w_4, n2, bias4 = rnd(N4, H, s=0.03), (1 + 0.1 * torch.randn(H, generator=g, device="cuda")).bfloat16(), rnd(N4)
+    a_4 = rnd(48, H, s=0.03)
+    b_4, down4 = rnd(3, N4, r, s=0.05), torch.randn(t, 3 * r, generator=g, device="cuda")
+    w_5 = rnd(300, N4, s=0.03)
+    tok_ad = torch.tensor([(i % 3) - 1 for i in range(t)], dtype=torch.int32, device="cuda")
+    tok_ad[0] = 1
+
+    def phases(x, gu, y4, sh4, y5):
+        return [
+            (attn, w_o, dict(lora_a=a_o, lora_b=b_o, lora_scale=0.5, tok_adapter=tok_ad.clamp(max=1),
+                             residual=x, out=x, weights_static=True)),
+            (x, w_gu, dict(prologue=1, norm_weight=n1, norm_eps=1e-6, out=gu, weights_static=True)),
+            (gu, w_dn, dict(prologue=2, residual=x, out=x, weights_static=True)),
+            (x, w_4, dict(prologue=1, norm_weight=n2, norm_eps=1e-6, bias=bias4, lora_down=down4, lora_b=b_4,
+                          slice_ends=(200, 420), tok_adapter=tok_ad, out=y4, shrink_a=a_4, shrink_out=sh4,
+                          weights_static=True)),
+            (y4, w_5, dict(out=y5, weights_static=True)),
+        ]
+
+    def bufs():
+        return (x0.clone(), torch.empty(t, 2 * I, dtype=torch.bfloat16, device="cuda"),
+                torch.empty(t, N4, dtype=torch.bfloat16, device="cuda"),
+                torch.empty(t, 48, dtype=torch.float32, device="cuda"),
+                torch.empty(t, 300, dtype=torch.bfloat16, device="cuda"))
+
+    ref = bufs()
+    for x_, w_, kw in phases(*ref):
+        K.linear_lora_fused(x_, w_, **kw)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    barrier = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for _ in range(2):  # the second call reuses the barrier the first one reset
+        got = bufs()
+        K.linear_lora_chain(phases(*got), grid_barrier=barrier, status=status)
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)
+        assert int(barrier.item()) == 0 and int(status.item()) == 0
+    # one phase: no barrier needed
+    one = bufs()
+    K.linear_lora_chain(phases(*one)[1:2], grid_barrier=None, status=status)
+    y_gu = K.linear_lora_fused(x0, w_gu, prologue=1, norm_weight=n1, norm_eps=1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(one[1], y_gu)
+
+
 def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
     """fp64 restatement of the multi-token LoRA linear epilogue (per-token adapter)."""
 
