@@ -494,6 +494,38 @@ typedef struct PlGemvPhase {
 } PlGemvPhase;
 
 /*
+ * The projection that the next pl_linear_lora_phase call on the stream will
+ * run: its weight rows (w [n_out, k_in], then shrink_a [n_shrink, k_in]),
+ * its token count, and how many of its first ring stages (16 rows x up to
+ * 2048 columns each) every CTA should find in L2.
+ */
+typedef struct PlGemvPrefetch {
+  const void *w;
+  int32_t n_out;
+  const void *shrink_a;
+  int32_t n_shrink;
+  int32_t k_in;
+  int32_t num_tokens;
+  int32_t units;
+} PlGemvPrefetch;
+
+/*
+ * pl_linear_lora_expand_fused with its arguments in a PlGemvPhase, plus an
+ * optional hand-over to the next projection: once a CTA has issued the
+ * copies of its own weight rows, it asks for the first `next->units` ring
+ * stages that the same CTA of the `next` launch will read to be fetched into
+ * L2 (no destination, no wait).  The next launch's first stages then arrive
+ * from L2 while DRAM is still busy with this launch's last rows.  next may
+ * be NULL (or units 0): no prefetch.  No reference counterpart: a schedule
+ * of this build for the o_proj / mlp / qkv_proj sequence of
+ * model/flashinfer/layer_runner.py:283-396.  The next launch is expected to
+ * have the same number of CTAs per SM (pl_linear_set_tuning).
+ */
+int32_t pl_linear_lora_phase(const PlGemvPhase *phase,
+                             const PlGemvPrefetch *next, int32_t *status_dev,
+                             void *stream);
+
+/*
  * Consecutive projections of one decoder layer in ONE launch, each with the
  * semantics and rounding of pl_linear_lora_expand_fused, e.g. o (LoRA
  * expand + residual) -> gate_up (RMSNorm) -> down (SiLU-and-mul + residual)

@@ -65,6 +65,13 @@ class GemvPhase(Structure):
                 ("shrink_stride", c_int64), ("flags", c_int32)]
 
 
+class GemvPrefetch(Structure):
+    """PlGemvPrefetch: the next projection of pl_linear_lora_phase's L2 hand-over."""
+
+    _fields_ = [("w", c_void_p), ("n_out", c_int32), ("shrink_a", c_void_p), ("n_shrink", c_int32),
+                ("k_in", c_int32), ("num_tokens", c_int32), ("units", c_int32)]
+
+
 _P = c_void_p
 _I32 = c_int32
 _I64 = c_int64
@@ -121,6 +128,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _I64, _P, _I32, _P, _I64, _I32, _P, _P],
     ),
     "pl_linear_lora_chain": (_I32, [POINTER(GemvPhase), _I32, _P, _P, _P]),
+    "pl_linear_lora_phase": (_I32, [POINTER(GemvPhase), POINTER(GemvPrefetch), _P, _P]),
     "pl_linear_set_tuning": (_I32, [_I32, _I32, _I32, _I32, _I32]),
     "pl_linear_set_l2_prefetch": (_I32, [_I64]),
     "pl_linear_gemm_plan": (_I32, [_I32, _I32, _I32, _I32, POINTER(GemmPlan)]),

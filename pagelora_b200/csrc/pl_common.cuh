@@ -146,6 +146,12 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return pol;
 }
 
+// Pull `bytes` (a multiple of 16, src 16-byte aligned) into L2 without a
+// destination: the bulk-copy engine fetches them while the SM goes on.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar`.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,

@@ -300,6 +300,10 @@ __global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(con
     }
     named_barrier(1, 32 * kConsumerWarps);
     if (ctid == 0 && kvh == 0) PL_TRACE_POINT(9);
+    // Every CTA of the cluster has started (the merge pushes into their
+    // shared memory): waited for here, while the first pages are in flight,
+    // rather than at the merge.
+    if (args.cluster) cluster_wait();
 
     uint32_t qa[D / 16][4];
 #pragma unroll
@@ -477,7 +481,6 @@ __global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(con
     if (ctid == 0 && kvh == 0) PL_TRACE_POINT(8);
 
     const bool single = args.num_splits == 1;
-    if (args.cluster) cluster_wait();  // every CTA of the cluster has started
     // One float4 chunk (row r, columns d..d+3) per thread and pass: combine
     // the consumer warps' states, then write the output (one split), push
     // the chunk to the CTA of the cluster that reduces it, or leave it in

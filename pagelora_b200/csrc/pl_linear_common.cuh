@@ -43,6 +43,12 @@ struct GemvArgs {
   int32_t kc;             // columns per stage (multiple of 16)
   int32_t prefetch_tiles; // tiles per CTA whose weights are pulled into L2 before the dependency resolves
   int32_t* status;
+  // L2 prefetch of the next projection's first ring stages (pl_linear_lora_phase): weight rows
+  // [n_out) from pf_w, rows past it from pf_shrink, split over pf_grid CTAs as that launch splits them
+  const bf16* pf_w;
+  const bf16* pf_shrink;
+  int64_t pf_rows_total;
+  int32_t pf_n_out, pf_k, pf_kc, pf_units, pf_grid;
   int32_t coherent;       // activations / residual may have been written by other CTAs of this launch: read them
                           // from L2 (ld.global.cg), never from a possibly stale L1 line
 };

@@ -359,6 +359,27 @@ __device__ __forceinline__ void gemv_drain(const GemvRing& R, int issued) {
     (void)mbar_wait(&R.full_bar[u % R.S], (u / R.S) & 1);
 }
 
+// After this CTA's own copies: pull into L2 the first pf_units ring units
+// (16 rows x pf_kc columns each) that CTA blockIdx.x of the NEXT projection
+// will load, so that launch's first stages come from L2 instead of DRAM.
+__device__ __forceinline__ void gemv_prefetch_next(const GemvArgs& a, int lane) {
+  if (a.pf_units <= 0 || (int)blockIdx.x >= a.pf_grid) return;
+  const int64_t r0 = a.pf_rows_total * blockIdx.x / a.pf_grid;
+  const int64_t r1 = a.pf_rows_total * (blockIdx.x + 1) / a.pf_grid;
+  const int n_kc = (a.pf_k + a.pf_kc - 1) / a.pf_kc;
+  for (int u = 0; u < a.pf_units; ++u) {
+    const int64_t row0 = r0 + (int64_t)(u / n_kc) * kTileRows;
+    if (row0 >= r1) break;
+    const int k0 = (u % n_kc) * a.pf_kc;
+    const int kw = min(a.pf_kc, a.pf_k - k0);
+    const int64_t row = row0 + lane;
+    if (lane < kTileRows && row < r1) {
+      const bf16* src = row < a.pf_n_out ? a.pf_w + row * a.pf_k : a.pf_shrink + (row - a.pf_n_out) * a.pf_k;
+      bulk_prefetch_l2(src + k0, (uint32_t)kw * 2);
+    }
+  }
+}
+
 // Consumer warps: multiply the ring units u_base, ... (weight rows [r0, r1)
 // of one projection) against the staged activations with mma.sync
 // m16n8k16 (weight rows = M, tokens = N); the warps split the k-steps of
@@ -493,6 +514,7 @@ __global__ void __launch_bounds__(32 * (1 + NCW), 1) linear_lora_kernel(const Ge
     // --------------------------------------------------------- producer warp
     if (!a.early_weights) pdl_wait();
     const int issued = gemv_produce(a, R, r0, r1, 0, l2_evict_first_policy(), lane);
+    if (!*R.abort_flag) gemv_prefetch_next(a, lane);
     if (lane == 0) PL_TRACE_POINT(3);
     if (lane == 0 && *R.abort_flag) gemv_drain(R, issued);
     return;
@@ -1022,6 +1044,10 @@ bool gemv_ring_shape(int T, int k_max, int down_floats, int* stages_out, int* kc
 }
 }  // namespace
 
+namespace {
+int32_t launch_gemv_phase(const PlGemvPhase& q, const PlGemvPrefetch* next, int32_t* status_dev, void* stream);
+}  // namespace
+
 extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
                                                int32_t prologue, const void* norm_w, float norm_eps, const void* w,
                                                int32_t n_out, const void* bias, const float* lora_down,
@@ -1061,14 +1087,20 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   q.shrink_out = shrink_out;
   q.shrink_stride = shrink_stride;
   q.flags = flags;
+  if (num_slices > 1 && slice_end == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  return launch_gemv_phase(q, nullptr, status_dev, stream);
+}
+
+namespace {
+int32_t launch_gemv_phase(const PlGemvPhase& q, const PlGemvPrefetch* next, int32_t* status_dev, void* stream) {
   pl::GemvArgs a;
   bool skip = false;
-  if (num_slices > 1 && slice_end == nullptr) return PL_ERR_INVALID_ARGUMENT;
   int32_t st0 = gemv_args_from(q, a, &skip);
   if (st0 != PL_OK || skip) return st0;
   a.status = status_dev;
   const bool down_from_x = a.pro_a != nullptr;
-  n_shrink = a.n_shrink;
+  const int32_t num_tokens = q.num_tokens, k_in = q.k_in, n_out = q.n_out, lora_rank = q.lora_rank;
+  const int32_t n_shrink = a.n_shrink;
 
   int sms = pl_host::sm_count();
   if (sms <= 0) sms = 148;
@@ -1102,6 +1134,22 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   if (!gemv_ring_shape(num_tokens, k_in, down_floats, &stages, &kc, &smem)) return PL_ERR_UNSUPPORTED;
   a.stages = stages;
   a.kc = kc;
+  if (next != nullptr && next->units > 0) {
+    // the next launch's split: its grid and ring shape, as it will compute them
+    const int64_t n_rows = (int64_t)next->n_out + next->n_shrink;
+    const int64_t n_tiles = (n_rows + pl::kTileRows - 1) / pl::kTileRows;
+    int n_stages, n_kc, n_smem;
+    if (n_rows > 0 && gemv_ring_shape(next->num_tokens, next->k_in, 0, &n_stages, &n_kc, &n_smem)) {
+      a.pf_w = static_cast<const pl::bf16*>(next->w);
+      a.pf_shrink = static_cast<const pl::bf16*>(next->shrink_a);
+      a.pf_rows_total = n_rows;
+      a.pf_n_out = next->n_out;
+      a.pf_k = next->k_in;
+      a.pf_kc = n_kc;
+      a.pf_units = next->units;
+      a.pf_grid = (int)(n_tiles < max_ctas ? n_tiles : max_ctas);
+    }
+  }
   if (g_gemv_consumers == 8) {
     int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<8>), smem);
     if (st != PL_OK) return st;
@@ -1110,6 +1158,23 @@ extern "C" int32_t pl_linear_lora_expand_fused(const void* x, int64_t x_stride, 
   int32_t st = pl_host::ensure_smem_attr(reinterpret_cast<const void*>(pl::linear_lora_kernel<4>), smem);
   if (st != PL_OK) return st;
   return pl_host::launch_pdl(pl::linear_lora_kernel<4>, dim3(grid), dim3(32 * 5), smem, stream, a);
+}
+
+}  // namespace
+
+extern "C" int32_t pl_linear_lora_phase(const PlGemvPhase* phase, const PlGemvPrefetch* next, int32_t* status_dev,
+                                        void* stream) {
+  if (phase == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  if (phase->num_slices > 4) return PL_ERR_INVALID_ARGUMENT;
+  if (next != nullptr && next->units != 0) {
+    if (next->units < 0 || next->units > 64 || next->w == nullptr || next->n_out < 0 || next->n_shrink < 0 ||
+        (next->n_shrink > 0 && next->shrink_a == nullptr) || next->k_in <= 0 || next->num_tokens < 1 ||
+        next->num_tokens > pl::kMaxTok || (reinterpret_cast<uintptr_t>(next->w) & 15) ||
+        (reinterpret_cast<uintptr_t>(next->shrink_a) & 15))
+      return PL_ERR_INVALID_ARGUMENT;
+    if (next->k_in % 16) return PL_ERR_UNSUPPORTED;
+  }
+  return launch_gemv_phase(*phase, next, status_dev, stream);
 }
 
 extern "C" int32_t pl_linear_lora_chain(const PlGemvPhase* phases, int32_t num_phases, int32_t* grid_barrier,

@@ -74,17 +74,37 @@ __device__ __forceinline__ void qkv_head_transform(const QkvHeadArgs& a, int t, 
   const bool lora = a.down != nullptr && a.lora_b != nullptr;
   const bf16* nw = kind == 0 ? a.q_norm_w : (kind == 1 ? a.k_norm_w : nullptr);
   // independent loads first: the projection row, the position, the adapter
-  // id, the norm weights
+  // id, the norm weights, the RoPE (cos, sin) pairs of the step's table
   {
     const bf16* src = a.qkv + (int64_t)t * a.qkv_stride + col + d0;
+    if constexpr (E == 4) {
+      if ((reinterpret_cast<uintptr_t>(src) & 7) == 0) {
+        const uint2 u = *reinterpret_cast<const uint2*>(src);
+        const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+        v[0] = f0.x;
+        v[1] = f0.y;
+        v[2] = f1.x;
+        v[3] = f1.y;
+      } else {
 #pragma unroll
-    for (int e = 0; e < E; ++e) v[e] = bf2f(src[e]);
+        for (int e = 0; e < E; ++e) v[e] = bf2f(src[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = bf2f(src[e]);
+    }
   }
   const float pos = (kind < 2 && a.rope_cs == nullptr) ? (float)a.positions[t] : 0.f;
   const int ad = (lora && a.tok_adapter != nullptr) ? a.tok_adapter[t] : 0;
   float wn[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) wn[e] = nw != nullptr ? bf2f(nw[d0 + e]) : 1.f;
+  float csn[2 * E];  // (cos, sin) of the E rotation angles of this lane
+  if (kind < 2 && a.rope_cs != nullptr) {
+    const float* src = a.rope_cs + ((int64_t)t * (D / 2) + d0 % (D / 2)) * 2;
+#pragma unroll
+    for (int e = 0; e < 2 * E; e += 4) *reinterpret_cast<float4*>(csn + e) = *reinterpret_cast<const float4*>(src + e);
+  }
   if (trace && lane == 0) {
     asm volatile("" ::"f"(v[0]), "f"(pos), "f"(wn[0]), "r"(ad));
     PL_TRACE_POINT(10);
@@ -151,12 +171,7 @@ __device__ __forceinline__ void qkv_head_transform(const QkvHeadArgs& a, int t, 
       PL_TRACE_POINT(15);
     }
     float out[E];
-    float csn[2 * E];  // (cos, sin) of the E rotation angles of this lane
-    if (a.rope_cs != nullptr) {
-      const float* src = a.rope_cs + ((int64_t)t * (D / 2) + d0 % (D / 2)) * 2;
-#pragma unroll
-      for (int e = 0; e < 2 * E; e += 4) *reinterpret_cast<float4*>(csn + e) = *reinterpret_cast<const float4*>(src + e);
-    } else {
+    if (a.rope_cs == nullptr) {
 #pragma unroll
       for (int e = 0; e < E; ++e) rope_angle_cs(pos, (d0 + e) % (D / 2), D, a.theta, csn[2 * e], csn[2 * e + 1]);
     }

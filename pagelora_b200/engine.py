@@ -100,6 +100,10 @@ class DecodeEngine:
         # they replace (config 2: 3.57 vs 3.37 ms per step); it pays where
         # launches are issued one by one from the host.
         self.chain_projections = False
+        # every projection launch pulls the first two ring stages of the next
+        # projection's rows (same CTA) into L2 once its own copies are issued
+        # (pl_linear_lora_phase); 0 turns the hand-over off
+        self.l2_handover_units = 2
         dev, bf = self.device, torch.bfloat16
         H, D = spec.hidden, spec.head_dim
 
@@ -333,8 +337,18 @@ class DecodeEngine:
 
         head = (self.x, self.lm_head, dict(prologue=PL_PROLOGUE_RMSNORM, norm_weight=self.final_norm,
                                            norm_eps=s.rms_eps, out=self.logits, weights_static=True))
-        x0, w0, kw0 = qkv_phase(self.layers[0])
-        K.linear_lora_fused(x0, w0, status=st, **kw0)
+        # every projection of the step in launch order (attention in between)
+        proj = [qkv_phase(self.layers[0])]
+        for li, L in enumerate(self.layers):
+            proj += [o_phase(L)] + mlp_phases(L) + [qkv_phase(self.layers[li + 1]) if li + 1 < len(self.layers)
+                                                    else head]
+
+        def launch(i: int) -> None:
+            x_, w_, kw_ = proj[i]
+            nxt = proj[i + 1] if i + 1 < len(proj) and self.l2_handover_units > 0 else None
+            K.linear_lora_fused(x_, w_, status=st, prefetch_next=nxt, prefetch_units=self.l2_handover_units, **kw_)
+
+        launch(0)
         for li, L in enumerate(self.layers):
             # q/k head norm + RoPE + KV append + paged decode: one launch
             K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len,
@@ -346,13 +360,12 @@ class DecodeEngine:
                                norm_eps=s.rms_eps, out=self.attn, status=st, rope_cos_sin=self.rope_cs)
             if not (self.fold_o_shrink and L.a_o is not None) and L.a_o is not None:
                 K.lora_shrink_seg(attn2d, L.a_o, self.seg_indptr, self.seg_adapter, out=self.down_o)
-            nxt = qkv_phase(self.layers[li + 1]) if li + 1 < len(self.layers) else head
-            phases = [o_phase(L)] + mlp_phases(L) + [nxt]
+            base = 1 + 4 * li
             if self.chain_projections:
-                K.linear_lora_chain(phases, grid_barrier=self.chain_barrier, status=st)
+                K.linear_lora_chain(proj[base:base + 4], grid_barrier=self.chain_barrier, status=st)
             else:
-                for x_, w_, kw_ in phases:
-                    K.linear_lora_fused(x_, w_, status=st, **kw_)
+                for i in range(base, base + 4):
+                    launch(i)
         K.argmax(self.logits, self.token_buf, self.argmax_ws)
 
     def launches_per_step(self) -> int:

@@ -428,6 +428,8 @@ def linear_lora_fused(
     weight: torch.Tensor,
     *,
     status: torch.Tensor | None = None,
+    prefetch_next: tuple | None = None,
+    prefetch_units: int = 1,
     **kw,
 ) -> torch.Tensor:
     """y = x . W^T (+bias) (+ LoRA expand) (+ residual) for <= 8 tokens.
@@ -441,9 +443,27 @@ def linear_lora_fused(
     Keywords: bias, prologue, norm_weight, norm_eps, lora_down, lora_b,
     lora_scale, slice_ends, tok_adapter, residual, out, shrink_a, shrink_out,
     lora_a, weights_static.
+    ``prefetch_next`` = (x, weight, keywords) of the projection launched next
+    on the stream: once a CTA has issued its own weight copies it pulls the
+    first ``prefetch_units`` ring stages of that launch's rows into L2
+    (pl_linear_lora_phase); the results are unchanged.
     """
 
     ph, out, keep = _gemv_phase(x, weight, **kw)
+    if prefetch_next is not None and prefetch_units > 0:
+        import ctypes
+
+        nx, nw, nkw = prefetch_next
+        _need_cuda(nw)
+        n_shrink_a = nkw.get("shrink_a") if nkw.get("lora_a") is None else None
+        pf = _capi.GemvPrefetch()
+        pf.w, pf.n_out, pf.k_in = ptr(nw), int(nw.shape[0]), int(nw.shape[1])
+        pf.shrink_a = ptr(n_shrink_a)
+        pf.n_shrink = 0 if n_shrink_a is None else int(n_shrink_a.shape[0])
+        pf.num_tokens, pf.units = int(nx.shape[0]), int(prefetch_units)
+        call("pl_linear_lora_phase", ctypes.byref(ph), ctypes.byref(pf), ptr(status), stream_handle())
+        del keep
+        return out
     slice_ptr, slice_keepalive = None, None
     if ph.num_slices > 1:
         slice_ptr, slice_keepalive = ctypes_int32_array(list(ph.slice_end)[: ph.num_slices - 1])

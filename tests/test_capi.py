@@ -76,33 +76,37 @@ def test_kernels_refuse_cpu_tensors():
                              torch.zeros(1, dtype=torch.int32), num_splits=1, workspace=None)
 
 
-def test_gemv_phase_struct_matches_the_header(tmp_path):
-    """ctypes GemvPhase has the size and field offsets of the C PlGemvPhase."""
+@pytest.mark.parametrize("struct_name", ["GemvPhase", "GemvPrefetch"])
+def test_gemv_structs_match_the_header(tmp_path, struct_name):
+    """The ctypes GemvPhase / GemvPrefetch have the size and field offsets of
+    the C PlGemvPhase / PlGemvPrefetch."""
 
     import ctypes
     import shutil
     import subprocess
 
-    from pagelora_b200._capi import GemvPhase
+    from pagelora_b200 import _capi
 
     gcc = shutil.which("gcc")
     if gcc is None:
         pytest.skip("gcc not available")
-    fields = [f[0] for f in GemvPhase._fields_]
+    cls = getattr(_capi, struct_name)
+    c_name = "Pl" + struct_name
+    fields = [f[0] for f in cls._fields_]
     src = tmp_path / "layout.c"
     src.write_text(
         '#include <stddef.h>\n#include <stdio.h>\n#include "pagelora_b200.h"\n'
         "int main(void) {\n"
-        '  printf("size %zu\\n", sizeof(PlGemvPhase));\n'
-        + "".join(f'  printf("{f} %zu\\n", offsetof(PlGemvPhase, {f}));\n' for f in fields)
+        f'  printf("size %zu\\n", sizeof({c_name}));\n'
+        + "".join(f'  printf("{f} %zu\\n", offsetof({c_name}, {f}));\n' for f in fields)
         + "  return 0;\n}\n")
     exe = tmp_path / "layout"
     subprocess.run([gcc, "-std=c11", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
     out = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
                                                        text=True).stdout.splitlines())
-    assert int(out["size"]) == ctypes.sizeof(GemvPhase)
+    assert int(out["size"]) == ctypes.sizeof(cls)
     for f in fields:
-        assert int(out[f]) == getattr(GemvPhase, f).offset, f
+        assert int(out[f]) == getattr(cls, f).offset, f
 
 
 def _phase(tokens=1, k=64, n=32, **over):
@@ -140,3 +144,27 @@ def test_linear_lora_chain_host_checks(lib):
     reader = _phase(lora_b=0x70000, lora_rank=16, lora_down=0x60000 + 16 * 4, down_stride=48)
     dep = (GemvPhase * 2)(shrink, reader)
     assert lib.pl_linear_lora_chain(dep, 2, barrier, None, None) == 2
+
+
+def test_linear_lora_phase_host_checks(lib):
+    """Argument errors of pl_linear_lora_phase's hand-over are found on the
+    host, before any device call."""
+
+    import ctypes
+
+    from pagelora_b200._capi import GemvPrefetch
+
+    ph = _phase()
+    def pf(**over):
+        p = GemvPrefetch()
+        p.w, p.n_out, p.k_in, p.num_tokens, p.units = 0x20000, 64, 64, 1, 1
+        for k, v in over.items():
+            setattr(p, k, v)
+        return ctypes.byref(p)
+    assert lib.pl_linear_lora_phase(None, None, None, None) == 1
+    assert lib.pl_linear_lora_phase(ctypes.byref(ph), pf(w=None), None, None) == 1
+    assert lib.pl_linear_lora_phase(ctypes.byref(ph), pf(units=-1), None, None) == 1
+    assert lib.pl_linear_lora_phase(ctypes.byref(ph), pf(num_tokens=9), None, None) == 1
+    assert lib.pl_linear_lora_phase(ctypes.byref(ph), pf(n_shrink=8), None, None) == 1   # rows without a matrix
+    assert lib.pl_linear_lora_phase(ctypes.byref(ph), pf(w=0x20008), None, None) == 1    # misaligned
+    assert lib.pl_linear_lora_phase(ctypes.byref(ph), pf(k_in=40), None, None) == 2      # K % 16

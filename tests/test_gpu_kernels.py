@@ -693,6 +693,30 @@ def test_linear_lora_chain_equals_single_launches(K, t):
     assert torch.equal(one[1], y_gu)
 
 
+@pytest.mark.parametrize("t,units", [(1, 1), (1, 5), (4, 2)])
+def test_linear_lora_fused_l2_handover_same_bits(K, t, units):
+    """pl_linear_lora_phase: the L2 hand-over to the next projection (with
+    shrink rows, and past the end of a CTA's share when `units` is large)
+    leaves this launch's and the next launch's outputs bit-identical."""
+
+    g = torch.Generator(device="cuda").manual_seed(9 + t)
+    x = torch.randn(t, 4096, generator=g, device="cuda").bfloat16()
+    w1 = (torch.randn(4096, 4096, generator=g, device="cuda") * 0.02).bfloat16()
+    w2 = (torch.randn(2000, 4096, generator=g, device="cuda") * 0.02).bfloat16()
+    a2 = (torch.randn(48, 4096, generator=g, device="cuda") * 0.02).bfloat16()
+    nw = (1 + 0.1 * torch.randn(4096, generator=g, device="cuda")).bfloat16()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    nxt_kw = dict(prologue=1, norm_weight=nw, shrink_a=a2, weights_static=True)
+    y_ref = K.linear_lora_fused(x, w1, residual=x, weights_static=True)
+    z_ref = K.linear_lora_fused(y_ref, w2, **nxt_kw)
+    y = K.linear_lora_fused(x, w1, residual=x, weights_static=True, status=status, prefetch_next=(y_ref, w2, nxt_kw),
+                            prefetch_units=units)
+    z = K.linear_lora_fused(y, w2, status=status, **nxt_kw)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(y, y_ref) and torch.equal(z, z_ref)
+
+
 def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
     """fp64 restatement of the multi-token LoRA linear epilogue (per-token adapter)."""
 
