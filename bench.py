@@ -27,7 +27,9 @@ workloads (``--no-extra`` skips them), reported under "workloads":
   config4  Qwen3-8B arch, 16 branches sharing a 2048-token prefix stored
            once (shared-prefix decode), rows sharded over the N ranks;
   config5  Llama-3-8B arch, 8 x 32768-token contexts, split-KV over the N
-           ranks with an NCCL all-gather of the partial (O, LSE) per layer.
+           ranks; per layer the partial (O, LSE) states are exchanged over
+           NVLink peer memory and merged in one kernel (PL_SPLITKV_EXCHANGE=nccl:
+           an NCCL all-gather and a merge launch instead).
 Their contexts hold random K/V (their prefill is not part of a decode step).
 Kernel-level workloads follow: the paged prefill kernel (prefill_config2 /
 prefill_config5, TFLOP/s against the bf16 peak) and the paged decode
@@ -518,8 +520,9 @@ def run_config4(ws: int, rank: int, device, barrier, steps: int, warmup: int) ->
 def run_config5(ws: int, rank: int, device, barrier, group, steps: int, warmup: int) -> dict:
     """Llama-3-8B arch, 8 rows of 32768-token contexts,
     rank-16 LoRA on q/v; split-KV across the ranks (each holds 1/N of every
-    row's pages; per layer one NCCL all-gather of the partial (O, LSE)).
-    The contexts' K/V are random values."""
+    row's pages; per layer the partial (O, LSE) states are exchanged and
+    merged: over NVLink peer memory by default, or with an NCCL all-gather
+    when PL_SPLITKV_EXCHANGE=nccl).  The contexts' K/V are random values."""
 
     import torch
 
@@ -534,7 +537,8 @@ def run_config5(ws: int, rank: int, device, barrier, group, steps: int, warmup: 
     pages = rows * (-(-ctx // 16) // ws + 2) + rows * (-(-(steps + warmup + 40) // 16)) + 64
     eng = BatchDecodeEngine(spec, w, adapters=[lo], lora_spec=lspec, row_adapter=[0] * rows, page_size=16,
                             max_context=ctx + steps + warmup + 40, num_pages=pages, device=device,
-                            kv_shard=(rank, ws), group=group)
+                            kv_shard=(rank, ws), group=group,
+                            exchange=os.environ.get("PL_SPLITKV_EXCHANGE", "p2p") if ws > 1 else "nccl")
     del w, lo
     eng.fill_random_context([ctx] * rows, seed=3)
     eng.capture()
@@ -542,8 +546,10 @@ def run_config5(ws: int, rank: int, device, barrier, group, steps: int, warmup: 
     eng._check_status()
     out = {"rows": rows, "context": ctx, "ms_per_step": ms, "launches_per_step": eng.launches_per_step(),
            "kv_bytes_per_step": rows * ctx * spec.num_kv_heads * spec.head_dim * 4 * spec.num_layers,
-           "weight_bytes_per_step_per_gpu": spec.weight_bytes()}
-    eng.graph = None
+           "weight_bytes_per_step_per_gpu": spec.weight_bytes(),
+           "exchange": (eng.exchange + (" (pl_splitkv_exchange_merge over NVLink peer memory)" if eng.peer else
+                                        " (all-gather + merge launch)")) if ws > 1 else "none"}
+    eng.close()
     del eng
     torch.cuda.empty_cache()
     return out
@@ -848,7 +854,7 @@ def run_ours(args) -> None:
         extra["config5"] = {
             "metric": "decode tok/s, 8 x 32768 ctx (Llama-3-8B arch, LoRA r16 q/v)",
             "value": c5["rows"] * 1000.0 / c5["ms_per_step"], "unit": "tok/s", "ms_per_step": c5["ms_per_step"],
-            "parallelism": (f"split-KV x{ws} (NCCL all-gather of partial O/LSE per layer)" if ws > 1
+            "parallelism": (f"split-KV x{ws} (partial O/LSE exchanged per layer: {c5['exchange']})" if ws > 1
                             else "1 GPU"), "scaling": "strong",
             "steps": xs, "warmup": xw, "achieved_gbs_all_gpus": c5_bytes / (c5["ms_per_step"] * 1e-3) / 1e9,
             "frac_of_peak_per_gpu": c5_bytes / ws / (c5["ms_per_step"] * 1e-3) / 1e9 / peak,

@@ -351,6 +351,55 @@ int32_t pl_merge_states_strided(const float *v_partial, int64_t v_row_stride,
                                 int32_t head_dim, void *out, int64_t out_stride,
                                 float *out_lse, void *stream);
 
+/* ------------------------------------------------- split-KV peer exchange */
+/*
+ * Split-KV decode over GPUs (one process per GPU): every GPU computes a
+ * partial (O fp32, LSE) over its page range, and the states are merged by
+ * log-sum-exp.  pl_splitkv_exchange_merge does the exchange and the merge in
+ * one kernel over NVLink peer memory, instead of an all-gather collective
+ * followed by pl_merge_states_strided.  No reference counterpart (the
+ * reference runs on one GPU).
+ *
+ * Set-up, once per GPU, on buffers the caller allocates (nothing here
+ * allocates):
+ *   gather  fp32 [2][world][slot] (slot = pl_splitkv_exchange_slot_floats),
+ *           zeroed;
+ *   flags   int32 [world][ctas] (ctas = pl_splitkv_exchange_ctas), zeroed;
+ *   epochs  int32 [ctas], zeroed.
+ * Export gather and flags with pl_ipc_export, share the handle bytes and
+ * offsets with the other GPUs (e.g. an all-gather at start-up), map the
+ * peers' buffers with pl_ipc_import, and put the world gather pointers and
+ * the world flag pointers (this GPU's own ones at index rank) into two
+ * device arrays.  Peer access needs GPUs that reach each other over NVLink
+ * or PCIe P2P.
+ *
+ *   part    this GPU's partial, packed: O [rows_h][head_dim] fp32, then LSE
+ *           [rows_h] (natural log, as pl_paged_decode_f32's out_lse);
+ *           16-byte aligned; head_dim % 4 == 0
+ *   out     bf16 [rows_h][head_dim]: the merged output, bit-identical to
+ *           pl_merge_states_strided over the all-gathered partials, and the
+ *           same on every GPU
+ * Every GPU must make the same sequence of calls (same rows_h, head_dim,
+ * rows_per_cta).  Each CTA waits (bounded, ~2 s) for the same CTA of every
+ * other GPU; a wait that runs out writes PL_ERR_TIMEOUT to *status_dev and
+ * the CTA returns without merging.
+ */
+int32_t pl_ipc_handle_bytes(void);
+int32_t pl_ipc_export(const void *dev_ptr, void *handle_out,
+                      int64_t *offset_out);
+int32_t pl_ipc_import(const void *handle, int64_t offset, void **dev_ptr_out);
+int32_t pl_ipc_close(void *dev_ptr, int64_t offset);
+int64_t pl_splitkv_exchange_slot_floats(int32_t rows_h, int32_t head_dim);
+int32_t pl_splitkv_exchange_ctas(int32_t rows_h, int32_t rows_per_cta);
+int32_t pl_splitkv_exchange_merge(const float *part,
+                                  void *const *peer_gather_dev,
+                                  int32_t *const *peer_flags_dev,
+                                  const int32_t *flags_local, int32_t *epochs,
+                                  int32_t rank, int32_t world, int32_t rows_h,
+                                  int32_t head_dim, int32_t rows_per_cta,
+                                  void *out, int32_t *status_dev,
+                                  void *stream);
+
 /* ------------------------------------------------------ prefill attention */
 /*
  * Ragged paged prefill attention on the tcgen05 tensor cores.  Replaces

@@ -116,6 +116,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pl_decode_cluster_capacity": (_I32, [_I32, _I32, _I32]),
     "pl_merge_states": (_I32, [_P, _P, _I32, _I32, _I32, _P, _I64, _P, _P]),
     "pl_merge_states_strided": (_I32, [_P, _I64, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _I64, _P, _P]),
+    "pl_ipc_handle_bytes": (_I32, []),
+    "pl_ipc_export": (_I32, [_P, _P, POINTER(c_int64)]),
+    "pl_ipc_import": (_I32, [_P, _I64, POINTER(c_void_p)]),
+    "pl_ipc_close": (_I32, [_P, _I64]),
+    "pl_splitkv_exchange_slot_floats": (_I64, [_I32, _I32]),
+    "pl_splitkv_exchange_ctas": (_I32, [_I32, _I32]),
+    "pl_splitkv_exchange_merge": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P]),
     "pl_paged_prefill": (
         _I32,
         [_P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64,

@@ -56,7 +56,7 @@ class BatchDecodeEngine:
     def __init__(self, spec: ModelSpec, weights: dict[str, torch.Tensor], *, adapters: list[dict] | None,
                  lora_spec: LoRASpec | None, row_adapter: list[int], page_size: int = 16, max_context: int = 4096,
                  num_pages: int | None = None, device: torch.device | str = "cuda",
-                 kv_shard: tuple[int, int] = (0, 1), group=None) -> None:
+                 kv_shard: tuple[int, int] = (0, 1), group=None, exchange: str = "nccl") -> None:
         self.spec = spec
         # Split-KV: shard `rank` of `world` holds a contiguous page range of
         # every row's context; the last shard owns the growing tail.
@@ -65,6 +65,12 @@ class BatchDecodeEngine:
             raise ValueError("kv_shard must be (rank, world) with 0 <= rank < world")
         self.group = group
         self.owner = self.shard == self.world - 1
+        # Split-KV partial exchange: "nccl" (all-gather + merge launch) or
+        # "p2p" (pl_splitkv_exchange_merge over NVLink peer memory)
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.exchange = exchange
+        self.peer = None
         self.device = torch.device(device)
         self.page_size = page_size
         self.rows = len(row_adapter)
@@ -181,6 +187,10 @@ class BatchDecodeEngine:
             self.part = torch.zeros(rows_h * (D + 1), device=dev, dtype=torch.float32)
             self.gathered = torch.zeros(self.world, rows_h * (D + 1), device=dev, dtype=torch.float32)
             self.dummy_page = self._alloc_page()  # append target of the shards that do not own the tail
+            if exchange == "p2p":
+                from pagelora_b200.peer_exchange import PeerExchange
+
+                self.peer = PeerExchange(rows_h, D, group=group, device=dev)
         self.host_pages: list[list[int]] = [[] for _ in range(B)]
         self.host_last = [0] * B
         self.context_len = [0] * B
@@ -555,10 +565,27 @@ class BatchDecodeEngine:
         lse_part = self.part[nd:].view(self.rows, s.num_qo_heads)
         K.paged_decode_qkv(self.qkv, self.kv[li], self.indptr, self.indices, self.last_page_len, out=o_part,
                            out_lse=lse_part, **qkv_args)
+        if self.peer is not None:
+            self.peer.merge(self.part, self.attn.view(rows_h, s.head_dim), self.status)
+            return
         dist.all_gather_into_tensor(self.gathered, self.part, group=self.group)
         v = self.gathered[:, :nd].view(self.world, rows_h, s.head_dim).permute(1, 0, 2)
         lse = self.gathered[:, nd:].permute(1, 0)
         K.merge_states_strided(v, lse, self.attn.view(rows_h, s.head_dim))
+
+    def close(self) -> None:
+        """Release the graph and unmap the peers' exchange buffers (call on
+        every rank once no step is in flight anywhere, before the process
+        group goes)."""
+
+        self.graph = None
+        if self.peer is not None:
+            import torch.distributed as dist
+
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            self.peer.close()
+            self.peer = None
 
     def launches_per_step(self) -> int:
         """Kernel launches of one step (all of them this library's kernels;

@@ -15,7 +15,7 @@ def _declared() -> set[str]:
     names = set()
     for h in (REPO / "include").glob("*.h"):
         text = h.read_text()
-        names |= set(re.findall(r"^\s*(?:int32_t|const char \*)\s*(pl_\w+)\s*\(", text, flags=re.M))
+        names |= set(re.findall(r"^\s*(?:int32_t|int64_t|const char \*)\s*(pl_\w+)\s*\(", text, flags=re.M))
     return names
 
 
