@@ -453,6 +453,29 @@ int32_t pl_lora_shrink_seg(const void *x, int64_t x_stride,
                            int32_t num_tokens,
                            float *down, int64_t down_stride, void *stream);
 
+/*
+ * Per-token LoRA shrink with an optional RMSNorm in front, one launch:
+ *   xn[t]      = bf16(x[t] * rsqrt(mean(x[t]^2) + eps) * norm_w)  (norm_w != NULL;
+ *                bit-identical to pl_rmsnorm; written to xn_out when it is
+ *                not NULL)
+ *   down[t, j] = xn[t] . A[adapter(t)][j, :]  (fp32; x[t] itself without norm_w)
+ * adapter(t) = tok_adapter[t] (device, NULL = adapter 0); an adapter
+ * outside [0, num_adapters) gives zeros.  A is bf16 [num_adapters, rank,
+ * k_in].  Replaces the x . A^T of multilora/linear.py:226-227 and
+ * model/flashinfer/packed_ops.py:324 (F.linear(hidden, packed.a)) for
+ * per-row adapters, and with norm_w also the RMSNorm of
+ * model/flashinfer/norm.py in front of the packed q/k/v projection.  One
+ * CTA per (token, 4 rank rows): k_in % 8 == 0 and k_in <= 8192
+ * (PL_ERR_UNSUPPORTED otherwise).
+ */
+int32_t pl_lora_shrink_rows(const void *x, int64_t x_stride,
+                            int32_t num_tokens, int32_t k_in,
+                            const void *norm_w, float norm_eps, void *xn_out,
+                            int64_t xn_stride, const void *a,
+                            int32_t num_adapters, int32_t rank,
+                            const int32_t *tok_adapter, float *down,
+                            int64_t down_stride, void *stream);
+
 /* Epilogue/prologue selectors of pl_linear_lora_expand_fused. */
 #define PL_PROLOGUE_NONE 0     /* x used as given                                    */
 #define PL_PROLOGUE_RMSNORM 1  /* x <- bf16(x * rsqrt(mean(x^2)+eps) * norm_w)       */

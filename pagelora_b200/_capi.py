@@ -129,6 +129,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _P, _P, _P],
     ),
     "pl_lora_shrink_seg": (_I32, [_P, _I64, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _I64, _P]),
+    "pl_lora_shrink_rows": (_I32, [_P, _I64, _I32, _I32, _P, _F, _P, _I64, _P, _I32, _I32, _P, _P, _I64, _P]),
     "pl_linear_lora_expand_fused": (
         _I32,
         [_P, _I64, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _I64, _P, _I32, _F, _P, _I32, _P, _P, _I64, _P,

@@ -506,10 +506,14 @@ class BatchDecodeEngine:
         lora = self.lora_rank > 0
         for li, L in enumerate(self.layers):
             if lora:
-                # The shrink reads the normalised rows, so the norm is its own
-                # launch and the projection takes them as they are.
-                K.rmsnorm(self.x, L["input_norm"], s.rms_eps, out=self.xn)
-                K.lora_shrink_seg(self.xn, L["a_qkv"], self.seg_indptr, self.seg_adapter, out=self.down_qkv)
+                # The shrink reads the normalised rows: one launch normalises
+                # them (written to xn for the projection) and shrinks them.
+                if s.hidden <= K.SHRINK_ROWS_MAX_K:
+                    K.lora_shrink_rows(self.x, L["a_qkv"], tok_adapter=self.tok_adapter, out=self.down_qkv,
+                                       norm_weight=L["input_norm"], norm_eps=s.rms_eps, xn_out=self.xn)
+                else:
+                    K.rmsnorm(self.x, L["input_norm"], s.rms_eps, out=self.xn)
+                    K.lora_shrink_seg(self.xn, L["a_qkv"], self.seg_indptr, self.seg_adapter, out=self.down_qkv)
                 self._linear(self.xn, L["w_qkv"], out=self.qkv)
             else:
                 self._linear(self.x, L["w_qkv"], prologue=PL_PROLOGUE_RMSNORM, norm_weight=L["input_norm"],
@@ -540,7 +544,10 @@ class BatchDecodeEngine:
             else:
                 self._split_kv_attention(li, qkv_args)
             if lora:
-                K.lora_shrink_seg(attn2d, L["a_o"], self.seg_indptr, self.seg_adapter, out=self.down_o)
+                if s.q_dim <= K.SHRINK_ROWS_MAX_K:
+                    K.lora_shrink_rows(attn2d, L["a_o"], tok_adapter=self.tok_adapter, out=self.down_o)
+                else:
+                    K.lora_shrink_seg(attn2d, L["a_o"], self.seg_indptr, self.seg_adapter, out=self.down_o)
             self._linear(attn2d, L["w_o"], lora_down=self.down_o if lora else None, lora_b=L["b_o"] if lora else None,
                          lora_scale=self.lora_scale, tok_adapter=self.tok_adapter if lora else None,
                          residual=self.x, out=self.x)
@@ -598,8 +605,12 @@ class BatchDecodeEngine:
         per_layer = 4 if self.cascade is not None else 1
         if self.world > 1:
             per_layer += 1  # partial-state merge
-        # q/k/v: with LoRA the norm is a launch of its own (the shrink reads it)
-        per_layer += 3 if lora else (1 if uses_gemv(B, s.hidden) else 2)
+        # q/k/v: with LoRA the norm and the shrink are one launch (up to 8192
+        # features), then the projection
+        if lora:
+            per_layer += 2 if s.hidden <= K.SHRINK_ROWS_MAX_K else 3
+        else:
+            per_layer += 1 if uses_gemv(B, s.hidden) else 2
         per_layer += 2 if lora else 1  # (o shrink +) o projection
         per_layer += 1 if uses_gemv(B, s.hidden) else 2  # (norm +) gate_up
         per_layer += 1 if uses_gemv(B, s.intermediate) else 2  # (SiLU-mul +) down

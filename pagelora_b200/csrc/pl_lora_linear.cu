@@ -881,6 +881,123 @@ __global__ void __launch_bounds__(256) lora_shrink_kernel(const bf16* __restrict
   }
 }
 
+// ---------------------------------------------------------- row shrink
+// down[t][j] = row_t . A[adapter(t)][j] for rank rows j of one block: CTA
+// (t, jb) takes token t and rank rows [4 jb, 4 jb + 4).  The token's row is
+// loaded once into registers (thread `tid` holds the 8-element chunks
+// k = tid * 8 + i * 2048, i < 4, so K <= 8192), optionally RMS-normalised
+// first with the partition and sum order of rmsnorm_kernel (so the
+// normalised row is bit-identical to pl_rmsnorm's; every CTA of the token
+// recomputes the norm and the jb == 0 CTA writes the row out), then the
+// CTA's four A rows (requested together with the row) are reduced by warp
+// shuffles and the 8 warps' sums in warp order.  The A rows are spread over
+// T x R/4 CTAs, so the launch has enough CTAs to read them in parallel.
+constexpr int kShrinkThreads = 256;
+constexpr int kShrinkChunks = 4;
+constexpr int kShrinkRowsPerCta = 4;
+
+__global__ void __launch_bounds__(kShrinkThreads, 2) lora_shrink_rows_kernel(
+    const bf16* __restrict__ x, int64_t x_stride, int K, const bf16* __restrict__ norm_w, float eps,
+    bf16* __restrict__ xn, int64_t xn_stride, const bf16* __restrict__ A, int num_adapters, int R,
+    const int32_t* __restrict__ tok_adapter, float* __restrict__ down, int64_t down_stride) {
+  __shared__ float part[kShrinkThreads / 32][kShrinkRowsPerCta];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x, j0 = blockIdx.y * kShrinkRowsPerCta;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  constexpr int kStep = kShrinkThreads * 8;
+  const int ad = tok_adapter != nullptr ? tok_adapter[t] : 0;
+  const bool lora = ad >= 0 && ad < num_adapters;
+  const bf16* xr = x + (int64_t)t * x_stride;
+  const bf16* Aad = A + (int64_t)(lora ? ad : 0) * R * K;
+  uint4 v[kShrinkChunks], av[kShrinkRowsPerCta][kShrinkChunks];
+#pragma unroll
+  for (int i = 0; i < kShrinkChunks; ++i) {
+    const int k = tid * 8 + i * kStep;
+    v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+  }
+  // the A rows do not depend on the row: requested with it
+#pragma unroll
+  for (int jj = 0; jj < kShrinkRowsPerCta; ++jj)
+#pragma unroll
+    for (int i = 0; i < kShrinkChunks; ++i) {
+      const int k = tid * 8 + i * kStep;
+      av[jj][i] = (lora && j0 + jj < R && k < K)
+                      ? __ldg(reinterpret_cast<const uint4*>(Aad + (int64_t)(j0 + jj) * K + k))
+                      : make_uint4(0, 0, 0, 0);
+    }
+  if (norm_w != nullptr) {
+    __shared__ float ssq[kShrinkThreads / 32];
+    uint4 wv[kShrinkChunks];
+#pragma unroll
+    for (int i = 0; i < kShrinkChunks; ++i) {
+      const int k = tid * 8 + i * kStep;
+      wv[i] = k < K ? *reinterpret_cast<const uint4*>(norm_w + k) : make_uint4(0, 0, 0, 0);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kShrinkChunks; ++i) {
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(u[q]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) ssq[wid] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kShrinkThreads / 32; ++w) tot += ssq[w];
+    const float r = rsqrtf(tot / (float)K + eps);
+#pragma unroll
+    for (int i = 0; i < kShrinkChunks; ++i) {
+      const int k = tid * 8 + i * kStep;
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+      const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv[i]);
+      uint4 o;
+      uint32_t* uo = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(u[q]);
+        const float2 g = unpack_bf16x2(uw[q]);
+        uo[q] = pack_bf16x2(f.x * r * g.x, f.y * r * g.y);
+      }
+      v[i] = o;
+      if (k < K && xn != nullptr && blockIdx.y == 0) *reinterpret_cast<uint4*>(xn + (int64_t)t * xn_stride + k) = o;
+    }
+  }
+  float acc[kShrinkRowsPerCta] = {};
+#pragma unroll
+  for (int i = 0; i < kShrinkChunks; ++i) {
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+#pragma unroll
+    for (int jj = 0; jj < kShrinkRowsPerCta; ++jj) {
+      const uint32_t* ua = reinterpret_cast<const uint32_t*>(&av[jj][i]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(u[q]);
+        const float2 g = unpack_bf16x2(ua[q]);
+        acc[jj] = fmaf(f.x, g.x, acc[jj]);
+        acc[jj] = fmaf(f.y, g.y, acc[jj]);
+      }
+    }
+  }
+#pragma unroll
+  for (int jj = 0; jj < kShrinkRowsPerCta; ++jj) {
+    const float sv = warp_sum(acc[jj]);
+    if (lane == 0) part[wid][jj] = sv;
+  }
+  __syncthreads();
+  if (tid < kShrinkRowsPerCta && j0 + tid < R) {
+    float sv = 0.f;
+#pragma unroll
+    for (int w = 0; w < kShrinkThreads / 32; ++w) sv += part[w][tid];
+    down[(int64_t)t * down_stride + j0 + tid] = lora ? sv : 0.f;
+  }
+}
+
 // ------------------------------------------------------------ merge weight
 __global__ void lora_merge_weight_kernel(const bf16* __restrict__ w_in, bf16* __restrict__ w_out,
                                          const bf16* __restrict__ A, const bf16* __restrict__ B, int N, int K,
@@ -1289,6 +1406,29 @@ extern "C" int32_t pl_lora_shrink_seg(const void* x, int64_t x_stride, const voi
                              static_cast<const pl::bf16*>(x), x_stride, static_cast<const pl::bf16*>(a),
                              (int)num_adapters, (int)rank, (int)in_features, seg_indptr, seg_adapter, down,
                              down_stride);
+}
+
+extern "C" int32_t pl_lora_shrink_rows(const void* x, int64_t x_stride, int32_t num_tokens, int32_t k_in,
+                                       const void* norm_w, float norm_eps, void* xn_out, int64_t xn_stride,
+                                       const void* a, int32_t num_adapters, int32_t rank,
+                                       const int32_t* tok_adapter, float* down, int64_t down_stride, void* stream) {
+  if (num_tokens == 0 || rank == 0) return PL_OK;
+  if (x == nullptr || a == nullptr || down == nullptr || num_tokens < 0 || k_in <= 0 || rank < 0 ||
+      num_adapters <= 0 || num_tokens > 2147483647 / 2 || (xn_out != nullptr && norm_w == nullptr) ||
+      down_stride < rank)
+    return PL_ERR_INVALID_ARGUMENT;
+  if (k_in % 8 || k_in > pl::kShrinkThreads * 8 * pl::kShrinkChunks || x_stride % 8 ||
+      (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(a) & 15) ||
+      (norm_w != nullptr && (reinterpret_cast<uintptr_t>(norm_w) & 15)) ||
+      (xn_out != nullptr && ((reinterpret_cast<uintptr_t>(xn_out) & 15) || xn_stride % 8)))
+    return PL_ERR_UNSUPPORTED;
+  const int jb = (rank + pl::kShrinkRowsPerCta - 1) / pl::kShrinkRowsPerCta;
+  if (jb > 65535) return PL_ERR_UNSUPPORTED;
+  return pl_host::launch_pdl(pl::lora_shrink_rows_kernel, dim3(num_tokens, jb), dim3(pl::kShrinkThreads), 0,
+                             stream, static_cast<const pl::bf16*>(x), x_stride, (int)k_in,
+                             static_cast<const pl::bf16*>(norm_w), norm_eps, static_cast<pl::bf16*>(xn_out),
+                             xn_stride, static_cast<const pl::bf16*>(a), (int)num_adapters, (int)rank, tok_adapter,
+                             down, down_stride);
 }
 
 extern "C" int32_t pl_lora_merge_weight(const void* w_in, void* w_out, const void* a, const void* b, int32_t n_out,

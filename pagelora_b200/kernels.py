@@ -349,6 +349,37 @@ def lora_shrink_seg(x: torch.Tensor, a_stack: torch.Tensor, seg_indptr: torch.Te
     return out
 
 
+SHRINK_ROWS_MAX_K = 8192
+
+
+def lora_shrink_rows(x: torch.Tensor, a_stack: torch.Tensor, *, tok_adapter: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
+                     norm_eps: float = 1e-6, xn_out: torch.Tensor | None = None) -> torch.Tensor:
+    """down[t] = x[t] . A[tok_adapter[t]]^T (fp32, a_stack [n_adapters, rank,
+    in]); with ``norm_weight`` the rows are RMS-normalised first (bit-identical
+    to :func:`rmsnorm`) and written to ``xn_out`` when given.  ``in`` <= 8192."""
+
+    _need_cuda(x, a_stack)
+    _need(x, torch.bfloat16, "x")
+    _need(a_stack, torch.bfloat16, "a_stack")
+    if a_stack.dim() == 2:
+        a_stack = a_stack.unsqueeze(0)
+    if not a_stack.is_contiguous():
+        raise ValueError("a_stack must be a contiguous [n_adapters, rank, in] stack")
+    n_ad, rank, k = a_stack.shape
+    t = x.shape[0]
+    if x.shape[1] != k:
+        raise ValueError("x and a_stack disagree on the input features")
+    if out is None:
+        out = torch.empty(t, rank, dtype=torch.float32, device=x.device)
+    if tok_adapter is not None:
+        _need(tok_adapter, torch.int32, "tok_adapter")
+    call("pl_lora_shrink_rows", ptr(x), _row_stride(x, "x"), int(t), int(k), ptr(norm_weight), float(norm_eps),
+         ptr(xn_out), 0 if xn_out is None else _row_stride(xn_out, "xn_out"), ptr(a_stack), int(n_ad), int(rank),
+         ptr(tok_adapter), ptr(out), _row_stride(out, "down"), stream_handle())
+    return out
+
+
 def _gemv_phase(
     x: torch.Tensor,
     weight: torch.Tensor,

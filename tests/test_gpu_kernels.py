@@ -717,6 +717,34 @@ def test_linear_lora_fused_l2_handover_same_bits(K, t, units):
     assert torch.equal(y, y_ref) and torch.equal(z, z_ref)
 
 
+@pytest.mark.parametrize("t,k,r", [(1, 4096, 48), (16, 4096, 16), (64, 4096, 48), (5, 8192, 30), (3, 600, 24)])
+def test_lora_shrink_rows_vs_rmsnorm_and_oracle(K, t, k, r):
+    """pl_lora_shrink_rows: the normalised rows are bit-identical to
+    pl_rmsnorm's, and the per-row-adapter shrink (adapters -1 and out of
+    range give zeros; rank not a multiple of the 4-row block) matches the
+    fp64 product of those rows within fp32 rounding, with and without the
+    norm."""
+
+    g = torch.Generator(device="cuda").manual_seed(t * 7 + r)
+    x = torch.randn(t, k, generator=g, device="cuda").bfloat16()
+    nw = (1 + 0.1 * torch.randn(k, generator=g, device="cuda")).bfloat16()
+    a = (torch.randn(3, r, k, generator=g, device="cuda") * 0.03).bfloat16()
+    ad = torch.tensor([(i % 5) - 1 for i in range(t)], dtype=torch.int32, device="cuda")  # -1, 0, 1, 2, 3
+    xn = torch.zeros_like(x)
+    down = K.lora_shrink_rows(x, a, tok_adapter=ad, norm_weight=nw, norm_eps=1e-6, xn_out=xn)
+    down_plain = K.lora_shrink_rows(x, a, tok_adapter=ad)
+    xn_ref = K.rmsnorm(x, nw, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(xn, xn_ref)
+    adl = ad.cpu().tolist()
+    for src, got in ((xn_ref, down), (x, down_plain)):
+        want = np.zeros((t, r))
+        for i in range(t):
+            if 0 <= adl[i] < 3:
+                want[i] = src[i].double().cpu().numpy() @ a[adl[i]].double().cpu().numpy().T
+        np.testing.assert_allclose(_np(got), want, rtol=1e-4, atol=1e-4)
+
+
 def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
     """fp64 restatement of the multi-token LoRA linear epilogue (per-token adapter)."""
 
