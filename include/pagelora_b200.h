@@ -699,7 +699,17 @@ int32_t pl_linear_gemm_lora_precompute(int32_t num_tokens, int32_t k_in,
  *   workspace   256-byte aligned, pl_linear_gemm_plan's workspace_bytes for
  *               the same num_ctas; its first 4 * ceil(n_out / 128) bytes
  *               are arrival counters: zero before the first call, left zero.
+ *   flags       PL_FLAG_WEIGHTS_STATIC as for the GEMV; PL_FLAG_SILU_PAIRS:
+ *               w is a gate/up stack interleaved in blocks of 64 rows (rows
+ *               128j .. 128j+63 = gate rows 64j .. 64j+63, the next 64 = the
+ *               same up rows) and y gets the SiLU-and-mul instead,
+ *               y[t, c] = bf16(silu(bf16(g)) * bf16(u)) for c < n_out / 2:
+ *               the gate_up projection and pl_silu_mul of
+ *               model/flashinfer/packed_ops.py:168-239 in one launch, with the
+ *               same rounding.  Needs n_out % 128 == 0, y_stride % 4 == 0, y
+ *               8-byte aligned, and no bias, LoRA or residual.
  */
+#define PL_FLAG_SILU_PAIRS 8
 int32_t pl_linear_lora_gemm(const void *x, int64_t x_stride, int32_t num_tokens,
                             int32_t k_in, const void *w, int32_t n_out,
                             const void *bias, const float *lora_down,

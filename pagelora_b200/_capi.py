@@ -33,6 +33,7 @@ PL_PROLOGUE_RMSNORM = 1
 PL_PROLOGUE_SILU_MUL = 2
 PL_FLAG_WEIGHTS_STATIC = 1
 PL_FLAG_DOWN_FROM_X = 2
+PL_FLAG_SILU_PAIRS = 8
 PL_DECODE_OUT_F32 = 1
 
 # Messages of the reference's ValueErrors for malformed spans

@@ -74,6 +74,11 @@ class BatchDecodeEngine:
         self.device = torch.device(device)
         self.page_size = page_size
         self.rows = len(row_adapter)
+        # gate_up and down both on the tcgen05 GEMM: the gate/up weights are
+        # stored interleaved in blocks of 64 rows and the gate_up launch writes
+        # the SiLU-and-mul directly (PL_FLAG_SILU_PAIRS), one launch fewer
+        self.silu_pairs = (not uses_gemv(self.rows, spec.hidden) and not uses_gemv(self.rows, spec.intermediate)
+                           and spec.intermediate % 64 == 0)
         if any(b < a for a, b in zip(row_adapter, row_adapter[1:])):
             raise ValueError("rows must be grouped by adapter (non-decreasing adapter ids)")
         n_ad = len(adapters) if adapters else 0
@@ -94,8 +99,8 @@ class BatchDecodeEngine:
             p = f"model.layers.{i}."
             w_qkv = torch.cat([take(p + f"self_attn.{m}_proj.weight") for m in "qkv"], 0).contiguous()
             L = dict(w_qkv=w_qkv, w_o=take(p + "self_attn.o_proj.weight"),
-                     w_gate_up=torch.cat([take(p + "mlp.gate_proj.weight"), take(p + "mlp.up_proj.weight")],
-                                         0).contiguous(),
+                     w_gate_up=self._gate_up(torch.cat([take(p + "mlp.gate_proj.weight"),
+                                                        take(p + "mlp.up_proj.weight")], 0)),
                      w_down=take(p + "mlp.down_proj.weight"), input_norm=take(p + "input_layernorm.weight"),
                      post_norm=take(p + "post_attention_layernorm.weight"),
                      q_norm=take(p + "self_attn.q_norm.weight") if spec.qk_norm else None,
@@ -316,7 +321,11 @@ class BatchDecodeEngine:
             x = x + o
             h2 = _rmsnorm_fused(x, L["post_norm"], s.rms_eps)
             gu = F.linear(h2, L["w_gate_up"])
-            g, u = gu[:, : s.intermediate].float(), gu[:, s.intermediate:].float()
+            if self.silu_pairs:  # interleaved rows: blocks of 64 gate outputs, then 64 up outputs
+                gu = gu.view(n, s.intermediate // 64, 2, 64)
+                g, u = gu[:, :, 0].reshape(n, -1).float(), gu[:, :, 1].reshape(n, -1).float()
+            else:
+                g, u = gu[:, : s.intermediate].float(), gu[:, s.intermediate:].float()
             x = x + F.linear((g / (1.0 + torch.exp(-g)) * u).to(torch.bfloat16), L["w_down"])
         return F.linear(_rmsnorm_fused(x[-1:], self.final_norm, s.rms_eps), self.lm_head)[0]
 
@@ -551,9 +560,17 @@ class BatchDecodeEngine:
             self._linear(attn2d, L["w_o"], lora_down=self.down_o if lora else None, lora_b=L["b_o"] if lora else None,
                          lora_scale=self.lora_scale, tok_adapter=self.tok_adapter if lora else None,
                          residual=self.x, out=self.x)
-            self._linear(self.x, L["w_gate_up"], prologue=PL_PROLOGUE_RMSNORM, norm_weight=L["post_norm"],
-                         out=self.gate_up)
-            self._linear(self.gate_up, L["w_down"], prologue=PL_PROLOGUE_SILU_MUL, residual=self.x, out=self.x)
+            if self.silu_pairs:
+                xn = K.rmsnorm(self.x, L["post_norm"], s.rms_eps, out=self.xn)
+                K.linear_lora_gemm(xn, L["w_gate_up"], silu_pairs=True, out=self.act, workspace=self.gemm_ws,
+                                   weights_static=True, status=st)
+                K.linear_lora_gemm(self.act, L["w_down"], residual=self.x, out=self.x, workspace=self.gemm_ws,
+                                   weights_static=True, status=st)
+            else:
+                self._linear(self.x, L["w_gate_up"], prologue=PL_PROLOGUE_RMSNORM, norm_weight=L["post_norm"],
+                             out=self.gate_up)
+                self._linear(self.gate_up, L["w_down"], prologue=PL_PROLOGUE_SILU_MUL, residual=self.x,
+                             out=self.x)
         self._linear(self.x, self.lm_head, prologue=PL_PROLOGUE_RMSNORM, norm_weight=self.final_norm,
                      out=self.logits)
         K.argmax(self.logits, self.token_buf, self.argmax_ws)
@@ -579,6 +596,11 @@ class BatchDecodeEngine:
         v = self.gathered[:, :nd].view(self.world, rows_h, s.head_dim).permute(1, 0, 2)
         lse = self.gathered[:, nd:].permute(1, 0)
         K.merge_states_strided(v, lse, self.attn.view(rows_h, s.head_dim))
+
+    def _gate_up(self, w: torch.Tensor) -> torch.Tensor:
+        """The [gate; up] stack as the decode projection reads it."""
+
+        return K.interleave_gate_up(w) if self.silu_pairs else w.contiguous()
 
     def close(self) -> None:
         """Release the graph and unmap the peers' exchange buffers (call on
@@ -613,7 +635,8 @@ class BatchDecodeEngine:
             per_layer += 1 if uses_gemv(B, s.hidden) else 2
         per_layer += 2 if lora else 1  # (o shrink +) o projection
         per_layer += 1 if uses_gemv(B, s.hidden) else 2  # (norm +) gate_up
-        per_layer += 1 if uses_gemv(B, s.intermediate) else 2  # (SiLU-mul +) down
+        # (SiLU-mul +) down; with silu_pairs the gate_up launch writes the SiLU-mul
+        per_layer += 1 if (uses_gemv(B, s.intermediate) or self.silu_pairs) else 2
         head = 1 if uses_gemv(B, s.hidden) else 2  # (norm +) lm_head
         advance = 1 if (self.world == 1 or self.owner) else 0
         return advance + 2 + per_layer * s.num_layers + head + 1  # + RoPE table, embed; argmax

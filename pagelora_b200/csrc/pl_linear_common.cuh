@@ -49,6 +49,7 @@ struct GemvArgs {
   const bf16* pf_shrink;
   int64_t pf_rows_total;
   int32_t pf_n_out, pf_k, pf_kc, pf_units, pf_grid;
+  int32_t silu_pairs;     // GEMM: 128-row tiles of 64 gate rows then the 64 matching up rows; y = the SiLU-and-mul
   int32_t coherent;       // activations / residual may have been written by other CTAs of this launch: read them
                           // from L2 (ld.global.cg), never from a possibly stale L1 line
 };
@@ -136,6 +137,30 @@ __device__ __forceinline__ void epilogue_rows4(const GemvArgs& a, int64_t o0, in
 }
 
 constexpr int kGemmTileRows = 128;  // weight rows of one tcgen05 GEMM tile
+
+// SiLU-and-mul epilogue of GEMM tile `tile` whose rows [0, 64) are gate rows
+// and [64, 128) the matching up rows (the gate/up weights interleaved in
+// blocks of 64): lane l < 16 holds gate rows 4l .. 4l+3 of tokens tok[0..nt),
+// lane l + 16 the up rows, which come over by a shuffle; then
+// y[tok][64 * tile + 4l + i] = bf16(silu(bf16(g)) * bf16(u)), the rounding of
+// a bf16 gate_up output followed by the SiLU-and-mul kernel.  Every lane of
+// the warp calls it (full-mask shuffles).
+__device__ __forceinline__ void epilogue_silu_pairs(const GemvArgs& a, int64_t tile, int lane, const int (&tok)[4],
+                                                    int nt, const float (&v)[4][4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float up[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) up[i] = __shfl_down_sync(0xffffffffu, v[k][i], 16);
+    if (lane < 16 && k < nt) {
+      float r[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r[i] = silu_mul(bfr(v[k][i]), bfr(up[i]));
+      *reinterpret_cast<uint2*>(a.y + tok[k] * a.y_stride + 64 * tile + 4 * lane) =
+          make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+    }
+  }
+}
 
 // Rank-16 LoRA dot product with the B row held in registers (16 bf16) and
 // the down row already rounded to bf16: the fma order of lora_dot.

@@ -352,8 +352,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               vals[h][3] = r4.w;
               if (16 * c + j < T) nt = h + 1;
             }
-            epilogue_rows4_x4(g.e, o4, toks, nt, vals, sdown, R, sad, t == t_pre ? sdl : nullptr,
-                              (int64_t)t * kGemmM);
+            if (g.e.silu_pairs)
+              epilogue_silu_pairs(g.e, t, lane, toks, nt, vals);
+            else
+              epilogue_rows4_x4(g.e, o4, toks, nt, vals, sdown, R, sad, t == t_pre ? sdl : nullptr,
+                                (int64_t)t * kGemmM);
           }
           named_barrier(1, kEpiThreads);
         }
@@ -423,9 +426,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                   a4[h][3] += p[h][k].w;
                 }
             }
-            if (!flags[0])
-              epilogue_rows4_x4(g.e, o4, toks, nt, a4, sdown, R, sad, t == t_pre ? sdl : nullptr,
-                                (int64_t)t * kGemmM);
+            if (!flags[0]) {
+              if (g.e.silu_pairs)
+                epilogue_silu_pairs(g.e, t, lane, toks, nt, a4);
+              else
+                epilogue_rows4_x4(g.e, o4, toks, nt, a4, sdown, R, sad, t == t_pre ? sdl : nullptr,
+                                  (int64_t)t * kGemmM);
+            }
           }
           if (ew == 0 && lane == 0) g.counters[t] = 0;
         }
@@ -780,6 +787,13 @@ extern "C" int32_t pl_linear_lora_gemm(const void* x, int64_t x_stride, int32_t 
   a.y = static_cast<pl::bf16*>(y);
   a.y_stride = y_stride;
   a.early_weights = (flags & PL_FLAG_WEIGHTS_STATIC) ? 1 : 0;
+  if (flags & PL_FLAG_SILU_PAIRS) {
+    // y gets n_out / 2 columns: 64 per tile, 8-byte stores
+    if (lora_b != nullptr || residual != nullptr || bias != nullptr) return PL_ERR_UNSUPPORTED;
+    if (n_out % pl::kGemmM != 0 || y_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(y) & 7))
+      return PL_ERR_INVALID_ARGUMENT;
+    a.silu_pairs = 1;
+  }
   a.status = status_dev;
   g.kblocks = sh.kblocks;
   g.units = sh.units;

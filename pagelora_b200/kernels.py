@@ -572,6 +572,7 @@ def linear_lora_gemm(
     workspace: torch.Tensor | None = None,
     num_ctas: int = 0,
     weights_static: bool = False,
+    silu_pairs: bool = False,
     status: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """y = x . W^T (+bias) (+ per-token LoRA expand) (+ residual) for 1..128
@@ -579,7 +580,9 @@ def linear_lora_gemm(
     :func:`rmsnorm` / :func:`silu_mul` first); the epilogue arguments are those
     of :func:`linear_lora_fused`.  ``workspace`` (uint8, zeroed once) is sized
     by :func:`gemm_plan` for the same ``num_ctas``; one is allocated when
-    omitted."""
+    omitted.  ``silu_pairs``: ``weight`` is a gate/up stack interleaved by
+    :func:`interleave_gate_up` and the output [T, N/2] is the SiLU-and-mul of
+    the gate and up projections (PL_FLAG_SILU_PAIRS)."""
 
     _need_cuda(x, weight)
     _need(x, torch.bfloat16, "x")
@@ -589,7 +592,7 @@ def linear_lora_gemm(
     t = x.shape[0]
     n, k = weight.shape
     if out is None:
-        out = torch.empty(t, n, dtype=torch.bfloat16, device=x.device)
+        out = torch.empty(t, n // 2 if silu_pairs else n, dtype=torch.bfloat16, device=x.device)
     if workspace is None:
         need = int(gemm_plan(t, k, n, num_ctas).workspace_bytes)
         workspace = torch.zeros(need, dtype=torch.uint8, device=x.device)
@@ -603,7 +606,7 @@ def linear_lora_gemm(
         num_slices = len(slice_ends) + 1 if slice_ends else 1
         if slice_ends:
             slice_ptr, slice_keepalive = ctypes_int32_array(slice_ends)
-    flags = _capi.PL_FLAG_WEIGHTS_STATIC if weights_static else 0
+    flags = (_capi.PL_FLAG_WEIGHTS_STATIC if weights_static else 0) | (_capi.PL_FLAG_SILU_PAIRS if silu_pairs else 0)
     call("pl_linear_lora_gemm", ptr(x), _row_stride(x, "x"), int(t), int(k), ptr(weight), int(n), ptr(bias),
          ptr(lora_down), 0 if lora_down is None else _row_stride(lora_down, "lora_down"), ptr(lora_b), int(rank),
          float(lora_scale), slice_ptr, int(num_slices), ptr(tok_adapter), ptr(residual),
@@ -611,6 +614,18 @@ def linear_lora_gemm(
          int(num_ctas), ptr(workspace), int(workspace.numel()), int(flags), ptr(status), stream_handle())
     del slice_keepalive
     return out
+
+
+def interleave_gate_up(w_gate_up: torch.Tensor) -> torch.Tensor:
+    """[gate; up] rows ([2I, K], I % 64 == 0) reordered into the blocks of
+    PL_FLAG_SILU_PAIRS: 64 gate rows, then the same 64 up rows, and so on."""
+
+    n, k = w_gate_up.shape
+    i = n // 2
+    if n % 2 or i % 64:
+        raise ValueError("the gate/up stack needs an even row count with I % 64 == 0")
+    g, u = w_gate_up[:i].view(i // 64, 64, k), w_gate_up[i:].view(i // 64, 64, k)
+    return torch.stack([g, u], dim=1).reshape(n, k).contiguous()
 
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -745,6 +745,29 @@ def test_lora_shrink_rows_vs_rmsnorm_and_oracle(K, t, k, r):
         np.testing.assert_allclose(_np(got), want, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("t", [9, 16, 64, 128])
+def test_linear_lora_gemm_silu_pairs_vs_oracle(K, t):
+    """PL_FLAG_SILU_PAIRS: the GEMM over the interleaved gate/up stack writes
+    bf16(silu(bf16(g)) * bf16(u)) (the reference's bf16 gate_up output, then
+    SiLU-and-mul), checked against the fp64 products; and it agrees with the
+    plain GEMM followed by pl_silu_mul."""
+
+    rng = np.random.default_rng(31 + t)
+    k_in, inter = 1024, 1536
+    x = bf16(rng.normal(size=(t, k_in)))
+    w = bf16(rng.normal(size=(2 * inter, k_in)) * 0.03)
+    wt = _t(w)
+    act = K.linear_lora_gemm(_t(x), K.interleave_gate_up(wt), silu_pairs=True)
+    plain = K.silu_mul(K.linear_lora_gemm(_t(x), wt))
+    torch.cuda.synchronize()
+    gu = x.astype(np.float64) @ w.T.astype(np.float64)
+    g, u = bf16(gu[:, :inter]), bf16(gu[:, inter:])
+    want = bf16(silu(g) * u)
+    # a 1-ulp difference in bf16(g) or bf16(u) moves the product by about one ulp of it
+    _ulps_close(_np(act), want, ulps=3, magnitude=np.abs(g * u))
+    _ulps_close(_np(act), _np(plain), ulps=3, magnitude=np.abs(g * u))
+
+
 def _gemm_oracle(x, w, bias, down, bmat, tok_ad, split_at, res, scale=1.0):
     """fp64 restatement of the multi-token LoRA linear epilogue (per-token adapter)."""
 
