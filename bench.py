@@ -538,7 +538,7 @@ def run_config5(ws: int, rank: int, device, barrier, group, steps: int, warmup: 
     eng = BatchDecodeEngine(spec, w, adapters=[lo], lora_spec=lspec, row_adapter=[0] * rows, page_size=16,
                             max_context=ctx + steps + warmup + 40, num_pages=pages, device=device,
                             kv_shard=(rank, ws), group=group,
-                            exchange=os.environ.get("PL_SPLITKV_EXCHANGE", "p2p") if ws > 1 else "nccl")
+                            exchange=os.environ.get("PL_SPLITKV_EXCHANGE", "auto") if ws > 1 else "nccl")
     del w, lo
     eng.fill_random_context([ctx] * rows, seed=3)
     eng.capture()

@@ -351,6 +351,32 @@ int32_t pl_merge_states_strided(const float *v_partial, int64_t v_row_stride,
                                 int32_t head_dim, void *out, int64_t out_stride,
                                 float *out_lse, void *stream);
 
+/*
+ * pl_paged_decode merged with a prior attention state of the same query
+ * rows: out[r, h] = the log-sum-exp merge of (prior_o[r, h], prior_lse[r, h])
+ * and this launch's state, with the arithmetic of pl_merge_states_strided
+ * over [prior, this], so the bf16 result equals writing this launch's fp32
+ * state and merging the two in a separate launch.  prior_o fp32 [batch,
+ * num_qo_heads, head_dim] contiguous, 16-byte aligned; prior_lse fp32
+ * [batch, num_qo_heads], natural log.  Used for the second pass of a
+ * shared-prefix decode (the rows' suffixes after the shared prefix), which
+ * the reference runs as one attention over repeated prefix pages
+ * (model/flashinfer/generation.py:872-1132).  bf16 out only.
+ */
+int32_t pl_paged_decode_merge_prior(const void *q, int64_t q_stride_b,
+                                    int64_t q_stride_h, const void *kv_cache,
+                                    int64_t num_pages, const int32_t *indptr,
+                                    const int32_t *indices,
+                                    const int32_t *last_page_len, int32_t batch,
+                                    int32_t num_qo_heads, int32_t num_kv_heads,
+                                    int32_t head_dim, int32_t page_size,
+                                    float sm_scale, int32_t num_splits,
+                                    void *out, int64_t o_stride_b,
+                                    int64_t o_stride_h, const float *prior_o,
+                                    const float *prior_lse, void *workspace,
+                                    int64_t workspace_bytes, int32_t *status_dev,
+                                    void *stream);
+
 /* ------------------------------------------------- split-KV peer exchange */
 /*
  * Split-KV decode over GPUs (one process per GPU): every GPU computes a

@@ -117,6 +117,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pl_decode_cluster_capacity": (_I32, [_I32, _I32, _I32]),
     "pl_merge_states": (_I32, [_P, _P, _I32, _I32, _I32, _P, _I64, _P, _P]),
     "pl_merge_states_strided": (_I32, [_P, _I64, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _I64, _P, _P]),
+    "pl_paged_decode_merge_prior": (
+        _I32,
+        [_P, _I64, _I64, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _I64, _P, _P, _P,
+         _I64, _P, _P],
+    ),
     "pl_ipc_handle_bytes": (_I32, []),
     "pl_ipc_export": (_I32, [_P, _P, POINTER(c_int64)]),
     "pl_ipc_import": (_I32, [_P, _I64, POINTER(c_void_p)]),

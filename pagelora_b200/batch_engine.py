@@ -65,10 +65,11 @@ class BatchDecodeEngine:
             raise ValueError("kv_shard must be (rank, world) with 0 <= rank < world")
         self.group = group
         self.owner = self.shard == self.world - 1
-        # Split-KV partial exchange: "nccl" (all-gather + merge launch) or
-        # "p2p" (pl_splitkv_exchange_merge over NVLink peer memory)
-        if exchange not in ("nccl", "p2p"):
-            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        # Split-KV partial exchange: "nccl" (all-gather + merge launch), "p2p"
+        # (pl_splitkv_exchange_merge over NVLink peer memory) or "auto" (p2p,
+        # and nccl on every rank when the peer mappings fail on any rank)
+        if exchange not in ("nccl", "p2p", "auto"):
+            raise ValueError("exchange must be 'nccl', 'p2p' or 'auto'")
         self.exchange = exchange
         self.peer = None
         self.device = torch.device(device)
@@ -192,10 +193,16 @@ class BatchDecodeEngine:
             self.part = torch.zeros(rows_h * (D + 1), device=dev, dtype=torch.float32)
             self.gathered = torch.zeros(self.world, rows_h * (D + 1), device=dev, dtype=torch.float32)
             self.dummy_page = self._alloc_page()  # append target of the shards that do not own the tail
-            if exchange == "p2p":
-                from pagelora_b200.peer_exchange import PeerExchange
+            if exchange in ("p2p", "auto"):
+                from pagelora_b200.peer_exchange import PeerExchange, PeerExchangeUnavailable
 
-                self.peer = PeerExchange(rows_h, D, group=group, device=dev)
+                try:
+                    self.peer = PeerExchange(rows_h, D, group=group, device=dev)
+                    self.exchange = "p2p"
+                except PeerExchangeUnavailable:
+                    if exchange == "p2p":
+                        raise
+                    self.exchange = "nccl"
         self.host_pages: list[list[int]] = [[] for _ in range(B)]
         self.host_last = [0] * B
         self.context_len = [0] * B
@@ -623,8 +630,8 @@ class BatchDecodeEngine:
         s, B = self.spec, self.rows
         lora = self.lora_rank > 0
         # q/k norm + RoPE + append + paged decode; with a shared prefix:
-        # RoPE + append, prefix pass, suffix pass, merge
-        per_layer = 4 if self.cascade is not None else 1
+        # RoPE + append, prefix pass, suffix pass (merging the prefix state)
+        per_layer = 3 if self.cascade is not None else 1
         if self.world > 1:
             per_layer += 1  # partial-state merge
         # q/k/v: with LoRA the norm and the shrink are one launch (up to 8192

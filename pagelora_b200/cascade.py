@@ -13,11 +13,14 @@ attention passes whose partial states are merged by log-sum-exp:
                16 for MHA);
   suffix pass  every row over its own pages (the branch suffix and the
                decoded tokens);
-  merge        pl_merge_states_strided over the two fp32 partials.
+  merge        the log-sum-exp merge of the two states, done by the suffix
+               pass as it writes its output.
 
 The prefix pass is pl_paged_decode_shared (the folding happens in the
 kernel's q staging and output addressing), the suffix pass
-pl_paged_decode_f32; three launches, no copies.
+pl_paged_decode_merge_prior (pl_merge_states_strided's arithmetic over
+[prefix, suffix], bit-identical to a separate merge launch); two launches,
+no copies.
 """
 
 from __future__ import annotations
@@ -59,9 +62,10 @@ class SharedPrefixDecode:
         self.pre_indices = torch.tensor(prefix_pages * self.Bv if n_pre else [0], **i32)
         self.pre_last = torch.full((self.Bv,), prefix_last_len if n_pre else 0, **i32)
         f32 = dict(device=dev, dtype=torch.float32)
-        # partial states: [2 passes][B*Hq] LSE and [2][B*Hq][D] O
-        self.o_parts = torch.zeros(2, self.B * self.Hq, self.D, **f32)
-        self.lse_parts = torch.zeros(2, self.B * self.Hq, **f32)
+        # the prefix pass's state, merged into the suffix pass's output:
+        # [1][B*Hq][D] O and [1][B*Hq] LSE
+        self.o_parts = torch.zeros(1, self.B * self.Hq, self.D, **f32)
+        self.lse_parts = torch.zeros(1, self.B * self.Hq, **f32)
         p_pre = K.decode_plan(self.Bv, self.Hkv * self.R * self.group, self.Hkv, self.D, page_size,
                               max(1, self.Bv * n_pre))
         p_suf = K.decode_plan(self.B, self.Hq, self.Hkv, self.D, page_size, max(1, self.B * max_suffix_pages))
@@ -78,12 +82,11 @@ class SharedPrefixDecode:
                               num_splits=self.splits_pre, workspace=self.ws_pre, status=status,
                               out=self.o_parts[0].view(self.B, self.Hq, self.D),
                               out_lse=self.lse_parts[0].view(self.B, self.Hq))
+        # the suffix pass merges the prefix pass's state into its output
+        # (the log-sum-exp merge of pl_merge_states_strided, no extra launch)
         K.paged_decode(q, kv_cache, suffix_indptr, suffix_indices, suffix_last_len, num_splits=self.splits_suf,
-                       workspace=self.ws_suf, status=status,
-                       out=self.o_parts[1].view(self.B, self.Hq, self.D),
-                       out_lse=self.lse_parts[1].view(self.B, self.Hq))
-        K.merge_states_strided(self.o_parts.permute(1, 0, 2), self.lse_parts.permute(1, 0),
-                               out.view(self.B * self.Hq, self.D))
+                       workspace=self.ws_suf, status=status, out=out,
+                       prior=(self.o_parts[0], self.lse_parts[0]))
         return out
 
     def prefix_bytes_per_layer(self) -> int:

@@ -72,6 +72,11 @@ struct DecodeArgs {
   float* partial_o;     // [batch, Hq, splits, D]
   float* partial_lse;   // [batch, Hq, splits] (log2 domain)
   int32_t* status;
+  // nullable: a prior state per (query row, head) -- O fp32 [rows][Hq][D],
+  // LSE [rows][Hq] (natural log) -- merged into the bf16 output with the
+  // arithmetic of merge_states_strided_kernel over [prior, this launch]
+  const float* prior_o;
+  const float* prior_lse;
 };
 
 template <int D, int PS, int NCW>
@@ -135,6 +140,35 @@ __global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(con
   const int mrows = group * args.fold;  // tile rows in use (<= 16)
   auto row_of = [&](int m) { return (int)blockIdx.z * args.fold + m / group; };
   auto head_of = [&](int m) { return kvh * group + m % group; };
+  // This launch's normalised output chunk v (LSE lse_nat, natural log)
+  // merged with the prior state of (orow, ohead): merge_states_strided's
+  // expressions over the states [prior, this], so the bf16 result equals the
+  // separate merge launch's.
+  auto with_prior = [&](int orow, int ohead, int d, float4 v, float lse_nat) -> float4 {
+    const int64_t rh = (int64_t)orow * args.num_qo_heads + ohead;
+    const float l0 = args.prior_lse[rh], l1 = lse_nat;
+    float M = -INFINITY;
+    M = fmaxf(M, l0);
+    M = fmaxf(M, l1);
+    float L = 0.f;
+    if (M != -INFINITY) {
+      L += expf(l0 - M);
+      L += expf(l1 - M);
+    }
+    const float4 p = *reinterpret_cast<const float4*>(args.prior_o + rh * D + d);
+    const float pv[4] = {p.x, p.y, p.z, p.w}, tv[4] = {v.x, v.y, v.z, v.w};
+    float r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float acc = 0.f;
+      if (M != -INFINITY) {
+        acc += expf(l0 - M) * pv[i];
+        acc += expf(l1 - M) * tv[i];
+      }
+      r[i] = L > 0.f ? acc / L : 0.f;
+    }
+    return make_float4(r[0], r[1], r[2], r[3]);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -512,11 +546,12 @@ __global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(con
       if (single) {
         if (live) {
           const int64_t oi = (int64_t)orow * args.o_stride_b + (int64_t)ohead * args.o_stride_h + d;
-          if (args.out_f32 != nullptr)
+          if (args.out_f32 != nullptr) {
             *reinterpret_cast<float4*>(args.out_f32 + oi) = val;
-          else
-            reinterpret_cast<uint2*>(args.out + oi)[0] =
-                make_uint2(pack_bf16x2(val.x, val.y), pack_bf16x2(val.z, val.w));
+          } else {
+            const float4 w = args.prior_o != nullptr ? with_prior(orow, ohead, d, val, lse2 * kLn2) : val;
+            reinterpret_cast<uint2*>(args.out + oi)[0] = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
+          }
           if (args.out_lse != nullptr && d == 0)
             args.out_lse[(int64_t)orow * args.num_qo_heads + ohead] = lse2 * kLn2;
         }
@@ -570,6 +605,7 @@ __global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(con
             L += wt;
           }
           inv_l[ctid] = L > 0.f ? 1.f / L : 0.f;
+          inv_l[mrows + ctid] = (L > 0.f) ? (M + log2f(L)) * kLn2 : -INFINITY;  // for a prior-state merge
           if (args.out_lse != nullptr && row_of(ctid) < args.rows_real)
             args.out_lse[(int64_t)row_of(ctid) * args.num_qo_heads + head_of(ctid)] =
                 (L > 0.f) ? (M + log2f(L)) * kLn2 : -INFINITY;
@@ -596,8 +632,9 @@ __global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(con
           if (args.out_f32 != nullptr) {
             *reinterpret_cast<float4*>(args.out_f32 + oi) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
           } else {
-            reinterpret_cast<uint2*>(args.out + oi)[0] = make_uint2(pack_bf16x2(acc.x * il, acc.y * il),
-                                                                     pack_bf16x2(acc.z * il, acc.w * il));
+            float4 w = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
+            if (args.prior_o != nullptr) w = with_prior(row_of(r), head_of(r), d, w, inv_l[mrows + r]);
+            reinterpret_cast<uint2*>(args.out + oi)[0] = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
           }
         }
         if (ctid == 0) args.counters[b * args.num_kv_heads + kvh] = 0;
@@ -649,8 +686,10 @@ __global__ void __launch_bounds__(decode_threads<NCW>()) paged_decode_kernel(con
       if (args.out_f32 != nullptr) {
         *reinterpret_cast<float4*>(args.out_f32 + oi) = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
       } else {
-        reinterpret_cast<uint2*>(args.out + oi)[0] =
-            make_uint2(pack_bf16x2(acc.x * il, acc.y * il), pack_bf16x2(acc.z * il, acc.w * il));
+        float4 w = make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
+        if (args.prior_o != nullptr)
+          w = with_prior(row_of(r), head_of(r), d, w, L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY);
+        reinterpret_cast<uint2*>(args.out + oi)[0] = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
       }
       if (args.out_lse != nullptr && d == 0)
         args.out_lse[(int64_t)row_of(r) * args.num_qo_heads + head_of(r)] =
@@ -922,8 +961,12 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                           int64_t workspace_bytes, int32_t* status_dev, void* stream,
                           const pl::QkvHeadArgs* fused = nullptr, const int32_t* slot_page = nullptr,
                           const int32_t* slot_off = nullptr, void* q_out = nullptr, int fold = 1,
-                          int64_t counter_bytes = 0) {
+                          int64_t counter_bytes = 0, const float* prior_o = nullptr,
+                          const float* prior_lse = nullptr) {
   if (batch == 0) return PL_OK;
+  if ((prior_o == nullptr) != (prior_lse == nullptr) ||
+      (prior_o != nullptr && (out_is_f32 || (reinterpret_cast<uintptr_t>(prior_o) & 15))))
+    return PL_ERR_INVALID_ARGUMENT;
   if (fused != nullptr) {  // q comes from the projection row: validate that instead
     if (fused->qkv == nullptr || fused->positions == nullptr || slot_page == nullptr || slot_off == nullptr ||
         (fused->down != nullptr && fused->lora_b != nullptr && fused->rank <= 0) ||
@@ -996,6 +1039,8 @@ int32_t paged_decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_h,
     a.partial_lse = reinterpret_cast<float*>(ws + c_bytes + o_bytes);
   }
   a.status = status_dev;
+  a.prior_o = prior_o;
+  a.prior_lse = prior_lse;
 
   if (head_dim == 128 && page_size == 16) return launch_decode<128, 16>(map, a, vrows, num_kv_heads, num_splits, stream);
   if (head_dim == 128 && page_size == 32) return launch_decode<128, 32>(map, a, vrows, num_kv_heads, num_splits, stream);
@@ -1040,6 +1085,21 @@ extern "C" int32_t pl_paged_decode_shared(const void* q, int64_t q_stride_b, int
                            num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out,
                            (flags & PL_DECODE_OUT_F32) != 0, o_stride_b, o_stride_h, out_lse, workspace,
                            workspace_bytes, status_dev, stream, nullptr, nullptr, nullptr, nullptr, fold);
+}
+
+extern "C" int32_t pl_paged_decode_merge_prior(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                               const void* kv_cache, int64_t num_pages, const int32_t* indptr,
+                                               const int32_t* indices, const int32_t* last_page_len, int32_t batch,
+                                               int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+                                               int32_t page_size, float sm_scale, int32_t num_splits, void* out,
+                                               int64_t o_stride_b, int64_t o_stride_h, const float* prior_o,
+                                               const float* prior_lse, void* workspace, int64_t workspace_bytes,
+                                               int32_t* status_dev, void* stream) {
+  if (prior_o == nullptr || prior_lse == nullptr) return PL_ERR_INVALID_ARGUMENT;
+  return paged_decode_impl(q, q_stride_b, q_stride_h, kv_cache, num_pages, indptr, indices, last_page_len, batch,
+                           num_qo_heads, num_kv_heads, head_dim, page_size, sm_scale, num_splits, out, false,
+                           o_stride_b, o_stride_h, nullptr, workspace, workspace_bytes, status_dev, stream, nullptr,
+                           nullptr, nullptr, nullptr, 1, 0, prior_o, prior_lse);
 }
 
 extern "C" int32_t pl_paged_decode_qkv(const void* qkv, int64_t qkv_stride, const float* lora_down,

@@ -108,9 +108,12 @@ def paged_decode(
     sm_scale: float | None = None,
     out: torch.Tensor | None = None,
     out_lse: torch.Tensor | None = None,
+    prior: tuple[torch.Tensor, torch.Tensor] | None = None,
 ) -> torch.Tensor:
     """Paged decode attention: q [B, Hq, D] bf16, kv_cache [P, 2, PS, Hkv, D] bf16;
-    ``out`` bf16, or fp32 for a split-KV shard's partial state."""
+    ``out`` bf16, or fp32 for a split-KV shard's partial state.  ``prior`` =
+    (O fp32 [B, Hq, D], LSE [B, Hq] natural log): a state merged into the
+    bf16 output (pl_paged_decode_merge_prior)."""
 
     _need_cuda(q, kv_cache, indptr, indices, last_page_len)
     _need(q, torch.bfloat16, "q")
@@ -129,6 +132,17 @@ def paged_decode(
         out = torch.empty_like(q)
     scale = (1.0 / math.sqrt(d)) if sm_scale is None else float(sm_scale)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    if prior is not None:
+        po, pl = prior
+        if (out.dtype != torch.bfloat16 or out_lse is not None or po.dtype != torch.float32 or
+                pl.dtype != torch.float32 or not po.is_contiguous() or not pl.is_contiguous() or
+                po.numel() < batch * hq * d or pl.numel() < batch * hq):
+            raise ValueError("prior needs contiguous fp32 [B, Hq, D] / [B, Hq] states and a bf16 out without out_lse")
+        call("pl_paged_decode_merge_prior", ptr(q), q.stride(0), q.stride(1), ptr(kv_cache), int(num_pages),
+             ptr(indptr), ptr(indices), ptr(last_page_len), int(batch), int(hq), int(hkv), int(d), int(page_size),
+             scale, int(num_splits), ptr(out), out.stride(0), out.stride(1), ptr(po), ptr(pl), ptr(workspace),
+             int(ws_bytes), ptr(status), stream_handle())
+        return out
     fn = "pl_paged_decode_f32" if out.dtype == torch.float32 else "pl_paged_decode"
     call(fn, ptr(q), q.stride(0), q.stride(1), ptr(kv_cache), int(num_pages), ptr(indptr),
          ptr(indices), ptr(last_page_len), int(batch), int(hq), int(hkv), int(d), int(page_size), scale,

@@ -24,6 +24,10 @@ from pagelora_b200 import _capi
 from pagelora_b200._capi import call, ptr, stream_handle
 
 
+class PeerExchangeUnavailable(RuntimeError):
+    """The peer mappings could not be set up on every rank (raised on all of them)."""
+
+
 class PeerExchange:
     """Per-GPU state of the peer exchange for partials of ``rows_h`` rows of
     ``head_dim``; every rank of ``group`` constructs one with the same shape,
@@ -50,11 +54,15 @@ class PeerExchange:
         # Swap (handle, offset) of both buffers with every rank.
         hb = int(lib.pl_ipc_handle_bytes())
         mine = []
-        for t in (self.gather, self.flags):
-            h = (ctypes.c_uint8 * hb)()
-            off = ctypes.c_int64(0)
-            call("pl_ipc_export", ptr(t), h, ctypes.byref(off))
-            mine.append((bytes(h), off.value))
+        error = None
+        try:
+            for t in (self.gather, self.flags):
+                h = (ctypes.c_uint8 * hb)()
+                off = ctypes.c_int64(0)
+                call("pl_ipc_export", ptr(t), h, ctypes.byref(off))
+                mine.append((bytes(h), off.value))
+        except Exception as e:  # noqa: BLE001 - every rank still joins the collectives below
+            error, mine = e, [(bytes(hb), 0), (bytes(hb), 0)]
         blob = torch.zeros(2 * (hb + 8), dtype=torch.uint8)
         for i, (h, off) in enumerate(mine):
             blob[i * (hb + 8): i * (hb + 8) + hb] = torch.frombuffer(bytearray(h), dtype=torch.uint8)
@@ -67,6 +75,8 @@ class PeerExchange:
         self._opened: list[tuple[int, int]] = []  # (mapped pointer, offset) to close
         gptrs, fptrs = [], []
         try:
+            if error is not None:
+                raise error
             for p in range(self.world):
                 if p == self.rank:
                     gptrs.append(ptr(self.gather))
@@ -81,9 +91,14 @@ class PeerExchange:
                     call("pl_ipc_import", h, off, ctypes.byref(out))
                     self._opened.append((out.value, off))
                     dst.append(out.value)
-        except Exception:
+        except Exception as e:  # noqa: BLE001 - reported on every rank below
+            error = e
+        # every rank learns whether all of them mapped their peers
+        ok = torch.tensor([0 if error is not None else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
             self.close()
-            raise
+            raise PeerExchangeUnavailable(f"peer mappings failed on some rank ({error or 'another rank'})")
         self.peer_gather = torch.tensor(gptrs, dtype=torch.int64, device=dev)
         self.peer_flags = torch.tensor(fptrs, dtype=torch.int64, device=dev)
         torch.cuda.synchronize(dev)

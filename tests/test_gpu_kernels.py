@@ -301,6 +301,50 @@ def test_paged_decode_qkv_matches_rope_then_decode(K, d, hq, hkv, qk_norm):
                                                                    workspace=ws))[0], atol=2 ** -7 * 4)
 
 
+@pytest.mark.parametrize("cluster", [True, False])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 16)])
+def test_paged_decode_merge_prior_equals_separate_merge(K, hq, hkv, cluster):
+    """pl_paged_decode_merge_prior: merging a prior state into the bf16 output
+    gives the same bits as writing this launch's fp32 state and merging the
+    two with pl_merge_states_strided, for one split, the cluster merge and
+    the workspace merge; rows with no pages take the prior state alone."""
+
+    from pagelora_b200._capi import load_library
+
+    lib = load_library()
+    g = torch.Generator(device="cuda").manual_seed(hq + hkv)
+    d, ps = 128, 16
+    lens = [0, 5, 40, 300]
+    b = len(lens)
+    pages = [-(-n // ps) for n in lens]
+    pool = sum(pages) + 3
+    cache = torch.randn(pool, 2, ps, hkv, d, generator=g, device="cuda").bfloat16()
+    perm = torch.randperm(pool, generator=g, device="cuda")[: sum(pages)].to(torch.int32)
+    indptr = _i32(np.cumsum([0] + pages))
+    last = _i32([n - (p - 1) * ps if p else 0 for n, p in zip(lens, pages)])
+    q = torch.randn(b, hq, d, generator=g, device="cuda").bfloat16()
+    prior_o = torch.randn(b, hq, d, generator=g, device="cuda")
+    prior_lse = torch.randn(b, hq, generator=g, device="cuda") * 3
+    ws = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+    assert lib.pl_decode_set_cluster_merge(1 if cluster else 0) == 0
+    try:
+        for splits in (1, 3, 8):
+            o32 = torch.empty(b, hq, d, device="cuda")
+            lse = torch.empty(b, hq, device="cuda")
+            K.paged_decode(q, cache, indptr, perm, last, num_splits=splits, workspace=ws, out=o32, out_lse=lse)
+            ref = torch.empty(b * hq, d, dtype=torch.bfloat16, device="cuda")
+            K.merge_states_strided(torch.stack([prior_o.view(b * hq, d), o32.view(b * hq, d)], 1),
+                                   torch.stack([prior_lse.view(-1), lse.view(-1)], 1), ref)
+            got = K.paged_decode(q, cache, indptr, perm, last, num_splits=splits, workspace=ws,
+                                 out=torch.empty(b, hq, d, dtype=torch.bfloat16, device="cuda"),
+                                 prior=(prior_o, prior_lse))
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(b * hq, d), ref), splits
+            assert torch.equal(got[0].float(), prior_o[0].bfloat16().float())  # no pages: the prior alone
+    finally:
+        assert lib.pl_decode_set_cluster_merge(1) == 0
+
+
 @pytest.mark.parametrize("rows,hq,hkv,fold", [(7, 32, 8, 4), (5, 16, 16, 16), (6, 8, 2, 3)])
 def test_paged_decode_shared_folded_rows(K, rows, hq, hkv, fold):
     """Rows folded onto shared page-table rows (fold x group tile rows) equal
