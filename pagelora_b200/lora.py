@@ -88,6 +88,16 @@ def _gemm_workspace(device: torch.device, tokens: int, k_in: int, n_out: int) ->
     return ws
 
 
+def _shrink(x2: torch.Tensor, a_stack: torch.Tensor) -> torch.Tensor:
+    """x2 . A^T (fp32) for one adapter: the row kernel (one CTA per token and
+    4 rank rows) up to 8192 input features, the segment kernel beyond."""
+
+    if x2.shape[1] <= K.SHRINK_ROWS_MAX_K and x2.shape[1] % 8 == 0:
+        return K.lora_shrink_rows(x2, a_stack)
+    seg_indptr, seg_adapter = _single_segment(x2.device, x2.shape[0])
+    return K.lora_shrink_seg(x2, a_stack, seg_indptr, seg_adapter)
+
+
 def _kernel_kind(x2: torch.Tensor, k_in: int) -> str | None:
     """Which kernel projects the rows of ``x2`` [T, K]: "gemv", "gemm" or None (torch)."""
 
@@ -256,8 +266,7 @@ class LoRALinear(nn.Module):
         if self.serve_a is None or self.serve_b is None:
             raise RuntimeError("serve mode active without bound serve parameters")
         a = self.serve_a.detach().contiguous()
-        seg_indptr, seg_adapter = _single_segment(x.device, x2.shape[0])
-        down = K.lora_shrink_seg(x2, a.unsqueeze(0), seg_indptr, seg_adapter)
+        down = _shrink(x2, a.unsqueeze(0))
         if return_lora_down:
             base = _project(kind, x2, w, bias=self.bias).view(*shape[:-1], self.out_features)
             return base, down.to(x.dtype).view(*shape[:-1], -1)
@@ -492,8 +501,7 @@ def _project_group(group: PackedGroup, modules: tuple, hidden: torch.Tensor) -> 
     ends = tuple(itertools.accumulate(dims[:-1]))
     packed_delta = _env_enabled("MINI_OPENCLAW_FLASHINFER_PACKED_LORA_DELTA", default=True)
     if group.a_cat is not None and packed_delta and len(dims) <= 4:
-        seg_indptr, seg_adapter = _single_segment(x2.device, x2.shape[0])
-        down = K.lora_shrink_seg(x2, group.a_cat.unsqueeze(0), seg_indptr, seg_adapter)
+        down = _shrink(x2, group.a_cat.unsqueeze(0))
         out = _project(kind, x2, group.weight, bias=group.bias, lora_down=down, lora_b=group.b_cat,
                        slice_ends=ends)
         return tuple(torch.split(out.view(*shape[:-1], -1), dims, dim=-1))
