@@ -50,7 +50,8 @@ class PeerExchange:
         self.gather = torch.zeros(2, self.world, self.slot, device=dev, dtype=torch.float32)
         self.flags = torch.zeros(self.world, self.ctas, device=dev, dtype=torch.int32)
         self.epochs = torch.zeros(self.ctas, device=dev, dtype=torch.int32)
-        torch.cuda.synchronize(dev)
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
         # Swap (handle, offset) of both buffers with every rank.
         hb = int(lib.pl_ipc_handle_bytes())
         mine = []
@@ -69,9 +70,9 @@ class PeerExchange:
             blob[i * (hb + 8) + hb: (i + 1) * (hb + 8)] = torch.frombuffer(
                 bytearray(off.to_bytes(8, "little", signed=True)), dtype=torch.uint8)
         send = blob.to(dev)
-        recv = torch.zeros(self.world, send.numel(), dtype=torch.uint8, device=dev)
+        recv = torch.zeros(self.world * send.numel(), dtype=torch.uint8, device=dev)
         dist.all_gather_into_tensor(recv, send, group=group)
-        recv = recv.cpu()
+        recv = recv.cpu().view(self.world, send.numel())
         self._opened: list[tuple[int, int]] = []  # (mapped pointer, offset) to close
         gptrs, fptrs = [], []
         try:
@@ -101,7 +102,8 @@ class PeerExchange:
             raise PeerExchangeUnavailable(f"peer mappings failed on some rank ({error or 'another rank'})")
         self.peer_gather = torch.tensor(gptrs, dtype=torch.int64, device=dev)
         self.peer_flags = torch.tensor(fptrs, dtype=torch.int64, device=dev)
-        torch.cuda.synchronize(dev)
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
     def merge(self, part: torch.Tensor, out: torch.Tensor, status: torch.Tensor | None = None) -> torch.Tensor:
